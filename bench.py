@@ -1,0 +1,361 @@
+"""Benchmark: Q4_K decode matvec weight GB/s on B200 (Llama-3-8B FFN-down layer).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--act x16|x8] [--copies C]
+
+Workload (n x k = 4096 x 14336, the "4096x14336-class" Llama-3-8B down
+projection, Q4_K, 33,030,144 weight bytes): one step = C matvecs, each over a
+distinct resident copy of the weights (C * 33 MB > 2 x the 126 MB L2, so every
+step streams its weights from HBM), x ~ N(0, 1) fp32, W ~ N(0, 0.02) packed to
+Q4_K. value = weight bytes / device time (GB/s), all ranks summed; each rank
+runs the same per-GPU work (weak scaling, no collective on the data path).
+
+Rank 0 prints one JSON line. `--impl reference` times the reference engine's
+own CPU op (oracle/_ref/libref_qm.so, compiled from its sources) on the host
+cores over a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+N_ROWS, K_DIM = 4096, 14336
+QT_Q4_K = 12
+METRIC = "Q4_K matvec weight GB/s (4096x14336 Llama-3-8B FFN-down layer)"
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def _weights(seed: int = 0) -> np.ndarray:
+    from cybel_b200 import quantize as Q
+
+    rng = np.random.default_rng(seed)
+    w = rng.normal(0.0, 0.02, size=(N_ROWS, K_DIM)).astype(np.float32)
+    return Q.quantize_q4_k(w)
+
+
+def _peak_hbm():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def _traffic_per_launch():
+    p = ROOT / "profiles" / "gemv_q4k_4096x14336_traffic.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+        except Exception:
+            return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, device: int):
+        self.device = device
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
+                    capture_output=True, text=True, timeout=5,
+                ).stdout.strip()
+                if out:
+                    self.samples.append([s.strip() for s in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 5 + i and s[5 + i] == "Active"})
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons,
+            "samples": len(self.samples),
+        }
+
+
+def _cpu_reference_sample(W: np.ndarray, x: np.ndarray, budget_s: float = 12.0):
+    """The reference's compiled simd_matvec_q4k on the host cores: GB/s."""
+    from oracle import oracle as O
+
+    threads = len(os.sched_getaffinity(0))
+    if O.ref_available():
+        os.environ["ANVIL_NUM_THREADS"] = str(threads)
+        O.ref_matvec(QT_Q4_K, W, x, K_DIM, N_ROWS)  # warm-up
+        calls, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget_s or calls < 3:
+            O.ref_matvec(QT_Q4_K, W, x, K_DIM, N_ROWS)
+            calls += 1
+        dt = time.perf_counter() - t0
+        return {
+            "value": round(W.nbytes * calls / dt / 1e9, 3),
+            "unit": "GB/s",
+            "cores": threads,
+            "kind": "reference",
+            "sample": f"{calls} x simd_matvec_q4k {N_ROWS}x{K_DIM} (one weight copy) in {dt:.1f} s, ANVIL_NUM_THREADS={threads}",
+        }
+    # Fallback: the oracle's scalar restatement, single thread.
+    n_rows = 256
+    Ws = np.ascontiguousarray(W[:n_rows])
+    calls, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or calls < 1:
+        O.matvec_f64(Ws, QT_Q4_K, x, K_DIM, n_rows)
+        calls += 1
+    dt = time.perf_counter() - t0
+    return {
+        "value": round(Ws.nbytes * calls / dt / 1e9, 3),
+        "unit": "GB/s",
+        "cores": 1,
+        "kind": "port",
+        "sample": f"{calls} x oracle matvec of {n_rows} rows of the {N_ROWS}x{K_DIM} layer in {dt:.1f} s",
+    }
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    W = _weights()
+    x = np.random.default_rng(1).standard_normal(K_DIM).astype(np.float32)
+    samples = []
+    for _ in range(args.warmup):
+        _cpu_reference_sample(W, x, budget_s=0.5)
+    for _ in range(args.steps):
+        samples.append(_cpu_reference_sample(W, x, budget_s=2.0))
+    vals = [s["value"] for s in samples]
+    v = float(np.mean(vals))
+    base = samples[-1]
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(v, 3),
+        "unit": "GB/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(W.nbytes * args.copies / (v * 1e9) * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"q4k_matvec_{N_ROWS}x{K_DIM}", "copies": args.copies, "l2": "inputs > L2"},
+        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": base["cores"], "kind": base["kind"],
+                         "sample": base["sample"]},
+        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+
+    from cybel_b200 import _native
+    from cybel_b200.quantized_matmul import DeviceMatrix, QuantizedMatrix, matmul_device
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    act = _native.ACT_X8 if args.act == "x8" else _native.ACT_X16
+    W = _weights()
+    x = np.random.default_rng(1).standard_normal(K_DIM).astype(np.float32)
+    C = args.copies
+    mats = [DeviceMatrix(QT_Q4_K, K_DIM, N_ROWS, W) for _ in range(C)]
+    xt = torch.from_numpy(x).to(dev)
+    ys = [torch.empty(N_ROWS, dtype=torch.float32, device=dev) for _ in range(C)]
+    if args.pdl:
+        _native.lib().b200q_set_pdl(1)
+
+    def step():
+        for i in range(C):
+            matmul_device(xt, mats[i], out=ys[i], act_mode=act)
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        e0.record(st)
+        for _ in range(args.steps):
+            step()
+        e1.record(st)
+        barrier()
+    ms_total = e0.elapsed_time(e1)
+    # Per-launch kernel duration (events around each launch, same stream).
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(4 * C)]
+    for j, (a, b) in enumerate(evs):
+        a.record(st)
+        matmul_device(xt, mats[j % C], out=ys[j % C], act_mode=act)
+        b.record(st)
+    torch.cuda.synchronize(dev)
+    launch_ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+
+    t = torch.tensor([ms_total, launch_ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms_total, launch_ms = float(t[0]), float(t[1])
+
+    # End to end through the public drop-in (host buffers, pinned).
+    qms = [QuantizedMatrix(name=f"w{i}", qtype=QT_Q4_K, shape=(K_DIM, N_ROWS), data=W.copy()) for i in range(C)]
+    xh = torch.from_numpy(x).pin_memory().numpy()
+    yh = torch.empty(N_ROWS, dtype=torch.float32).pin_memory().numpy()
+    import ctypes
+
+    L = _native.lib()
+    L.b200q_set_act_mode(act)
+    fp = ctypes.POINTER(ctypes.c_float)
+    xp, yp = xh.ctypes.data_as(fp), yh.ctypes.data_as(fp)
+    ptrs = [q.ensure_packed().ctypes.data for q in qms]
+
+    def e2e_step():
+        for i in range(C):
+            L.simd_matvec_q4k(xp, ptrs[i], yp, K_DIM, N_ROWS)
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    assert L.b200q_last_error() == 0, L.b200q_last_error()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if ws > 1:
+        torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+    e2e_s = float(te[0])
+    L.b200q_weight_cache_clear()
+
+    wbytes = W.nbytes
+    value = ws * wbytes * C * args.steps / (ms_total / 1e3) / 1e9
+    e2e_val = ws * wbytes * C * args.steps / e2e_s / 1e9
+    peak, peak_kind = _peak_hbm()
+    achieved = wbytes / (launch_ms / 1e3) / 1e9
+    cpu = _cpu_reference_sample(W, x) if (rank == 0 and ws == 1 and not args.no_cpu) else None
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": ws,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_total / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int8 dp4a (x8)" if act == _native.ACT_X8 else "int16-in-int8x2 dp4a (x16)",
+            "data": "synthetic",
+            "config": {
+                "workload": f"q4k_matvec_{N_ROWS}x{K_DIM}",
+                "weight_bytes_per_matvec": wbytes,
+                "copies_per_step": C,
+                "l2": f"inputs > L2 ({C} distinct weight copies, {C * wbytes / 1e6:.0f} MB per step)",
+                "act_mode": args.act,
+                "pdl": bool(args.pdl),
+            },
+            "roofline": {
+                "bound": "hbm",
+                "achieved": round(achieved, 1),
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4),
+                "peak_source": peak_kind,
+                "traffic": _traffic_per_launch(),
+                "kernel_ms": round(launch_ms, 5),
+            },
+            "e2e": {
+                "value": round(e2e_val, 2),
+                "unit": "GB/s",
+                "h2d_bytes_per_step": C * K_DIM * 4,
+                "d2h_bytes_per_step": C * N_ROWS * 4,
+            },
+            "gpu_launches": C * args.steps,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--act", default="x8", choices=["x8", "x16"])
+    ap.add_argument("--copies", type=int, default=8)
+    ap.add_argument("--pdl", type=int, default=0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    ws, rank, local = _dist()
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+        return
+    run_ours(args, ws, rank, local)
+
+
+if __name__ == "__main__":
+    main()

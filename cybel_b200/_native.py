@@ -1,0 +1,86 @@
+"""Loader for libb200q.so (the sm_100a kernels behind the C ABI in
+include/b200q.h).
+
+There is no CPU fallback: if the library is missing or cannot be loaded,
+``lib()`` raises. Build it with ``python -m cybel_b200.build``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libb200q.so"
+
+ACT_X8 = 1
+ACT_X16 = 2
+
+STATUS = {
+    0: "ok",
+    -1: "invalid argument",
+    -2: "unsupported qtype",
+    -3: "unsupported shape",
+    -4: "pointer not 16-byte aligned",
+    -5: "CUDA runtime error",
+    -6: "device allocation failed",
+    -7: "kernel pipeline wait timed out",
+    -8: "no usable sm_100 device",
+}
+
+# Every symbol include/b200q.h declares: (name, argtypes, restype).
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_fp = ctypes.POINTER(ctypes.c_float)
+SIGNATURES: dict[str, tuple[list, object]] = {}
+for _q in ("q4k", "q4k_r4", "q6k", "q6k_r4", "q6k_lm", "q8_0", "q4_0"):
+    SIGNATURES[f"simd_matvec_{_q}"] = ([_fp, _vp, _fp, _i, _i], None)
+for _q in ("q4k", "q4k_r4", "q6k", "q6k_r4", "q8_0", "q4_0"):
+    SIGNATURES[f"simd_matmul_{_q}"] = ([_fp, _vp, _fp, _i, _i, _i], None)
+SIGNATURES.update(
+    {
+        "b200q_matmul": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
+        "b200q_matvec_isums": ([_i, _i, _vp, _vp, _vp, _vp, _i, _i, _vp], _i),
+        "b200q_set_act_mode": ([_i], _i),
+        "b200q_get_act_mode": ([], _i),
+        "b200q_last_error": ([], _i),
+        "b200q_status_string": ([_i], ctypes.c_char_p),
+        "b200q_device_status": ([_i], _i),
+        "b200q_weight_cache_clear": ([], None),
+        "b200q_weight_cache_evict": ([_vp], _i),
+        "b200q_weight_cache_bytes": ([], ctypes.c_longlong),
+        "b200q_set_pdl": ([_i], _i),
+        "b200q_version": ([], ctypes.c_char_p),
+    }
+)
+
+_LIB: ctypes.CDLL | None = None
+
+
+class NativeError(RuntimeError):
+    """A libb200q entry point returned a non-zero status."""
+
+    def __init__(self, status: int, what: str = ""):
+        self.status = int(status)
+        super().__init__(f"{what}: {STATUS.get(self.status, 'unknown status')} ({self.status})")
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH} is missing: build the CUDA library with `python -m cybel_b200.build` "
+                "(there is no CPU fallback)"
+            )
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _LIB = L
+    return _LIB
+
+
+def check(status: int, what: str) -> None:
+    if int(status) != 0:
+        raise NativeError(status, what)

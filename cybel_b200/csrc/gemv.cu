@@ -1,0 +1,180 @@
+// Launch planning and dispatch for the decode GEMV kernels (gemv.cuh).
+#include <algorithm>
+#include <mutex>
+
+#include "gemv.cuh"
+#include "internal.h"
+
+namespace b200q {
+
+bool fmt_info(int qtype, FmtInfo& f) {
+    switch (qtype) {
+        case QT_Q4_K: f = {256, 144, 4, 8, 32, false}; return true;
+        case QT_Q4_K_R4: f = {256, 144, 4, 8, 32, true}; return true;
+        case QT_Q6_K: f = {256, 210, 8, 4, 16, false}; return true;
+        case QT_Q6_K_R4: f = {256, 210, 8, 4, 16, true}; return true;
+        case QT_Q6_K_LM: f = {256, 276, 8, 4, 16, false}; return true;
+        case QT_Q8_0: f = {32, 34, 1, 32, 32, false}; return true;
+        case QT_Q4_0: f = {32, 18, 1, 32, 32, false}; return true;
+        default: return false;
+    }
+}
+
+long long row_bytes_of(int qtype, int k) {
+    FmtInfo f;
+    if (!fmt_info(qtype, f) || k <= 0 || k % f.elems) return -1;
+    return static_cast<long long>(k / f.elems) * f.bytes;
+}
+
+namespace {
+
+constexpr int kStageTarget = 24 * 1024;   // preferred bytes per stage
+constexpr int kStageMax = 64 * 1024;      // largest stage
+constexpr int kSmemBudget = 200 * 1024;   // ring + bookkeeping per CTA
+constexpr int kMaxStages = 8;
+
+struct Plan {
+    GemvParams p;
+    int threads;
+    int smem;
+    int grid;
+};
+
+int make_plan(int qtype, int k, int n, int MR, int num_sms, Plan& pl) {
+    FmtInfo f;
+    if (!fmt_info(qtype, f)) return B200Q_EQTYPE;
+    if (k <= 0 || n <= 0) return B200Q_EINVAL;
+    if (k % f.elems) return B200Q_ESHAPE;
+    const int nb = k / f.elems;
+    const long long rb = static_cast<long long>(nb) * f.bytes;
+    const int S = (nb + f.blocks_per_slice - 1) / f.blocks_per_slice;
+    if (S > kGemvMaxConsumerWarps) return B200Q_ESHAPE;
+    const int WR = std::max(1, kGemvMaxConsumerWarps / S);
+    int R, step;
+    if (f.r4) {
+        R = ((WR + 3) / 4) * 4;
+        step = 4;
+    } else {
+        R = WR;
+        step = WR;
+    }
+    // A stage copies the 16-byte-aligned window around its rows: at most
+    // rows * rb + 30 bytes; kSlotPad also covers the 4-byte over-read of the
+    // unaligned word loads.
+    constexpr int kSlotPad = 48;
+    while ((R + step) * rb + kSlotPad <= kStageTarget) R += step;
+    if (R * rb + kSlotPad > kStageMax) {
+        if (f.r4) return B200Q_ESHAPE;
+        R = std::max<int>(1, static_cast<int>((kStageMax - kSlotPad) / rb));
+        if (R * rb + kSlotPad > kStageMax) return B200Q_ESHAPE;
+    }
+    const int stage_stride = static_cast<int>(((R * rb + kSlotPad) + 127) / 128 * 128);
+    const int part_bytes = 2 * R * MR * S * 4;
+    int NS = (kSmemBudget - part_bytes - 64) / (stage_stride + 16);
+    NS = std::min(kMaxStages, NS);
+    if (NS < 2) return B200Q_ESHAPE;
+    GemvParams& p = pl.p;
+    p = GemvParams{};
+    p.row_bytes = rb;
+    p.k = k;
+    p.n = n;
+    p.nb = nb;
+    p.S = S;
+    p.WR = WR;
+    p.R = R;
+    p.NS = NS;
+    p.stage_stride = stage_stride;
+    p.n_quads = (n + 3) / 4;
+    pl.threads = (S * WR + 1) * 32;
+    pl.smem = NS * stage_stride + 2 * NS * 8 + part_bytes + 16;
+    pl.grid = std::min(num_sms, p.n_quads);
+    return B200Q_OK;
+}
+
+template <int QT, int DIG, int MR, bool DBG>
+cudaError_t launch_kernel(const Plan& pl, cudaStream_t st, bool pdl) {
+    auto kern = gemv_kernel<QT, DIG, MR, DBG>;
+    // Raise the dynamic shared-memory limit once per kernel instance (the
+    // attribute is per function; the largest plan is set).
+    static std::mutex mu;
+    static int configured = 0;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (pl.smem > configured) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+            if (e != cudaSuccess) return e;
+            configured = 227 * 1024;
+        }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(pl.grid);
+    cfg.blockDim = dim3(pl.threads);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kern, pl.p);
+}
+
+template <int QT>
+cudaError_t dispatch_qt(int dig, int MR, bool dbg, const Plan& pl, cudaStream_t st, bool pdl) {
+    if (dbg) return dig == 1 ? launch_kernel<QT, 1, 1, true>(pl, st, pdl) : launch_kernel<QT, 2, 1, true>(pl, st, pdl);
+    if (dig == 1) {
+        if (MR == 4) return launch_kernel<QT, 1, 4, false>(pl, st, pdl);
+        if (MR == 2) return launch_kernel<QT, 1, 2, false>(pl, st, pdl);
+        return launch_kernel<QT, 1, 1, false>(pl, st, pdl);
+    }
+    if (MR == 2) return launch_kernel<QT, 2, 2, false>(pl, st, pdl);
+    return launch_kernel<QT, 2, 1, false>(pl, st, pdl);
+}
+
+cudaError_t dispatch(int qtype, int dig, int MR, bool dbg, const Plan& pl, cudaStream_t st, bool pdl) {
+    switch (qtype) {
+        case QT_Q4_K: return dispatch_qt<QT_Q4_K>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q4_K_R4: return dispatch_qt<QT_Q4_K_R4>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q6_K: return dispatch_qt<QT_Q6_K>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q6_K_R4: return dispatch_qt<QT_Q6_K_R4>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q6_K_LM: return dispatch_qt<QT_Q6_K_LM>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q8_0: return dispatch_qt<QT_Q8_0>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q4_0: return dispatch_qt<QT_Q4_0>(dig, MR, dbg, pl, st, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+int launch_gemv(int qtype, int act_mode, const void* w, const float* x, float* y, int m, int k, int n,
+                long long x_stride, long long y_stride, int32_t* isums, Device* dev, cudaStream_t st, bool pdl) {
+    if (!w || !x || !y || m <= 0 || k <= 0 || n <= 0 || !dev) return B200Q_EINVAL;
+    if (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(w) & 15u) || (reinterpret_cast<uintptr_t>(x) & 15u) || (x_stride & 3))
+        return B200Q_EALIGN;
+    if (isums && m != 1) return B200Q_EINVAL;
+    const int dig = act_mode == B200Q_ACT_X8 ? 1 : 2;
+    const int mr_max = dig == 1 ? 4 : 2;
+    for (int m0 = 0; m0 < m;) {
+        const int left = m - m0;
+        const int MR = isums ? 1 : (left >= mr_max ? mr_max : (left >= 2 ? 2 : 1));
+        Plan pl;
+        int rc = make_plan(qtype, k, n, MR, dev->num_sms, pl);
+        if (rc != B200Q_OK) return rc;
+        pl.p.W = static_cast<const uint8_t*>(w);
+        pl.p.x = x + m0 * x_stride;
+        pl.p.y = y + m0 * y_stride;
+        pl.p.x_stride = x_stride;
+        pl.p.y_stride = y_stride;
+        pl.p.dbg = isums;
+        pl.p.status = dev->status;
+        cudaError_t e = dispatch(qtype, dig, MR, isums != nullptr, pl, st, pdl);
+        if (e != cudaSuccess) return B200Q_ECUDA;
+        m0 += MR;
+    }
+    return B200Q_OK;
+}
+
+}  // namespace b200q

@@ -1,0 +1,130 @@
+/*
+ * b200q.h -- C ABI of libb200q.so, the B200 (sm_100a) GGUF dequant-matvec.
+ *
+ * Two groups of entry points:
+ *
+ * 1. Drop-in replacements, with the exact names, signatures, argument
+ *    meaning and error behaviour of the reference engine's CPU kernels
+ *    (Team-Ferrous/Cybel, JSBuild/src/verso/Anvil/core/native/
+ *    quantized_matmul.cpp, "QM" below). Pointers are HOST pointers, as in
+ *    the reference: x is copied in, y copied out, and the packed weights are
+ *    uploaded to HBM on first use and kept resident (keyed by host address
+ *    and size; see b200q_weight_cache_*). Invalid arguments return silently
+ *    without writing y (void kernels) or return 0 (int kernels), like the
+ *    reference; the reason is available from b200q_last_error().
+ *
+ * 2. Device-pointer entry points (prefix b200q_), for callers that own
+ *    device buffers (the Python layer, graph-captured decode loops). They
+ *    take a cudaStream_t (as void*), are asynchronous, and return a status
+ *    code (B200Q_OK = 0, negative on error).
+ *
+ * Activation arithmetic ("act mode"):
+ *   B200Q_ACT_X16 (default)  x is quantized per 32 elements to 16-bit codes
+ *                            and dotted with dp4a in two byte planes; the
+ *                            result is within 1e-5 of ||w_row||*||x|| of the
+ *                            reference's fp32 result.
+ *   B200Q_ACT_X8             x is quantized per 32 elements to int8 (one
+ *                            dp4a plane): fastest, ~5e-4 normalised error.
+ * The drop-in entry points use the mode set by b200q_set_act_mode() or the
+ * B200Q_ACT environment variable ("x16" | "x8"); default x16.
+ */
+#ifndef B200Q_H
+#define B200Q_H
+
+#if defined(__GNUC__)
+#define B200Q_API __attribute__((visibility("default")))
+#else
+#define B200Q_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* qtype ids: GGUF ids (QM:39-44) plus ggml's Q4_0. */
+#define B200Q_Q4_0 2
+#define B200Q_Q8_0 8
+#define B200Q_Q4_K 12
+#define B200Q_Q6_K 14
+#define B200Q_Q4_K_R4 112
+#define B200Q_Q6_K_R4 114
+#define B200Q_Q6_K_LM 214
+
+#define B200Q_ACT_X8 1
+#define B200Q_ACT_X16 2
+
+/* status codes */
+#define B200Q_OK 0
+#define B200Q_EINVAL (-1)      /* null pointer, non-positive size */
+#define B200Q_EQTYPE (-2)      /* unknown or unsupported qtype */
+#define B200Q_ESHAPE (-3)      /* k not a multiple of the block, shape too large */
+#define B200Q_EALIGN (-4)      /* device pointer not 16-byte aligned */
+#define B200Q_ECUDA (-5)       /* CUDA runtime error */
+#define B200Q_ENOMEM (-6)      /* device allocation failed */
+#define B200Q_ETIMEOUT (-7)    /* a kernel's bounded pipeline wait gave up */
+#define B200Q_ENODEV (-8)      /* no usable sm_100 device */
+
+/* ---------------------------------------------------------------------
+ * 1. Drop-in entry points (host pointers), reference signatures.
+ * ------------------------------------------------------------------- */
+
+/* y[n] = W x. Replace QM:1536 simd_matvec_q4k, QM:1585 simd_matvec_q4k_r4,
+ * QM:1647 simd_matvec_q6k, QM:1717 simd_matvec_q6k_r4, QM:1781
+ * simd_matvec_q6k_lm, QM:1818 simd_matvec_q8_0. simd_matvec_q4_0 has no
+ * reference counterpart (ggml Q4_0, same argument convention). */
+B200Q_API void simd_matvec_q4k(const float* x, const void* a_quant, float* y, int k, int n);
+B200Q_API void simd_matvec_q4k_r4(const float* x, const void* a_quant_r4, float* y, int k, int n);
+B200Q_API void simd_matvec_q6k(const float* x, const void* a_quant, float* y, int k, int n);
+B200Q_API void simd_matvec_q6k_r4(const float* x, const void* a_quant_r4, float* y, int k, int n);
+B200Q_API void simd_matvec_q6k_lm(const float* x, const void* a_quant_lm, float* y, int k, int n);
+B200Q_API void simd_matvec_q8_0(const float* x, const void* a_quant, float* y, int k, int n);
+B200Q_API void simd_matvec_q4_0(const float* x, const void* a_quant, float* y, int k, int n);
+
+/* Y[m][n] = X[m][k] W^T. Replace QM:1944 simd_matmul_q4k, QM:1975
+ * simd_matmul_q4k_r4, QM:2034 simd_matmul_q6k, QM:2065 simd_matmul_q6k_r4,
+ * QM:2125 simd_matmul_q8_0 (m == 1 behaves as the matvec, QM:1953-1956).
+ * simd_matmul_q4_0 has no reference counterpart. */
+B200Q_API void simd_matmul_q4k(const float* x, const void* a_quant, float* y, int m, int k, int n);
+B200Q_API void simd_matmul_q4k_r4(const float* x, const void* a_quant_r4, float* y, int m, int k, int n);
+B200Q_API void simd_matmul_q6k(const float* x, const void* a_quant, float* y, int m, int k, int n);
+B200Q_API void simd_matmul_q6k_r4(const float* x, const void* a_quant_r4, float* y, int m, int k, int n);
+B200Q_API void simd_matmul_q8_0(const float* x, const void* a_quant, float* y, int m, int k, int n);
+B200Q_API void simd_matmul_q4_0(const float* x, const void* a_quant, float* y, int m, int k, int n);
+
+/* ---------------------------------------------------------------------
+ * 2. Device-pointer entry points.
+ * ------------------------------------------------------------------- */
+
+/* Y[m][n] = X[m][k] W^T with X, W, Y device pointers (16-byte aligned,
+ * row strides k and n), on `stream`. Any qtype above. Replaces the
+ * computation of QM:1536-2154 for callers whose buffers live in HBM. */
+B200Q_API int b200q_matmul(int qtype, int act_mode, const float* x, const void* w, float* y, int m, int k, int n,
+                 void* stream);
+
+/* Debug form of b200q_matmul for m == 1: additionally writes the exact
+ * per-group integer dot sums  sum_i code_i * q_i  to isums[n][k / G]
+ * (G = 16 for Q6_K-family types, else 32). No reference counterpart: the
+ * reference dots are fp32; this exposes the integer stage for bit-exact
+ * checks against the CPU restatement. */
+B200Q_API int b200q_matvec_isums(int qtype, int act_mode, const float* x, const void* w, float* y, int* isums, int k, int n,
+                       void* stream);
+
+/* ---------------------------------------------------------------------
+ * Runtime controls.
+ * ------------------------------------------------------------------- */
+B200Q_API int b200q_set_act_mode(int act_mode);       /* drop-in mode; returns previous */
+B200Q_API int b200q_get_act_mode(void);
+B200Q_API int b200q_last_error(void);                 /* last status of this host thread */
+B200Q_API const char* b200q_status_string(int status);
+B200Q_API int b200q_device_status(int device);        /* STATUS bits of a device, cleared on read */
+B200Q_API void b200q_weight_cache_clear(void);        /* free all resident weight copies */
+B200Q_API int b200q_weight_cache_evict(const void* host_ptr); /* 1 if an entry was freed */
+B200Q_API long long b200q_weight_cache_bytes(void);   /* bytes resident */
+B200Q_API int b200q_set_pdl(int enable);              /* programmatic dependent launch on/off; returns previous */
+B200Q_API const char* b200q_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200Q_H */

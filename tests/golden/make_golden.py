@@ -1,0 +1,91 @@
+"""Generate the golden fixtures of the reference's own CPU op.
+
+    make -C oracle ref            # compiles the reference op into oracle/_ref
+    python tests/golden/make_golden.py
+
+Runs the reference engine's compiled kernels
+(JSBuild/src/verso/Anvil/core/native/quantized_matmul.cpp, built from its
+sources by oracle/Makefile) on seeded synthetic inputs and stores inputs and
+outputs in ``tests/golden/reference_ops.npz``. The tests then pin both the
+oracle restatement and the CUDA kernels against these vectors without needing
+the reference tree.
+
+Inputs: weights N(0, 0.02) packed with cybel_b200.quantize (Q4_K / Q6_K /
+Q8_0), repacked by the reference's own simd_repack_* for the R4 / LM types;
+activations N(0, 1). Seeds are fixed below.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT))
+
+from cybel_b200 import quantize as Q  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+
+OUT = Path(__file__).resolve().parent / "reference_ops.npz"
+
+CASES = [
+    # (name, qtype, n, k, seed)
+    ("q4k", O.Q4_K, 66, 512, 11),
+    ("q6k", O.Q6_K, 37, 512, 12),
+    ("q8_0", O.Q8_0, 45, 512, 13),
+    ("q4k_r4", O.Q4_K_R4, 66, 512, 14),
+    ("q6k_r4", O.Q6_K_R4, 37, 512, 15),
+    ("q6k_lm", O.Q6_K_LM, 37, 512, 16),
+]
+
+
+def main() -> None:
+    if not O.ref_available():
+        O.build(ref=True)
+    os.environ.setdefault("ANVIL_NUM_THREADS", "4")
+    ref = O.ref()
+    fp = ctypes.POINTER(ctypes.c_float)
+    out: dict[str, np.ndarray] = {}
+    for name, qt, n, k, seed in CASES:
+        rng = np.random.default_rng(seed)
+        w = rng.normal(0.0, 0.02, size=(n, k)).astype(np.float32)
+        base = {O.Q4_K: O.Q4_K, O.Q4_K_R4: O.Q4_K, O.Q6_K: O.Q6_K, O.Q6_K_R4: O.Q6_K, O.Q6_K_LM: O.Q6_K, O.Q8_0: O.Q8_0}[qt]
+        W = Q.quantize(w, base)
+        if qt == O.Q4_K_R4:
+            dst = np.empty_like(W)
+            assert ref.simd_repack_q4k_r4(W.ctypes.data, dst.ctypes.data, k, n) == 1
+            W = dst
+        elif qt == O.Q6_K_R4:
+            dst = np.empty_like(W)
+            assert ref.simd_repack_q6k_r4(W.ctypes.data, dst.ctypes.data, k, n) == 1
+            W = dst
+        elif qt == O.Q6_K_LM:
+            dst = np.empty((n, (k // 256) * 276), dtype=np.uint8)
+            assert ref.simd_repack_q6k_lm(W.ctypes.data, dst.ctypes.data, k, n) == 1
+            W = dst
+        x = rng.standard_normal(k).astype(np.float32)
+        y = O.ref_matvec(qt, W, x, k, n)
+        out[f"{name}/W"] = W
+        out[f"{name}/x"] = x
+        out[f"{name}/y"] = y
+        out[f"{name}/meta"] = np.array([qt, n, k], dtype=np.int64)
+        if qt != O.Q6_K_LM:
+            X = rng.standard_normal((3, k)).astype(np.float32)
+            out[f"{name}/X"] = X
+            out[f"{name}/Y"] = O.ref_matmul(qt, W, X, k, n)
+        rows = [0, n // 2, n - 1]
+        deq = np.zeros((len(rows), k), dtype=np.float32)
+        for i, r in enumerate(rows):
+            assert ref.simd_dequantize_row(W.ctypes.data, qt, r, deq[i].ctypes.data_as(fp), k) == 1
+        out[f"{name}/deq_rows"] = np.array(rows, dtype=np.int64)
+        out[f"{name}/deq"] = deq
+    np.savez_compressed(OUT, **out)
+    print(f"wrote {OUT} ({OUT.stat().st_size} bytes)")
+
+
+if __name__ == "__main__":
+    main()
