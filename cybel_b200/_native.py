@@ -14,6 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libb200q.so"
 
 ACT_X8 = 1
 ACT_X16 = 2
+WEIGHTS_STATIC = 1
 
 STATUS = {
     0: "ok",
@@ -25,6 +26,7 @@ STATUS = {
     -6: "device allocation failed",
     -7: "kernel pipeline wait timed out",
     -8: "no usable sm_100 device",
+    -9: "scratch must grow during stream capture",
 }
 
 # Every symbol include/b200q.h declares: (name, argtypes, restype).
@@ -39,6 +41,7 @@ for _q in ("q4k", "q4k_r4", "q6k", "q6k_r4", "q8_0", "q4_0"):
 SIGNATURES.update(
     {
         "b200q_matmul": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
+        "b200q_matmul_ex": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
         "b200q_matvec_isums": ([_i, _i, _vp, _vp, _vp, _vp, _i, _i, _vp], _i),
         "b200q_set_act_mode": ([_i], _i),
         "b200q_get_act_mode": ([], _i),

@@ -38,7 +38,7 @@ bool env_flag(const char* name, bool dflt) {
 void set_last_error(int status) { t_last_error = status; }
 
 bool pdl_enabled() {
-    if (g_pdl < 0) g_pdl = env_flag("B200Q_PDL", false) ? 1 : 0;
+    if (g_pdl < 0) g_pdl = env_flag("B200Q_PDL", true) ? 1 : 0;
     return g_pdl == 1;
 }
 
@@ -213,7 +213,8 @@ int dropin(int qtype, const float* x, const void* w, float* y, int m, int k, int
             rc = B200Q_ECUDA;
     }
     if (rc == B200Q_OK)
-        rc = launch_gemv(qtype, act_mode_now(), dw, s->dx, s->dy, m, k, n, k, n, nullptr, dev, s->stream, pdl_enabled());
+        rc = launch_gemv(qtype, act_mode_now(), dw, s->dx, s->dy, m, k, n, k, n, nullptr, dev, s->stream, pdl_enabled(),
+                         B200Q_WEIGHTS_STATIC);
     if (rc == B200Q_OK) {
         if (cudaMemcpyAsync(y, s->dy, sizeof(float) * m * n, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess)
             rc = B200Q_ECUDA;
@@ -259,15 +260,20 @@ B200Q_MATMUL(simd_matmul_q4_0, QT_Q4_0)
 #undef B200Q_MATMUL
 
 // ---- device-pointer API ----------------------------------------------------
-int b200q_matmul(int qtype, int act_mode, const float* x, const void* w, float* y, int m, int k, int n,
-                 void* stream) {
+int b200q_matmul_ex(int qtype, int act_mode, const float* x, const void* w, float* y, int m, int k, int n, int flags,
+                    void* stream) {
     Device* dev = nullptr;
     int rc = current_device_state(&dev);
     if (rc == B200Q_OK)
         rc = launch_gemv(qtype, act_mode, w, x, y, m, k, n, k, n, nullptr, dev, static_cast<cudaStream_t>(stream),
-                         pdl_enabled());
+                         pdl_enabled(), flags);
     set_last_error(rc);
     return rc;
+}
+
+int b200q_matmul(int qtype, int act_mode, const float* x, const void* w, float* y, int m, int k, int n,
+                 void* stream) {
+    return b200q_matmul_ex(qtype, act_mode, x, w, y, m, k, n, 0, stream);
 }
 
 int b200q_matvec_isums(int qtype, int act_mode, const float* x, const void* w, float* y, int* isums, int k, int n,
@@ -304,6 +310,7 @@ const char* b200q_status_string(int status) {
         case B200Q_ENOMEM: return "device allocation failed";
         case B200Q_ETIMEOUT: return "kernel pipeline wait timed out";
         case B200Q_ENODEV: return "no usable sm_100 device";
+        case B200Q_ECAPTURE: return "scratch must grow during stream capture";
         default: return "unknown status";
     }
 }

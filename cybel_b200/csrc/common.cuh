@@ -52,14 +52,18 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// try_wait with a suspend-time hint: a waiting thread is parked until the
+// phase completes (or ~kSuspendHintNs elapse) instead of spinning.
+constexpr uint32_t kSuspendHintNs = 20000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
         : "memory");
     return ok != 0;
 }
@@ -70,7 +74,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
     const uint64_t t0 = global_timer_ns();
     for (uint32_t it = 1; it < kWaitMaxPolls; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 127u) == 0u && global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+        if ((it & 7u) == 0u && global_timer_ns() - t0 > kWaitTimeoutNs) return false;
     }
     return false;
 }

@@ -1,6 +1,8 @@
 // Launch planning and dispatch for the decode GEMV kernels (gemv.cuh).
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "gemv.cuh"
 #include "internal.h"
@@ -9,13 +11,13 @@ namespace b200q {
 
 bool fmt_info(int qtype, FmtInfo& f) {
     switch (qtype) {
-        case QT_Q4_K: f = {256, 144, 4, 8, 32, false}; return true;
-        case QT_Q4_K_R4: f = {256, 144, 4, 8, 32, true}; return true;
+        case QT_Q4_K: f = {256, 144, 2, 16, 32, false}; return true;
+        case QT_Q4_K_R4: f = {256, 144, 2, 16, 32, true}; return true;
         case QT_Q6_K: f = {256, 210, 8, 4, 16, false}; return true;
         case QT_Q6_K_R4: f = {256, 210, 8, 4, 16, true}; return true;
         case QT_Q6_K_LM: f = {256, 276, 8, 4, 16, false}; return true;
-        case QT_Q8_0: f = {32, 34, 1, 32, 32, false}; return true;
-        case QT_Q4_0: f = {32, 18, 1, 32, 32, false}; return true;
+        case QT_Q8_0: f = {32, 34, 1, 64, 32, false}; return true;
+        case QT_Q4_0: f = {32, 18, 1, 64, 32, false}; return true;
         default: return false;
     }
 }
@@ -28,9 +30,9 @@ long long row_bytes_of(int qtype, int k) {
 
 namespace {
 
-constexpr int kStageTarget = 24 * 1024;   // preferred bytes per stage
-constexpr int kStageMax = 64 * 1024;      // largest stage
-constexpr int kSmemBudget = 200 * 1024;   // ring + bookkeeping per CTA
+constexpr int kSmemBudget = 220 * 1024;   // ring + bookkeeping per CTA
+constexpr int kStageTarget = 32 * 1024;   // preferred bytes per stage
+constexpr int kStageMax = 96 * 1024;      // largest stage
 constexpr int kMaxStages = 8;
 
 struct Plan {
@@ -40,7 +42,7 @@ struct Plan {
     int grid;
 };
 
-int make_plan(int qtype, int k, int n, int MR, int num_sms, Plan& pl) {
+int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl) {
     FmtInfo f;
     if (!fmt_info(qtype, f)) return B200Q_EQTYPE;
     if (k <= 0 || n <= 0) return B200Q_EINVAL;
@@ -48,30 +50,28 @@ int make_plan(int qtype, int k, int n, int MR, int num_sms, Plan& pl) {
     const int nb = k / f.elems;
     const long long rb = static_cast<long long>(nb) * f.bytes;
     const int S = (nb + f.blocks_per_slice - 1) / f.blocks_per_slice;
-    if (S > kGemvMaxConsumerWarps) return B200Q_ESHAPE;
-    const int WR = std::max(1, kGemvMaxConsumerWarps / S);
-    int R, step;
-    if (f.r4) {
-        R = ((WR + 3) / 4) * 4;
-        step = 4;
-    } else {
-        R = WR;
-        step = WR;
-    }
+    const int max_warps = (dig == 1 && MR == 1) ? 16 : 12;  // kGemvWarps in gemv.cuh
+    if (S > max_warps) return B200Q_ESHAPE;
+    const int WR = std::max(1, max_warps / S);
+    // Stage rows: WR (one row per walker) grown in steps of WR towards
+    // kStageTarget bytes; the R4 layouts need whole 4-row groups.
     // A stage copies the 16-byte-aligned window around its rows: at most
     // rows * rb + 30 bytes; kSlotPad also covers the 4-byte over-read of the
     // unaligned word loads.
     constexpr int kSlotPad = 48;
+    const int step = f.r4 ? ((WR + 3) / 4) * 4 : WR;
+    int R = step;
     while ((R + step) * rb + kSlotPad <= kStageTarget) R += step;
     if (R * rb + kSlotPad > kStageMax) {
-        if (f.r4) return B200Q_ESHAPE;
-        R = std::max<int>(1, static_cast<int>((kStageMax - kSlotPad) / rb));
+        R = f.r4 ? 4 : std::max<int>(1, static_cast<int>((kStageMax - kSlotPad) / rb));
         if (R * rb + kSlotPad > kStageMax) return B200Q_ESHAPE;
     }
     const int stage_stride = static_cast<int>(((R * rb + kSlotPad) + 127) / 128 * 128);
-    const int part_bytes = 2 * R * MR * S * 4;
-    int NS = (kSmemBudget - part_bytes - 64) / (stage_stride + 16);
-    NS = std::min(kMaxStages, NS);
+    const int n_quads = (n + 3) / 4;
+    const int grid = std::min(num_sms, n_quads);
+    const int rows_cta = 4 * ((n_quads + grid - 1) / grid);
+    const int part_bytes = rows_cta * MR * S * 4;
+    int NS = std::min(kMaxStages, (kSmemBudget - part_bytes - 64) / (stage_stride + 16));
     if (NS < 2) return B200Q_ESHAPE;
     GemvParams& p = pl.p;
     p = GemvParams{};
@@ -84,10 +84,11 @@ int make_plan(int qtype, int k, int n, int MR, int num_sms, Plan& pl) {
     p.R = R;
     p.NS = NS;
     p.stage_stride = stage_stride;
-    p.n_quads = (n + 3) / 4;
+    p.n_quads = n_quads;
+    p.rows_cta = rows_cta;
     pl.threads = (S * WR + 1) * 32;
     pl.smem = NS * stage_stride + 2 * NS * 8 + part_bytes + 16;
-    pl.grid = std::min(num_sms, p.n_quads);
+    pl.grid = grid;
     return B200Q_OK;
 }
 
@@ -121,15 +122,28 @@ cudaError_t launch_kernel(const Plan& pl, cudaStream_t st, bool pdl) {
     return cudaLaunchKernelEx(&cfg, kern, pl.p);
 }
 
+// Most activation rows one launch carries, per qtype and mode (the Q4_K
+// lanes hold four activation runs, so they carry fewer rows).
+int max_rows_per_launch(int qtype, int dig) {
+    const bool q4k = qtype == QT_Q4_K || qtype == QT_Q4_K_R4;
+    if (dig == 1) return q4k ? 2 : 4;
+    return q4k ? 1 : 2;
+}
+
 template <int QT>
 cudaError_t dispatch_qt(int dig, int MR, bool dbg, const Plan& pl, cudaStream_t st, bool pdl) {
+    constexpr bool q4k = QT == QT_Q4_K || QT == QT_Q4_K_R4;
     if (dbg) return dig == 1 ? launch_kernel<QT, 1, 1, true>(pl, st, pdl) : launch_kernel<QT, 2, 1, true>(pl, st, pdl);
     if (dig == 1) {
-        if (MR == 4) return launch_kernel<QT, 1, 4, false>(pl, st, pdl);
+        if constexpr (!q4k) {
+            if (MR == 4) return launch_kernel<QT, 1, 4, false>(pl, st, pdl);
+        }
         if (MR == 2) return launch_kernel<QT, 1, 2, false>(pl, st, pdl);
         return launch_kernel<QT, 1, 1, false>(pl, st, pdl);
     }
-    if (MR == 2) return launch_kernel<QT, 2, 2, false>(pl, st, pdl);
+    if constexpr (!q4k) {
+        if (MR == 2) return launch_kernel<QT, 2, 2, false>(pl, st, pdl);
+    }
     return launch_kernel<QT, 2, 1, false>(pl, st, pdl);
 }
 
@@ -146,30 +160,92 @@ cudaError_t dispatch(int qtype, int dig, int MR, bool dbg, const Plan& pl, cudaS
     }
 }
 
+// Quantized-activation scratch, one growable buffer per (device, stream):
+// calls on one stream are ordered, so they can share it.
+struct Scratch {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+std::mutex g_scratch_mu;
+std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
+
+int scratch_for(Device* dev, cudaStream_t st, size_t bytes, void** out) {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    Scratch& s = g_scratch[std::make_pair(dev->id, st)];
+    if (s.bytes < bytes) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+            return B200Q_ECAPTURE;  // size the scratch with one call before capturing
+        if (s.ptr) {
+            cudaStreamSynchronize(st);
+            cudaFree(s.ptr);
+            s.ptr = nullptr;
+            s.bytes = 0;
+        }
+        const size_t want = std::max<size_t>(bytes, 1u << 20);
+        if (cudaMalloc(&s.ptr, want) != cudaSuccess) return B200Q_ENOMEM;
+        s.bytes = want;
+    }
+    *out = s.ptr;
+    return B200Q_OK;
+}
+
+template <int DIG>
+cudaError_t launch_quantize(const float* x, long long x_stride, int m, int k, uint8_t* xq, cudaStream_t st, bool pdl) {
+    const long long threads = static_cast<long long>(m) * (k / 32);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((threads + 127) / 128));
+    cfg.blockDim = dim3(128);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, quantize_act_kernel<DIG>, x, x_stride, m, k, xq);
+}
+
 }  // namespace
 
 int launch_gemv(int qtype, int act_mode, const void* w, const float* x, float* y, int m, int k, int n,
-                long long x_stride, long long y_stride, int32_t* isums, Device* dev, cudaStream_t st, bool pdl) {
+                long long x_stride, long long y_stride, int32_t* isums, Device* dev, cudaStream_t st, bool pdl,
+                int flags) {
     if (!w || !x || !y || m <= 0 || k <= 0 || n <= 0 || !dev) return B200Q_EINVAL;
     if (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
     if ((reinterpret_cast<uintptr_t>(w) & 15u) || (reinterpret_cast<uintptr_t>(x) & 15u) || (x_stride & 3))
         return B200Q_EALIGN;
     if (isums && m != 1) return B200Q_EINVAL;
+    if (k % 32) return B200Q_ESHAPE;
     const int dig = act_mode == B200Q_ACT_X8 ? 1 : 2;
-    const int mr_max = dig == 1 ? 4 : 2;
+    const int mr_max = max_rows_per_launch(qtype, dig);
+    {  // validate the shape before any launch
+        Plan probe;
+        const int rc0 = make_plan(qtype, dig, k, n, 1, dev->num_sms, probe);
+        if (rc0 != B200Q_OK) return rc0;
+    }
+    const long long xq_row = xq_row_bytes(k, dig);
+    void* xq = nullptr;
+    int rcs = scratch_for(dev, st, static_cast<size_t>(xq_row) * m, &xq);
+    if (rcs != B200Q_OK) return rcs;
+    cudaError_t eq = dig == 1 ? launch_quantize<1>(x, x_stride, m, k, static_cast<uint8_t*>(xq), st, pdl)
+                              : launch_quantize<2>(x, x_stride, m, k, static_cast<uint8_t*>(xq), st, pdl);
+    if (eq != cudaSuccess) return B200Q_ECUDA;
     for (int m0 = 0; m0 < m;) {
         const int left = m - m0;
-        const int MR = isums ? 1 : (left >= mr_max ? mr_max : (left >= 2 ? 2 : 1));
+        const int MR = isums ? 1 : (left >= mr_max ? mr_max : (left >= 2 && mr_max >= 2 ? 2 : 1));
         Plan pl;
-        int rc = make_plan(qtype, k, n, MR, dev->num_sms, pl);
+        int rc = make_plan(qtype, dig, k, n, MR, dev->num_sms, pl);
         if (rc != B200Q_OK) return rc;
         pl.p.W = static_cast<const uint8_t*>(w);
-        pl.p.x = x + m0 * x_stride;
+        pl.p.xq = static_cast<const uint8_t*>(xq) + m0 * xq_row;
+        pl.p.xq_stride = xq_row;
         pl.p.y = y + m0 * y_stride;
-        pl.p.x_stride = x_stride;
         pl.p.y_stride = y_stride;
         pl.p.dbg = isums;
         pl.p.status = dev->status;
+        pl.p.w_static = (flags & B200Q_WEIGHTS_STATIC) ? 1 : 0;
         cudaError_t e = dispatch(qtype, dig, MR, isums != nullptr, pl, st, pdl);
         if (e != cudaSuccess) return B200Q_ECUDA;
         m0 += MR;

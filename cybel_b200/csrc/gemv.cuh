@@ -10,10 +10,13 @@
 //    ring of shared-memory stages with 1-D bulk copies (cp.async.bulk, no
 //    multicast) that complete on mbarriers. Weights are touched once, with an
 //    L2 evict-first policy.
-//  * Consumer warps own a fixed k-slice of the row ("slice") and walk rows.
-//    Each lane quantizes its own piece of x into registers at start-up
-//    (per 32-element group: int8 "x8" or int16 split in two byte planes
-//    "x16"), so activations never travel through memory again.
+//  * Activations are quantized once per call by quantize_act_kernel (per
+//    32-element group: int8 "x8", or int16 split in two byte planes "x16").
+//    Consumer warps own a fixed k-slice of the row ("slice") and walk rows;
+//    each lane loads its activation codes into registers once.
+//  * Both kernels use programmatic dependent launch: the GEMV streams its
+//    (static) weights while the quantizer runs and waits for it only before
+//    reading the codes.
 //  * Per row a lane decodes its weight codes from shared memory and forms
 //    exact integer dot sums with dp4a; each group sum is scaled in fp32 by
 //    the weight and activation scales; partials are reduced per warp with
@@ -27,17 +30,21 @@
 
 namespace b200q {
 
-constexpr int kGemvMaxConsumerWarps = 16;
-constexpr int kGemvMaxThreads = (kGemvMaxConsumerWarps + 1) * 32;
+// Consumer warps per CTA (one more warp is the producer). With 17 warps a
+// thread may hold up to 96 registers (each SM sub-partition runs 5 warps);
+// with 13, up to 128 -- the heavier instantiations (x16, several activation
+// rows) take 12 consumer warps.
+template <int DIG, int MR>
+constexpr int kGemvWarps = (DIG == 1 && MR == 1) ? 16 : 12;
 
 struct GemvParams {
     const uint8_t* W;      // packed weight rows (device, 16-byte aligned)
-    const float* x;        // [MR][x_stride] fp32 activations (device, 16-byte aligned)
+    const uint8_t* xq;     // [MR] quantized activation rows (quantize_act_kernel layout)
+    long long xq_stride;   // bytes between quantized rows
     float* y;              // [MR][y_stride] fp32 outputs
     int32_t* dbg;          // optional [n][k/G] integer group sums (MR == 1 only)
     volatile int* status;  // status word (host-mapped); kernels store STATUS_* values
     long long row_bytes;   // bytes per packed row
-    long long x_stride;    // floats between activation rows
     long long y_stride;    // floats between output rows
     int k, n;
     int nb;                // blocks per row
@@ -47,7 +54,11 @@ struct GemvParams {
     int NS;                // ring stages
     int stage_stride;      // bytes between ring slots (multiple of 128)
     int n_quads;           // ceil(n / 4)
+    int rows_cta;          // most rows any CTA owns
+    int w_static;          // weights not written by the preceding kernel: stream them before the grid dependency resolves
 };
+
+
 
 // ---------------------------------------------------------------------------
 // Per-format lane geometry. A warp covers kBlocksPerSlice consecutive blocks
@@ -60,11 +71,19 @@ struct Fmt;
 
 template <>
 struct Fmt<QT_Q4_K> {
-    static constexpr int kElems = 256, kBytes = 144, kLanesPerBlock = 4, kBlocksPerSlice = 8;
-    static constexpr int kRun = 32, kRuns = 2, kGroup = 32;
+    // Lane p (0, 1) of a block holds sub-blocks 2p, 2p+1 (qs pair p, scale
+    // encoding "lower") and 2p+4, 2p+5 (qs pair p+2, "upper").
+    static constexpr int kElems = 256, kBytes = 144, kBlocksPerLane = 1, kLanesPerBlock = 2, kBlocksPerSlice = 16;
+    static constexpr int kRun = 32, kRuns = 4, kGroup = 32, kGroupsPerLane = 4;
     static constexpr bool kR4 = false;
-    __device__ static int run_start(int blk, int t, int r) { return blk * 256 + t * 64 + r * 32; }
-    __device__ static int group_index(int blk, int t, int r) { return blk * 8 + 2 * t + r; }
+    // Lane l takes block l % 16 and half l / 16: each quarter-warp of a
+    // 128-bit shared load then reads 8 blocks 144 B apart (bank offsets 4b),
+    // conflict-free.
+    __device__ static int lane_part(int lane) { return lane >> 4; }
+    __device__ static int lane_block(int lane) { return lane & 15; }
+    __device__ static int sub(int p, int r) { return 2 * p + r + (r >= 2 ? 2 : 0); }
+    __device__ static int run_start(int blk, int p, int r) { return blk * 256 + sub(p, r) * 32; }
+    __device__ static int group_index(int blk, int p, int r) { return blk * 8 + sub(p, r); }
 };
 template <>
 struct Fmt<QT_Q4_K_R4> : Fmt<QT_Q4_K> {
@@ -73,9 +92,11 @@ struct Fmt<QT_Q4_K_R4> : Fmt<QT_Q4_K> {
 
 template <>
 struct Fmt<QT_Q6_K> {
-    static constexpr int kElems = 256, kBytes = 210, kLanesPerBlock = 8, kBlocksPerSlice = 4;
-    static constexpr int kRun = 16, kRuns = 2, kGroup = 16;
+    static constexpr int kElems = 256, kBytes = 210, kBlocksPerLane = 1, kLanesPerBlock = 8, kBlocksPerSlice = 4;
+    static constexpr int kRun = 16, kRuns = 2, kGroup = 16, kGroupsPerLane = 2;
     static constexpr bool kR4 = false;
+    __device__ static int lane_part(int lane) { return lane % kLanesPerBlock; }
+    __device__ static int lane_block(int lane) { return (lane / kLanesPerBlock) * kBlocksPerLane; }
     // lane t = 4h + 2c + i16 holds groups g = 4h + c (r = 0) and 4h + c + 2 (r = 1).
     __device__ static int grp(int t, int r) { return 4 * (t >> 2) + ((t >> 1) & 1) + 2 * r; }
     __device__ static int run_start(int blk, int t, int r) { return blk * 256 + grp(t, r) * 32 + (t & 1) * 16; }
@@ -88,11 +109,14 @@ struct Fmt<QT_Q6_K_R4> : Fmt<QT_Q6_K> {
 
 template <>
 struct Fmt<QT_Q8_0> {
-    static constexpr int kElems = 32, kBytes = 34, kLanesPerBlock = 1, kBlocksPerSlice = 32;
-    static constexpr int kRun = 32, kRuns = 1, kGroup = 32;
+    // Lane l holds two consecutive blocks (2l, 2l+1 of its slice).
+    static constexpr int kElems = 32, kBytes = 34, kLanesPerBlock = 1, kBlocksPerLane = 2, kBlocksPerSlice = 64;
+    static constexpr int kRun = 32, kRuns = 2, kGroup = 32, kGroupsPerLane = 2;
     static constexpr bool kR4 = false;
-    __device__ static int run_start(int blk, int, int) { return blk * 32; }
-    __device__ static int group_index(int blk, int, int) { return blk; }
+    __device__ static int lane_part(int lane) { return lane % kLanesPerBlock; }
+    __device__ static int lane_block(int lane) { return (lane / kLanesPerBlock) * kBlocksPerLane; }
+    __device__ static int run_start(int blk, int, int r) { return (blk + r) * 32; }
+    __device__ static int group_index(int blk, int, int r) { return blk + r; }
 };
 template <>
 struct Fmt<QT_Q4_0> : Fmt<QT_Q8_0> {
@@ -101,17 +125,19 @@ struct Fmt<QT_Q4_0> : Fmt<QT_Q8_0> {
 
 template <>
 struct Fmt<QT_Q6_K_LM> {
-    static constexpr int kElems = 256, kBytes = 276, kLanesPerBlock = 8, kBlocksPerSlice = 4;
-    static constexpr int kRun = 32, kRuns = 1, kGroup = 16;
+    static constexpr int kElems = 256, kBytes = 276, kBlocksPerLane = 1, kLanesPerBlock = 8, kBlocksPerSlice = 4;
+    static constexpr int kRun = 32, kRuns = 1, kGroup = 16, kGroupsPerLane = 2;
     static constexpr bool kR4 = false;
+    __device__ static int lane_part(int lane) { return lane % kLanesPerBlock; }
+    __device__ static int lane_block(int lane) { return (lane / kLanesPerBlock) * kBlocksPerLane; }
     __device__ static int run_start(int blk, int t, int) { return blk * 256 + t * 32; }
     __device__ static int group_index(int blk, int t, int r) { return blk * 16 + 2 * t + r; }
 };
 
 // ---------------------------------------------------------------------------
-// Activation quantization of one lane's run (restated in the oracle as
-// orc_quantize_act): per 32-element group, amax, iscale = QMAX/amax (IEEE),
-// q = rint(x * iscale) (one rounded multiply, half-even), d = amax/QMAX.
+// One lane's activation codes: a run of RUN consecutive elements of a
+// quantized row (per 32-element group: int8 "x8" codes, or int16 "x16" codes
+// split in a signed high byte plane and an unsigned low byte plane).
 // ---------------------------------------------------------------------------
 template <int DIG, int RUN>
 struct XRun {
@@ -119,6 +145,7 @@ struct XRun {
     uint32_t lo[DIG == 2 ? RUN / 4 : 1];  // packed unsigned low bytes (x16 only)
     float d;               // group scale
     int sum;               // sum of the codes in this run
+    float fsum;            // the same sum as a float (exact: |sum| < 2^20)
 };
 
 __device__ __forceinline__ int round_half_even_small(float v) {
@@ -127,12 +154,35 @@ __device__ __forceinline__ int round_half_even_small(float v) {
     return __float_as_int(t) - 0x4B400000;
 }
 
-template <int DIG, int RUN>
-__device__ __forceinline__ void quantize_run(const float* xp, bool active, XRun<DIG, RUN>& out) {
-    float v[RUN];
+// Activation rows quantized once per call by quantize_act_kernel, in the
+// layout the GEMV lanes read: per row, k signed code bytes (x8: the code;
+// x16: its high byte), k unsigned low bytes (x16 only), k/32 fp32 group
+// scales and k/32 int32 group code sums; xq_row_bytes(k, DIG) bytes per row.
+__host__ __device__ constexpr long long xq_row_bytes(int k, int dig) {
+    return ((static_cast<long long>(k) * dig + (k / 32) * 8) + 15) / 16 * 16;
+}
+
+// One thread per 32-element group; the arithmetic is restated in the
+// oracle as orc_quantize_act: amax, iscale = QMAX / amax (IEEE division),
+// q = rint(x * iscale) (one rounded multiply, half-even), d = amax / QMAX.
+template <int DIG>
+__global__ void __launch_bounds__(128) quantize_act_kernel(const float* __restrict__ x, long long x_stride, int m, int k,
+                                                           uint8_t* __restrict__ xq) {
+    // Let the GEMV behind this kernel launch now, so it can stream its
+    // weights while this grid waits for x; x may be produced by the
+    // preceding kernel in the stream.
+    griddep_launch_dependents();
+    griddep_wait();
+    const int groups = k / 32;
+    const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (gid >= static_cast<long long>(groups) * m) return;
+    const int row = static_cast<int>(gid / groups), g = static_cast<int>(gid % groups);
+    const float* xr = x + row * x_stride + g * 32;
+    uint8_t* base = xq + row * xq_row_bytes(k, DIG);
+    float v[32];
 #pragma unroll
-    for (int i = 0; i < RUN; i += 4) {
-        float4 f = active ? __ldg(reinterpret_cast<const float4*>(xp + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < 32; i += 4) {
+        const float4 f = __ldg(reinterpret_cast<const float4*>(xr + i));
         v[i] = f.x;
         v[i + 1] = f.y;
         v[i + 2] = f.z;
@@ -140,30 +190,97 @@ __device__ __forceinline__ void quantize_run(const float* xp, bool active, XRun<
     }
     float amax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < RUN; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    if (RUN == 16) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
     constexpr float QMAX = DIG == 1 ? 127.0f : 32767.0f;
     const float iscale = amax > 0.0f ? __fdiv_rn(QMAX, amax) : 0.0f;
-    out.d = amax > 0.0f ? __fdiv_rn(amax, QMAX) : 0.0f;
-    int s = 0;
+    int sum = 0;
+    uint32_t hw[8], lw[8];
 #pragma unroll
-    for (int w = 0; w < RUN / 4; ++w) {
-        uint32_t hw = 0, lw = 0;
+    for (int w = 0; w < 8; ++w) {
+        uint32_t h = 0, l = 0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int q = round_half_even_small(__fmul_rn(v[4 * w + j], iscale));
-            s += q;
+            sum += q;
             if (DIG == 1) {
-                hw |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * j);
+                h |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * j);
             } else {
-                hw |= (static_cast<uint32_t>(q >> 8) & 0xFFu) << (8 * j);
-                lw |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * j);
+                h |= (static_cast<uint32_t>(q >> 8) & 0xFFu) << (8 * j);
+                l |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * j);
             }
         }
-        out.hi[w] = hw;
-        if (DIG == 2) out.lo[w] = lw;
+        hw[w] = h;
+        lw[w] = l;
     }
-    out.sum = s;
+    uint4* dh = reinterpret_cast<uint4*>(base + g * 32);
+    dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+    if (DIG == 2) {
+        uint4* dl = reinterpret_cast<uint4*>(base + k + g * 32);
+        dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+    }
+    float* gd = reinterpret_cast<float*>(base + static_cast<long long>(k) * DIG);
+    gd[g] = amax > 0.0f ? __fdiv_rn(amax, QMAX) : 0.0f;
+    reinterpret_cast<int*>(gd + groups)[g] = sum;
+}
+
+// One lane's run of RUN codes starting at element e (a multiple of 16) of a
+// quantized row. The run's code sum is recomputed from the bytes when the
+// run is half a group.
+template <int DIG, int RUN>
+__device__ __forceinline__ void load_run(const uint8_t* row, int k, int e, XRun<DIG, RUN>& out) {
+    const uint4* h = reinterpret_cast<const uint4*>(row + e);
+#pragma unroll
+    for (int i = 0; i < RUN / 16; ++i) {
+        const uint4 v = __ldg(h + i);
+        out.hi[4 * i] = v.x;
+        out.hi[4 * i + 1] = v.y;
+        out.hi[4 * i + 2] = v.z;
+        out.hi[4 * i + 3] = v.w;
+    }
+    if (DIG == 2) {
+        const uint4* l = reinterpret_cast<const uint4*>(row + k + e);
+#pragma unroll
+        for (int i = 0; i < RUN / 16; ++i) {
+            const uint4 v = __ldg(l + i);
+            out.lo[4 * i] = v.x;
+            out.lo[4 * i + 1] = v.y;
+            out.lo[4 * i + 2] = v.z;
+            out.lo[4 * i + 3] = v.w;
+        }
+    }
+    const float* gd = reinterpret_cast<const float*>(row + static_cast<long long>(k) * DIG);
+    out.d = __ldg(gd + e / 32);
+    if (RUN == 32) {
+        out.sum = __ldg(reinterpret_cast<const int*>(gd + k / 32) + e / 32);
+    } else {
+        int hs = 0, ls = 0;
+#pragma unroll
+        for (int w = 0; w < RUN / 4; ++w) {
+            hs = dp4a_ss(out.hi[w], 0x01010101u, hs);
+            if (DIG == 2) ls = dp4a_uu(out.lo[w], 0x01010101u, ls);
+        }
+        out.sum = DIG == 2 ? hs * 256 + ls : hs;
+    }
+    out.fsum = static_cast<float>(out.sum);
+}
+
+// Exact float of a signed integer |v| < 2^22 without a convert instruction:
+// add it to the mantissa of 1.5 * 2^23 and subtract 1.5 * 2^23.
+__device__ __forceinline__ float i2f_small(int v) { return __int_as_float(v + 0x4B400000) - 12582912.0f; }
+
+// Float of a dot sum kept as two digit sums (x16: 256 * hi + lo, each
+// |.| < 2^21), rounded once.
+template <int DIG>
+__device__ __forceinline__ float digits_to_float(int hi, int lo) {
+    return DIG == 2 ? fmaf(256.0f, i2f_small(hi), i2f_small(lo)) : i2f_small(hi);
+}
+
+// Exact float of a small non-negative integer (< 2^23) without a convert:
+// place it in the mantissa of 2^23 and subtract 2^23.
+__device__ __forceinline__ float small_uint_to_float(uint32_t v) {
+    return __uint_as_float(0x4B000000u | v) - 8388608.0f;
 }
 
 // sum_i code_i * q_i for four packed weight bytes (unsigned codes 0..255 or
@@ -192,54 +309,70 @@ __device__ __forceinline__ int combine_digits(int hi, int lo) {
 template <int QT, int DIG, int MR>
 struct RowDot;
 
-// Q4_K (quantized_matmul.cpp:411-515). Lane t of a block holds sub-blocks
-// 2t (low nibbles) and 2t+1 (high nibbles) of qs bytes [32t, 32t+32).
+// Exact float of byte 0 / byte 1 of v: the byte placed in the mantissa of
+// 2^23 with one byte permute, then 2^23 subtracted.
+__device__ __forceinline__ float byte0_to_float(uint32_t v) {
+    return __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7540)) - 8388608.0f;
+}
+__device__ __forceinline__ float byte1_to_float(uint32_t v) {
+    return __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7541)) - 8388608.0f;
+}
+
+// Q4_K (quantized_matmul.cpp:411-515, scale decode :423-437). Lane p of a
+// block reads qs pairs p and p+2 (bytes [32p, 32p+32) and [64+32p, 96+32p)):
+// sub-blocks 2p and 2p+4 are their low nibbles, 2p+1 and 2p+5 the high
+// nibbles. High nibbles are masked in place (0xF0 per byte), so their dp4a
+// sums come out x16 and the 1/16 is folded into the activation scale
+// (xdd). Scales and mins of the lane's four sub-blocks need no selects:
+// pair p uses the "lower" 6-bit encoding, pair p+2 the "upper" one.
 template <int DIG, int MR>
 struct Q4KDot {
     using X = XRun<DIG, 32>;
-    __device__ static void run(uint32_t ba, int t, const X (&x)[MR][2], const float (&xsd)[MR][2], float (&acc)[MR],
-                               int (&isum)[2]) {
+    __device__ static void run(uint32_t ba, int p, const X (&x)[MR][4], const float (&xdd)[MR][4],
+                               const float (&xsd)[MR][4], float (&acc)[MR], int (&isum)[4]) {
         const uint4 h = lds128(ba);
-        const uint4 qa = lds128(ba + 16u + 32u * t);
-        const uint4 qb = lds128(ba + 32u + 32u * t);
+        const uint32_t qa = ba + 16u + 32u * p;
+        const uint4 a0 = lds128(qa), a1 = lds128(qa + 16u);
+        const uint4 b0 = lds128(qa + 64u), b1 = lds128(qa + 80u);
         const float d = half_bits_to_float(h.x);
         const float dmin = half_bits_to_float(h.x >> 16);
-        const uint32_t sh = (t & 1) * 16;
-        const uint32_t w0 = h.y >> sh, w1 = h.z >> sh, w2 = h.w >> sh;
-        const bool upper = t >= 2;
-        const uint32_t sc2 = upper ? ((w2 & 0x0F0Fu) | ((w0 >> 2) & 0x3030u)) : (w0 & 0x3F3Fu);
-        const uint32_t mn2 = upper ? (((w2 >> 4) & 0x0F0Fu) | ((w1 >> 2) & 0x3030u)) : (w1 & 0x3F3Fu);
-        const float dsc0 = d * static_cast<float>(sc2 & 0xFFu);
-        const float dsc1 = d * static_cast<float>((sc2 >> 8) & 0xFFu);
-        const float dmn0 = dmin * static_cast<float>(mn2 & 0xFFu);
-        const float dmn1 = dmin * static_cast<float>((mn2 >> 8) & 0xFFu);
-        const uint32_t q[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-        uint32_t lo[8], hi[8];
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-            lo[w] = q[w] & 0x0F0F0F0Fu;
-            hi[w] = (q[w] >> 4) & 0x0F0F0F0Fu;
-        }
+        const uint32_t sh = 16u * p;
+        const uint32_t A = h.y >> sh, B = h.z >> sh, C = h.w >> sh;
+        const uint32_t scl = A & 0x3F3Fu, mnl = B & 0x3F3Fu;
+        const uint32_t sch = (C & 0x0F0Fu) | ((A >> 2) & 0x3030u);
+        const uint32_t mnh = ((C >> 4) & 0x0F0Fu) | ((B >> 2) & 0x3030u);
+        const float sc[4] = {byte0_to_float(scl), byte1_to_float(scl), byte0_to_float(sch), byte1_to_float(sch)};
+        const float mn[4] = {byte0_to_float(mnl), byte1_to_float(mnl), byte0_to_float(mnh), byte1_to_float(mnh)};
+        const uint32_t qw[2][8] = {{a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w},
+                                   {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w}};
 #pragma unroll
         for (int m = 0; m < MR; ++m) {
-            int a_hi = 0, a_lo = 0, b_hi = 0, b_lo = 0;
+            int hs[4] = {0, 0, 0, 0}, ls[4] = {0, 0, 0, 0};
 #pragma unroll
-            for (int w = 0; w < 8; ++w) {
-                dot4<DIG, false>(lo[w], x[m][0].hi[w], DIG == 2 ? x[m][0].lo[w] : 0u, a_hi, a_lo);
-                dot4<DIG, false>(hi[w], x[m][1].hi[w], DIG == 2 ? x[m][1].lo[w] : 0u, b_hi, b_lo);
+            for (int pr = 0; pr < 2; ++pr) {
+#pragma unroll
+                for (int w = 0; w < 8; ++w) {
+                    const uint32_t lo = qw[pr][w] & 0x0F0F0F0Fu;
+                    const uint32_t hi16 = qw[pr][w] & 0xF0F0F0F0u;
+                    dot4<DIG, false>(lo, x[m][2 * pr].hi[w], DIG == 2 ? x[m][2 * pr].lo[w] : 0u, hs[2 * pr], ls[2 * pr]);
+                    dot4<DIG, false>(hi16, x[m][2 * pr + 1].hi[w], DIG == 2 ? x[m][2 * pr + 1].lo[w] : 0u, hs[2 * pr + 1],
+                                     ls[2 * pr + 1]);
+                }
             }
-            const int ia = combine_digits<DIG>(a_hi, a_lo);
-            const int ib = combine_digits<DIG>(b_hi, b_lo);
             if (m == 0) {
-                isum[0] = ia;
-                isum[1] = ib;
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int v = combine_digits<DIG>(hs[r], ls[r]);
+                    isum[r] = (r & 1) ? (v >> 4) : v;
+                }
             }
-            float a = acc[m];
-            a = fmaf(dsc0, x[m][0].d * static_cast<float>(ia), a);
-            a = fmaf(-dmn0, xsd[m][0], a);
-            a = fmaf(dsc1, x[m][1].d * static_cast<float>(ib), a);
-            a = fmaf(-dmn1, xsd[m][1], a);
-            acc[m] = a;
+            float S = 0.0f, M = 0.0f;
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                S = fmaf(sc[r], xdd[m][r] * digits_to_float<DIG>(hs[r], ls[r]), S);
+                M = fmaf(mn[r], xsd[m][r], M);
+            }
+            acc[m] = fmaf(d, S, fmaf(-dmin, M, acc[m]));
         }
     }
 };
@@ -250,15 +383,15 @@ struct Q4KDot {
 template <int DIG, int MR>
 struct Q6KDot {
     using X = XRun<DIG, 16>;
-    __device__ static void run(uint32_t ba, int t, const X (&x)[MR][2], float (&acc)[MR], int (&isum)[2]) {
+    __device__ static void run(uint32_t ba, int t, const X (&x)[MR][2], float (&acc)[MR], int (&isum)[4]) {
         const int h = t >> 2, c = (t >> 1) & 1, i16 = t & 1;
         uint32_t ql[4], qh[4];
         lds_words_unaligned<4>(ba + 64u * h + 32u * c + 16u * i16, ql);
         lds_words_unaligned<4>(ba + 128u + 32u * h + 16u * i16, qh);
         const int g0 = 4 * h + c, g1 = g0 + 2;
         const float d = half_bits_to_float(lds_u16(ba + 208u));
-        const float s0 = d * static_cast<float>(lds_s8(ba + 192u + 2u * g0 + i16));
-        const float s1 = d * static_cast<float>(lds_s8(ba + 192u + 2u * g1 + i16));
+        const float s0 = d * i2f_small(lds_s8(ba + 192u + 2u * g0 + i16));
+        const float s1 = d * i2f_small(lds_s8(ba + 192u + 2u * g1 + i16));
         const uint32_t sh0 = 2u * c, sh1 = 2u * c + 4u;
         uint32_t u0[4], u1[4];
 #pragma unroll
@@ -281,60 +414,69 @@ struct Q6KDot {
                 isum[0] = ia;
                 isum[1] = ib;
             }
+            const float fa = fmaf(-32.0f, x[m][0].fsum, digits_to_float<DIG>(a_hi, a_lo));
+            const float fb = fmaf(-32.0f, x[m][1].fsum, digits_to_float<DIG>(b_hi, b_lo));
             float a = acc[m];
-            a = fmaf(s0, x[m][0].d * static_cast<float>(ia), a);
-            a = fmaf(s1, x[m][1].d * static_cast<float>(ib), a);
+            a = fmaf(s0, x[m][0].d * fa, a);
+            a = fmaf(s1, x[m][1].d * fb, a);
             acc[m] = a;
         }
     }
 };
 
-// Q8_0 (quantized_matmul.cpp:1041-1081): fp16 d then 32 int8 codes.
+// Q8_0 (quantized_matmul.cpp:1041-1081): fp16 d then 32 int8 codes. The
+// lane's two blocks are consecutive; `v1` is false when the second lies past
+// the end of the row (its contribution is dropped).
 template <int DIG, int MR>
 struct Q80Dot {
     using X = XRun<DIG, 32>;
-    __device__ static void run(uint32_t ba, const X (&x)[MR][1], float (&acc)[MR], int (&isum)[2]) {
-        uint32_t q[8];
-        lds_words_unaligned<8>(ba + 2u, q);
-        const float d = half_bits_to_float(lds_u16(ba));
+    __device__ static void run(uint32_t ba, bool v1, const X (&x)[MR][2], float (&acc)[MR], int (&isum)[4]) {
+        uint32_t q[2][8];
+        lds_words_unaligned<8>(ba + 2u, q[0]);
+        lds_words_unaligned<8>(ba + 36u, q[1]);
+        const float d[2] = {half_bits_to_float(lds_u16(ba)), v1 ? half_bits_to_float(lds_u16(ba + 34u)) : 0.0f};
 #pragma unroll
         for (int m = 0; m < MR; ++m) {
-            int a_hi = 0, a_lo = 0;
 #pragma unroll
-            for (int w = 0; w < 8; ++w) dot4<DIG, true>(q[w], x[m][0].hi[w], DIG == 2 ? x[m][0].lo[w] : 0u, a_hi, a_lo);
-            const int ia = combine_digits<DIG>(a_hi, a_lo);
-            if (m == 0) isum[0] = ia;
-            acc[m] = fmaf(d, x[m][0].d * static_cast<float>(ia), acc[m]);
+            for (int b = 0; b < 2; ++b) {
+                int a_hi = 0, a_lo = 0;
+#pragma unroll
+                for (int w = 0; w < 8; ++w)
+                    dot4<DIG, true>(q[b][w], x[m][b].hi[w], DIG == 2 ? x[m][b].lo[w] : 0u, a_hi, a_lo);
+                if (m == 0) isum[b] = combine_digits<DIG>(a_hi, a_lo);
+                acc[m] = fmaf(d[b], x[m][b].d * digits_to_float<DIG>(a_hi, a_lo), acc[m]);
+            }
         }
     }
 };
 
 // Q4_0 (ggml type 2): fp16 d then 16 bytes; element i < 16 is the low
-// nibble of byte i, element 16 + i the high nibble; value d * (q - 8).
+// nibble of byte i, element 16 + i the high nibble; value d * (q - 8). Two
+// consecutive blocks per lane, as for Q8_0.
 template <int DIG, int MR>
 struct Q40Dot {
     using X = XRun<DIG, 32>;
-    __device__ static void run(uint32_t ba, const X (&x)[MR][1], float (&acc)[MR], int (&isum)[2]) {
-        uint32_t q[4];
-        lds_words_unaligned<4>(ba + 2u, q);
-        const float d = half_bits_to_float(lds_u16(ba));
-        uint32_t lo[4], hi[4];
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            lo[w] = q[w] & 0x0F0F0F0Fu;
-            hi[w] = (q[w] >> 4) & 0x0F0F0F0Fu;
-        }
+    __device__ static void run(uint32_t ba, bool v1, const X (&x)[MR][2], float (&acc)[MR], int (&isum)[4]) {
+        uint32_t q[2][4];
+        lds_words_unaligned<4>(ba + 2u, q[0]);
+        lds_words_unaligned<4>(ba + 20u, q[1]);
+        const float d[2] = {half_bits_to_float(lds_u16(ba)), v1 ? half_bits_to_float(lds_u16(ba + 18u)) : 0.0f};
 #pragma unroll
         for (int m = 0; m < MR; ++m) {
-            int a_hi = 0, a_lo = 0;
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
-                dot4<DIG, false>(lo[w], x[m][0].hi[w], DIG == 2 ? x[m][0].lo[w] : 0u, a_hi, a_lo);
-                dot4<DIG, false>(hi[w], x[m][0].hi[4 + w], DIG == 2 ? x[m][0].lo[4 + w] : 0u, a_hi, a_lo);
+            for (int b = 0; b < 2; ++b) {
+                int a_hi = 0, a_lo = 0;
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    const uint32_t lo = q[b][w] & 0x0F0F0F0Fu;
+                    const uint32_t hi = (q[b][w] >> 4) & 0x0F0F0F0Fu;
+                    dot4<DIG, false>(lo, x[m][b].hi[w], DIG == 2 ? x[m][b].lo[w] : 0u, a_hi, a_lo);
+                    dot4<DIG, false>(hi, x[m][b].hi[4 + w], DIG == 2 ? x[m][b].lo[4 + w] : 0u, a_hi, a_lo);
+                }
+                if (m == 0) isum[b] = combine_digits<DIG>(a_hi, a_lo) - 8 * x[m][b].sum;
+                const float fa = fmaf(-8.0f, x[m][b].fsum, digits_to_float<DIG>(a_hi, a_lo));
+                acc[m] = fmaf(d[b], x[m][b].d * fa, acc[m]);
             }
-            const int ia = combine_digits<DIG>(a_hi, a_lo) - 8 * x[m][0].sum;
-            if (m == 0) isum[0] = ia;
-            acc[m] = fmaf(d, x[m][0].d * static_cast<float>(ia), acc[m]);
         }
     }
 };
@@ -345,7 +487,7 @@ struct Q40Dot {
 template <int DIG, int MR>
 struct Q6KLMDot {
     using X = XRun<DIG, 32>;
-    __device__ static void run(uint32_t ba, int t, const X (&x)[MR][1], float (&acc)[MR], int (&isum)[2]) {
+    __device__ static void run(uint32_t ba, int t, const X (&x)[MR][1], float (&acc)[MR], int (&isum)[4]) {
         uint32_t q[8];
 #pragma unroll
         for (int w = 0; w < 8; ++w) q[w] = lds32(ba + 32u * t + 4u * w);
@@ -355,8 +497,8 @@ struct Q6KLMDot {
             const uint32_t db = lds32(ba + 272u);
             dd = __uint_as_float(db);
         }
-        const float s0 = dd * static_cast<float>(static_cast<int8_t>(scw & 0xFFu));
-        const float s1 = dd * static_cast<float>(static_cast<int8_t>((scw >> 8) & 0xFFu));
+        const float s0 = dd * i2f_small(static_cast<int8_t>(scw & 0xFFu));
+        const float s1 = dd * i2f_small(static_cast<int8_t>((scw >> 8) & 0xFFu));
 #pragma unroll
         for (int m = 0; m < MR; ++m) {
             int a_hi = 0, a_lo = 0, b_hi = 0, b_lo = 0;
@@ -371,14 +513,14 @@ struct Q6KLMDot {
                 isum[0] = ia;
                 isum[1] = ib;
             }
-            acc[m] = fmaf(s0, x[m][0].d * static_cast<float>(ia), acc[m]);
-            acc[m] = fmaf(s1, x[m][0].d * static_cast<float>(ib), acc[m]);
+            acc[m] = fmaf(s0, x[m][0].d * digits_to_float<DIG>(a_hi, a_lo), acc[m]);
+            acc[m] = fmaf(s1, x[m][0].d * digits_to_float<DIG>(b_hi, b_lo), acc[m]);
         }
     }
 };
 
-// Byte offset of (row, blk) inside a stage whose first row is `r0`
-// (a multiple of 4 for the R4 layouts).
+// Byte offset of (row, blk) inside a stage whose first row is `r0` (a
+// multiple of 4 for the R4 layouts).
 template <int QT>
 __device__ __forceinline__ uint32_t stage_offset(int row, int r0, int blk, long long row_bytes, int n) {
     using F = Fmt<QT>;
@@ -393,26 +535,31 @@ __device__ __forceinline__ uint32_t stage_offset(int row, int r0, int blk, long 
 }
 
 // ---------------------------------------------------------------------------
-// The kernel.
+// The kernel: one CTA per SM streams a contiguous slab of rows through a
+// ring of NS shared-memory stages. Warp NW (the producer) issues one bulk
+// copy per stage (~32 KB, L2 evict-first); the NW consumer warps are a grid
+// of S k-slices x WR walkers, and every consumer warp takes its rows of every
+// stage (rows walker, walker + WR, ...), so all warps release each stage at
+// about the same time.
 // ---------------------------------------------------------------------------
 template <int QT, int DIG, int MR, bool DBG>
-__global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(const GemvParams p) {
     using F = Fmt<QT>;
     constexpr int RUN = F::kRun;
     constexpr int RUNS = F::kRuns;
+    constexpr int NG = F::kGroupsPerLane;
     using X = XRun<DIG, RUN>;
 
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const int n_cons_warps = p.S * p.WR;
-    const int n_cons_threads = n_cons_warps * 32;
+    const int nwarps = p.S * p.WR;
+    const int nthreads = nwarps * 32;
 
     uint8_t* ring = smem;
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + static_cast<size_t>(p.NS) * p.stage_stride);
     uint64_t* empty = full + p.NS;
-    float* part = reinterpret_cast<float*>(empty + p.NS);  // [2][R][MR][S]
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(part + 2 * p.R * MR * p.S);
+    float* part = reinterpret_cast<float*>(empty + p.NS);  // [rows of this CTA][MR][S]
 
     const int q0 = static_cast<int>(static_cast<long long>(blockIdx.x) * p.n_quads / gridDim.x);
     const int q1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * p.n_quads / gridDim.x);
@@ -423,25 +570,31 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvPara
     if (tid == 0) {
         for (int i = 0; i < p.NS; ++i) {
             mbar_init(smem_addr(full + i), 1);
-            mbar_init(smem_addr(empty + i), static_cast<uint32_t>(n_cons_warps));
+            mbar_init(smem_addr(empty + i), static_cast<uint32_t>(nwarps));
         }
-        *abort_flag = 0;
         fence_mbar_init();
     }
     __syncthreads();
+    // Let the next kernel in the stream launch as soon as SMs free up; it
+    // still waits (griddepcontrol.wait) for this grid before touching its
+    // own inputs.
+    griddep_launch_dependents();
 
-    if (warp == n_cons_warps) {
+    if (warp == nwarps) {
         // ---------------- producer ----------------
+        // Weights may stream before the preceding kernel finishes only when
+        // the caller declared them static.
+        if (!p.w_static) griddep_wait();
         if (lane == 0 && n_stages > 0) {
             const uint64_t pol = l2_policy_evict_first();
             int issued = 0;
-            for (int s = 0; s < n_stages; ++s) {
+            bool ok = true;
+            for (int s = 0; s < n_stages && ok; ++s) {
                 const int slot = s % p.NS;
                 const uint32_t use = static_cast<uint32_t>(s / p.NS);
-                if (*abort_flag) break;
                 if (!mbar_wait_bounded(smem_addr(empty + slot), (use & 1u) ^ 1u)) {
                     *p.status = STATUS_TIMEOUT;
-                    *abort_flag = 1;
+                    ok = false;
                     break;
                 }
                 // Copy the 16-byte-aligned window around the stage's rows;
@@ -458,11 +611,8 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvPara
             }
             // Do not let the CTA retire with copies in flight: wait (bounded)
             // for the last stages issued.
-            for (int s = max(0, issued - p.NS); s < issued; ++s) {
-                const int slot = s % p.NS;
-                const uint32_t use = static_cast<uint32_t>(s / p.NS);
-                (void)mbar_wait_bounded(smem_addr(full + slot), use & 1u);
-            }
+            for (int s = max(0, issued - p.NS); s < issued; ++s)
+                (void)mbar_wait_bounded(smem_addr(full + s % p.NS), static_cast<uint32_t>((s / p.NS) & 1));
         }
         return;
     }
@@ -470,36 +620,37 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvPara
     // ---------------- consumers ----------------
     const int slice = warp % p.S;
     const int walker = warp / p.S;
-    const int t = lane % F::kLanesPerBlock;
-    const int blk = slice * F::kBlocksPerSlice + lane / F::kLanesPerBlock;
+    const int t = F::lane_part(lane);
+    const int blk = slice * F::kBlocksPerSlice + F::lane_block(lane);
     const bool active = blk < p.nb;
+    const bool active1 = blk + 1 < p.nb;  // second block of a two-block lane
+    const int blk_c = active ? blk : 0;
 
-    // Activations may be written by the preceding kernel in the stream.
+    // The quantized activations are written by the preceding kernel.
     griddep_wait();
-
     X x[MR][RUNS];
-    float xsd[MR][RUNS];
+    float xdd[MR][RUNS];  // group scale (with the x16 factor of in-place high nibbles folded in)
+    float xsd[MR][RUNS];  // group scale * group code sum (Q4_K mins)
 #pragma unroll
     for (int m = 0; m < MR; ++m) {
 #pragma unroll
         for (int r = 0; r < RUNS; ++r) {
-            const int e = active ? F::run_start(blk, t, r) : 0;
-            quantize_run<DIG, RUN>(p.x + m * p.x_stride + e, active, x[m][r]);
-            xsd[m][r] = x[m][r].d * static_cast<float>(x[m][r].sum);
+            const int e = F::run_start(blk_c, t, r);
+            load_run<DIG, RUN>(p.xq + m * p.xq_stride, p.k, e < p.k ? e : 0, x[m][r]);
+            xdd[m][r] = ((QT == QT_Q4_K || QT == QT_Q4_K_R4) && (r & 1)) ? x[m][r].d * 0.0625f : x[m][r].d;
+            xsd[m][r] = x[m][r].d * x[m][r].fsum;
         }
     }
 
+    bool ok = true;
     const uint32_t ring_base = smem_addr(ring);
     for (int s = 0; s < n_stages; ++s) {
         const int slot = s % p.NS;
         const uint32_t use = static_cast<uint32_t>(s / p.NS);
         const int r0 = r_begin + s * p.R;
         const int rows = min(p.R, r_end - r0);
-        const int buf = s & 1;
-        bool ok = !*abort_flag;
         if (ok && !mbar_wait_bounded(smem_addr(full + slot), use & 1u)) {
             if (lane == 0) *p.status = STATUS_TIMEOUT;
-            *abort_flag = 1;
             ok = false;
         }
         const uint32_t sbase = ring_base + static_cast<uint32_t>(slot) * static_cast<uint32_t>(p.stage_stride) +
@@ -509,49 +660,52 @@ __global__ void __launch_bounds__(kGemvMaxThreads, 1) gemv_kernel(const GemvPara
             float acc[MR];
 #pragma unroll
             for (int m = 0; m < MR; ++m) acc[m] = 0.0f;
-            int isum[2] = {0, 0};
-            if (ok && active) {
-                const uint32_t ba = sbase + stage_offset<QT>(row, r0, blk, p.row_bytes, p.n);
+            int isum[4] = {0, 0, 0, 0};
+            if (ok) {
+                const uint32_t ba = sbase + stage_offset<QT>(row, r0, blk_c, p.row_bytes, p.n);
                 if constexpr (QT == QT_Q4_K || QT == QT_Q4_K_R4) {
-                    Q4KDot<DIG, MR>::run(ba, t, x, xsd, acc, isum);
+                    Q4KDot<DIG, MR>::run(ba, t, x, xdd, xsd, acc, isum);
                 } else if constexpr (QT == QT_Q6_K || QT == QT_Q6_K_R4) {
                     Q6KDot<DIG, MR>::run(ba, t, x, acc, isum);
                 } else if constexpr (QT == QT_Q8_0) {
-                    Q80Dot<DIG, MR>::run(ba, x, acc, isum);
+                    Q80Dot<DIG, MR>::run(ba, active1, x, acc, isum);
                 } else if constexpr (QT == QT_Q4_0) {
-                    Q40Dot<DIG, MR>::run(ba, x, acc, isum);
+                    Q40Dot<DIG, MR>::run(ba, active1, x, acc, isum);
                 } else if constexpr (QT == QT_Q6_K_LM) {
                     Q6KLMDot<DIG, MR>::run(ba, t, x, acc, isum);
                 }
                 if constexpr (DBG) {
-                    const int ng = p.k / F::kGroup;
+                    if (active) {
+                        const int ng = p.k / F::kGroup;
 #pragma unroll
-                    for (int r = 0; r < 2; ++r) {
-                        const bool has = (QT == QT_Q8_0 || QT == QT_Q4_0) ? (r == 0) : true;
-                        if (has) p.dbg[static_cast<long long>(row) * ng + F::group_index(blk, t, r)] = isum[r];
+                        for (int r = 0; r < NG; ++r)
+                            if (F::kBlocksPerLane == 1 || r == 0 || active1)
+                                p.dbg[static_cast<long long>(row) * ng + F::group_index(blk, t, r)] = isum[r];
                     }
                 }
             }
 #pragma unroll
             for (int m = 0; m < MR; ++m) {
-                float v = acc[m];
+                float v = active ? acc[m] : 0.0f;
 #pragma unroll
                 for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-                if (lane == 0) part[((buf * p.R + rl) * MR + m) * p.S + slice] = v;
+                if (lane == 0) part[((row - r_begin) * MR + m) * p.S + slice] = v;
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_addr(empty + slot));
-        named_bar_sync(1, static_cast<uint32_t>(n_cons_threads));
-        for (int i = tid; i < rows * MR; i += n_cons_threads) {
-            const int rl = i / MR, m = i % MR;
-            const float* pp = part + ((buf * p.R + rl) * MR + m) * p.S;
-            float v = 0.0f;
-            for (int j = 0; j < p.S; ++j) v += pp[j];
-            p.y[m * p.y_stride + r0 + rl] = v;
-        }
     }
-    griddep_launch_dependents();
+    // One barrier for the consumers: sum the slice partials of every row in a
+    // fixed order and write y (zeros for rows a timed-out wait skipped are
+    // flagged through the status word).
+    named_bar_sync(1, static_cast<uint32_t>(nthreads));
+    for (int i = tid; i < (r_end - r_begin) * MR; i += nthreads) {
+        const int rl = i / MR, m = i % MR;
+        const float* pp = part + (rl * MR + m) * p.S;
+        float v = 0.0f;
+        for (int j = 0; j < p.S; ++j) v += pp[j];
+        p.y[m * p.y_stride + r_begin + rl] = v;
+    }
 }
 
 }  // namespace b200q

@@ -33,7 +33,8 @@ int current_device_state(Device** out);
 // Launch the decode GEMV for m activation rows (looping over row chunks).
 // All pointers are device pointers. Returns a B200Q_* status.
 int launch_gemv(int qtype, int act_mode, const void* w, const float* x, float* y, int m, int k, int n,
-                long long x_stride, long long y_stride, int32_t* isums, Device* dev, cudaStream_t st, bool pdl);
+                long long x_stride, long long y_stride, int32_t* isums, Device* dev, cudaStream_t st, bool pdl,
+                int flags = 0);
 
 bool pdl_enabled();
 void set_last_error(int status);

@@ -204,6 +204,9 @@ class DeviceMatrix:
         # +16 bytes: kernels copy 16-byte-aligned windows around rows.
         buf = torch.empty(flat.numel() + 16, dtype=torch.uint8, device=flat.device)
         buf[: flat.numel()].copy_(flat)
+        # Weights are immutable from here on: once the upload has completed,
+        # kernels may stream them ahead of their grid dependency.
+        torch.cuda.synchronize(flat.device)
         self.buffer = buf
         self.qtype = int(qtype)
         self.input_dim = int(input_dim)
@@ -234,10 +237,11 @@ def matmul_device(x, matrix: DeviceMatrix, out=None, act_mode: int = _native.ACT
     if out is None:
         out = torch.empty((m, matrix.output_dim), dtype=torch.float32, device=xx.device)
     st = torch.cuda.current_stream(xx.device).cuda_stream
-    rc = _native.lib().b200q_matmul(
-        matrix.qtype, int(act_mode), xx.data_ptr(), matrix.ptr, out.data_ptr(), m, matrix.input_dim, matrix.output_dim, st
+    rc = _native.lib().b200q_matmul_ex(
+        matrix.qtype, int(act_mode), xx.data_ptr(), matrix.ptr, out.data_ptr(), m, matrix.input_dim, matrix.output_dim,
+        _native.WEIGHTS_STATIC, st,
     )
-    _native.check(rc, "b200q_matmul")
+    _native.check(rc, "b200q_matmul_ex")
     return out.reshape(-1) if squeeze else out
 
 

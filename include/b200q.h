@@ -63,6 +63,7 @@ extern "C" {
 #define B200Q_ENOMEM (-6)      /* device allocation failed */
 #define B200Q_ETIMEOUT (-7)    /* a kernel's bounded pipeline wait gave up */
 #define B200Q_ENODEV (-8)      /* no usable sm_100 device */
+#define B200Q_ECAPTURE (-9)    /* scratch must grow while the stream is being captured */
 
 /* ---------------------------------------------------------------------
  * 1. Drop-in entry points (host pointers), reference signatures.
@@ -100,6 +101,15 @@ B200Q_API void simd_matmul_q4_0(const float* x, const void* a_quant, float* y, i
  * computation of QM:1536-2154 for callers whose buffers live in HBM. */
 B200Q_API int b200q_matmul(int qtype, int act_mode, const float* x, const void* w, float* y, int m, int k, int n,
                  void* stream);
+
+/* b200q_matmul with flags. B200Q_WEIGHTS_STATIC declares that no kernel
+ * still running or queued ahead of this call on `stream` writes `w`; with
+ * programmatic dependent launch (default on, see b200q_set_pdl) the kernel
+ * then starts streaming weights while the preceding kernel drains, and only
+ * waits for it before reading x and writing y. */
+#define B200Q_WEIGHTS_STATIC 1
+B200Q_API int b200q_matmul_ex(int qtype, int act_mode, const float* x, const void* w, float* y, int m, int k, int n,
+                              int flags, void* stream);
 
 /* Debug form of b200q_matmul for m == 1: additionally writes the exact
  * per-group integer dot sums  sum_i code_i * q_i  to isums[n][k / G]
