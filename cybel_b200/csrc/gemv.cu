@@ -1,5 +1,6 @@
 // Launch planning and dispatch for the decode GEMV kernels (gemv.cuh).
 #include <algorithm>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -30,8 +31,15 @@ long long row_bytes_of(int qtype, int k) {
 
 namespace {
 
+int env_int(const char* name, int dflt) {
+    const char* e = std::getenv(name);
+    if (!e || !*e) return dflt;
+    const int v = std::atoi(e);
+    return v > 0 ? v : dflt;
+}
+
 constexpr int kSmemBudget = 220 * 1024;   // ring + bookkeeping per CTA
-constexpr int kStageTarget = 32 * 1024;   // preferred bytes per stage
+constexpr int kStageTargetKB = 48;        // preferred bytes per stage (KB)
 constexpr int kStageMax = 96 * 1024;      // largest stage
 constexpr int kMaxStages = 8;
 
@@ -52,16 +60,17 @@ int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl) {
     const int S = (nb + f.blocks_per_slice - 1) / f.blocks_per_slice;
     const int max_warps = (dig == 1 && MR == 1) ? 16 : 12;  // kGemvWarps in gemv.cuh
     if (S > max_warps) return B200Q_ESHAPE;
-    const int WR = std::max(1, max_warps / S);
-    // Stage rows: WR (one row per walker) grown in steps of WR towards
-    // kStageTarget bytes; the R4 layouts need whole 4-row groups.
+    const int U = MR == 1 ? 2 : 1;  // kRowsPerIter in gemv.cuh
+    // Stage = WR walkers x U rows (x4-row groups for R4); walkers are capped
+    // so a stage stays near the target size (B200Q_STAGE_KB overrides it).
+    static const int target = env_int("B200Q_STAGE_KB", kStageTargetKB) * 1024;
+    int WR = std::max(1, max_warps / S);
+    while (WR > 1 && static_cast<long long>(WR) * U * rb > target) --WR;
     // A stage copies the 16-byte-aligned window around its rows: at most
     // rows * rb + 30 bytes; kSlotPad also covers the 4-byte over-read of the
     // unaligned word loads.
     constexpr int kSlotPad = 48;
-    const int step = f.r4 ? ((WR + 3) / 4) * 4 : WR;
-    int R = step;
-    while ((R + step) * rb + kSlotPad <= kStageTarget) R += step;
+    int R = f.r4 ? ((WR * U + 3) / 4) * 4 : WR * U;
     if (R * rb + kSlotPad > kStageMax) {
         R = f.r4 ? 4 : std::max<int>(1, static_cast<int>((kStageMax - kSlotPad) / rb));
         if (R * rb + kSlotPad > kStageMax) return B200Q_ESHAPE;

@@ -36,6 +36,10 @@ namespace b200q {
 // rows) take 12 consumer warps.
 template <int DIG, int MR>
 constexpr int kGemvWarps = (DIG == 1 && MR == 1) ? 16 : 12;
+// Rows a consumer warp carries per iteration (independent chains, and the
+// loop and reduction overhead shared between them).
+template <int DIG, int MR>
+constexpr int kRowsPerIter = MR == 1 ? 2 : 1;
 
 struct GemvParams {
     const uint8_t* W;      // packed weight rows (device, 16-byte aligned)
@@ -522,16 +526,49 @@ struct Q6KLMDot {
 // Byte offset of (row, blk) inside a stage whose first row is `r0` (a
 // multiple of 4 for the R4 layouts).
 template <int QT>
-__device__ __forceinline__ uint32_t stage_offset(int row, int r0, int blk, long long row_bytes, int n) {
+__device__ __forceinline__ uint32_t stage_offset(int row, int r0, int blk, uint32_t row_bytes, int n) {
     using F = Fmt<QT>;
     if (F::kR4) {
         const int full4 = (n / 4) * 4;
-        if (row < full4) {
-            const int g0 = row & ~3;
-            return static_cast<uint32_t>((g0 - r0) * row_bytes) + static_cast<uint32_t>((blk * 4 + (row & 3)) * F::kBytes);
-        }
+        if (row < full4)
+            return static_cast<uint32_t>((row & ~3) - r0) * row_bytes + static_cast<uint32_t>(blk * 4 + (row & 3)) * F::kBytes;
     }
-    return static_cast<uint32_t>((row - r0) * row_bytes) + static_cast<uint32_t>(blk * F::kBytes);
+    return static_cast<uint32_t>(row - r0) * row_bytes + static_cast<uint32_t>(blk) * F::kBytes;
+}
+
+// Sum V values across the warp, V in {1, 2, 4}: the first log2(V) butterfly
+// levels trade halves of the value set (each lane keeps one half), the rest
+// reduce the survivor. On return, lane (i >> 1) * 16 + (i & 1) * 8 ... more
+// precisely the lane whose bits 4..(5 - log2 V) spell index i holds sum i;
+// warp_sum_lane(i) gives it.
+template <int V>
+__device__ __forceinline__ float warp_sum_multi(float (&v)[V], int lane) {
+    if constexpr (V == 1) {
+        float a = v[0];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+        return a;
+    } else if constexpr (V == 2) {
+        const bool hi = (lane & 16) != 0;
+        float a = (hi ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, hi ? v[0] : v[1], 16);
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+        return a;
+    } else {
+        const bool h16 = (lane & 16) != 0;
+        const float b0 = (h16 ? v[2] : v[0]) + __shfl_xor_sync(0xffffffffu, h16 ? v[0] : v[2], 16);
+        const float b1 = (h16 ? v[3] : v[1]) + __shfl_xor_sync(0xffffffffu, h16 ? v[1] : v[3], 16);
+        const bool h8 = (lane & 8) != 0;
+        float a = (h8 ? b1 : b0) + __shfl_xor_sync(0xffffffffu, h8 ? b0 : b1, 8);
+#pragma unroll
+        for (int off = 4; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+        return a;
+    }
+}
+// Lane holding sum i after warp_sum_multi<V>.
+template <int V>
+__device__ __forceinline__ int warp_sum_lane(int i) {
+    return V == 1 ? 0 : (V == 2 ? 16 * i : 16 * (i >> 1) + 8 * (i & 1));
 }
 
 // ---------------------------------------------------------------------------
@@ -642,8 +679,11 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(
         }
     }
 
+    constexpr int U = kRowsPerIter<DIG, MR>;
+    constexpr int V = U * MR;
     bool ok = true;
     const uint32_t ring_base = smem_addr(ring);
+    const uint32_t rb32 = static_cast<uint32_t>(p.row_bytes);
     for (int s = 0; s < n_stages; ++s) {
         const int slot = s % p.NS;
         const uint32_t use = static_cast<uint32_t>(s / p.NS);
@@ -655,41 +695,61 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(
         }
         const uint32_t sbase = ring_base + static_cast<uint32_t>(slot) * static_cast<uint32_t>(p.stage_stride) +
                                static_cast<uint32_t>((r0 * p.row_bytes) & 15ll);
-        for (int rl = walker; rl < rows; rl += p.WR) {
-            const int row = r0 + rl;
-            float acc[MR];
+        for (int rl0 = walker * U; rl0 < rows; rl0 += p.WR * U) {
+            float acc[U][MR];
+            int isum[U][4];
 #pragma unroll
-            for (int m = 0; m < MR; ++m) acc[m] = 0.0f;
-            int isum[4] = {0, 0, 0, 0};
+            for (int u = 0; u < U; ++u) {
+#pragma unroll
+                for (int m = 0; m < MR; ++m) acc[u][m] = 0.0f;
+            }
             if (ok) {
-                const uint32_t ba = sbase + stage_offset<QT>(row, r0, blk_c, p.row_bytes, p.n);
-                if constexpr (QT == QT_Q4_K || QT == QT_Q4_K_R4) {
-                    Q4KDot<DIG, MR>::run(ba, t, x, xdd, xsd, acc, isum);
-                } else if constexpr (QT == QT_Q6_K || QT == QT_Q6_K_R4) {
-                    Q6KDot<DIG, MR>::run(ba, t, x, acc, isum);
-                } else if constexpr (QT == QT_Q8_0) {
-                    Q80Dot<DIG, MR>::run(ba, active1, x, acc, isum);
-                } else if constexpr (QT == QT_Q4_0) {
-                    Q40Dot<DIG, MR>::run(ba, active1, x, acc, isum);
-                } else if constexpr (QT == QT_Q6_K_LM) {
-                    Q6KLMDot<DIG, MR>::run(ba, t, x, acc, isum);
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    // A short last group repeats its last row; the copy's
+                    // results are discarded.
+                    const int row = r0 + min(rl0 + u, rows - 1);
+                    const uint32_t ba = sbase + stage_offset<QT>(row, r0, blk_c, rb32, p.n);
+                    if constexpr (QT == QT_Q4_K || QT == QT_Q4_K_R4) {
+                        Q4KDot<DIG, MR>::run(ba, t, x, xdd, xsd, acc[u], isum[u]);
+                    } else if constexpr (QT == QT_Q6_K || QT == QT_Q6_K_R4) {
+                        Q6KDot<DIG, MR>::run(ba, t, x, acc[u], isum[u]);
+                    } else if constexpr (QT == QT_Q8_0) {
+                        Q80Dot<DIG, MR>::run(ba, active1, x, acc[u], isum[u]);
+                    } else if constexpr (QT == QT_Q4_0) {
+                        Q40Dot<DIG, MR>::run(ba, active1, x, acc[u], isum[u]);
+                    } else if constexpr (QT == QT_Q6_K_LM) {
+                        Q6KLMDot<DIG, MR>::run(ba, t, x, acc[u], isum[u]);
+                    }
                 }
                 if constexpr (DBG) {
                     if (active) {
                         const int ng = p.k / F::kGroup;
 #pragma unroll
-                        for (int r = 0; r < NG; ++r)
-                            if (F::kBlocksPerLane == 1 || r == 0 || active1)
-                                p.dbg[static_cast<long long>(row) * ng + F::group_index(blk, t, r)] = isum[r];
+                        for (int u = 0; u < U; ++u) {
+                            if (rl0 + u < rows) {
+#pragma unroll
+                                for (int r = 0; r < NG; ++r)
+                                    if (F::kBlocksPerLane == 1 || r == 0 || active1)
+                                        p.dbg[static_cast<long long>(r0 + rl0 + u) * ng + F::group_index(blk, t, r)] =
+                                            isum[u][r];
+                            }
+                        }
                     }
                 }
             }
+            float v[V];
 #pragma unroll
-            for (int m = 0; m < MR; ++m) {
-                float v = active ? acc[m] : 0.0f;
+            for (int u = 0; u < U; ++u) {
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-                if (lane == 0) part[((row - r_begin) * MR + m) * p.S + slice] = v;
+                for (int m = 0; m < MR; ++m) v[u * MR + m] = active ? acc[u][m] : 0.0f;
+            }
+            const float tot = warp_sum_multi<V>(v, lane);
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                const int u = i / MR, m = i % MR;
+                if (lane == warp_sum_lane<V>(i) && rl0 + u < rows)
+                    part[((r0 - r_begin + rl0 + u) * MR + m) * p.S + slice] = tot;
             }
         }
         __syncwarp();
