@@ -38,8 +38,25 @@ for _q in ("q4k", "q4k_r4", "q6k", "q6k_r4", "q6k_lm", "q8_0", "q4_0"):
     SIGNATURES[f"simd_matvec_{_q}"] = ([_fp, _vp, _fp, _i, _i], None)
 for _q in ("q4k", "q4k_r4", "q6k", "q6k_r4", "q8_0", "q4_0"):
     SIGNATURES[f"simd_matmul_{_q}"] = ([_fp, _vp, _fp, _i, _i, _i], None)
+_ip = ctypes.POINTER(ctypes.c_int)
+_vpp = ctypes.POINTER(ctypes.c_void_p)
+_fpp = ctypes.POINTER(ctypes.POINTER(ctypes.c_float))
+_f = ctypes.c_float
 SIGNATURES.update(
     {
+        "simd_repack_q4k_r4": ([_vp, _vp, _i, _i], _i),
+        "simd_repack_q6k_r4": ([_vp, _vp, _i, _i], _i),
+        "simd_repack_q6k_lm": ([_vp, _vp, _i, _i], _i),
+        "simd_dequantize_row": ([_vp, _i, _i, _fp, _i], _i),
+        "simd_fused_qkv_matvec_quant": ([_fp, _vp, _i, _fp, _i, _vp, _i, _fp, _i, _vp, _i, _fp, _i, _i], _i),
+        "simd_fused_quad_matvec_quant": ([_fp, _vp, _i, _fp, _i, _vp, _i, _fp, _i, _vp, _i, _fp, _i, _vp, _i, _fp, _i, _i], _i),
+        "simd_fused_expert_swiglu": ([_fp, _i, _vp, _i, _i, _vp, _i, _vp, _i, _i, _fp], None),
+        "simd_fused_moe_ffn": ([_fp, _i, _ip, _fp, _i, _vpp, _i, _i, _vpp, _i, _vpp, _i, _i, _fp, _i], None),
+        "b200q_repack": ([_i, _vp, _vp, _i, _i, _vp], _i),
+        "b200q_dequantize_rows": ([_i, _vp, _vp, _i, _vp, _i, _i, _vp], _i),
+        "b200q_fused_matvec": ([_i, _vp, _i, _i, _vpp, _ip, _vpp, _ip, _i, _vp], _i),
+        "b200q_expert_swiglu": ([_i, _vp, _i, _vp, _i, _i, _vp, _i, _vp, _i, _i, _vp, _f, _f, _i, _vp], _i),
+        "b200q_moe_ffn": ([_i, _vp, _i, _ip, _fp, _i, _vpp, _i, _i, _vpp, _i, _vpp, _i, _i, _vp, _i, _i, _vp], _i),
         "b200q_matmul": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
         "b200q_matmul_ex": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
         "b200q_matvec_isums": ([_i, _i, _vp, _vp, _vp, _vp, _i, _i, _vp], _i),

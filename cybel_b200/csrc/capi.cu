@@ -1,6 +1,7 @@
 // C ABI of libb200q.so (declared in include/b200q.h): per-device state, the
 // resident weight cache behind the host-pointer drop-ins, and the drop-in and
 // device-pointer entry points.
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <map>
@@ -109,7 +110,25 @@ namespace {
 struct WeightEntry {
     void* dptr = nullptr;
     size_t bytes = 0;
+    uint64_t fingerprint = 0;
 };
+
+// FNV-1a over the size and three 64-byte samples (start, middle, end) of a
+// host matrix: a cheap guard against a freed buffer's address being reused
+// for different weights. It does not detect in-place edits of the middle of
+// a buffer; callers that mutate or free weights call b200q_weight_cache_evict.
+uint64_t fingerprint(const void* host, size_t bytes) {
+    const uint8_t* p = static_cast<const uint8_t*>(host);
+    uint64_t h = 1469598103934665603ull ^ bytes;
+    auto mix = [&](size_t off) {
+        const size_t end = std::min(bytes, off + 64);
+        for (size_t i = off; i < end; ++i) h = (h ^ p[i]) * 1099511628211ull;
+    };
+    mix(0);
+    if (bytes > 128) mix(bytes / 2 - 32);
+    if (bytes > 64) mix(bytes - 64);
+    return h;
+}
 std::mutex g_w_mu;
 std::map<std::pair<int, const void*>, WeightEntry> g_weights;
 long long g_weight_bytes = 0;
@@ -136,8 +155,9 @@ int weights_for(int dev, const void* host, size_t bytes, void** dptr, bool* temp
     std::lock_guard<std::mutex> lk(g_w_mu);
     auto key = std::make_pair(dev, host);
     auto it = g_weights.find(key);
+    const uint64_t fp = fingerprint(host, bytes);
     if (it != g_weights.end()) {
-        if (it->second.bytes == bytes) {
+        if (it->second.bytes == bytes && it->second.fingerprint == fp) {
             *dptr = it->second.dptr;
             return B200Q_OK;
         }
@@ -148,7 +168,7 @@ int weights_for(int dev, const void* host, size_t bytes, void** dptr, bool* temp
     void* d = nullptr;
     int rc = upload_weights(dev, host, bytes, &d);
     if (rc != B200Q_OK) return rc;
-    g_weights[key] = WeightEntry{d, bytes};
+    g_weights[key] = WeightEntry{d, bytes, fp};
     g_weight_bytes += static_cast<long long>(bytes);
     *dptr = d;
     return B200Q_OK;
@@ -162,6 +182,10 @@ struct Staging {
     size_t xcap = 0;
     float* dy = nullptr;
     size_t ycap = 0;
+    void* db = nullptr;  // generic device bytes (repack / dequant staging)
+    size_t bcap = 0;
+    void* db2 = nullptr;
+    size_t bcap2 = 0;
 };
 thread_local std::vector<Staging> t_staging;
 
@@ -184,6 +208,26 @@ int ensure_cap(float** p, size_t* cap, size_t floats) {
     if (cudaMalloc(reinterpret_cast<void**>(p), want * sizeof(float)) != cudaSuccess) return B200Q_ENOMEM;
     *cap = want;
     return B200Q_OK;
+}
+
+int ensure_bytes(void** p, size_t* cap, size_t bytes) {
+    if (*cap >= bytes) return B200Q_OK;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    const size_t want = std::max<size_t>(bytes + 16, 1u << 16);
+    if (cudaMalloc(p, want) != cudaSuccess) return B200Q_ENOMEM;
+    *cap = want;
+    return B200Q_OK;
+}
+
+// Device copy of a cached host matrix, if one is resident and covers
+// `need` bytes (no upload).
+void* cached_weights(int dev, const void* host, size_t need) {
+    std::lock_guard<std::mutex> lk(g_w_mu);
+    auto it = g_weights.find(std::make_pair(dev, host));
+    if (it != g_weights.end() && it->second.bytes >= need) return it->second.dptr;
+    return nullptr;
 }
 
 int act_mode_now() {
@@ -286,6 +330,339 @@ int b200q_matvec_isums(int qtype, int act_mode, const float* x, const void* w, f
                          static_cast<cudaStream_t>(stream), false);
     set_last_error(rc);
     return rc;
+}
+
+// ---- layout repacks ----------------------------------------------------------
+int b200q_repack(int dst_qtype, const void* src, void* dst, int k, int n, void* stream) {
+    const int rc = launch_repack(dst_qtype, src, dst, k, n, static_cast<cudaStream_t>(stream));
+    set_last_error(rc);
+    return rc;
+}
+
+namespace {
+// Host-pointer repack: upload, repack on the device, download. Returns 1 on
+// success, 0 otherwise (quantized_matmul.cpp:250-300 return convention).
+int host_repack(int dst_qtype, int src_block, int dst_block, const void* src, void* dst, int k, int n) {
+    if (!src || !dst || k <= 0 || n <= 0 || k % 256) {
+        set_last_error(B200Q_EINVAL);
+        return 0;
+    }
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    Staging* s = rc == B200Q_OK ? staging_for(dev->id) : nullptr;
+    if (!s) {
+        set_last_error(rc == B200Q_OK ? B200Q_ECUDA : rc);
+        return 0;
+    }
+    const size_t in_bytes = static_cast<size_t>(k / 256) * src_block * n;
+    const size_t out_bytes = static_cast<size_t>(k / 256) * dst_block * n;
+    rc = ensure_bytes(&s->db, &s->bcap, in_bytes);
+    if (rc == B200Q_OK) rc = ensure_bytes(&s->db2, &s->bcap2, out_bytes);
+    if (rc == B200Q_OK && cudaMemcpyAsync(s->db, src, in_bytes, cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
+        rc = B200Q_ECUDA;
+    if (rc == B200Q_OK) rc = launch_repack(dst_qtype, s->db, s->db2, k, n, s->stream);
+    if (rc == B200Q_OK && cudaMemcpyAsync(dst, s->db2, out_bytes, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess)
+        rc = B200Q_ECUDA;
+    if (cudaStreamSynchronize(s->stream) != cudaSuccess && rc == B200Q_OK) rc = B200Q_ECUDA;
+    set_last_error(rc);
+    return rc == B200Q_OK ? 1 : 0;
+}
+}  // namespace
+
+int simd_repack_q4k_r4(const void* src_q4k, void* dst_q4k_r4, int k, int n) {
+    return host_repack(QT_Q4_K_R4, 144, 144, src_q4k, dst_q4k_r4, k, n);
+}
+int simd_repack_q6k_r4(const void* src_q6k, void* dst_q6k_r4, int k, int n) {
+    return host_repack(QT_Q6_K_R4, 210, 210, src_q6k, dst_q6k_r4, k, n);
+}
+int simd_repack_q6k_lm(const void* src_q6k, void* dst_q6k_lm, int k, int n) {
+    return host_repack(QT_Q6_K_LM, 210, 276, src_q6k, dst_q6k_lm, k, n);
+}
+
+// ---- row dequantization -------------------------------------------------------
+int b200q_dequantize_rows(int qtype, const void* w, const int* rows, int nrows, float* out, int k, int n, void* stream) {
+    const int rc = launch_dequant_rows(qtype, w, rows, nrows, out, k, n, true, static_cast<cudaStream_t>(stream));
+    set_last_error(rc);
+    return rc;
+}
+
+int simd_dequantize_row(const void* quant_data, int qtype, int row, float* out, int k) {
+    FmtInfo f;
+    if (!quant_data || !out || row < 0 || k <= 0 || !fmt_info(qtype, f) || k % f.elems) {
+        set_last_error(B200Q_EINVAL);
+        return 0;
+    }
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    Staging* s = rc == B200Q_OK ? staging_for(dev->id) : nullptr;
+    if (!s) {
+        set_last_error(rc == B200Q_OK ? B200Q_ECUDA : rc);
+        return 0;
+    }
+    // Bytes the reference addressing reads for this row: the row itself, or
+    // its whole 4-row group for the R4 layouts (group = row / 4).
+    const size_t rb = static_cast<size_t>(k / f.elems) * f.bytes;
+    const size_t off = f.r4 ? static_cast<size_t>(row / 4) * 4 * rb : static_cast<size_t>(row) * rb;
+    const size_t len = f.r4 ? 4 * rb : rb;
+    const int local_row = f.r4 ? row % 4 : 0;
+    const void* dw = cached_weights(dev->id, quant_data, off + len);
+    int rows_host[1] = {dw ? row : local_row};
+    rc = ensure_bytes(&s->db, &s->bcap, (dw ? 0 : len) + 16);
+    if (rc == B200Q_OK) rc = ensure_cap(&s->dy, &s->ycap, static_cast<size_t>(k));
+    uint8_t* dbytes = static_cast<uint8_t*>(s->db);
+    int* drow = reinterpret_cast<int*>(dbytes);
+    uint8_t* dsrc = dbytes + 16;
+    if (rc == B200Q_OK && !dw &&
+        cudaMemcpyAsync(dsrc, static_cast<const uint8_t*>(quant_data) + off, len, cudaMemcpyHostToDevice, s->stream) !=
+            cudaSuccess)
+        rc = B200Q_ECUDA;
+    if (rc == B200Q_OK && cudaMemcpyAsync(drow, rows_host, sizeof(int), cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
+        rc = B200Q_ECUDA;
+    if (rc == B200Q_OK)
+        rc = launch_dequant_rows(qtype, dw ? dw : static_cast<const void*>(dsrc), drow, 1, s->dy, k, dw ? 0 : 4, false,
+                                 s->stream);
+    if (rc == B200Q_OK && cudaMemcpyAsync(out, s->dy, sizeof(float) * k, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess)
+        rc = B200Q_ECUDA;
+    if (cudaStreamSynchronize(s->stream) != cudaSuccess && rc == B200Q_OK) rc = B200Q_ECUDA;
+    set_last_error(rc);
+    return rc == B200Q_OK ? 1 : 0;
+}
+
+// ---- fused multi-matrix matvec (one activation quantization) -----------------
+int b200q_fused_matvec(int act_mode, const float* x, int cols, int count, const void* const* w, const int* qtypes,
+                       float* const* y, const int* rows, int flags, void* stream) {
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (rc == B200Q_OK && (!x || !w || !qtypes || !y || !rows || count <= 0 || cols <= 0)) rc = B200Q_EINVAL;
+    for (int i = 0; rc == B200Q_OK && i < count; ++i) {
+        if (!w[i] || !y[i] || rows[i] <= 0) rc = B200Q_EINVAL;
+        else rc = gemv_check_shape(qtypes[i], act_mode, cols, rows[i], dev);
+    }
+    const uint8_t* xq = nullptr;
+    long long xq_row = 0;
+    if (rc == B200Q_OK) rc = quantize_activations(act_mode, x, cols, 1, cols, dev, st, pdl_enabled(), 1, &xq, &xq_row);
+    for (int i = 0; rc == B200Q_OK && i < count; ++i)
+        rc = gemv_from_xq(qtypes[i], act_mode, w[i], xq, xq_row, y[i], 1, cols, rows[i], rows[i], 1.0f, 0.0f, nullptr,
+                          dev, st, pdl_enabled(), flags);
+    set_last_error(rc);
+    return rc;
+}
+
+namespace {
+bool fused_supported(int q) { return q == QT_Q4_K || q == QT_Q4_K_R4 || q == QT_Q6_K || q == QT_Q6_K_R4; }
+
+// Host-pointer fused matvec: count matrices sharing x (quantized_matmul.cpp:
+// 1855-1942). Returns 1 on success, 0 on invalid arguments (outputs untouched).
+int host_fused(const float* x, int cols, int count, const void* const* data, const int* qt, float* const* outs,
+               const int* rows) {
+    if (!x || cols <= 0) return 0;
+    for (int i = 0; i < count; ++i)
+        if (!data[i] || !outs[i] || rows[i] <= 0 || !fused_supported(qt[i]) || row_bytes_of(qt[i], cols) < 0) return 0;
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    Staging* s = rc == B200Q_OK ? staging_for(dev->id) : nullptr;
+    if (!s) {
+        set_last_error(rc == B200Q_OK ? B200Q_ECUDA : rc);
+        return 0;
+    }
+    const void* dws[4];
+    float* dys[4];
+    size_t total_rows = 0;
+    for (int i = 0; i < count; ++i) total_rows += static_cast<size_t>(rows[i]);
+    rc = ensure_cap(&s->dx, &s->xcap, static_cast<size_t>(cols));
+    if (rc == B200Q_OK) rc = ensure_cap(&s->dy, &s->ycap, total_rows);
+    size_t o = 0;
+    for (int i = 0; rc == B200Q_OK && i < count; ++i) {
+        bool temporary = false;
+        void* dw = nullptr;
+        rc = weights_for(dev->id, data[i], static_cast<size_t>(row_bytes_of(qt[i], cols)) * rows[i], &dw, &temporary);
+        if (temporary) {  // residency disabled: keep the upload for this call only
+            cudaStreamSynchronize(s->stream);
+        }
+        dws[i] = dw;
+        dys[i] = s->dy + o;
+        o += static_cast<size_t>(rows[i]);
+    }
+    if (rc == B200Q_OK && cudaMemcpyAsync(s->dx, x, sizeof(float) * cols, cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
+        rc = B200Q_ECUDA;
+    if (rc == B200Q_OK) {
+        *dev->status_host = 0;
+        rc = b200q_fused_matvec(act_mode_now(), s->dx, cols, count, dws, qt, dys, rows, B200Q_WEIGHTS_STATIC, s->stream);
+    }
+    for (int i = 0; rc == B200Q_OK && i < count; ++i)
+        if (cudaMemcpyAsync(outs[i], dys[i], sizeof(float) * rows[i], cudaMemcpyDeviceToHost, s->stream) != cudaSuccess)
+            rc = B200Q_ECUDA;
+    if (cudaStreamSynchronize(s->stream) != cudaSuccess && rc == B200Q_OK) rc = B200Q_ECUDA;
+    if (rc == B200Q_OK && *dev->status_host != 0) rc = B200Q_ETIMEOUT;
+    set_last_error(rc);
+    return rc == B200Q_OK ? 1 : 0;
+}
+}  // namespace
+
+int simd_fused_qkv_matvec_quant(const float* x, const void* q_data, int q_qtype, float* q_out, int q_rows,
+                                const void* k_data, int k_qtype, float* k_out, int k_rows, const void* v_data,
+                                int v_qtype, float* v_out, int v_rows, int cols) {
+    const void* d[3] = {q_data, k_data, v_data};
+    const int qt[3] = {q_qtype, k_qtype, v_qtype};
+    float* o[3] = {q_out, k_out, v_out};
+    const int r[3] = {q_rows, k_rows, v_rows};
+    return host_fused(x, cols, 3, d, qt, o, r);
+}
+
+int simd_fused_quad_matvec_quant(const float* x, const void* a_data, int a_qtype, float* a_out, int a_rows,
+                                 const void* b_data, int b_qtype, float* b_out, int b_rows, const void* c_data,
+                                 int c_qtype, float* c_out, int c_rows, const void* d_data, int d_qtype, float* d_out,
+                                 int d_rows, int cols) {
+    const void* d[4] = {a_data, b_data, c_data, d_data};
+    const int qt[4] = {a_qtype, b_qtype, c_qtype, d_qtype};
+    float* o[4] = {a_out, b_out, c_out, d_out};
+    const int r[4] = {a_rows, b_rows, c_rows, d_rows};
+    return host_fused(x, cols, 4, d, qt, o, r);
+}
+
+// ---- fused SwiGLU expert and MoE FFN -------------------------------------------
+int b200q_expert_swiglu(int act_mode, const float* x, int in_dim, const void* gate, int gq, int hidden, const void* up,
+                        int uq, const void* down, int dq, int out_dim, float* out, float alpha, float beta, int flags,
+                        void* stream) {
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    if (rc == B200Q_OK)
+        rc = expert_swiglu(act_mode, x, in_dim, gate, gq, hidden, up, uq, down, dq, out_dim, out, alpha, beta, dev,
+                           static_cast<cudaStream_t>(stream), pdl_enabled(), flags);
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_moe_ffn(int act_mode, const float* x, int in_dim, const int* expert_indices, const float* expert_weights,
+                  int top_k, const void* const* gate_ptrs, int gq, int hidden, const void* const* up_ptrs, int uq,
+                  const void* const* down_ptrs, int dq, int out_dim, float* out, int write_mode, int flags,
+                  void* stream) {
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (rc == B200Q_OK && (!x || !out || top_k <= 0 || !expert_indices || !expert_weights)) rc = B200Q_EINVAL;
+    // Experts with a non-positive weight or a missing matrix are skipped;
+    // write_mode 0 overwrites out (zero when no expert contributes), other
+    // values accumulate into it (quantized_matmul.cpp:2426-2525).
+    bool have = write_mode != 0;
+    for (int e = 0; rc == B200Q_OK && e < top_k; ++e) {
+        const int idx = expert_indices[e];
+        const float w = expert_weights[e];
+        if (!(w > 0.0f) || idx < 0) continue;
+        if (!gate_ptrs[idx] || !up_ptrs[idx] || !down_ptrs[idx]) continue;
+        rc = expert_swiglu(act_mode, x, in_dim, gate_ptrs[idx], gq, hidden, up_ptrs[idx], uq, down_ptrs[idx], dq, out_dim,
+                           out, w, have ? 1.0f : 0.0f, dev, st, pdl_enabled(), flags);
+        have = true;
+    }
+    if (rc == B200Q_OK && !have && cudaMemsetAsync(out, 0, sizeof(float) * out_dim, st) != cudaSuccess) rc = B200Q_ECUDA;
+    set_last_error(rc);
+    return rc;
+}
+
+namespace {
+bool ffn_supported(int q) { return fused_supported(q) || q == QT_Q6_K_LM || q == QT_Q8_0; }
+
+// Upload one expert's three matrices (resident cache) and return device
+// pointers.
+int resolve_expert(int dev, const void* g, int gq, const void* u, int uq, const void* d, int dq, int in_dim,
+                   int hidden, int out_dim, const void** dg, const void** du, const void** dd) {
+    bool t = false;
+    void* p = nullptr;
+    int rc = weights_for(dev, g, static_cast<size_t>(row_bytes_of(gq, in_dim)) * hidden, &p, &t);
+    *dg = p;
+    if (rc == B200Q_OK) rc = weights_for(dev, u, static_cast<size_t>(row_bytes_of(uq, in_dim)) * hidden, &p, &t);
+    *du = p;
+    if (rc == B200Q_OK) rc = weights_for(dev, d, static_cast<size_t>(row_bytes_of(dq, hidden)) * out_dim, &p, &t);
+    *dd = p;
+    return rc;
+}
+}  // namespace
+
+void simd_fused_expert_swiglu(const float* x, int in_dim, const void* gate_data, int gate_qtype, int hidden_dim,
+                              const void* up_data, int up_qtype, const void* down_data, int down_qtype, int out_dim,
+                              float* output) {
+    if (!x || !output || in_dim <= 0 || hidden_dim <= 0 || out_dim <= 0 || !gate_data || !up_data || !down_data ||
+        !ffn_supported(gate_qtype) || !ffn_supported(up_qtype) || !ffn_supported(down_qtype) ||
+        row_bytes_of(gate_qtype, in_dim) < 0 || row_bytes_of(up_qtype, in_dim) < 0 ||
+        row_bytes_of(down_qtype, hidden_dim) < 0) {
+        set_last_error(B200Q_EINVAL);
+        return;
+    }
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    Staging* s = rc == B200Q_OK ? staging_for(dev->id) : nullptr;
+    if (!s) {
+        set_last_error(rc == B200Q_OK ? B200Q_ECUDA : rc);
+        return;
+    }
+    const void *dg = nullptr, *du = nullptr, *dd = nullptr;
+    rc = resolve_expert(dev->id, gate_data, gate_qtype, up_data, up_qtype, down_data, down_qtype, in_dim, hidden_dim,
+                        out_dim, &dg, &du, &dd);
+    if (rc == B200Q_OK) rc = ensure_cap(&s->dx, &s->xcap, static_cast<size_t>(in_dim));
+    if (rc == B200Q_OK) rc = ensure_cap(&s->dy, &s->ycap, static_cast<size_t>(out_dim));
+    if (rc == B200Q_OK && cudaMemcpyAsync(s->dx, x, sizeof(float) * in_dim, cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
+        rc = B200Q_ECUDA;
+    if (rc == B200Q_OK) {
+        *dev->status_host = 0;
+        rc = expert_swiglu(act_mode_now(), s->dx, in_dim, dg, gate_qtype, hidden_dim, du, up_qtype, dd, down_qtype,
+                           out_dim, s->dy, 1.0f, 0.0f, dev, s->stream, pdl_enabled(), B200Q_WEIGHTS_STATIC);
+    }
+    if (rc == B200Q_OK &&
+        cudaMemcpyAsync(output, s->dy, sizeof(float) * out_dim, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess)
+        rc = B200Q_ECUDA;
+    if (cudaStreamSynchronize(s->stream) != cudaSuccess && rc == B200Q_OK) rc = B200Q_ECUDA;
+    if (rc == B200Q_OK && *dev->status_host != 0) rc = B200Q_ETIMEOUT;
+    set_last_error(rc);
+}
+
+void simd_fused_moe_ffn(const float* x, int in_dim, const int* expert_indices, const float* expert_weights, int top_k,
+                        const void* const* gate_data_ptrs, int gate_qtype, int hidden_dim,
+                        const void* const* up_data_ptrs, int up_qtype, const void* const* down_data_ptrs,
+                        int down_qtype, int out_dim, float* output, int write_mode) {
+    if (!x || !output || top_k <= 0 || !expert_indices || !expert_weights || !gate_data_ptrs || !up_data_ptrs ||
+        !down_data_ptrs || in_dim <= 0 || hidden_dim <= 0 || out_dim <= 0 || !ffn_supported(gate_qtype) ||
+        !ffn_supported(up_qtype) || !ffn_supported(down_qtype)) {
+        set_last_error(B200Q_EINVAL);
+        return;
+    }
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    Staging* s = rc == B200Q_OK ? staging_for(dev->id) : nullptr;
+    if (!s) {
+        set_last_error(rc == B200Q_OK ? B200Q_ECUDA : rc);
+        return;
+    }
+    rc = ensure_cap(&s->dx, &s->xcap, static_cast<size_t>(in_dim));
+    if (rc == B200Q_OK) rc = ensure_cap(&s->dy, &s->ycap, static_cast<size_t>(out_dim));
+    if (rc == B200Q_OK && cudaMemcpyAsync(s->dx, x, sizeof(float) * in_dim, cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
+        rc = B200Q_ECUDA;
+    if (rc == B200Q_OK && write_mode != 0 &&
+        cudaMemcpyAsync(s->dy, output, sizeof(float) * out_dim, cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
+        rc = B200Q_ECUDA;
+    // Resolve each contributing expert's device copies (same skip rules).
+    std::vector<const void*> g(top_k, nullptr), u(top_k, nullptr), d(top_k, nullptr);
+    std::vector<int> idx(top_k);
+    for (int e = 0; rc == B200Q_OK && e < top_k; ++e) {
+        idx[e] = e;
+        const int i = expert_indices[e];
+        if (!(expert_weights[e] > 0.0f) || i < 0) continue;
+        if (!gate_data_ptrs[i] || !up_data_ptrs[i] || !down_data_ptrs[i]) continue;
+        rc = resolve_expert(dev->id, gate_data_ptrs[i], gate_qtype, up_data_ptrs[i], up_qtype, down_data_ptrs[i],
+                            down_qtype, in_dim, hidden_dim, out_dim, &g[e], &u[e], &d[e]);
+    }
+    if (rc == B200Q_OK) {
+        *dev->status_host = 0;
+        rc = b200q_moe_ffn(act_mode_now(), s->dx, in_dim, idx.data(), expert_weights, top_k, g.data(), gate_qtype,
+                           hidden_dim, u.data(), up_qtype, d.data(), down_qtype, out_dim, s->dy, write_mode,
+                           B200Q_WEIGHTS_STATIC, s->stream);
+    }
+    if (rc == B200Q_OK &&
+        cudaMemcpyAsync(output, s->dy, sizeof(float) * out_dim, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess)
+        rc = B200Q_ECUDA;
+    if (cudaStreamSynchronize(s->stream) != cudaSuccess && rc == B200Q_OK) rc = B200Q_ECUDA;
+    if (rc == B200Q_OK && *dev->status_host != 0) rc = B200Q_ETIMEOUT;
+    set_last_error(rc);
 }
 
 // ---- controls ----------------------------------------------------------------

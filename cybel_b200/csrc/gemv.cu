@@ -3,6 +3,7 @@
 #include <cstdlib>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
 
 #include "gemv.cuh"
@@ -169,18 +170,21 @@ cudaError_t dispatch(int qtype, int dig, int MR, bool dbg, const Plan& pl, cudaS
     }
 }
 
-// Quantized-activation scratch, one growable buffer per (device, stream):
-// calls on one stream are ordered, so they can share it.
+// Activation scratch: growable buffers per (device, stream, slot); calls on
+// one stream are ordered, so they can share them. Slots let one call keep
+// several quantized vectors alive (e.g. x and the SwiGLU hidden vector).
 struct Scratch {
     void* ptr = nullptr;
     size_t bytes = 0;
 };
 std::mutex g_scratch_mu;
-std::map<std::pair<int, cudaStream_t>, Scratch> g_scratch;
+std::map<std::tuple<int, cudaStream_t, int>, Scratch> g_scratch;
 
-int scratch_for(Device* dev, cudaStream_t st, size_t bytes, void** out) {
+}  // namespace
+
+int scratch_for(Device* dev, cudaStream_t st, int slot, size_t bytes, void** out) {
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    Scratch& s = g_scratch[std::make_pair(dev->id, st)];
+    Scratch& s = g_scratch[std::make_tuple(dev->id, st, slot)];
     if (s.bytes < bytes) {
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
@@ -198,6 +202,8 @@ int scratch_for(Device* dev, cudaStream_t st, size_t bytes, void** out) {
     *out = s.ptr;
     return B200Q_OK;
 }
+
+namespace {
 
 template <int DIG>
 cudaError_t launch_quantize(const float* x, long long x_stride, int m, int k, uint8_t* xq, cudaStream_t st, bool pdl) {
@@ -218,48 +224,82 @@ cudaError_t launch_quantize(const float* x, long long x_stride, int m, int k, ui
 
 }  // namespace
 
-int launch_gemv(int qtype, int act_mode, const void* w, const float* x, float* y, int m, int k, int n,
-                long long x_stride, long long y_stride, int32_t* isums, Device* dev, cudaStream_t st, bool pdl,
-                int flags) {
-    if (!w || !x || !y || m <= 0 || k <= 0 || n <= 0 || !dev) return B200Q_EINVAL;
+int quantize_activations(int act_mode, const float* x, long long x_stride, int m, int k, Device* dev, cudaStream_t st,
+                         bool pdl, int slot, const uint8_t** xq_out, long long* xq_row_out) {
+    if (!x || m <= 0 || k <= 0 || !dev) return B200Q_EINVAL;
     if (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
-    if ((reinterpret_cast<uintptr_t>(w) & 15u) || (reinterpret_cast<uintptr_t>(x) & 15u) || (x_stride & 3))
-        return B200Q_EALIGN;
-    if (isums && m != 1) return B200Q_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) || (x_stride & 3)) return B200Q_EALIGN;
     if (k % 32) return B200Q_ESHAPE;
     const int dig = act_mode == B200Q_ACT_X8 ? 1 : 2;
-    const int mr_max = max_rows_per_launch(qtype, dig);
-    {  // validate the shape before any launch
-        Plan probe;
-        const int rc0 = make_plan(qtype, dig, k, n, 1, dev->num_sms, probe);
-        if (rc0 != B200Q_OK) return rc0;
-    }
     const long long xq_row = xq_row_bytes(k, dig);
     void* xq = nullptr;
-    int rcs = scratch_for(dev, st, static_cast<size_t>(xq_row) * m, &xq);
+    const int rcs = scratch_for(dev, st, slot, static_cast<size_t>(xq_row) * m, &xq);
     if (rcs != B200Q_OK) return rcs;
-    cudaError_t eq = dig == 1 ? launch_quantize<1>(x, x_stride, m, k, static_cast<uint8_t*>(xq), st, pdl)
-                              : launch_quantize<2>(x, x_stride, m, k, static_cast<uint8_t*>(xq), st, pdl);
-    if (eq != cudaSuccess) return B200Q_ECUDA;
+    const cudaError_t e = dig == 1 ? launch_quantize<1>(x, x_stride, m, k, static_cast<uint8_t*>(xq), st, pdl)
+                                   : launch_quantize<2>(x, x_stride, m, k, static_cast<uint8_t*>(xq), st, pdl);
+    if (e != cudaSuccess) return B200Q_ECUDA;
+    *xq_out = static_cast<const uint8_t*>(xq);
+    *xq_row_out = xq_row;
+    return B200Q_OK;
+}
+
+int gemv_from_xq(int qtype, int act_mode, const void* w, const uint8_t* xq, long long xq_row, float* y, int m, int k,
+                 int n, long long y_stride, float alpha, float beta, int32_t* isums, Device* dev, cudaStream_t st,
+                 bool pdl, int flags) {
+    if (!w || !xq || !y || m <= 0 || k <= 0 || n <= 0 || !dev) return B200Q_EINVAL;
+    if (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
+    if (reinterpret_cast<uintptr_t>(w) & 15u) return B200Q_EALIGN;
+    if (isums && m != 1) return B200Q_EINVAL;
+    const int dig = act_mode == B200Q_ACT_X8 ? 1 : 2;
+    const int mr_max = max_rows_per_launch(qtype, dig);
     for (int m0 = 0; m0 < m;) {
         const int left = m - m0;
         const int MR = isums ? 1 : (left >= mr_max ? mr_max : (left >= 2 && mr_max >= 2 ? 2 : 1));
         Plan pl;
-        int rc = make_plan(qtype, dig, k, n, MR, dev->num_sms, pl);
+        const int rc = make_plan(qtype, dig, k, n, MR, dev->num_sms, pl);
         if (rc != B200Q_OK) return rc;
         pl.p.W = static_cast<const uint8_t*>(w);
-        pl.p.xq = static_cast<const uint8_t*>(xq) + m0 * xq_row;
+        pl.p.xq = xq + m0 * xq_row;
         pl.p.xq_stride = xq_row;
         pl.p.y = y + m0 * y_stride;
         pl.p.y_stride = y_stride;
         pl.p.dbg = isums;
         pl.p.status = dev->status;
         pl.p.w_static = (flags & B200Q_WEIGHTS_STATIC) ? 1 : 0;
-        cudaError_t e = dispatch(qtype, dig, MR, isums != nullptr, pl, st, pdl);
+        pl.p.alpha = alpha;
+        pl.p.beta = beta;
+        const cudaError_t e = dispatch(qtype, dig, MR, isums != nullptr, pl, st, pdl);
         if (e != cudaSuccess) return B200Q_ECUDA;
         m0 += MR;
     }
     return B200Q_OK;
 }
 
+int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev) {
+    if (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
+    if (k % 32) return B200Q_ESHAPE;
+    Plan probe;
+    return make_plan(qtype, act_mode == B200Q_ACT_X8 ? 1 : 2, k, n, 1, dev->num_sms, probe);
+}
+
+int launch_gemv(int qtype, int act_mode, const void* w, const float* x, float* y, int m, int k, int n,
+                long long x_stride, long long y_stride, int32_t* isums, Device* dev, cudaStream_t st, bool pdl,
+                int flags) {
+    if (!w || !x || !y || m <= 0 || k <= 0 || n <= 0 || !dev) return B200Q_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(w) & 15u) || (reinterpret_cast<uintptr_t>(x) & 15u) || (x_stride & 3))
+        return B200Q_EALIGN;
+    if (isums && m != 1) return B200Q_EINVAL;
+    int rc = gemv_check_shape(qtype, act_mode, k, n, dev);  // validate before any launch
+    if (rc != B200Q_OK) return rc;
+    const uint8_t* xq = nullptr;
+    long long xq_row = 0;
+    rc = quantize_activations(act_mode, x, x_stride, m, k, dev, st, pdl, 0, &xq, &xq_row);
+    if (rc != B200Q_OK) return rc;
+    return gemv_from_xq(qtype, act_mode, w, xq, xq_row, y, m, k, n, y_stride, 1.0f, 0.0f, isums, dev, st, pdl, flags);
+}
+
+}  // namespace b200q
+
+namespace b200q {
+long long xq_bytes_per_row(int k, int act_mode) { return xq_row_bytes(k, act_mode == B200Q_ACT_X8 ? 1 : 2); }
 }  // namespace b200q

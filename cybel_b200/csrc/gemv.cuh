@@ -60,6 +60,7 @@ struct GemvParams {
     int n_quads;           // ceil(n / 4)
     int rows_cta;          // most rows any CTA owns
     int w_static;          // weights not written by the preceding kernel: stream them before the grid dependency resolves
+    float alpha, beta;     // y = alpha * (W x) + beta * y
 };
 
 
@@ -166,32 +167,12 @@ __host__ __device__ constexpr long long xq_row_bytes(int k, int dig) {
     return ((static_cast<long long>(k) * dig + (k / 32) * 8) + 15) / 16 * 16;
 }
 
-// One thread per 32-element group; the arithmetic is restated in the
-// oracle as orc_quantize_act: amax, iscale = QMAX / amax (IEEE division),
+// Quantize one 32-element group v into a quantized row at `base` (group g
+// of a row of k elements). The arithmetic is restated in the oracle as
+// orc_quantize_act: amax, iscale = QMAX / amax (IEEE division),
 // q = rint(x * iscale) (one rounded multiply, half-even), d = amax / QMAX.
 template <int DIG>
-__global__ void __launch_bounds__(128) quantize_act_kernel(const float* __restrict__ x, long long x_stride, int m, int k,
-                                                           uint8_t* __restrict__ xq) {
-    // Let the GEMV behind this kernel launch now, so it can stream its
-    // weights while this grid waits for x; x may be produced by the
-    // preceding kernel in the stream.
-    griddep_launch_dependents();
-    griddep_wait();
-    const int groups = k / 32;
-    const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (gid >= static_cast<long long>(groups) * m) return;
-    const int row = static_cast<int>(gid / groups), g = static_cast<int>(gid % groups);
-    const float* xr = x + row * x_stride + g * 32;
-    uint8_t* base = xq + row * xq_row_bytes(k, DIG);
-    float v[32];
-#pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-        const float4 f = __ldg(reinterpret_cast<const float4*>(xr + i));
-        v[i] = f.x;
-        v[i + 1] = f.y;
-        v[i + 2] = f.z;
-        v[i + 3] = f.w;
-    }
+__device__ __forceinline__ void quantize_group(const float (&v)[32], uint8_t* base, int k, int g) {
     float amax = 0.0f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
@@ -226,7 +207,36 @@ __global__ void __launch_bounds__(128) quantize_act_kernel(const float* __restri
     }
     float* gd = reinterpret_cast<float*>(base + static_cast<long long>(k) * DIG);
     gd[g] = amax > 0.0f ? __fdiv_rn(amax, QMAX) : 0.0f;
-    reinterpret_cast<int*>(gd + groups)[g] = sum;
+    reinterpret_cast<int*>(gd + k / 32)[g] = sum;
+}
+
+__device__ __forceinline__ void load_group(const float* p, float (&v)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+        const float4 f = __ldg(reinterpret_cast<const float4*>(p + i));
+        v[i] = f.x;
+        v[i + 1] = f.y;
+        v[i + 2] = f.z;
+        v[i + 3] = f.w;
+    }
+}
+
+// One thread per 32-element group of m activation rows.
+template <int DIG>
+__global__ void __launch_bounds__(128) quantize_act_kernel(const float* __restrict__ x, long long x_stride, int m, int k,
+                                                           uint8_t* __restrict__ xq) {
+    // Let the GEMV behind this kernel launch now, so it can stream its
+    // weights while this grid waits for x; x may be produced by the
+    // preceding kernel in the stream.
+    griddep_launch_dependents();
+    griddep_wait();
+    const int groups = k / 32;
+    const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (gid >= static_cast<long long>(groups) * m) return;
+    const int row = static_cast<int>(gid / groups), g = static_cast<int>(gid % groups);
+    float v[32];
+    load_group(x + row * x_stride + g * 32, v);
+    quantize_group<DIG>(v, xq + row * xq_row_bytes(k, DIG), k, g);
 }
 
 // One lane's run of RUN codes starting at element e (a multiple of 16) of a
@@ -764,7 +774,8 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(
         const float* pp = part + (rl * MR + m) * p.S;
         float v = 0.0f;
         for (int j = 0; j < p.S; ++j) v += pp[j];
-        p.y[m * p.y_stride + r_begin + rl] = v;
+        float* yp = p.y + m * p.y_stride + r_begin + rl;
+        *yp = p.beta != 0.0f ? fmaf(p.alpha, v, p.beta * *yp) : p.alpha * v;
     }
 }
 

@@ -36,6 +36,27 @@ int launch_gemv(int qtype, int act_mode, const void* w, const float* x, float* y
                 long long x_stride, long long y_stride, int32_t* isums, Device* dev, cudaStream_t st, bool pdl,
                 int flags = 0);
 
+// Quantize m activation rows (act mode x8/x16) into scratch slot `slot`;
+// returns the codes and their row pitch.
+int quantize_activations(int act_mode, const float* x, long long x_stride, int m, int k, Device* dev, cudaStream_t st,
+                         bool pdl, int slot, const uint8_t** xq, long long* xq_row);
+// y = alpha * (W xq) + beta * y for quantized activation rows.
+int gemv_from_xq(int qtype, int act_mode, const void* w, const uint8_t* xq, long long xq_row, float* y, int m, int k,
+                 int n, long long y_stride, float alpha, float beta, int32_t* isums, Device* dev, cudaStream_t st,
+                 bool pdl, int flags);
+int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev);
+int scratch_for(Device* dev, cudaStream_t st, int slot, size_t bytes, void** out);
+long long xq_bytes_per_row(int k, int act_mode);
+
+int launch_repack(int dst_qtype, const void* src, void* dst, int k, int n, cudaStream_t st);
+int launch_dequant_rows(int qtype, const void* w, const int* rows, int nrows, float* out, int k, int n,
+                        bool tail_canonical, cudaStream_t st);
+int launch_swiglu_quantize(int act_mode, const float* g, const float* u, int hidden, uint8_t* xq, cudaStream_t st,
+                           bool pdl);
+int expert_swiglu(int act_mode, const float* x, int in_dim, const void* gate, int gq, int hidden, const void* up, int uq,
+                  const void* down, int dq, int out_dim, float* out, float alpha, float beta, Device* dev,
+                  cudaStream_t st, bool pdl, int flags);
+
 bool pdl_enabled();
 void set_last_error(int status);
 

@@ -92,6 +92,41 @@ B200Q_API void simd_matmul_q6k_r4(const float* x, const void* a_quant_r4, float*
 B200Q_API void simd_matmul_q8_0(const float* x, const void* a_quant, float* y, int m, int k, int n);
 B200Q_API void simd_matmul_q4_0(const float* x, const void* a_quant, float* y, int m, int k, int n);
 
+/* Layout repacks: QM:1573 simd_repack_q4k_r4, QM:1577 simd_repack_q6k_r4,
+ * QM:1581 simd_repack_q6k_lm (layouts QM:250-365). Host pointers; run on the
+ * GPU. Return 1 on success, 0 on invalid arguments. */
+B200Q_API int simd_repack_q4k_r4(const void* src_q4k, void* dst_q4k_r4, int k, int n);
+B200Q_API int simd_repack_q6k_r4(const void* src_q6k, void* dst_q6k_r4, int k, int n);
+B200Q_API int simd_repack_q6k_lm(const void* src_q6k, void* dst_q6k_lm, int k, int n);
+
+/* One dequantized row (embedding lookup): QM:2179 simd_dequantize_row.
+ * fp32 values bit-identical to the reference. Like the reference (which has
+ * no row-count argument), R4 layouts are addressed as whole 4-row groups.
+ * Returns 1 on success, 0 otherwise. */
+B200Q_API int simd_dequantize_row(const void* quant_data, int qtype, int row, float* out, int k);
+
+/* Three / four matvecs sharing x, x quantized once: QM:1855
+ * simd_fused_qkv_matvec_quant, QM:1898 simd_fused_quad_matvec_quant.
+ * Qtypes Q4_K, Q4_K_R4, Q6_K, Q6_K_R4 (as the reference). 1 / 0. */
+B200Q_API int simd_fused_qkv_matvec_quant(const float* x, const void* q_data, int q_qtype, float* q_out, int q_rows,
+                                          const void* k_data, int k_qtype, float* k_out, int k_rows,
+                                          const void* v_data, int v_qtype, float* v_out, int v_rows, int cols);
+B200Q_API int simd_fused_quad_matvec_quant(const float* x, const void* a_data, int a_qtype, float* a_out, int a_rows,
+                                           const void* b_data, int b_qtype, float* b_out, int b_rows,
+                                           const void* c_data, int c_qtype, float* c_out, int c_rows,
+                                           const void* d_data, int d_qtype, float* d_out, int d_rows, int cols);
+
+/* SwiGLU expert FFN out = down(silu(gate x) * (up x)): QM:2307
+ * simd_fused_expert_swiglu. Top-k MoE FFN sum_e w_e * expert_e(x) with
+ * write_mode 0 = overwrite / else accumulate: QM:2426 simd_fused_moe_ffn. */
+B200Q_API void simd_fused_expert_swiglu(const float* x, int in_dim, const void* gate_data, int gate_qtype,
+                                        int hidden_dim, const void* up_data, int up_qtype, const void* down_data,
+                                        int down_qtype, int out_dim, float* output);
+B200Q_API void simd_fused_moe_ffn(const float* x, int in_dim, const int* expert_indices, const float* expert_weights,
+                                  int top_k, const void* const* gate_data_ptrs, int gate_qtype, int hidden_dim,
+                                  const void* const* up_data_ptrs, int up_qtype, const void* const* down_data_ptrs,
+                                  int down_qtype, int out_dim, float* output, int write_mode);
+
 /* ---------------------------------------------------------------------
  * 2. Device-pointer entry points.
  * ------------------------------------------------------------------- */
@@ -118,6 +153,33 @@ B200Q_API int b200q_matmul_ex(int qtype, int act_mode, const float* x, const voi
  * checks against the CPU restatement. */
 B200Q_API int b200q_matvec_isums(int qtype, int act_mode, const float* x, const void* w, float* y, int* isums, int k, int n,
                        void* stream);
+
+/* Repack device buffers into dst_qtype (B200Q_Q4_K_R4 / Q6_K_R4 from the
+ * canonical type, B200Q_Q6_K_LM from Q6_K). Layouts of QM:250-365. */
+B200Q_API int b200q_repack(int dst_qtype, const void* src, void* dst, int k, int n, void* stream);
+
+/* out[i][k] = dequantized row rows[i] (device int array) of a matrix with n
+ * rows; the R4 tail rows are addressed canonically (QM:2179-2296 values). */
+B200Q_API int b200q_dequantize_rows(int qtype, const void* w, const int* rows, int nrows, float* out, int k, int n,
+                                    void* stream);
+
+/* count matvecs y[i] = W[i] x sharing one x (quantized once); w, qtypes, y,
+ * rows are host arrays of device pointers / values (QM:1855-1942). */
+B200Q_API int b200q_fused_matvec(int act_mode, const float* x, int cols, int count, const void* const* w,
+                                 const int* qtypes, float* const* y, const int* rows, int flags, void* stream);
+
+/* out = alpha * down(silu(gate x) * (up x)) + beta * out on device buffers
+ * (QM:2307-2416); the SiLU * up product is re-quantized for the down GEMV. */
+B200Q_API int b200q_expert_swiglu(int act_mode, const float* x, int in_dim, const void* gate, int gate_qtype,
+                                  int hidden, const void* up, int up_qtype, const void* down, int down_qtype,
+                                  int out_dim, float* out, float alpha, float beta, int flags, void* stream);
+
+/* Top-k MoE FFN on device buffers (QM:2426-2525); expert_indices,
+ * expert_weights and the pointer arrays are host arrays. */
+B200Q_API int b200q_moe_ffn(int act_mode, const float* x, int in_dim, const int* expert_indices,
+                            const float* expert_weights, int top_k, const void* const* gate_ptrs, int gate_qtype,
+                            int hidden, const void* const* up_ptrs, int up_qtype, const void* const* down_ptrs,
+                            int down_qtype, int out_dim, float* out, int write_mode, int flags, void* stream);
 
 /* ---------------------------------------------------------------------
  * Runtime controls.

@@ -113,6 +113,12 @@ def ref() -> ctypes.CDLL:
         L.simd_dequantize_row.restype = _i
         L.simd_fused_expert_swiglu.argtypes = [fp, _i, _vp, _i, _i, _vp, _i, _vp, _i, _i, fp]
         L.simd_fused_expert_swiglu.restype = None
+        L.simd_fused_qkv_matvec_quant.argtypes = [fp, _vp, _i, fp, _i, _vp, _i, fp, _i, _vp, _i, fp, _i, _i]
+        L.simd_fused_qkv_matvec_quant.restype = _i
+        vpp = ctypes.POINTER(ctypes.c_void_p)
+        L.simd_fused_moe_ffn.argtypes = [fp, _i, ctypes.POINTER(ctypes.c_int), fp, _i, vpp, _i, _i, vpp, _i, vpp, _i,
+                                         _i, fp, _i]
+        L.simd_fused_moe_ffn.restype = None
         _ref = L
     return _ref
 

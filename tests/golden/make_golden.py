@@ -83,6 +83,53 @@ def main() -> None:
             assert ref.simd_dequantize_row(W.ctypes.data, qt, r, deq[i].ctypes.data_as(fp), k) == 1
         out[f"{name}/deq_rows"] = np.array(rows, dtype=np.int64)
         out[f"{name}/deq"] = deq
+    # Fused ops of the reference (quantized_matmul.cpp:1855-1896, 2307-2525).
+    rng = np.random.default_rng(21)
+    cols = 512
+    qkv = {}
+    for nm, rows in (("q", 64), ("k", 32), ("v", 32)):
+        qkv[nm] = Q.quantize_q4_k(rng.normal(0.0, 0.02, size=(rows, cols)).astype(np.float32))
+    x = rng.standard_normal(cols).astype(np.float32)
+    outs = {nm: np.zeros(qkv[nm].shape[0], np.float32) for nm in qkv}
+    ok = ref.simd_fused_qkv_matvec_quant(
+        x.ctypes.data_as(fp),
+        qkv["q"].ctypes.data, O.Q4_K, outs["q"].ctypes.data_as(fp), 64,
+        qkv["k"].ctypes.data, O.Q4_K, outs["k"].ctypes.data_as(fp), 32,
+        qkv["v"].ctypes.data, O.Q4_K, outs["v"].ctypes.data_as(fp), 32,
+        cols)
+    assert ok == 1
+    for nm in qkv:
+        out[f"qkv/{nm}/W"] = qkv[nm]
+        out[f"qkv/{nm}/y"] = outs[nm]
+    out["qkv/x"] = x
+
+    in_dim, hidden, out_dim = 512, 512, 256
+    experts = []
+    for e in range(2):
+        g = Q.quantize_q4_k(rng.normal(0.0, 0.02, size=(hidden, in_dim)).astype(np.float32))
+        u = Q.quantize_q4_k(rng.normal(0.0, 0.02, size=(hidden, in_dim)).astype(np.float32))
+        d = Q.quantize_q6_k(rng.normal(0.0, 0.02, size=(out_dim, hidden)).astype(np.float32))
+        experts.append((g, u, d))
+        out[f"ffn/e{e}/gate"], out[f"ffn/e{e}/up"], out[f"ffn/e{e}/down"] = g, u, d
+    xf = rng.standard_normal(in_dim).astype(np.float32) * 4.0
+    out["ffn/x"] = xf
+    y0 = np.zeros(out_dim, np.float32)
+    ref.simd_fused_expert_swiglu(xf.ctypes.data_as(fp), in_dim, experts[0][0].ctypes.data, O.Q4_K, hidden,
+                                 experts[0][1].ctypes.data, O.Q4_K, experts[0][2].ctypes.data, O.Q6_K, out_dim,
+                                 y0.ctypes.data_as(fp))
+    out["ffn/expert0_y"] = y0
+    idx = np.array([0, 1], dtype=np.int32)
+    wts = np.array([0.625, 0.375], dtype=np.float32)
+    vp = ctypes.c_void_p
+    gp = (vp * 2)(experts[0][0].ctypes.data, experts[1][0].ctypes.data)
+    upp = (vp * 2)(experts[0][1].ctypes.data, experts[1][1].ctypes.data)
+    dp = (vp * 2)(experts[0][2].ctypes.data, experts[1][2].ctypes.data)
+    ymoe = np.zeros(out_dim, np.float32)
+    ref.simd_fused_moe_ffn(xf.ctypes.data_as(fp), ctypes.c_int(in_dim), idx.ctypes.data_as(ctypes.POINTER(ctypes.c_int)),
+                           wts.ctypes.data_as(fp), ctypes.c_int(2), gp, ctypes.c_int(O.Q4_K), ctypes.c_int(hidden),
+                           upp, ctypes.c_int(O.Q4_K), dp, ctypes.c_int(O.Q6_K), ctypes.c_int(out_dim),
+                           ymoe.ctypes.data_as(fp), ctypes.c_int(0))
+    out["ffn/moe_idx"], out["ffn/moe_w"], out["ffn/moe_y"] = idx, wts, ymoe
     np.savez_compressed(OUT, **out)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes)")
 

@@ -118,23 +118,32 @@ def test_small_batch_matmul(oracle_mod, qt, n, k, m, digits):
 
 
 def test_dropins_match_reference_golden(oracle_mod, golden):
-    """Host-pointer drop-ins (x16 default) against the reference op's outputs."""
+    """Host-pointer C drop-ins (x16 default) against the reference op's outputs."""
+    from cybel_b200 import _native
     from cybel_b200 import quantized_matmul as qm
 
     O = oracle_mod
+    L = _native.lib()
+    fp = ctypes.POINTER(ctypes.c_float)
     assert qm.set_act_mode("x16") in (1, 2)
     for name in ("q4k", "q6k", "q8_0", "q4k_r4", "q6k_r4", "q6k_lm"):
         qt, n, k = (int(v) for v in golden[f"{name}/meta"])
-        W, x, yref = golden[f"{name}/W"], golden[f"{name}/x"], golden[f"{name}/y"]
-        mat = qm.QuantizedMatrix(name=name, qtype=qt, shape=(k, n), data=W)
-        y = qm.matvec(x, mat)
+        W, x, yref = np.ascontiguousarray(golden[f"{name}/W"]), golden[f"{name}/x"], golden[f"{name}/y"]
+        y = np.zeros(n, np.float32)
+        getattr(L, f"simd_matvec_{name}")(x.ctypes.data_as(fp), W.ctypes.data, y.ctypes.data_as(fp), k, n)
+        assert L.b200q_last_error() == 0
         wn = O.row_norms(W, qt, k, n)
         assert O.normalized_error(y, yref, wn, x) <= NORM_TOL, name
         assert O.max_rel_error(y, yref) <= REL_TOL, name
         if f"{name}/X" in golden.files:
-            X, Yref = golden[f"{name}/X"], golden[f"{name}/Y"]
-            Y = qm.matmul(X, mat)
+            X, Yref = np.ascontiguousarray(golden[f"{name}/X"]), golden[f"{name}/Y"]
+            Y = np.zeros((X.shape[0], n), np.float32)
+            getattr(L, f"simd_matmul_{name}")(X.ctypes.data_as(fp), W.ctypes.data, Y.ctypes.data_as(fp), X.shape[0], k, n)
+            assert L.b200q_last_error() == 0
             assert O.normalized_error(Y, Yref, wn, X) <= NORM_TOL, name
+        # the Python mirror (device API) agrees with the C drop-in bit for bit
+        mat = qm.QuantizedMatrix(name=name, qtype=qt, shape=(k, n), data=W)
+        assert np.array_equal(qm.matvec(x, mat), y), name
 
 
 def test_dropin_invalid_arguments_leave_y_untouched():
@@ -173,17 +182,23 @@ def test_device_api_rejects_misaligned_pointer():
 
 def test_weight_cache_residency(oracle_mod):
     from cybel_b200 import _native
-    from cybel_b200 import quantized_matmul as qm
 
     O = oracle_mod
     L = _native.lib()
+    fp = ctypes.POINTER(ctypes.c_float)
     L.b200q_weight_cache_clear()
     W = _weights(O, 12, 64, 512, seed=3)
-    mat = qm.QuantizedMatrix(name="w", qtype=12, shape=(512, 64), data=W)
     x = np.ones(512, dtype=np.float32)
-    y1 = qm.matvec(x, mat)
+    y1, y2, y3 = (np.zeros(64, np.float32) for _ in range(3))
+    L.simd_matvec_q4k(x.ctypes.data_as(fp), W.ctypes.data, y1.ctypes.data_as(fp), 512, 64)
     assert L.b200q_weight_cache_bytes() == W.nbytes
-    y2 = qm.matvec(x, mat)
+    L.simd_matvec_q4k(x.ctypes.data_as(fp), W.ctypes.data, y2.ctypes.data_as(fp), 512, 64)
     assert np.array_equal(y1, y2) and L.b200q_weight_cache_bytes() == W.nbytes
-    assert L.b200q_weight_cache_evict(mat._data_ptr) == 1
+    # Same address, different bytes (a reused buffer): re-uploaded, not stale.
+    W2 = _weights(O, 12, 64, 512, seed=4)
+    W[...] = W2
+    L.simd_matvec_q4k(x.ctypes.data_as(fp), W.ctypes.data, y3.ctypes.data_as(fp), 512, 64)
+    exact = O.matvec_f64(W2, 12, x, 512, 64)
+    assert O.normalized_error(y3, exact, O.row_norms(W2, 12, 512, 64), x) <= NORM_TOL
+    assert L.b200q_weight_cache_evict(W.ctypes.data) == 1
     assert L.b200q_weight_cache_bytes() == 0

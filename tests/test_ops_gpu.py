@@ -1,0 +1,250 @@
+"""Parity of the repack, row-dequantization and fused-op entry points with the
+reference op's golden outputs and the CPU oracle (GPU required).
+
+* repacks (R4 / LM): bit-exact against the reference's own simd_repack_*;
+* simd_dequantize_row: bit-exact fp32 against the reference and gguf-py;
+* fused QKV / quad matvec: bit-identical to the separate matvecs and within
+  the matvec tolerances of the reference outputs;
+* fused SwiGLU expert and MoE FFN: within tolerance of the reference
+  outputs and of the double-precision oracle.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+FP = ctypes.POINTER(ctypes.c_float)
+
+
+def _fp(a):
+    return a.ctypes.data_as(FP)
+
+
+@pytest.mark.parametrize("name,src_qt,fn,block", [
+    ("q4k_r4", 12, "simd_repack_q4k_r4", 144),
+    ("q6k_r4", 14, "simd_repack_q6k_r4", 210),
+    ("q6k_lm", 14, "simd_repack_q6k_lm", 276),
+])
+def test_repack_matches_reference(oracle_mod, golden, name, src_qt, fn, block):
+    from cybel_b200 import _native
+    from cybel_b200 import quantize as Q
+
+    O = oracle_mod
+    qt, n, k = (int(v) for v in golden[f"{name}/meta"])
+    seed = {"q4k_r4": 14, "q6k_r4": 15, "q6k_lm": 16}[name]
+    rng = np.random.default_rng(seed)
+    src = Q.quantize(rng.normal(0.0, 0.02, size=(n, k)).astype(np.float32), src_qt)
+    dst = np.zeros((n, (k // 256) * block), dtype=np.uint8)
+    assert getattr(_native.lib(), fn)(src.ctypes.data, dst.ctypes.data, k, n) == 1
+    assert np.array_equal(dst, golden[f"{name}/W"])
+    # invalid shape: returns 0 like the reference
+    assert getattr(_native.lib(), fn)(src.ctypes.data, dst.ctypes.data, k + 1, n) == 0
+
+
+def test_device_repack_ragged_rows(oracle_mod):
+    import torch
+    from cybel_b200 import _native
+    from cybel_b200 import quantize as Q
+
+    O = oracle_mod
+    for n in (1, 3, 4, 5, 130):
+        k = 512
+        src = Q.quantize_q4_k(np.random.default_rng(n).normal(0, 0.02, size=(n, k)).astype(np.float32))
+        s_dev = torch.from_numpy(src).cuda()
+        d_dev = torch.empty_like(s_dev)
+        rc = _native.lib().b200q_repack(112, s_dev.data_ptr(), d_dev.data_ptr(), k, n,
+                                        torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        assert np.array_equal(d_dev.cpu().numpy(), O.repack_r4(src, k, n, 144))
+
+
+def test_dequantize_row_matches_reference(oracle_mod, golden):
+    from cybel_b200 import _native
+
+    O = oracle_mod
+    L = _native.lib()
+    for name in ("q4k", "q6k", "q8_0", "q4k_r4", "q6k_r4", "q6k_lm"):
+        qt, n, k = (int(v) for v in golden[f"{name}/meta"])
+        W = np.ascontiguousarray(golden[f"{name}/W"])
+        for i, r in enumerate(golden[f"{name}/deq_rows"]):
+            if qt in (112, 114) and r >= (n // 4) * 4:
+                continue  # the reference reads past the matrix for R4 tail rows
+            out = np.zeros(k, dtype=np.float32)
+            assert L.simd_dequantize_row(W.ctypes.data, qt, int(r), _fp(out), k) == 1
+            assert np.array_equal(out.view(np.uint32), golden[f"{name}/deq"][i].view(np.uint32)), name
+    out = np.zeros(16, dtype=np.float32)
+    assert L.simd_dequantize_row(None, 12, 0, _fp(out), 256) == 0
+    assert L.simd_dequantize_row(W.ctypes.data, 99, 0, _fp(out), 256) == 0
+
+
+@pytest.mark.parametrize("qt", [2, 8, 12, 14, 112, 114, 214])
+def test_device_dequantize_rows_bitexact(oracle_mod, qt):
+    import torch
+    from cybel_b200 import _native
+    from cybel_b200.quantized_matmul import DeviceMatrix
+    from test_gemv_gpu import _weights
+
+    O = oracle_mod
+    n, k = 66, 512
+    W = _weights(O, qt, n, k, seed=qt)
+    dm = DeviceMatrix(qt, k, n, W)
+    rows = np.array([0, 1, 31, 63, 64, 65], dtype=np.int32)
+    rd = torch.from_numpy(rows).cuda()
+    out = torch.empty((rows.size, k), dtype=torch.float32, device="cuda")
+    rc = _native.lib().b200q_dequantize_rows(qt, dm.ptr, rd.data_ptr(), rows.size, out.data_ptr(), k, n,
+                                             torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    ref = O.dequant(W, qt, k, n)[rows]
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+def test_python_dequantize_rows_and_full(oracle_mod):
+    import gguf
+    from cybel_b200 import quantize as Q
+    from cybel_b200.quantized_matmul import QuantizedMatrix, dequantize_full, dequantize_rows
+
+    n, k = 7, 512
+    W = Q.quantize_q6_k(np.random.default_rng(3).normal(0, 0.02, size=(n, k)).astype(np.float32))
+    m = QuantizedMatrix(name="w", qtype=14, shape=(k, n), data=W)
+    ref = gguf.dequantize(W, gguf.GGMLQuantizationType.Q6_K).reshape(n, k)
+    assert np.array_equal(dequantize_rows(m, [0, 6, 3]), ref[[0, 6, 3]])
+    assert np.array_equal(dequantize_full(m), ref)
+    assert dequantize_rows(m, []).shape == (0, k)
+
+
+def test_fused_qkv_matches_separate_and_reference(oracle_mod, golden):
+    from cybel_b200 import _native
+    from cybel_b200 import quantized_matmul as qm
+
+    O = oracle_mod
+    L = _native.lib()
+    qm.set_act_mode("x16")
+    x = golden["qkv/x"]
+    Ws = {nm: np.ascontiguousarray(golden[f"qkv/{nm}/W"]) for nm in "qkv"}
+    rows = {nm: Ws[nm].shape[0] for nm in "qkv"}
+    outs = {nm: np.zeros(rows[nm], np.float32) for nm in "qkv"}
+    ok = L.simd_fused_qkv_matvec_quant(
+        _fp(x), Ws["q"].ctypes.data, 12, _fp(outs["q"]), rows["q"],
+        Ws["k"].ctypes.data, 12, _fp(outs["k"]), rows["k"],
+        Ws["v"].ctypes.data, 12, _fp(outs["v"]), rows["v"], x.size)
+    assert ok == 1
+    for nm in "qkv":
+        sep = qm.matvec(x, qm.QuantizedMatrix(name=nm, qtype=12, shape=(x.size, rows[nm]), data=Ws[nm]))
+        assert np.array_equal(sep, outs[nm])
+        wn = O.row_norms(Ws[nm], 12, x.size, rows[nm])
+        assert O.normalized_error(outs[nm], golden[f"qkv/{nm}/y"], wn, x) <= 1e-5
+    # Q8_0 is not a fused-projection type in the reference: 0, outputs untouched
+    keep = outs["q"].copy()
+    ok = L.simd_fused_qkv_matvec_quant(
+        _fp(x), Ws["q"].ctypes.data, 8, _fp(outs["q"]), rows["q"],
+        Ws["k"].ctypes.data, 12, _fp(outs["k"]), rows["k"],
+        Ws["v"].ctypes.data, 12, _fp(outs["v"]), rows["v"], x.size)
+    assert ok == 0 and np.array_equal(keep, outs["q"])
+
+
+def test_fused_quad_matches_separate(oracle_mod):
+    from cybel_b200 import _native
+    from cybel_b200 import quantized_matmul as qm
+    from test_gemv_gpu import _weights
+
+    O = oracle_mod
+    k = 512
+    mats = [(_weights(O, qt, r, k, seed=r), qt, r) for qt, r in ((12, 40), (14, 24), (112, 16), (114, 12))]
+    x = np.random.default_rng(9).standard_normal(k).astype(np.float32)
+    outs = [np.zeros(r, np.float32) for _, _, r in mats]
+    args = []
+    for (W, qt, r), o in zip(mats, outs):
+        args += [W.ctypes.data, qt, _fp(o), r]
+    assert _native.lib().simd_fused_quad_matvec_quant(_fp(x), *args, k) == 1
+    for (W, qt, r), o in zip(mats, outs):
+        assert np.array_equal(o, qm.matvec(x, qm.QuantizedMatrix(name="m", qtype=qt, shape=(k, r), data=W)))
+
+
+def _rel(a, b):
+    return float(np.max(np.abs(np.asarray(a, np.float64) - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+def test_fused_expert_swiglu_matches_reference(oracle_mod, golden):
+    from cybel_b200 import quantized_matmul as qm
+
+    O = oracle_mod
+    qm.set_act_mode("x16")
+    x = golden["ffn/x"]
+    g, u, d = (np.ascontiguousarray(golden[f"ffn/e0/{p}"]) for p in ("gate", "up", "down"))
+    hidden, out_dim = g.shape[0], d.shape[0]
+    mats = (qm.QuantizedMatrix(name="g", qtype=12, shape=(x.size, hidden), data=g),
+            qm.QuantizedMatrix(name="u", qtype=12, shape=(x.size, hidden), data=u),
+            qm.QuantizedMatrix(name="d", qtype=14, shape=(hidden, out_dim), data=d))
+    y = qm.fused_expert_swiglu(x, *mats)
+    assert _rel(y, golden["ffn/expert0_y"].astype(np.float64)) <= 1e-3
+    exact = np.empty(out_dim, np.float64)
+    assert O.lib().orc_fused_expert_swiglu_f64(x.ctypes.data, x.size, g.ctypes.data, 12, hidden, u.ctypes.data, 12,
+                                               d.ctypes.data, 14, out_dim, exact.ctypes.data) == 1
+    assert _rel(y, exact) <= 1e-3
+
+
+def test_fused_moe_matches_reference_and_expert_sum(oracle_mod, golden):
+    from cybel_b200 import quantized_matmul as qm
+
+    qm.set_act_mode("x16")
+    x = golden["ffn/x"]
+    experts = []
+    for e in range(2):
+        g, u, d = (np.ascontiguousarray(golden[f"ffn/e{e}/{p}"]) for p in ("gate", "up", "down"))
+        experts.append((qm.QuantizedMatrix(name=f"g{e}", qtype=12, shape=(x.size, g.shape[0]), data=g),
+                        qm.QuantizedMatrix(name=f"u{e}", qtype=12, shape=(x.size, g.shape[0]), data=u),
+                        qm.QuantizedMatrix(name=f"d{e}", qtype=14, shape=(g.shape[0], d.shape[0]), data=d)))
+    w = golden["ffn/moe_w"]
+    y = qm.fused_moe_ffn(x, w, [e[0] for e in experts], [e[1] for e in experts], [e[2] for e in experts])
+    assert _rel(y, golden["ffn/moe_y"].astype(np.float64)) <= 1e-3
+    expected = sum(float(wi) * qm.fused_expert_swiglu(x, *e).astype(np.float64) for wi, e in zip(w, experts))
+    assert _rel(y, expected) <= 1e-5
+    # non-positive weights are skipped; all skipped -> zeros (write_mode 0)
+    y0 = qm.fused_moe_ffn(x, [0.0, -1.0], [e[0] for e in experts], [e[1] for e in experts], [e[2] for e in experts])
+    assert np.all(y0 == 0.0)
+
+
+def test_moe_write_mode_accumulates(oracle_mod, golden):
+    from cybel_b200 import _native
+    from cybel_b200 import quantized_matmul as qm
+
+    qm.set_act_mode("x16")
+    x = golden["ffn/x"]
+    g, u, d = (np.ascontiguousarray(golden[f"ffn/e0/{p}"]) for p in ("gate", "up", "down"))
+    hidden, out_dim = g.shape[0], d.shape[0]
+    base = np.linspace(-1, 1, out_dim).astype(np.float32)
+    out = base.copy()
+    idx = np.array([0], np.int32)
+    w = np.array([0.5], np.float32)
+    vp = ctypes.c_void_p
+    _native.lib().simd_fused_moe_ffn(
+        _fp(x), x.size, idx.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), _fp(w), 1,
+        (vp * 1)(g.ctypes.data), 12, hidden, (vp * 1)(u.ctypes.data), 12, (vp * 1)(d.ctypes.data), 14, out_dim,
+        _fp(out), 1)
+    assert _native.lib().b200q_last_error() == 0
+    single = qm.fused_expert_swiglu(x, qm.QuantizedMatrix(name="g", qtype=12, shape=(x.size, hidden), data=g),
+                                    qm.QuantizedMatrix(name="u", qtype=12, shape=(x.size, hidden), data=u),
+                                    qm.QuantizedMatrix(name="d", qtype=14, shape=(hidden, out_dim), data=d))
+    assert _rel(out, base.astype(np.float64) + 0.5 * single) <= 1e-5
+
+
+def test_interleaved_strict_mode(monkeypatch, golden):
+    from cybel_b200 import quantized_matmul as qm
+
+    x = golden["ffn/x"]
+    g, u, d = (np.ascontiguousarray(golden[f"ffn/e0/{p}"]) for p in ("gate", "up", "down"))
+    hidden, out_dim = g.shape[0], d.shape[0]
+    gm = qm.QuantizedMatrix(name="g", qtype=12, shape=(x.size, hidden), data=g)
+    um = qm.QuantizedMatrix(name="u", qtype=12, shape=(x.size, hidden), data=u)
+    dm = qm.QuantizedMatrix(name="d", qtype=14, shape=(hidden, out_dim), data=d)
+    gi = qm.interleave_quantized_rows(gm, 4)
+    monkeypatch.setenv("ANVIL_STRICT_NATIVE_QSG", "1")
+    with pytest.raises(RuntimeError, match="Strict native QSG"):
+        qm.fused_expert_swiglu(x, gi, um, dm)
+    monkeypatch.setenv("ANVIL_STRICT_NATIVE_QSG", "0")
+    assert np.array_equal(qm.fused_expert_swiglu(x, gi, um, dm), qm.fused_expert_swiglu(x, gm, um, dm))
