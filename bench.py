@@ -193,6 +193,95 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def _peak_bf16():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
+
+
+TILE_SHAPES = [(14336, 4096), (4096, 14336)]  # (n, k): Llama-3-8B gate/up and down
+TILE_MS = [8, 32, 128]
+
+
+def tile_bench(dev, steps: int, warmup: int, shapes=TILE_SHAPES, ms=TILE_MS, copies: int = 8):
+    """Speculative-verify batched matmul on the tile path (tcgen05, fp16
+    operands): per (shape, m), `copies` distinct resident Q4_K weight copies
+    (> 2 x L2 in total) are multiplied by an m-row activation block, replayed
+    as one CUDA graph; time per matmul from CUDA events on the replay
+    stream. Returns one record per case."""
+    import torch
+
+    from cybel_b200 import _native
+    from cybel_b200 import quantize as Q
+    from cybel_b200.quantized_matmul import DeviceMatrix, matmul_device
+
+    peak_hbm, _ = _peak_hbm()
+    peak_tc, _ = _peak_bf16()
+    out = []
+    for n, k in shapes:
+        rng = np.random.default_rng(n + k)
+        W = Q.quantize_q4_k(rng.normal(0.0, 0.02, size=(n, k)).astype(np.float32))
+        mats = [DeviceMatrix(QT_Q4_K, k, n, W) for _ in range(copies)]
+        for m in ms:
+            X = torch.from_numpy(np.random.default_rng(m).standard_normal((m, k)).astype(np.float32)).to(dev)
+            ys = [torch.empty((m, n), dtype=torch.float32, device=dev) for _ in range(copies)]
+
+            def step():
+                for i in range(copies):
+                    matmul_device(X, mats[i], out=ys[i], act_mode=_native.ACT_F16)
+
+            cap = torch.cuda.Stream(dev)
+            with torch.cuda.stream(cap):
+                for _ in range(max(3, warmup)):
+                    step()
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                step()
+            for _ in range(max(3, warmup)):
+                g.replay()
+            st = torch.cuda.current_stream(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize(dev)
+            e0.record(st)
+            for _ in range(steps):
+                g.replay()
+            e1.record(st)
+            torch.cuda.synchronize(dev)
+            us = e0.elapsed_time(e1) * 1e3 / (steps * copies)
+            del g
+            gbs = W.nbytes / (us * 1e-6) / 1e9
+            tflops = 2.0 * m * n * k / (us * 1e-6) / 1e12
+            out.append({
+                "n": n, "k": k, "m": m,
+                "us_per_matmul": round(us, 2),
+                "weight_gbs": round(gbs, 1),
+                "hbm_frac": round(gbs / peak_hbm, 4),
+                "tflops": round(tflops, 1),
+                "tensor_frac": round(tflops / peak_tc, 4),
+            })
+        del mats
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_tile_only(args, ws, rank, local):
+    """`--workload tile`: the tile path alone (one shape/m or all), one JSON line."""
+    import torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    shapes = TILE_SHAPES if args.tile_n is None else [(args.tile_n, args.tile_k)]
+    ms = TILE_MS if args.tile_m is None else [args.tile_m]
+    recs = tile_bench(dev, args.steps, args.warmup, shapes, ms, copies=args.copies)
+    if rank == 0:
+        print(json.dumps({"workload": "q4k_tile_matmul", "impl": "ours", "cases": recs}), flush=True)
+
+
 def run_ours(args, ws, rank, local):
     import torch
 
@@ -303,6 +392,11 @@ def run_ours(args, ws, rank, local):
     avg_launch_ms = ms_total / (C * args.steps)
     achieved = wbytes / (avg_launch_ms / 1e3) / 1e9
     cpu = _cpu_reference_sample(W, x) if (rank == 0 and ws == 1 and not args.no_cpu) else None
+    tile = None
+    if ws == 1 and not args.no_tile:
+        del mats, ys
+        torch.cuda.empty_cache()
+        tile = tile_bench(dev, max(10, args.steps // 2), args.warmup)
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -346,6 +440,7 @@ def run_ours(args, ws, rank, local):
             "gpu_launches": 2 * C * args.steps,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "tile": tile,
         }
         print(json.dumps(line), flush=True)
     if ws > 1:
@@ -363,12 +458,20 @@ def main():
     ap.add_argument("--copies", type=int, default=8)
     ap.add_argument("--pdl", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-tile", action="store_true", help="skip the tile-path (batched matmul) summary")
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "tile"])
+    ap.add_argument("--tile-m", type=int, default=None)
+    ap.add_argument("--tile-n", type=int, default=None)
+    ap.add_argument("--tile-k", type=int, default=None)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     ws, rank, local = _dist()
     if args.impl == "reference":
         run_reference(args, ws, rank)
+        return
+    if args.workload == "tile":
+        run_tile_only(args, ws, rank, local)
         return
     run_ours(args, ws, rank, local)
 

@@ -14,6 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libb200q.so"
 
 ACT_X8 = 1
 ACT_X16 = 2
+ACT_F16 = 3  # tile path (tcgen05, fp16 operands), Q4_K, device entry points
 WEIGHTS_STATIC = 1
 
 STATUS = {

@@ -86,7 +86,7 @@ def build(verbose: bool = False, ptxas_verbose: bool = False) -> Path:
         raise RuntimeError(f"nvcc failed for: {', '.join(failed)}")
     objs = [str(OBJ_DIR / (s.stem + ".o")) for s in srcs]
     if jobs or not LIB.exists():
-        cmd = [nvcc, *ARCH, "-shared", "-o", str(LIB), *objs, "-lcudart", "-lcuda"]
+        cmd = [nvcc, *ARCH, "-shared", "-o", str(LIB), *objs, "-lcudart"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

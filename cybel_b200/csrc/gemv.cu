@@ -282,6 +282,16 @@ int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev) {
     return make_plan(qtype, act_mode == B200Q_ACT_X8 ? 1 : 2, k, n, 1, dev->num_sms, probe);
 }
 
+// B200Q_ACT_F16 always takes the tile path; B200Q_ACT_X8 takes it for Q4_K
+// batches of at least B200Q_TILE_MIN_M rows (default 8), where the tile
+// kernel streams W once for the whole batch and its fp16 operands are more
+// accurate than int8 activations.
+bool uses_tile_path(int qtype, int act_mode, int m) {
+    static const int min_m = env_int("B200Q_TILE_MIN_M", 8);
+    if (act_mode == B200Q_ACT_F16) return qtype == QT_Q4_K;
+    return act_mode == B200Q_ACT_X8 && qtype == QT_Q4_K && min_m > 0 && m >= min_m;
+}
+
 int launch_gemv(int qtype, int act_mode, const void* w, const float* x, float* y, int m, int k, int n,
                 long long x_stride, long long y_stride, int32_t* isums, Device* dev, cudaStream_t st, bool pdl,
                 int flags) {
@@ -289,6 +299,16 @@ int launch_gemv(int qtype, int act_mode, const void* w, const float* x, float* y
     if ((reinterpret_cast<uintptr_t>(w) & 15u) || (reinterpret_cast<uintptr_t>(x) & 15u) || (x_stride & 3))
         return B200Q_EALIGN;
     if (isums && m != 1) return B200Q_EINVAL;
+    if (!isums && uses_tile_path(qtype, act_mode, m)) {
+        // Batches of up to kTileMaxM activation rows per tile-kernel call.
+        for (int r0 = 0; r0 < m; r0 += kTileMaxM) {
+            const int rc = launch_tile(qtype, w, x + r0 * x_stride, x_stride, y + r0 * y_stride,
+                                       std::min(kTileMaxM, m - r0), k, n, y_stride, dev, st, pdl);
+            if (rc != B200Q_OK) return rc;
+        }
+        return B200Q_OK;
+    }
+    if (act_mode == B200Q_ACT_F16) return B200Q_EQTYPE;
     int rc = gemv_check_shape(qtype, act_mode, k, n, dev);  // validate before any launch
     if (rc != B200Q_OK) return rc;
     const uint8_t* xq = nullptr;

@@ -57,6 +57,21 @@ int expert_swiglu(int act_mode, const float* x, int in_dim, const void* gate, in
                   const void* down, int dq, int out_dim, float* out, float alpha, float beta, Device* dev,
                   cudaStream_t st, bool pdl, int flags);
 
+// Scratch slots used by the tile path (0 = GEMV activations, 1-3 = fused FFN).
+constexpr int kScratchTileX = 4;     // fp16 activation chunks
+constexpr int kScratchTilePart = 5;  // split-K partial outputs
+
+// Tile path (tcgen05, fp16 operands, fp32 accumulators) for 1..kTileMaxM
+// activation rows of a Q4_K matrix; x rows at stride x_stride, y rows at
+// y_stride. Returns a B200Q_* status.
+constexpr int kTileMaxM = 128;
+int launch_tile(int qtype, const void* w, const float* x, long long x_stride, float* y, int m, int k, int n,
+                long long y_stride, Device* dev, cudaStream_t st, bool pdl);
+// Kernel launches one launch_tile call issues (2 or 3).
+int tile_kernel_launches(int k, int n, long long y_stride, int num_sms);
+// Whether launch_gemv hands (qtype, act_mode, m) to the tile path.
+bool uses_tile_path(int qtype, int act_mode, int m);
+
 bool pdl_enabled();
 void set_last_error(int status);
 

@@ -25,6 +25,14 @@
  *                            reference's fp32 result.
  *   B200Q_ACT_X8             x is quantized per 32 elements to int8 (one
  *                            dp4a plane): fastest, ~5e-4 normalised error.
+ *                            For Q4_K with m >= 8 activation rows
+ *                            (B200Q_TILE_MIN_M) the tile path below is used.
+ *   B200Q_ACT_F16            (device entry points, Q4_K only) the tile path:
+ *                            tcgen05 tensor cores on fp16 operands (the
+ *                            reference's fp32 dequantized weight and x, each
+ *                            rounded to fp16) with fp32 accumulation; W is
+ *                            streamed once per 128 activation rows; about
+ *                            3e-5 normalised error against the fp32 result.
  * The drop-in entry points use the mode set by b200q_set_act_mode() or the
  * B200Q_ACT environment variable ("x16" | "x8"); default x16.
  */
@@ -52,6 +60,7 @@ extern "C" {
 
 #define B200Q_ACT_X8 1
 #define B200Q_ACT_X16 2
+#define B200Q_ACT_F16 3
 
 /* status codes */
 #define B200Q_OK 0

@@ -202,6 +202,23 @@ def repack_q6k_lm(W: np.ndarray, k: int, n: int) -> np.ndarray:
     return dst
 
 
+def tile_matmul_f16(W: np.ndarray, qtype: int, X: np.ndarray, k: int, n: int, r0: int = 0, r1: int | None = None):
+    """Restatement of the tile path's operands: Y[m][r] for weight rows
+    [r0, r1) = sum_i fp16(w[r][i]) * fp16(x[m][i]), accumulated exactly (fp64).
+
+    w is the reference's fp32 dequantized weight (orc_dequant_rows, which
+    follows quantized_matmul.cpp:1323-1375 bit for bit) and each operand is
+    rounded once to IEEE binary16 with round-to-nearest-even (numpy's
+    float32 -> float16 conversion, subnormals included)."""
+    r1 = n if r1 is None else r1
+    W = np.ascontiguousarray(W, dtype=np.uint8)
+    wd = np.empty((r1 - r0, k), dtype=np.float32)
+    assert lib().orc_dequant_rows(_p(W), qtype, k, n, r0, r1 - r0, _p(wd)) == 1
+    w16 = wd.astype(np.float16).astype(np.float64)
+    x16 = np.atleast_2d(np.asarray(X, dtype=np.float32)).astype(np.float16).astype(np.float64)
+    return x16 @ w16.T
+
+
 def normalized_error(y: np.ndarray, y_ref: np.ndarray, wnorm: np.ndarray, x: np.ndarray) -> float:
     """max |y - y_ref| / (||w_row|| * ||x||), per activation row."""
     xx = np.atleast_2d(np.asarray(x, dtype=np.float64))
