@@ -28,6 +28,7 @@ STATUS = {
     -7: "kernel pipeline wait timed out",
     -8: "no usable sm_100 device",
     -9: "scratch must grow during stream capture",
+    -10: "request larger than the fixed no-alloc scratch",
 }
 
 # Every symbol include/b200q.h declares: (name, argtypes, restype).
@@ -61,6 +62,7 @@ SIGNATURES.update(
         "b200q_matmul": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, _vp], _i),
         "b200q_matmul_ex": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
         "b200q_matvec_isums": ([_i, _i, _vp, _vp, _vp, _vp, _i, _i, _vp], _i),
+        "b200q_matvec_noalloc": ([_i, _i, _vp, _vp, _vp, _i, _i, _vp], _i),
         "b200q_set_act_mode": ([_i], _i),
         "b200q_get_act_mode": ([], _i),
         "b200q_last_error": ([], _i),

@@ -688,6 +688,7 @@ const char* b200q_status_string(int status) {
         case B200Q_ETIMEOUT: return "kernel pipeline wait timed out";
         case B200Q_ENODEV: return "no usable sm_100 device";
         case B200Q_ECAPTURE: return "scratch must grow during stream capture";
+        case B200Q_ESCRATCH: return "request larger than the fixed no-alloc scratch";
         default: return "unknown status";
     }
 }

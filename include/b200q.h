@@ -73,6 +73,7 @@ extern "C" {
 #define B200Q_ETIMEOUT (-7)    /* a kernel's bounded pipeline wait gave up */
 #define B200Q_ENODEV (-8)      /* no usable sm_100 device */
 #define B200Q_ECAPTURE (-9)    /* scratch must grow while the stream is being captured */
+#define B200Q_ESCRATCH (-10)   /* request larger than b200q_matvec_noalloc's fixed scratch */
 
 /* ---------------------------------------------------------------------
  * 1. Drop-in entry points (host pointers), reference signatures.
@@ -162,6 +163,24 @@ B200Q_API int b200q_matmul_ex(int qtype, int act_mode, const float* x, const voi
  * checks against the CPU restatement. */
 B200Q_API int b200q_matvec_isums(int qtype, int act_mode, const float* x, const void* w, float* y, int* isums, int k, int n,
                        void* stream);
+
+/* Decode matvec (m = 1) that allocates nothing, for callers that cannot
+ * allocate device memory during a call: engines whose memory pool owns HBM
+ * after start-up, latency-bound decode loops that cannot absorb
+ * cudaMalloc/cudaFree, embedders that budget device memory up front. No
+ * counterpart in the reference (its CPU kernels need no device scratch).
+ * Same arguments and results as b200q_matmul with m = 1 (device pointers,
+ * act mode B200Q_ACT_X8 or B200Q_ACT_X16, any qtype of the GEMV).
+ * Its scratch is a fixed array of B200Q_NOALLOC_SCRATCH_BYTES in the
+ * library's device image, held by every GPU that loads the library until
+ * exit. The quantized activation row (2.25 k bytes in x16, 1.25 k in x8,
+ * rounded up to 16) must fit in that size minus 256 bytes: k <= 28992 (x16)
+ * or k <= 52224 (x8), else B200Q_ESCRATCH. The first call
+ * on a device resolves the array's address (make it before any stream
+ * capture). All calls share the array: calls that overlap on the GPU race. */
+#define B200Q_NOALLOC_SCRATCH_BYTES (64 * 1024)
+B200Q_API int b200q_matvec_noalloc(int qtype, int act_mode, const float* x, const void* w, float* y, int k, int n,
+                                   void* stream);
 
 /* Repack device buffers into dst_qtype (B200Q_Q4_K_R4 / Q6_K_R4 from the
  * canonical type, B200Q_Q6_K_LM from Q6_K). Layouts of QM:250-365. */
