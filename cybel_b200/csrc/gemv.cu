@@ -207,10 +207,10 @@ namespace {
 
 template <int DIG>
 cudaError_t launch_quantize(const float* x, long long x_stride, int m, int k, uint8_t* xq, cudaStream_t st, bool pdl) {
-    const long long threads = static_cast<long long>(m) * (k / 32);
+    const long long threads = static_cast<long long>(m) * (k / 4);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>((threads + 127) / 128));
-    cfg.blockDim = dim3(128);
+    cfg.gridDim = dim3(static_cast<unsigned>((threads + 255) / 256));
+    cfg.blockDim = dim3(256);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     if (pdl) {
@@ -219,7 +219,7 @@ cudaError_t launch_quantize(const float* x, long long x_stride, int m, int k, ui
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    return cudaLaunchKernelEx(&cfg, quantize_act_kernel<DIG>, x, x_stride, m, k, xq);
+    return cudaLaunchKernelEx(&cfg, quantize_act_quads_kernel<DIG>, x, x_stride, m, k, xq);
 }
 
 }  // namespace

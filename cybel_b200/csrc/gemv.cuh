@@ -239,6 +239,59 @@ __global__ void __launch_bounds__(128) quantize_act_kernel(const float* __restri
     quantize_group<DIG>(v, xq + row * xq_row_bytes(k, DIG), k, g);
 }
 
+// The same quantization with four elements per thread: the 8 threads of a
+// 32-element group meet through warp shuffles for amax and the code sum, so
+// a row of k elements is quantized by k/4 threads in one short step (the
+// launch latency of this kernel sits between x's producer and the GEMV).
+// Writes exactly what quantize_group writes. blockDim.x must be a multiple
+// of 32.
+template <int DIG>
+__global__ void __launch_bounds__(256) quantize_act_quads_kernel(const float* __restrict__ x, long long x_stride, int m,
+                                                                  int k, uint8_t* __restrict__ xq) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const int quads = k >> 2;
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const bool valid = i < static_cast<long long>(m) * quads;  // groups never straddle the end
+    const int row = valid ? static_cast<int>(i / quads) : 0;
+    const int q4 = valid ? static_cast<int>(i - static_cast<long long>(row) * quads) : 0;
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (valid) v = __ldg(reinterpret_cast<const float4*>(x + row * x_stride) + q4);
+    constexpr float QMAX = DIG == 1 ? 127.0f : 32767.0f;
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    const float iscale = amax > 0.0f ? __fdiv_rn(QMAX, amax) : 0.0f;
+    const int c0 = round_half_even_small(__fmul_rn(v.x, iscale));
+    const int c1 = round_half_even_small(__fmul_rn(v.y, iscale));
+    const int c2 = round_half_even_small(__fmul_rn(v.z, iscale));
+    const int c3 = round_half_even_small(__fmul_rn(v.w, iscale));
+    int sum = c0 + c1 + c2 + c3;
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if (!valid) return;
+    uint8_t* base = xq + row * xq_row_bytes(k, DIG);
+    uint32_t h, l = 0;
+    if (DIG == 1) {
+        h = (static_cast<uint32_t>(c0) & 0xFFu) | ((static_cast<uint32_t>(c1) & 0xFFu) << 8) |
+            ((static_cast<uint32_t>(c2) & 0xFFu) << 16) | (static_cast<uint32_t>(c3) << 24);
+    } else {
+        h = (static_cast<uint32_t>(c0 >> 8) & 0xFFu) | ((static_cast<uint32_t>(c1 >> 8) & 0xFFu) << 8) |
+            ((static_cast<uint32_t>(c2 >> 8) & 0xFFu) << 16) | (static_cast<uint32_t>(c3 >> 8) << 24);
+        l = (static_cast<uint32_t>(c0) & 0xFFu) | ((static_cast<uint32_t>(c1) & 0xFFu) << 8) |
+            ((static_cast<uint32_t>(c2) & 0xFFu) << 16) | (static_cast<uint32_t>(c3) << 24);
+    }
+    reinterpret_cast<uint32_t*>(base)[q4] = h;
+    if (DIG == 2) reinterpret_cast<uint32_t*>(base + k)[q4] = l;
+    if ((threadIdx.x & 7) == 0) {
+        float* gd = reinterpret_cast<float*>(base + static_cast<long long>(k) * DIG);
+        gd[q4 >> 3] = amax > 0.0f ? __fdiv_rn(amax, QMAX) : 0.0f;
+        reinterpret_cast<int*>(gd + k / 32)[q4 >> 3] = sum;
+    }
+}
+
 // One lane's run of RUN codes starting at element e (a multiple of 16) of a
 // quantized row. The run's code sum is recomputed from the bytes when the
 // run is half a group.
@@ -608,10 +661,14 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(
     uint64_t* empty = full + p.NS;
     float* part = reinterpret_cast<float*>(empty + p.NS);  // [rows of this CTA][MR][S]
 
-    const int q0 = static_cast<int>(static_cast<long long>(blockIdx.x) * p.n_quads / gridDim.x);
-    const int q1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * p.n_quads / gridDim.x);
-    const int r_begin = q0 * 4;
-    const int r_end = min(q1 * 4, p.n);
+    // Contiguous slab of rows per CTA, balanced to one row (to one 4-row
+    // group for the R4 layouts).
+    const int unit = F::kR4 ? 4 : 1;
+    const int n_units = F::kR4 ? p.n_quads : p.n;
+    const int u0 = static_cast<int>(static_cast<long long>(blockIdx.x) * n_units / gridDim.x);
+    const int u1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * n_units / gridDim.x);
+    const int r_begin = u0 * unit;
+    const int r_end = min(u1 * unit, p.n);
     const int n_stages = r_end > r_begin ? (r_end - r_begin + p.R - 1) / p.R : 0;
 
     if (tid == 0) {
