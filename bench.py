@@ -269,6 +269,85 @@ def tile_bench(dev, steps: int, warmup: int, shapes=TILE_SHAPES, ms=TILE_MS, cop
     return out
 
 
+def decode_bench(dev, steps: int, warmup: int, shape_name: str = "llama3_8b", ctx: int = 2048):
+    """Single-token decode of the Llama-3-8B-shaped stack at context `ctx`
+    (KV cache prefilled with random values): one step = embedding, 32 layers
+    of norm / qkv / rope / attention / o / norm / SwiGLU FFN, final norm and
+    the Q6_K LM head, replayed as one CUDA graph. Weights: one random-init
+    N(0, 0.02) layer quantized on the host and copied into each layer's own
+    HBM buffers; the 128256-row embedding and head are a random 16032-row
+    block repeated (every row still streams its own bytes). Also times the
+    same step's quantized linears alone (the matvec share of a token)."""
+    import torch
+
+    from cybel_b200 import decode as D
+    from cybel_b200.formats import Q4_K
+
+    shape = {"llama3_8b": D.LLAMA3_8B, "llama3_70b": D.LLAMA3_70B}[shape_name]
+    rng = np.random.default_rng(0)
+    layer = D.random_layer(shape, rng)
+    embed = D.random_rows(Q4_K, shape.vocab, shape.hidden, rng, block_rows=16032, std=1.0)
+    head = D.random_rows(shape.head_qtype, shape.vocab, shape.hidden, rng, block_rows=16032)
+    out_norm = (1 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
+    stack = D.DecodeStack(shape, ctx, [layer], embed, head, out_norm, act_mode=2)
+    del layer, embed, head
+    stack.k_cache.normal_()
+    stack.v_cache.normal_()
+    stack.set_token(128000 % shape.vocab)
+    pos = ctx - 1
+    res = {}
+    for name, lin in (("step", False), ("linears", True)):
+        cap = torch.cuda.Stream(dev)
+        with torch.cuda.stream(cap):
+            for _ in range(max(3, warmup)):
+                stack.step(pos, linears_only=lin)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            stack.step(pos, linears_only=lin)
+        for _ in range(3):
+            g.replay()
+        st = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record(st)
+        for _ in range(steps):
+            g.replay()
+        e1.record(st)
+        torch.cuda.synchronize(dev)
+        res[name] = e0.elapsed_time(e1) / steps
+        del g
+    peak, _ = _peak_hbm()
+    wbytes = shape.token_weight_bytes()
+    kv_bytes = 2 * shape.layers * shape.kv_heads * ctx * shape.head_dim * 2
+    out = {
+        "workload": f"{shape_name}_q4k_decode_ctx{ctx}",
+        "weight_bytes_per_token": wbytes,
+        "kv_bytes_per_token": kv_bytes,
+        "ms_per_token": round(res["step"], 4),
+        "tok_s": round(1e3 / res["step"], 1),
+        "matvec_ms_per_token": round(res["linears"], 4),
+        "matvec_tok_s": round(1e3 / res["linears"], 1),
+        "matvec_weight_gbs": round(wbytes / (res["linears"] * 1e-3) / 1e9, 1),
+        "matvec_hbm_frac": round(wbytes / (res["linears"] * 1e-3) / 1e9 / peak, 4),
+        "step_hbm_frac": round((wbytes + kv_bytes) / (res["step"] * 1e-3) / 1e9 / peak, 4),
+        "act_mode": "x16",
+    }
+    del stack
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_decode_only(args, ws, rank, local):
+    import torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    rec = decode_bench(dev, args.steps, args.warmup, args.decode_shape, args.ctx)
+    if rank == 0:
+        print(json.dumps({"impl": "ours", **rec}), flush=True)
+
+
 def run_tile_only(args, ws, rank, local):
     """`--workload tile`: the tile path alone (one shape/m or all), one JSON line."""
     import torch
@@ -397,6 +476,9 @@ def run_ours(args, ws, rank, local):
         del mats, ys
         torch.cuda.empty_cache()
         tile = tile_bench(dev, max(10, args.steps // 2), args.warmup)
+    decode = None
+    if ws == 1 and not args.no_decode:
+        decode = decode_bench(dev, max(10, args.steps // 2), args.warmup)
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -441,6 +523,7 @@ def run_ours(args, ws, rank, local):
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "tile": tile,
+            "decode": decode,
         }
         print(json.dumps(line), flush=True)
     if ws > 1:
@@ -459,7 +542,10 @@ def main():
     ap.add_argument("--pdl", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-tile", action="store_true", help="skip the tile-path (batched matmul) summary")
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "tile"])
+    ap.add_argument("--no-decode", action="store_true", help="skip the Llama-3-8B decode-step summary")
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "tile", "decode"])
+    ap.add_argument("--decode-shape", default="llama3_8b", choices=["llama3_8b", "llama3_70b"])
+    ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--tile-m", type=int, default=None)
     ap.add_argument("--tile-n", type=int, default=None)
     ap.add_argument("--tile-k", type=int, default=None)
@@ -472,6 +558,9 @@ def main():
         return
     if args.workload == "tile":
         run_tile_only(args, ws, rank, local)
+        return
+    if args.workload == "decode":
+        run_decode_only(args, ws, rank, local)
         return
     run_ours(args, ws, rank, local)
 

@@ -63,6 +63,11 @@ SIGNATURES.update(
         "b200q_matmul_ex": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
         "b200q_matvec_isums": ([_i, _i, _vp, _vp, _vp, _vp, _i, _i, _vp], _i),
         "b200q_matvec_noalloc": ([_i, _i, _vp, _vp, _vp, _i, _i, _vp], _i),
+        "b200q_add_rmsnorm": ([_vp, _vp, _vp, _vp, _i, _i, ctypes.c_float, _vp], _i),
+        "b200q_rope_kv": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float, _vp, _vp, _i, _vp], _i),
+        "b200q_attention_decode": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp], _i),
+        "b200q_swiglu": ([_vp, _vp, _vp, ctypes.c_longlong, _vp], _i),
+        "b200q_unshard_rows": ([_vp, _vp, _i, _i, _i, _vp], _i),
         "b200q_set_act_mode": ([_i], _i),
         "b200q_get_act_mode": ([], _i),
         "b200q_last_error": ([], _i),

@@ -380,6 +380,45 @@ int simd_repack_q6k_lm(const void* src_q6k, void* dst_q6k_lm, int k, int n) {
 }
 
 // ---- row dequantization -------------------------------------------------------
+// ---- decode-step glue ----------------------------------------------------------
+int b200q_add_rmsnorm(float* residual, const float* delta, const float* gamma, float* out, int n, int rows, float eps,
+                      void* stream) {
+    const int rc = launch_add_rmsnorm(residual, delta, gamma, out, n, rows, eps, static_cast<cudaStream_t>(stream));
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_rope_kv(float* q, float* k, const float* v, int batch, int n_heads, int n_kv_heads, int head_dim, int pos,
+                  float theta, void* k_cache, void* v_cache, int max_ctx, void* stream) {
+    const int rc = launch_rope_kv(q, k, v, batch, n_heads, n_kv_heads, head_dim, pos, theta, k_cache, v_cache, max_ctx,
+                                  static_cast<cudaStream_t>(stream));
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_attention_decode(const float* q, const void* k_cache, const void* v_cache, float* out, int batch,
+                           int n_heads, int n_kv_heads, int head_dim, int ctx_len, int max_ctx, void* stream) {
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    if (rc == B200Q_OK)
+        rc = launch_attention(q, k_cache, v_cache, out, batch, n_heads, n_kv_heads, head_dim, ctx_len, max_ctx, dev,
+                              static_cast<cudaStream_t>(stream));
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_swiglu(const float* gate, const float* up, float* out, long long n, void* stream) {
+    const int rc = launch_swiglu(gate, up, out, n, static_cast<cudaStream_t>(stream));
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_unshard_rows(const float* in, float* out, int shards, int rows, int cols, void* stream) {
+    const int rc = launch_unshard_rows(in, out, shards, rows, cols, static_cast<cudaStream_t>(stream));
+    set_last_error(rc);
+    return rc;
+}
+
 int b200q_dequantize_rows(int qtype, const void* w, const int* rows, int nrows, float* out, int k, int n, void* stream) {
     const int rc = launch_dequant_rows(qtype, w, rows, nrows, out, k, n, true, static_cast<cudaStream_t>(stream));
     set_last_error(rc);

@@ -1,0 +1,331 @@
+// Decode-step glue around the quantized linears: residual add + RMSNorm,
+// RoPE with the KV-cache append, and GQA attention of one query token over
+// the cache. These are the non-matvec stages of the reference's single-token
+// decode graph (JSBuild/src/verso/Anvil/core/native/model_graph.cpp:
+// rmsnorm_inplace 674-693, apply_rope_with_dim 1222-1323, the fused GQA
+// attention that follows), restated for one B200 so that a whole layer stack
+// runs on the device and can be captured in one CUDA graph.
+//
+//  * add_rmsnorm_kernel: one CTA per row; residual += delta, out = residual *
+//    (1 / sqrt(mean(residual^2) + eps)) * gamma (the reference's formula).
+//  * rope_kv_kernel: interleaved pairs (2p, 2p+1) rotated by pos *
+//    theta^(-2p / head_dim), as the reference; the rotated k and v are
+//    written to fp16 caches [sequence][kv_head][max_ctx][head_dim].
+//  * attention: split over the context (flash-decoding): one CTA per
+//    (kv head, 128-position chunk) scores the G = n_heads / n_kv_heads query
+//    heads of the group against the chunk, keeps the chunk's max and
+//    exp-sum, and accumulates exp-weighted V; a second kernel merges the
+//    chunks with the usual max rescaling.
+// All kernels take part in programmatic dependent launch (trigger first,
+// wait for the preceding kernel before reading its outputs).
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace b200q {
+
+namespace {
+
+constexpr int kNormThreads = 1024;
+constexpr int kAttnChunk = 128;  // cache positions per attention CTA
+constexpr int kHeadDim = 128;    // head_dim the attention kernels are built for
+constexpr int kMaxGroup = 8;     // query heads per kv head
+
+// One CTA per row of `rows` rows of n elements.
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __restrict__ res,
+                                                                   const float* __restrict__ delta,
+                                                                   const float* __restrict__ gamma,
+                                                                   float* __restrict__ out, int n, float eps) {
+    griddep_launch_dependents();
+    griddep_wait();
+    res += static_cast<long long>(blockIdx.x) * n;
+    out += static_cast<long long>(blockIdx.x) * n;
+    if (delta) delta += static_cast<long long>(blockIdx.x) * n;
+    __shared__ float red[kNormThreads / 32];
+    float ss = 0.0f;
+    for (int i = 4 * threadIdx.x; i < n; i += 4 * kNormThreads) {
+        float4 r = *reinterpret_cast<const float4*>(res + i);
+        if (delta) {
+            const float4 d = *reinterpret_cast<const float4*>(delta + i);
+            r.x += d.x;
+            r.y += d.y;
+            r.z += d.z;
+            r.w += d.w;
+            *reinterpret_cast<float4*>(res + i) = r;
+        }
+        ss = fmaf(r.x, r.x, ss);
+        ss = fmaf(r.y, r.y, ss);
+        ss = fmaf(r.z, r.z, ss);
+        ss = fmaf(r.w, r.w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < kNormThreads / 32 ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float inv_rms = 1.0f / sqrtf(red[0] / static_cast<float>(n) + eps);
+    for (int i = 4 * threadIdx.x; i < n; i += 4 * kNormThreads) {
+        const float4 r = *reinterpret_cast<const float4*>(res + i);
+        const float4 g = *reinterpret_cast<const float4*>(gamma + i);
+        *reinterpret_cast<float4*>(out + i) =
+            make_float4(r.x * inv_rms * g.x, r.y * inv_rms * g.y, r.z * inv_rms * g.z, r.w * inv_rms * g.w);
+    }
+}
+
+// Threads [0, (n_heads + n_kv) * hd/2): one rotation pair each; threads
+// [that, + n_kv * hd): one v element each. blockIdx.y = sequence of the
+// batch (its own q/k/v rows and cache).
+__global__ void rope_kv_kernel(float* __restrict__ q, float* __restrict__ k, const float* __restrict__ v, int n_heads,
+                               int n_kv, int hd, int pos, float log2_theta, __half* __restrict__ kc,
+                               __half* __restrict__ vc, int max_ctx) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const int b = blockIdx.y;
+    q += static_cast<long long>(b) * n_heads * hd;
+    k += static_cast<long long>(b) * n_kv * hd;
+    v += static_cast<long long>(b) * n_kv * hd;
+    kc += static_cast<long long>(b) * n_kv * max_ctx * hd;
+    vc += static_cast<long long>(b) * n_kv * max_ctx * hd;
+    const int half_dim = hd / 2;
+    const int n_pairs = (n_heads + n_kv) * half_dim;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t < n_pairs) {
+        const int head = t / half_dim, p = t - head * half_dim;
+        const float inv_freq = exp2f(-2.0f * static_cast<float>(p) / static_cast<float>(hd) * log2_theta);
+        float s, c;
+        sincosf(static_cast<float>(pos) * inv_freq, &s, &c);
+        float* ptr = head < n_heads ? q + head * hd : k + (head - n_heads) * hd;
+        const float x0 = ptr[2 * p], x1 = ptr[2 * p + 1];
+        const float r0 = x0 * c - x1 * s, r1 = x0 * s + x1 * c;
+        ptr[2 * p] = r0;
+        ptr[2 * p + 1] = r1;
+        if (head >= n_heads) {
+            __half* dst = kc + (static_cast<long long>(head - n_heads) * max_ctx + pos) * hd + 2 * p;
+            *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(r0, r1);
+        }
+    } else if (t < n_pairs + n_kv * hd) {
+        const int e = t - n_pairs, kvh = e / hd, d = e - kvh * hd;
+        vc[(static_cast<long long>(kvh) * max_ctx + pos) * hd + d] = __float2half_rn(v[e]);
+    }
+}
+
+// Partial record per (query head, chunk): o[kHeadDim], m, l.
+constexpr int kPartStride = kHeadDim + 2;
+
+__global__ void __launch_bounds__(128) attn_chunk_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
+                                                         const __half* __restrict__ vc, float* __restrict__ part,
+                                                         int n_heads, int n_kv, int ctx, int max_ctx, float scale) {
+    griddep_launch_dependents();
+    griddep_wait();
+    __shared__ float qs[kMaxGroup][kHeadDim];
+    __shared__ float sc[kMaxGroup][kAttnChunk];
+    __shared__ float ml[kMaxGroup][2];
+    const int kvh = blockIdx.x, c = blockIdx.y, n_chunks = gridDim.y, b = blockIdx.z;
+    const int G = n_heads / n_kv;
+    q += static_cast<long long>(b) * n_heads * kHeadDim;
+    kc += static_cast<long long>(b) * n_kv * max_ctx * kHeadDim;
+    vc += static_cast<long long>(b) * n_kv * max_ctx * kHeadDim;
+    part += static_cast<long long>(b) * n_heads * n_chunks * kPartStride;
+    const int p0 = c * kAttnChunk;
+    const int np = min(kAttnChunk, ctx - p0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < G * kHeadDim; i += blockDim.x)
+        qs[i / kHeadDim][i % kHeadDim] = q[(kvh * G) * kHeadDim + i] * scale;
+    __syncthreads();
+    // Scores: warp w takes positions w, w+4, ...; lane covers 4 dims.
+    const __half* kbase = kc + (static_cast<long long>(kvh) * max_ctx + p0) * kHeadDim + 4 * lane;
+    for (int p = warp; p < np; p += 4) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(kbase + static_cast<long long>(p) * kHeadDim);
+        const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+        const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+        for (int g = 0; g < G; ++g) {
+            const float* qg = qs[g] + 4 * lane;
+            float d = qg[0] * k01.x + qg[1] * k01.y + qg[2] * k23.x + qg[3] * k23.y;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+            if (lane == 0) sc[g][p] = d;
+        }
+    }
+    __syncthreads();
+    // Chunk max and exp-sum per query head (warp w takes heads w, w+4).
+    for (int g = warp; g < G; g += 4) {
+        float m = -INFINITY;
+        for (int p = lane; p < np; p += 32) m = fmaxf(m, sc[g][p]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int p = lane; p < np; p += 32) {
+            const float e = expf(sc[g][p] - m);
+            sc[g][p] = e;
+            l += e;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) {
+            ml[g][0] = m;
+            ml[g][1] = l;
+        }
+    }
+    __syncthreads();
+    // o[g][d] = sum_p e[g][p] * V[p][d]; thread d.
+    const int d = threadIdx.x;
+    float o[kMaxGroup];
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g) o[g] = 0.0f;
+    const __half* vbase = vc + (static_cast<long long>(kvh) * max_ctx + p0) * kHeadDim + d;
+    for (int p = 0; p < np; ++p) {
+        const float vv = __half2float(vbase[static_cast<long long>(p) * kHeadDim]);
+#pragma unroll
+        for (int g = 0; g < kMaxGroup; ++g)
+            if (g < G) o[g] = fmaf(sc[g][p], vv, o[g]);
+    }
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g) {
+        if (g < G) {
+            float* rec = part + (static_cast<long long>(kvh * G + g) * n_chunks + c) * kPartStride;
+            rec[d] = o[g];
+            if (d == 0) {
+                rec[kHeadDim] = ml[g][0];
+                rec[kHeadDim + 1] = ml[g][1];
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kHeadDim) attn_combine_kernel(const float* __restrict__ part, float* __restrict__ out,
+                                                                int n_chunks) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const int h = blockIdx.x, d = threadIdx.x, b = blockIdx.y, n_heads = gridDim.x;
+    const float* rec = part + (static_cast<long long>(b) * n_heads + h) * n_chunks * kPartStride;
+    out += static_cast<long long>(b) * n_heads * kHeadDim;
+    float M = -INFINITY;
+    for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, rec[c * kPartStride + kHeadDim]);
+    float L = 0.0f, acc = 0.0f;
+    for (int c = 0; c < n_chunks; ++c) {
+        const float w = expf(rec[c * kPartStride + kHeadDim] - M);
+        L = fmaf(rec[c * kPartStride + kHeadDim + 1], w, L);
+        acc = fmaf(rec[c * kPartStride + d], w, acc);
+    }
+    out[h * kHeadDim + d] = acc / L;
+}
+
+// out = silu(gate) * up, element-wise (the SiLU * up step of
+// quantized_matmul.cpp:2380-2412, as the fused expert kernel computes it).
+__global__ void swiglu_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ out,
+                              long long n) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float gv = g[i];
+    out[i] = gv / (1.0f + expf(-gv)) * u[i];
+}
+
+// out[r][s * cols + j] = in[s][r][j]: the row-major [rows][shards * cols]
+// view of an all-gather of per-shard [rows][cols] blocks.
+__global__ void unshard_rows_kernel(const float* __restrict__ in, float* __restrict__ out, int shards, int rows,
+                                    int cols) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const long long total = static_cast<long long>(shards) * rows * cols;
+    if (i >= total) return;
+    const int j = static_cast<int>(i % cols);
+    const long long t = i / cols;
+    const int r = static_cast<int>(t % rows), s = static_cast<int>(t / rows);
+    out[(static_cast<long long>(r) * shards + s) * cols + j] = in[i];
+}
+
+cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaStream_t st, cudaLaunchAttribute* attr) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    if (pdl_enabled()) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cfg;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int launch_add_rmsnorm(float* res, const float* delta, const float* gamma, float* out, int n, int rows, float eps,
+                       cudaStream_t st) {
+    if (!res || !gamma || !out || n <= 0 || rows <= 0) return B200Q_EINVAL;
+    if (n % 4) return B200Q_ESHAPE;
+    if (!aligned16(res) || !aligned16(gamma) || !aligned16(out) || (delta && !aligned16(delta))) return B200Q_EALIGN;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(rows), dim3(kNormThreads), st, attr);
+    return cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel, res, delta, gamma, out, n, eps) == cudaSuccess ? B200Q_OK
+                                                                                                    : B200Q_ECUDA;
+}
+
+int launch_rope_kv(float* q, float* k, const float* v, int batch, int n_heads, int n_kv, int hd, int pos, float theta,
+                   void* kc, void* vc, int max_ctx, cudaStream_t st) {
+    if (!q || !k || !v || !kc || !vc || batch <= 0 || n_heads <= 0 || n_kv <= 0 || hd <= 0 || max_ctx <= 0)
+        return B200Q_EINVAL;
+    if (hd % 2 || n_heads % n_kv || pos < 0 || pos >= max_ctx || !(theta > 0.0f)) return B200Q_ESHAPE;
+    if ((reinterpret_cast<uintptr_t>(kc) & 3u) || (reinterpret_cast<uintptr_t>(vc) & 1u)) return B200Q_EALIGN;
+    const int threads = (n_heads + n_kv) * (hd / 2) + n_kv * hd;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3((threads + 255) / 256, batch), dim3(256), st, attr);
+    return cudaLaunchKernelEx(&cfg, rope_kv_kernel, q, k, v, n_heads, n_kv, hd, pos, log2f(theta),
+                              static_cast<__half*>(kc), static_cast<__half*>(vc), max_ctx) == cudaSuccess
+               ? B200Q_OK
+               : B200Q_ECUDA;
+}
+
+int launch_attention(const float* q, const void* kc, const void* vc, float* out, int batch, int n_heads, int n_kv,
+                     int hd, int ctx, int max_ctx, Device* dev, cudaStream_t st) {
+    if (!q || !kc || !vc || !out || batch <= 0 || n_heads <= 0 || n_kv <= 0 || ctx <= 0 || !dev) return B200Q_EINVAL;
+    if (hd != kHeadDim || n_heads % n_kv || n_heads / n_kv > kMaxGroup || ctx > max_ctx) return B200Q_ESHAPE;
+    if ((reinterpret_cast<uintptr_t>(kc) & 7u) || (reinterpret_cast<uintptr_t>(vc) & 1u)) return B200Q_EALIGN;
+    const int n_chunks = (ctx + kAttnChunk - 1) / kAttnChunk;
+    void* part = nullptr;
+    int rc = scratch_for(dev, st, kScratchAttn,
+                         static_cast<size_t>(batch) * n_heads * n_chunks * kPartStride * sizeof(float), &part);
+    if (rc != B200Q_OK) return rc;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(n_kv, n_chunks, batch), dim3(128), st, attr);
+    if (cudaLaunchKernelEx(&cfg, attn_chunk_kernel, q, static_cast<const __half*>(kc), static_cast<const __half*>(vc),
+                           static_cast<float*>(part), n_heads, n_kv, ctx, max_ctx,
+                           1.0f / sqrtf(static_cast<float>(hd))) != cudaSuccess)
+        return B200Q_ECUDA;
+    cudaLaunchConfig_t cfg2 = pdl_cfg(dim3(n_heads, batch), dim3(kHeadDim), st, attr);
+    if (cudaLaunchKernelEx(&cfg2, attn_combine_kernel, static_cast<const float*>(part), out, n_chunks) != cudaSuccess)
+        return B200Q_ECUDA;
+    return B200Q_OK;
+}
+
+int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaStream_t st) {
+    if (!g || !u || !out || n <= 0) return B200Q_EINVAL;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), st, attr);
+    return cudaLaunchKernelEx(&cfg, swiglu_kernel, g, u, out, n) == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
+}
+
+int launch_unshard_rows(const float* in, float* out, int shards, int rows, int cols, cudaStream_t st) {
+    if (!in || !out || shards <= 0 || rows <= 0 || cols <= 0) return B200Q_EINVAL;
+    const long long total = static_cast<long long>(shards) * rows * cols;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), st, attr);
+    return cudaLaunchKernelEx(&cfg, unshard_rows_kernel, in, out, shards, rows, cols) == cudaSuccess ? B200Q_OK
+                                                                                                  : B200Q_ECUDA;
+}
+
+}  // namespace b200q

@@ -1,0 +1,228 @@
+"""Single-token decode of a Llama-style layer stack on one B200.
+
+The caller of the quantized linears in the reference is its C++ decode graph
+(JSBuild/src/verso/Anvil/core/native/model_graph.cpp): per layer RMSNorm,
+the q/k/v projections, RoPE and the KV-cache append, GQA attention over the
+cache, the o projection with the residual add, RMSNorm, and the SwiGLU FFN
+with its residual add; then the final norm and the LM head. ``DecodeStack``
+runs that step entirely on the device through libb200q's entry points:
+
+* ``b200q_fused_matvec`` -- q/k/v sharing one quantized activation vector;
+* ``b200q_matmul_ex`` -- the o projection and the LM head;
+* ``b200q_expert_swiglu`` with beta = 1 -- gate/up, SiLU * up, down, and the
+  residual add in the down projection's epilogue;
+* ``b200q_add_rmsnorm`` / ``b200q_rope_kv`` / ``b200q_attention_decode`` --
+  the glue, with the residual add of the o projection fused into the next
+  RMSNorm;
+
+all on one stream, so one token's step is one CUDA graph. The KV cache is
+fp16, [layer][kv_head][max_ctx][head_dim].
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _native
+from .formats import Q4_K, Q6_K
+from .quantized_matmul import DeviceMatrix
+
+
+@dataclass(frozen=True)
+class StackShape:
+    layers: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    ffn: int
+    vocab: int
+    rope_theta: float = 500000.0
+    eps: float = 1e-5
+    linear_qtype: int = Q4_K
+    head_qtype: int = Q6_K
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden // self.heads
+
+    @property
+    def kv_dim(self) -> int:
+        return self.kv_heads * self.head_dim
+
+    def layer_weight_bytes(self) -> int:
+        from .formats import row_bytes
+
+        h, kv, f, q = self.hidden, self.kv_dim, self.ffn, self.linear_qtype
+        return (2 * h + 2 * kv + 2 * f) * row_bytes(q, h) + h * row_bytes(q, f)
+
+    def token_weight_bytes(self) -> int:
+        """Packed weight bytes one decode step streams (layers + LM head)."""
+        from .formats import row_bytes
+
+        return self.layers * self.layer_weight_bytes() + self.vocab * row_bytes(self.head_qtype, self.hidden)
+
+
+# Llama-3-8B and Llama-3-70B shapes.
+LLAMA3_8B = StackShape(layers=32, hidden=4096, heads=32, kv_heads=8, ffn=14336, vocab=128256)
+LLAMA3_70B = StackShape(layers=80, hidden=8192, heads=64, kv_heads=8, ffn=28672, vocab=128256, head_qtype=Q4_K)
+
+LAYER_MATRICES = ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down")
+
+
+def layer_matrix_shapes(shape: StackShape) -> dict[str, tuple[int, int]]:
+    """(n_rows, k) of each linear of a layer."""
+    h, kv, f = shape.hidden, shape.kv_dim, shape.ffn
+    return {"wq": (h, h), "wk": (kv, h), "wv": (kv, h), "wo": (h, h), "w_gate": (f, h), "w_up": (f, h),
+            "w_down": (h, f)}
+
+
+def random_layer(shape: StackShape, rng: np.random.Generator, std: float = 0.02) -> dict[str, np.ndarray]:
+    """One layer's weights: N(0, std) linears packed to the linear qtype, and
+    RMSNorm gains near 1 (fp32)."""
+    from . import quantize as Q
+
+    out: dict[str, np.ndarray] = {}
+    for name, (n, k) in layer_matrix_shapes(shape).items():
+        out[name] = Q.quantize(rng.normal(0.0, std, size=(n, k)).astype(np.float32), shape.linear_qtype)
+    out["attn_norm"] = (1.0 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
+    out["ffn_norm"] = (1.0 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
+    return out
+
+
+def random_rows(qtype: int, n: int, k: int, rng: np.random.Generator, block_rows: int | None = None,
+                std: float = 0.02) -> np.ndarray:
+    """A packed [n][k] matrix of N(0, std) weights. With block_rows, one block
+    of that many rows is quantized and repeated to n rows (the bytes every
+    row streams are the same size; used for the 128K-row embedding and head
+    at benchmark scale)."""
+    from . import quantize as Q
+
+    if block_rows is None or block_rows >= n:
+        return Q.quantize(rng.normal(0.0, std, size=(n, k)).astype(np.float32), qtype)
+    blk = Q.quantize(rng.normal(0.0, std, size=(block_rows, k)).astype(np.float32), qtype)
+    reps = (n + block_rows - 1) // block_rows
+    return np.ascontiguousarray(np.tile(blk, (reps, 1))[:n])
+
+
+def _vp_array(vals):
+    return (ctypes.c_void_p * len(vals))(*vals)
+
+
+def _int_array(vals):
+    return (ctypes.c_int * len(vals))(*vals)
+
+
+@dataclass
+class _Layer:
+    mats: dict[str, DeviceMatrix]
+    attn_norm: object
+    ffn_norm: object
+    qkv_w: object = field(default=None)
+    qkv_y: object = field(default=None)
+
+
+class DecodeStack:
+    """Device-resident Llama-style stack; ``step(pos)`` issues one token.
+
+    ``layers`` holds one weight dict per layer (``random_layer`` layout); a
+    shorter list is cycled, each layer still getting its own device copy.
+    """
+
+    def __init__(self, shape: StackShape, max_ctx: int, layers: list[dict[str, np.ndarray]], embed: np.ndarray,
+                 head: np.ndarray, out_norm: np.ndarray, act_mode: int = _native.ACT_X16, device: int = 0):
+        import torch
+
+        if shape.head_dim != 128:
+            raise ValueError("the attention kernels are built for head_dim 128")
+        self.shape = shape
+        self.max_ctx = max_ctx
+        self.act_mode = act_mode
+        self.dev = torch.device("cuda", device)
+        self.lib = _native.lib()
+        f32 = dict(dtype=torch.float32, device=self.dev)
+        h, kv = shape.hidden, shape.kv_dim
+        self.layers: list[_Layer] = []
+        for i in range(shape.layers):
+            src = layers[i % len(layers)]
+            mats = {name: DeviceMatrix(shape.linear_qtype, k, n, src[name])
+                    for name, (n, k) in layer_matrix_shapes(shape).items()}
+            self.layers.append(_Layer(mats, torch.from_numpy(src["attn_norm"]).to(self.dev),
+                                      torch.from_numpy(src["ffn_norm"]).to(self.dev)))
+        self.embed = DeviceMatrix(shape.linear_qtype, h, shape.vocab, embed)
+        self.head = DeviceMatrix(shape.head_qtype, h, shape.vocab, head)
+        self.out_norm = torch.from_numpy(out_norm).to(self.dev)
+        cache_shape = (shape.layers, shape.kv_heads, max_ctx, shape.head_dim)
+        self.k_cache = torch.zeros(cache_shape, dtype=torch.float16, device=self.dev)
+        self.v_cache = torch.zeros(cache_shape, dtype=torch.float16, device=self.dev)
+        self.x = torch.zeros(h, **f32)       # residual stream
+        self.hn = torch.zeros(h, **f32)      # normed activations
+        self.q = torch.zeros(h, **f32)
+        self.k = torch.zeros(kv, **f32)
+        self.v = torch.zeros(kv, **f32)
+        self.attn = torch.zeros(h, **f32)
+        self.o = torch.zeros(h, **f32)
+        self.logits = torch.zeros(shape.vocab, **f32)
+        self.token = torch.zeros(1, dtype=torch.int32, device=self.dev)
+        qt3 = _int_array([shape.linear_qtype] * 3)
+        rows3 = _int_array([h, kv, kv])
+        ys = _vp_array([self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr()])
+        for lay in self.layers:
+            lay.qkv_w = _vp_array([lay.mats["wq"].ptr, lay.mats["wk"].ptr, lay.mats["wv"].ptr])
+            lay.qkv_y = ys
+        self._qt3, self._rows3 = qt3, rows3
+        torch.cuda.synchronize(self.dev)
+
+    # -- one token ----------------------------------------------------------------
+    def _check(self, rc, what):
+        _native.check(rc, what)
+
+    def step(self, pos: int, linears_only: bool = False) -> None:
+        """Append the token in ``self.token`` at position ``pos`` and leave the
+        next-token logits in ``self.logits`` (stream: the current one).
+
+        ``linears_only`` issues just the quantized linears of the step, on
+        the same buffers, for timing the matvec share of a token."""
+        import torch
+
+        if not 0 <= pos < self.max_ctx:
+            raise ValueError("position outside the KV cache")
+        s, L, st = self.shape, self.lib, torch.cuda.current_stream(self.dev).cuda_stream
+        W = _native.WEIGHTS_STATIC
+        act = self.act_mode
+        h, kv, hd = s.hidden, s.kv_dim, s.head_dim
+        if not linears_only:
+            self._check(L.b200q_dequantize_rows(s.linear_qtype, self.embed.ptr, self.token.data_ptr(), 1,
+                                                self.x.data_ptr(), h, s.vocab, st), "embedding")
+        for li, lay in enumerate(self.layers):
+            if not linears_only:
+                self._check(L.b200q_add_rmsnorm(self.x.data_ptr(), None, lay.attn_norm.data_ptr(), self.hn.data_ptr(),
+                                                h, 1, s.eps, st), "attn_norm")
+            self._check(L.b200q_fused_matvec(act, self.hn.data_ptr(), h, 3, lay.qkv_w, self._qt3, lay.qkv_y,
+                                             self._rows3, W, st), "qkv")
+            if not linears_only:
+                kc = self.k_cache[li].data_ptr()
+                vc = self.v_cache[li].data_ptr()
+                self._check(L.b200q_rope_kv(self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), 1, s.heads,
+                                            s.kv_heads, hd, pos, s.rope_theta, kc, vc, self.max_ctx, st), "rope_kv")
+                self._check(L.b200q_attention_decode(self.q.data_ptr(), kc, vc, self.attn.data_ptr(), 1, s.heads,
+                                                     s.kv_heads, hd, pos + 1, self.max_ctx, st), "attention")
+            self._check(L.b200q_matmul_ex(s.linear_qtype, act, self.attn.data_ptr(), lay.mats["wo"].ptr,
+                                          self.o.data_ptr(), 1, h, h, W, st), "o_proj")
+            if not linears_only:
+                self._check(L.b200q_add_rmsnorm(self.x.data_ptr(), self.o.data_ptr(), lay.ffn_norm.data_ptr(),
+                                                self.hn.data_ptr(), h, 1, s.eps, st), "ffn_norm")
+            self._check(L.b200q_expert_swiglu(act, self.hn.data_ptr(), h, lay.mats["w_gate"].ptr, s.linear_qtype,
+                                              s.ffn, lay.mats["w_up"].ptr, s.linear_qtype, lay.mats["w_down"].ptr,
+                                              s.linear_qtype, h, self.x.data_ptr(), 1.0, 1.0 if not linears_only
+                                              else 0.0, W, st), "ffn")
+        if not linears_only:
+            self._check(L.b200q_add_rmsnorm(self.x.data_ptr(), None, self.out_norm.data_ptr(), self.hn.data_ptr(), h,
+                                            1, s.eps, st), "out_norm")
+        self._check(L.b200q_matmul_ex(s.head_qtype, act, self.hn.data_ptr(), self.head.ptr, self.logits.data_ptr(), 1,
+                                      h, s.vocab, W, st), "lm_head")
+
+    def set_token(self, token: int) -> None:
+        self.token.fill_(int(token))

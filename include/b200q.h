@@ -210,6 +210,42 @@ B200Q_API int b200q_moe_ffn(int act_mode, const float* x, int in_dim, const int*
                             int down_qtype, int out_dim, float* out, int write_mode, int flags, void* stream);
 
 /* ---------------------------------------------------------------------
+ * Decode-step glue on device buffers, so a whole layer stack runs on the
+ * GPU around the quantized linears (one CUDA graph per token). These
+ * restate the non-matvec stages of the reference decode graph
+ * (model_graph.cpp "MG"); they are internal functions there, not exports.
+ * ------------------------------------------------------------------- */
+
+/* For each of `rows` rows of n elements: residual += delta (delta may be
+ * NULL), out = residual / sqrt(mean(residual^2) + eps) * gamma: MG:674-697
+ * rmsnorm_inplace / rmsnorm_copy with the residual add of the previous
+ * sub-layer fused in. n % 4 == 0, all pointers 16-byte aligned. */
+B200Q_API int b200q_add_rmsnorm(float* residual, const float* delta, const float* gamma, float* out, int n, int rows,
+                                float eps, void* stream);
+
+/* For each of `batch` sequences at the same position pos: RoPE on
+ * q [n_heads][head_dim] and k [n_kv_heads][head_dim] in place (interleaved
+ * pairs, theta^(-2p/head_dim): MG:1222-1323), then k and v appended to fp16
+ * caches [batch][n_kv_heads][max_ctx][head_dim] at pos. */
+B200Q_API int b200q_rope_kv(float* q, float* k, const float* v, int batch, int n_heads, int n_kv_heads, int head_dim,
+                            int pos, float theta, void* k_cache, void* v_cache, int max_ctx, void* stream);
+
+/* For each of `batch` sequences: out[h] = softmax(q[h] . K[0..ctx) /
+ * sqrt(head_dim)) V for one query token, query head h reading kv head
+ * h / (n_heads / n_kv_heads) (GQA), over the fp16 caches above; head_dim
+ * 128, at most 8 query heads per kv head. */
+B200Q_API int b200q_attention_decode(const float* q, const void* k_cache, const void* v_cache, float* out, int batch,
+                                     int n_heads, int n_kv_heads, int head_dim, int ctx_len, int max_ctx, void* stream);
+
+/* out[i] = silu(gate[i]) * up[i] for n elements (the SwiGLU product of
+ * QM:2380-2412, for FFNs whose gate/up and down run on different GPUs). */
+B200Q_API int b200q_swiglu(const float* gate, const float* up, float* out, long long n, void* stream);
+
+/* out[r][s * cols + j] = in[s][r][j]: rows of a row-sharded output from the
+ * all-gather of per-shard [rows][cols] blocks (identity for rows == 1). */
+B200Q_API int b200q_unshard_rows(const float* in, float* out, int shards, int rows, int cols, void* stream);
+
+/* ---------------------------------------------------------------------
  * Runtime controls.
  * ------------------------------------------------------------------- */
 B200Q_API int b200q_set_act_mode(int act_mode);       /* drop-in mode; returns previous */

@@ -1,0 +1,81 @@
+"""CPU restatement of one single-token decode step -- TEST INFRASTRUCTURE ONLY.
+
+Follows the reference decode graph (JSBuild/src/verso/Anvil/core/native/
+model_graph.cpp): rmsnorm_inplace (674-693: x / sqrt(mean(x^2) + eps) *
+gamma), the q/k/v projections, apply_rope_with_dim (1222-1323: interleaved
+pairs (2p, 2p+1) rotated by pos * theta^(-2p / head_dim)), GQA attention of
+the token over the cache (softmax(q . k / sqrt(head_dim)) v, query head h on
+kv head h / (heads / kv_heads)), the o projection and residual add, RMSNorm,
+the SwiGLU FFN (silu(gate) * up, down) and residual add, the final norm and
+the LM head. Weights are the reference's fp32 dequantized values
+(orc_dequant_rows); arithmetic is float64, except that cached k and v are
+rounded to fp16 as the device cache stores them.
+
+Only the tests import this module.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from . import oracle as O
+
+
+class DecodeRef:
+    def __init__(self, shape, layers, embed, head, out_norm, max_ctx: int):
+        self.s = shape
+        self.max_ctx = max_ctx
+        h, kv, f = shape.hidden, shape.kv_dim, shape.ffn
+        q = shape.linear_qtype
+        dims = {"wq": (h, h), "wk": (kv, h), "wv": (kv, h), "wo": (h, h), "w_gate": (f, h), "w_up": (f, h),
+                "w_down": (h, f)}
+        self.layers = []
+        for i in range(shape.layers):
+            src = layers[i % len(layers)]
+            lay = {name: O.dequant(src[name], q, k, n).astype(np.float64) for name, (n, k) in dims.items()}
+            lay["attn_norm"] = src["attn_norm"].astype(np.float64)
+            lay["ffn_norm"] = src["ffn_norm"].astype(np.float64)
+            self.layers.append(lay)
+        self.embed = O.dequant(embed, q, h, shape.vocab).astype(np.float64)
+        self.head = O.dequant(head, shape.head_qtype, h, shape.vocab).astype(np.float64)
+        self.out_norm = out_norm.astype(np.float64)
+        hd = shape.head_dim
+        self.kc = np.zeros((shape.layers, shape.kv_heads, max_ctx, hd))
+        self.vc = np.zeros((shape.layers, shape.kv_heads, max_ctx, hd))
+
+    def _rms(self, x, g):
+        return x / np.sqrt(np.mean(x * x) + self.s.eps) * g
+
+    def _rope(self, v, heads, pos):
+        hd = self.s.head_dim
+        p = np.arange(hd // 2)
+        ang = pos * self.s.rope_theta ** (-2.0 * p / hd)
+        c, s = np.cos(ang), np.sin(ang)
+        v = v.reshape(heads, hd).copy()
+        x0, x1 = v[:, 0::2].copy(), v[:, 1::2].copy()
+        v[:, 0::2] = x0 * c - x1 * s
+        v[:, 1::2] = x0 * s + x1 * c
+        return v
+
+    def step(self, token: int, pos: int) -> np.ndarray:
+        s = self.s
+        hd, G = s.head_dim, s.heads // s.kv_heads
+        x = self.embed[token].copy()
+        for li, L in enumerate(self.layers):
+            hn = self._rms(x, L["attn_norm"])
+            q = self._rope(L["wq"] @ hn, s.heads, pos)
+            k = self._rope(L["wk"] @ hn, s.kv_heads, pos)
+            v = (L["wv"] @ hn).reshape(s.kv_heads, hd)
+            self.kc[li, :, pos] = k.astype(np.float16).astype(np.float64)
+            self.vc[li, :, pos] = v.astype(np.float16).astype(np.float64)
+            att = np.zeros((s.heads, hd))
+            for hh in range(s.heads):
+                kvh = hh // G
+                sc = self.kc[li, kvh, : pos + 1] @ q[hh] / np.sqrt(hd)
+                e = np.exp(sc - sc.max())
+                att[hh] = (e / e.sum()) @ self.vc[li, kvh, : pos + 1]
+            x = x + L["wo"] @ att.reshape(-1)
+            hn = self._rms(x, L["ffn_norm"])
+            g, u = L["w_gate"] @ hn, L["w_up"] @ hn
+            x = x + L["w_down"] @ (g / (1.0 + np.exp(-g)) * u)
+        return self.head @ self._rms(x, self.out_norm)

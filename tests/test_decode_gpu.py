@@ -1,0 +1,147 @@
+"""Decode-step glue and a small layer stack against CPU restatements.
+
+* b200q_add_rmsnorm / b200q_rope_kv / b200q_attention_decode against float64
+  numpy restatements of the reference's rmsnorm_inplace, apply_rope_with_dim
+  and GQA attention (model_graph.cpp:674-693, 1222-1323), with the fp16 cache
+  rounding mirrored: max |d| / max |ref| <= 1e-5 (norm), <= 1e-4 (rope:
+  fp32 angles pos * theta^(-2p/hd) up to pos ~ 1e3, as the reference forms
+  them; attention: fp32 softmax and accumulation over up to 2048 positions).
+* DecodeStack (2 layers, hidden 512, 4 query / 2 kv heads, FFN 768, vocab 512)
+  for 12 consecutive tokens against oracle/decode_ref.py: logits within
+  ||d||_inf / ||ref||_inf <= 2e-3 (x16 activations, fp16 KV cache) and the
+  same argmax wherever the top logit leads the runner-up clearly.
+* CPU-only: the per-token weight bytes of the Llama-3-8B / 70B shapes.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+
+def test_token_weight_bytes_match_the_layer_inventory():
+    from cybel_b200.decode import LLAMA3_70B, LLAMA3_8B
+
+    assert LLAMA3_8B.layer_weight_bytes() == 122_683_392
+    assert LLAMA3_8B.token_weight_bytes() == 4_356_808_704
+    assert LLAMA3_70B.layer_weight_bytes() == 481_296_384
+    assert LLAMA3_70B.token_weight_bytes() == 39_094_714_368
+
+
+def _rel(a, b):
+    return float(np.max(np.abs(np.asarray(a, np.float64) - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("with_delta", [False, True])
+def test_add_rmsnorm(with_delta):
+    import torch
+    from cybel_b200 import _native
+
+    rng = np.random.default_rng(1)
+    n = 4096
+    res = rng.standard_normal(n).astype(np.float32)
+    delta = rng.standard_normal(n).astype(np.float32)
+    gamma = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    r, d, g = (torch.from_numpy(a).cuda() for a in (res, delta, gamma))
+    out = torch.empty(n, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    rc = _native.lib().b200q_add_rmsnorm(r.data_ptr(), d.data_ptr() if with_delta else None, g.data_ptr(),
+                                         out.data_ptr(), n, 1, 1e-5, st)
+    assert rc == 0
+    x = res.astype(np.float64) + (delta if with_delta else 0.0)
+    ref = x / np.sqrt(np.mean(x * x) + 1e-5) * gamma
+    assert _rel(out.cpu().numpy(), ref) <= 1e-5
+    assert _rel(r.cpu().numpy(), x) <= 1e-6
+
+
+@pytest.mark.gpu
+def test_rope_kv_append():
+    import torch
+    from cybel_b200 import _native
+
+    rng = np.random.default_rng(2)
+    H, KV, hd, pos, max_ctx, theta = 32, 8, 128, 777, 1024, 500000.0
+    q = rng.standard_normal(H * hd).astype(np.float32)
+    k = rng.standard_normal(KV * hd).astype(np.float32)
+    v = rng.standard_normal(KV * hd).astype(np.float32)
+    qt, kt, vt = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    kc = torch.zeros((KV, max_ctx, hd), dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    st = torch.cuda.current_stream().cuda_stream
+    assert _native.lib().b200q_rope_kv(qt.data_ptr(), kt.data_ptr(), vt.data_ptr(), 1, H, KV, hd, pos, theta,
+                                       kc.data_ptr(), vc.data_ptr(), max_ctx, st) == 0
+
+    def rope(a, heads):
+        p = np.arange(hd // 2)
+        ang = pos * theta ** (-2.0 * p / hd)
+        a = a.reshape(heads, hd).astype(np.float64)
+        out = a.copy()
+        out[:, 0::2] = a[:, 0::2] * np.cos(ang) - a[:, 1::2] * np.sin(ang)
+        out[:, 1::2] = a[:, 0::2] * np.sin(ang) + a[:, 1::2] * np.cos(ang)
+        return out
+
+    qr, kr = rope(q, H), rope(k, KV)
+    # fp32 angles pos * theta^(-2p/hd), as the reference computes them
+    assert _rel(qt.cpu().numpy().reshape(H, hd), qr) <= 1e-4
+    assert _rel(kt.cpu().numpy().reshape(KV, hd), kr) <= 1e-4
+    kcn, vcn = kc.float().cpu().numpy(), vc.float().cpu().numpy()
+    assert _rel(kcn[:, pos], kr.astype(np.float16).astype(np.float64)) <= 1e-3
+    assert np.array_equal(vcn[:, pos], v.reshape(KV, hd).astype(np.float16).astype(np.float32))
+    assert not kcn[:, :pos].any() and not kcn[:, pos + 1:].any()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,KV,ctx", [(32, 8, 1), (32, 8, 5), (32, 8, 128), (32, 8, 300), (32, 8, 2048), (4, 2, 129),
+                                      (64, 8, 1000)])
+def test_attention_decode(H, KV, ctx):
+    import torch
+    from cybel_b200 import _native
+
+    rng = np.random.default_rng(H + ctx)
+    hd, max_ctx = 128, max(ctx, 64) + 3
+    q = rng.standard_normal(H * hd).astype(np.float32)
+    kc = rng.standard_normal((KV, max_ctx, hd)).astype(np.float16)
+    vc = rng.standard_normal((KV, max_ctx, hd)).astype(np.float16)
+    qt = torch.from_numpy(q).cuda()
+    kct, vct = torch.from_numpy(kc).cuda(), torch.from_numpy(vc).cuda()
+    out = torch.empty(H * hd, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    assert _native.lib().b200q_attention_decode(qt.data_ptr(), kct.data_ptr(), vct.data_ptr(), out.data_ptr(), 1, H,
+                                                KV, hd, ctx, max_ctx, st) == 0
+    ref = np.zeros((H, hd))
+    G = H // KV
+    for h in range(H):
+        K = kc[h // G, :ctx].astype(np.float64)
+        V = vc[h // G, :ctx].astype(np.float64)
+        s = K @ q[h * hd:(h + 1) * hd].astype(np.float64) / np.sqrt(hd)
+        e = np.exp(s - s.max())
+        ref[h] = (e / e.sum()) @ V
+    assert _rel(out.cpu().numpy().reshape(H, hd), ref) <= 1e-4
+
+
+@pytest.mark.gpu
+def test_decode_stack_matches_restatement():
+    from cybel_b200.decode import DecodeStack, StackShape, random_layer, random_rows
+    from cybel_b200.formats import Q4_K, Q6_K
+    from oracle.decode_ref import DecodeRef
+
+    shape = StackShape(layers=2, hidden=512, heads=4, kv_heads=2, ffn=768, vocab=512)
+    rng = np.random.default_rng(7)
+    layers = [random_layer(shape, rng) for _ in range(shape.layers)]
+    embed = random_rows(Q4_K, shape.vocab, shape.hidden, rng, std=1.0)
+    head = random_rows(Q6_K, shape.vocab, shape.hidden, rng)
+    out_norm = (1 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
+    max_ctx = 64
+    dev = DecodeStack(shape, max_ctx, layers, embed, head, out_norm)
+    ref = DecodeRef(shape, layers, embed, head, out_norm, max_ctx)
+    tokens = [3, 17, 5, 100, 511, 0, 42, 42, 7, 300, 64, 1]
+    for pos, tok in enumerate(tokens):
+        dev.set_token(tok)
+        dev.step(pos)
+        got = dev.logits.cpu().numpy()
+        want = ref.step(tok, pos)
+        assert _rel(got, want) <= 2e-3, pos
+        top2 = np.sort(want)[-2:]
+        if top2[1] - top2[0] > 5e-3 * np.max(np.abs(want)):  # a clear winner
+            assert int(np.argmax(got)) == int(np.argmax(want)), pos
