@@ -338,6 +338,124 @@ def decode_bench(dev, steps: int, warmup: int, shape_name: str = "llama3_8b", ct
     return out
 
 
+def sharded_decode_bench(dev, ws, rank, local, steps: int, warmup: int, batch: int = 1, ctx: int = 2048,
+                         shape_name: str = "llama3_70b"):
+    """Llama-3-70B-shaped Q4_K decode row-sharded over the ws ranks of this
+    node (rank g holds rows [g n/ws, (g+1) n/ws) of every linear and the
+    matching heads; NCCL all-gathers of the partial outputs), `batch`
+    sequences at context `ctx` (KV caches prefilled with random values).
+    One step is captured as a CUDA graph (collectives included) and
+    replayed; time = max over ranks of the CUDA-event time. Weights: each
+    linear repeats one random N(0, 0.02) 2048-row block, embedding and head
+    one 16032-row block (bytes per token are those of the full model)."""
+    import torch
+
+    from cybel_b200 import _native
+    from cybel_b200 import decode as D
+    from cybel_b200.formats import Q4_K
+    from cybel_b200.sharded import GpuOps, ShardedDecode, ShardPlan, shard_layer, shard_rows
+
+    shape = {"llama3_8b": D.LLAMA3_8B, "llama3_70b": D.LLAMA3_70B}[shape_name]
+    plan = ShardPlan(shape, ws, rank)
+    rng = np.random.default_rng(0)
+    layer = D.random_layer(shape, rng, block_rows=2048)
+    embed = D.random_rows(Q4_K, shape.vocab, shape.hidden, rng, block_rows=16032, std=1.0)
+    head = D.random_rows(shape.head_qtype, shape.vocab, shape.hidden, rng, block_rows=16032)
+    out_norm = (1 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
+    act = _native.ACT_X16 if batch < 8 else _native.ACT_X8
+    ops = GpuOps(local, act_mode=act, world=ws)
+    model = ShardedDecode(plan, ctx, batch, [shard_layer(layer, plan)], embed, shard_rows(head, plan, "head"),
+                          out_norm, ops)
+    del layer, embed, head
+    model.k_cache.normal_()
+    model.v_cache.normal_()
+    model.tokens.fill_(128000 % shape.vocab)
+    pos = ctx - 1
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    cap = torch.cuda.Stream(dev)
+    with torch.cuda.stream(cap):
+        for _ in range(max(3, warmup)):
+            model.step(pos)
+    barrier()
+    graph = torch.cuda.CUDAGraph()
+    graphed = True
+    try:
+        with torch.cuda.graph(graph, stream=cap):
+            model.step(pos)
+    except Exception as e:  # collectives that cannot be captured: time the eager step
+        graphed = False
+        graph = None
+        err = f"{type(e).__name__}: {e}"[:200]
+    barrier()
+
+    def run():
+        if graphed:
+            graph.replay()
+        else:
+            model.step(pos)
+
+    for _ in range(3):
+        run()
+    barrier()
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        run()
+    e1.record(st)
+    barrier()
+    ms = e0.elapsed_time(e1) / steps
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t[0])
+    del graph
+    barrier()
+    wbytes = shape.token_weight_bytes()
+    peak, _ = _peak_hbm()
+    rec = {
+        "workload": f"{shape_name}_q4k_decode_rowsharded_b{batch}_ctx{ctx}",
+        "n_gpus": ws,
+        "batch": batch,
+        "ms_per_step": round(ms, 4),
+        "tok_s": round(batch * 1e3 / ms, 1),
+        "weight_bytes_per_token_all_gpus": wbytes,
+        "weight_gbs_per_gpu": round(wbytes / ws / (ms * 1e-3) / 1e9, 1),
+        "hbm_frac_per_gpu": round(wbytes / ws / (ms * 1e-3) / 1e9 / peak, 4),
+        "collectives_per_step": 4 * shape.layers + 1 if ws > 1 else 0,
+        "cuda_graph": graphed,
+        "act_mode": "x16" if act == _native.ACT_X16 else "x8 (tile path for Q4_K)",
+    }
+    if not graphed:
+        rec["graph_error"] = err
+    del model
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_sharded_only(args, ws, rank, local):
+    import torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    rec = sharded_decode_bench(dev, ws, rank, local, args.steps, args.warmup, args.batch, args.ctx, args.decode_shape)
+    if rank == 0:
+        print(json.dumps({"impl": "ours", **rec}), flush=True)
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def run_decode_only(args, ws, rank, local):
     import torch
 
@@ -543,8 +661,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-tile", action="store_true", help="skip the tile-path (batched matmul) summary")
     ap.add_argument("--no-decode", action="store_true", help="skip the Llama-3-8B decode-step summary")
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "tile", "decode"])
-    ap.add_argument("--decode-shape", default="llama3_8b", choices=["llama3_8b", "llama3_70b"])
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "tile", "decode", "sharded"])
+    ap.add_argument("--decode-shape", default=None, choices=["llama3_8b", "llama3_70b"])
+    ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--tile-m", type=int, default=None)
     ap.add_argument("--tile-n", type=int, default=None)
@@ -560,7 +679,12 @@ def main():
         run_tile_only(args, ws, rank, local)
         return
     if args.workload == "decode":
+        args.decode_shape = args.decode_shape or "llama3_8b"
         run_decode_only(args, ws, rank, local)
+        return
+    if args.workload == "sharded":
+        args.decode_shape = args.decode_shape or "llama3_70b"
+        run_sharded_only(args, ws, rank, local)
         return
     run_ours(args, ws, rank, local)
 

@@ -79,14 +79,14 @@ def layer_matrix_shapes(shape: StackShape) -> dict[str, tuple[int, int]]:
             "w_down": (h, f)}
 
 
-def random_layer(shape: StackShape, rng: np.random.Generator, std: float = 0.02) -> dict[str, np.ndarray]:
+def random_layer(shape: StackShape, rng: np.random.Generator, std: float = 0.02,
+                 block_rows: int | None = None) -> dict[str, np.ndarray]:
     """One layer's weights: N(0, std) linears packed to the linear qtype, and
-    RMSNorm gains near 1 (fp32)."""
-    from . import quantize as Q
-
+    RMSNorm gains near 1 (fp32). With block_rows, each linear repeats one
+    quantized block of that many rows (see random_rows)."""
     out: dict[str, np.ndarray] = {}
     for name, (n, k) in layer_matrix_shapes(shape).items():
-        out[name] = Q.quantize(rng.normal(0.0, std, size=(n, k)).astype(np.float32), shape.linear_qtype)
+        out[name] = random_rows(shape.linear_qtype, n, k, rng, block_rows=block_rows, std=std)
     out["attn_norm"] = (1.0 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
     out["ffn_norm"] = (1.0 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
     return out

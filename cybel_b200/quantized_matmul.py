@@ -234,6 +234,11 @@ class DeviceMatrix:
     def ptr(self) -> int:
         return int(self.buffer.data_ptr())
 
+    def clone(self) -> "DeviceMatrix":
+        """A second resident copy of the same rows (device-to-device)."""
+        return DeviceMatrix(self.qtype, self.input_dim, self.output_dim, self.buffer[: self.buffer.numel() - 16],
+                            name=self.name)
+
 
 def matmul_device(x, matrix: DeviceMatrix, out=None, act_mode: int = _native.ACT_X16):
     """Y = X @ W on the current CUDA stream; X float32 CUDA [m, in] or [in]."""

@@ -1,0 +1,260 @@
+"""Output-row-sharded decode across the GPUs of one node (one process per GPU).
+
+Every linear of the stack is split by output rows: rank g of G holds rows
+[g * n / G, (g + 1) * n / G) of each matrix, resident in its own HBM, and the
+partial outputs are all-gathered (NCCL over NVLink / NVSwitch) before the
+next consumer that needs the full vector. The q/k/v row slices are whole
+heads (q heads g * H/G.., kv heads g * KV/G..; G divides KV), so RoPE, the
+KV cache and attention stay local to the rank that owns the heads. Per layer
+the gathers are: the attention output (input of the o projection), the o
+projection (the residual), the SwiGLU hidden vector (input of the down
+projection) and the down projection (the residual); one more gathers the
+logits. Norms and the residual stream are replicated on every rank.
+
+``ShardedDecode`` holds that orchestration once; the arithmetic comes from
+an ops object: ``GpuOps`` (libb200q kernels + torch.distributed NCCL) on the
+device, or a CPU restatement in the tests, which checks the same
+orchestration with gloo ranks.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _native
+from .decode import StackShape, layer_matrix_shapes
+
+
+@dataclass(frozen=True)
+class ShardPlan:
+    shape: StackShape
+    world: int
+    rank: int
+
+    def __post_init__(self):
+        s, G = self.shape, self.world
+        if G < 1 or not 0 <= self.rank < G:
+            raise ValueError("bad rank / world size")
+        for what, v in (("heads", s.heads), ("kv_heads", s.kv_heads), ("hidden", s.hidden), ("ffn", s.ffn),
+                        ("vocab", s.vocab)):
+            if v % G:
+                raise ValueError(f"{what} = {v} is not divisible by {G} ranks")
+
+    @property
+    def heads(self) -> int:
+        return self.shape.heads // self.world
+
+    @property
+    def kv_heads(self) -> int:
+        return self.shape.kv_heads // self.world
+
+    def local_rows(self, name: str) -> int:
+        n = layer_matrix_shapes(self.shape)[name][0] if name != "head" else self.shape.vocab
+        return n // self.world
+
+    def row_range(self, name: str) -> tuple[int, int]:
+        """Rows of matrix `name` ("head" for the LM head) this rank owns."""
+        n_l = self.local_rows(name)
+        return self.rank * n_l, (self.rank + 1) * n_l
+
+
+def shard_rows(packed: np.ndarray, plan: ShardPlan, name: str) -> np.ndarray:
+    """This rank's rows of a packed row-major matrix (canonical layouts: a
+    row's blocks are contiguous, so a row range is a byte range)."""
+    r0, r1 = plan.row_range(name)
+    return np.ascontiguousarray(packed[r0:r1])
+
+
+def shard_layer(layer: dict[str, np.ndarray], plan: ShardPlan) -> dict[str, np.ndarray]:
+    out = {name: shard_rows(layer[name], plan, name) for name in layer_matrix_shapes(plan.shape)}
+    out["attn_norm"] = layer["attn_norm"]
+    out["ffn_norm"] = layer["ffn_norm"]
+    return out
+
+
+class ShardedDecode:
+    """One rank's part of a row-sharded single-token decode of ``batch``
+    sequences (all at the same position).
+
+    layers: this rank's shards (``shard_layer``) of one weight dict per layer;
+    a shorter list is cycled (each layer still gets its own copy); embed: the
+    full packed embedding (replicated); head: this rank's rows of the LM head.
+    """
+
+    def __init__(self, plan: ShardPlan, max_ctx: int, batch: int, layers, embed, head, out_norm, ops):
+        s = plan.shape
+        self.plan, self.shape, self.ops = plan, s, ops
+        self.max_ctx, self.batch = max_ctx, batch
+        B, G, hd = batch, plan.world, s.head_dim
+        shapes = layer_matrix_shapes(s)
+        self.layers = []
+        first = {}
+        for li in range(s.layers):
+            src = layers[li % len(layers)]
+            lay = {}
+            for name, (_, k) in shapes.items():
+                if li >= len(layers) and hasattr(ops, "clone_matrix"):
+                    lay[name] = ops.clone_matrix(first[li % len(layers)][name])
+                else:
+                    lay[name] = ops.matrix(s.linear_qtype, k, plan.local_rows(name), src[name])
+            lay["attn_norm"] = ops.vector(src["attn_norm"])
+            lay["ffn_norm"] = ops.vector(src["ffn_norm"])
+            if li < len(layers):
+                first[li] = lay
+            self.layers.append(lay)
+        self.embed = ops.matrix(s.linear_qtype, s.hidden, s.vocab, embed)
+        self.head = ops.matrix(s.head_qtype, s.hidden, plan.local_rows("head"), head)
+        self.out_norm = ops.vector(out_norm)
+        self.k_cache, self.v_cache = ops.cache(s.layers, B, plan.kv_heads, max_ctx, hd)
+        z = ops.zeros
+        h, h_l = s.hidden, s.hidden // G
+        q_l, kv_l, f_l = plan.heads * hd, plan.kv_heads * hd, s.ffn // G
+        self.x, self.hn = z(B * h), z(B * h)
+        self.q, self.k, self.v, self.a_l = z(B * q_l), z(B * kv_l), z(B * kv_l), z(B * q_l)
+        self.o_l, self.g_l, self.u_l, self.f_l, self.d_l = z(B * h_l), z(B * f_l), z(B * f_l), z(B * f_l), z(B * h_l)
+        self.logits_l = z(B * plan.local_rows("head"))
+        # gathered vectors [B][n]; with B > 1 the all-gather lands in a
+        # [G][B][n/G] buffer first and is re-laid out
+        if G > 1:
+            self.a, self.o, self.f, self.d = z(B * h), z(B * h), z(B * s.ffn), z(B * h)
+            self.logits = z(B * s.vocab)
+        else:  # one rank: the local vectors are the whole vectors
+            self.a, self.o, self.f, self.d, self.logits = self.a_l, self.o_l, self.f_l, self.d_l, self.logits_l
+        self.gbuf = z(B * max(s.ffn, s.vocab)) if (B > 1 and G > 1) else None
+        self.tokens = ops.tokens(B)
+
+    def _gather(self, full, local, n_local):
+        if self.plan.world > 1:
+            self.ops.all_gather(full, local, self.gbuf, self.batch, n_local)
+
+    def step(self, pos: int) -> None:
+        """Decode the tokens in ``self.tokens`` at position ``pos``; the full
+        logits of every sequence land in ``self.logits`` ([batch][vocab])."""
+        s, p, ops, B = self.shape, self.plan, self.ops, self.batch
+        if not 0 <= pos < self.max_ctx:
+            raise ValueError("position outside the KV cache")
+        h, hd, G = s.hidden, s.head_dim, p.world
+        ops.embed(self.embed, self.tokens, self.x, B, h, s.vocab)
+        delta = None
+        for li, lay in enumerate(self.layers):
+            ops.add_rmsnorm(self.x, delta, lay["attn_norm"], self.hn, h, B, s.eps)
+            ops.linear3([lay["wq"], lay["wk"], lay["wv"]], self.hn, [self.q, self.k, self.v], B, h,
+                        [p.heads * hd, p.kv_heads * hd, p.kv_heads * hd])
+            kc, vc = ops.cache_layer(self.k_cache, li), ops.cache_layer(self.v_cache, li)
+            ops.rope_kv(self.q, self.k, self.v, B, p.heads, p.kv_heads, hd, pos, s.rope_theta, kc, vc, self.max_ctx)
+            ops.attention(self.q, kc, vc, self.a_l, B, p.heads, p.kv_heads, hd, pos + 1, self.max_ctx)
+            self._gather(self.a, self.a_l, h // G)
+            ops.linear(lay["wo"], self.a, self.o_l, B, h, h // G)
+            self._gather(self.o, self.o_l, h // G)
+            ops.add_rmsnorm(self.x, self.o, lay["ffn_norm"], self.hn, h, B, s.eps)
+            ops.linear3([lay["w_gate"], lay["w_up"]], self.hn, [self.g_l, self.u_l], B, h, [s.ffn // G] * 2)
+            ops.swiglu(self.g_l, self.u_l, self.f_l, B * (s.ffn // G))
+            self._gather(self.f, self.f_l, s.ffn // G)
+            ops.linear(lay["w_down"], self.f, self.d_l, B, s.ffn, h // G)
+            self._gather(self.d, self.d_l, h // G)
+            delta = self.d
+        ops.add_rmsnorm(self.x, delta, self.out_norm, self.hn, h, B, s.eps)
+        ops.linear(self.head, self.hn, self.logits_l, B, h, p.local_rows("head"))
+        self._gather(self.logits, self.logits_l, p.local_rows("head"))
+
+
+class GpuOps:
+    """ShardedDecode arithmetic on one GPU: libb200q kernels on the current
+    stream, all-gathers through torch.distributed (NCCL) on the same stream.
+    With world 1 no collective runs."""
+
+    def __init__(self, device: int = 0, act_mode: int = _native.ACT_X16, group=None, world: int = 1):
+        import torch
+
+        self.torch = torch
+        self.dev = torch.device("cuda", device)
+        self.lib = _native.lib()
+        self.act = act_mode
+        self.group = group
+        self.world = world
+        self._keep = []  # ctypes arrays referenced by captured calls
+
+    # -- storage -------------------------------------------------------------------
+    def zeros(self, n: int):
+        return self.torch.zeros(n, dtype=self.torch.float32, device=self.dev)
+
+    def vector(self, a: np.ndarray):
+        return self.torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(self.dev)
+
+    def matrix(self, qtype: int, k: int, n_rows: int, packed: np.ndarray):
+        from .quantized_matmul import DeviceMatrix
+
+        return DeviceMatrix(qtype, k, n_rows, packed)
+
+    def clone_matrix(self, m):
+        return m.clone()
+
+    def cache(self, layers: int, batch: int, kv_heads: int, max_ctx: int, hd: int):
+        shape = (layers, batch, kv_heads, max_ctx, hd)
+        t = self.torch
+        return t.zeros(shape, dtype=t.float16, device=self.dev), t.zeros(shape, dtype=t.float16, device=self.dev)
+
+    def cache_layer(self, cache, li: int):
+        return cache[li]
+
+    def tokens(self, batch: int):
+        return self.torch.zeros(batch, dtype=self.torch.int32, device=self.dev)
+
+    # -- arithmetic ----------------------------------------------------------------
+    def _st(self):
+        return self.torch.cuda.current_stream(self.dev).cuda_stream
+
+    def _ok(self, rc, what):
+        _native.check(rc, what)
+
+    def embed(self, m, tokens, out, batch, hidden, vocab):
+        self._ok(self.lib.b200q_dequantize_rows(m.qtype, m.ptr, tokens.data_ptr(), batch, out.data_ptr(), hidden,
+                                                vocab, self._st()), "embedding")
+
+    def linear(self, m, x, out, batch, k, n_rows):
+        self._ok(self.lib.b200q_matmul_ex(m.qtype, self.act, x.data_ptr(), m.ptr, out.data_ptr(), batch, k, n_rows,
+                                          _native.WEIGHTS_STATIC, self._st()), "linear")
+
+    def linear3(self, ms, x, outs, batch, k, rows):
+        if batch != 1:
+            for m, o, n in zip(ms, outs, rows):
+                self.linear(m, x, o, batch, k, n)
+            return
+        import ctypes
+
+        c = len(ms)
+        w = (ctypes.c_void_p * c)(*[m.ptr for m in ms])
+        y = (ctypes.c_void_p * c)(*[o.data_ptr() for o in outs])
+        q = (ctypes.c_int * c)(*[m.qtype for m in ms])
+        r = (ctypes.c_int * c)(*rows)
+        self._keep.append((w, y, q, r))
+        self._ok(self.lib.b200q_fused_matvec(self.act, x.data_ptr(), k, c, w, q, y, r, _native.WEIGHTS_STATIC,
+                                             self._st()), "fused linears")
+
+    def add_rmsnorm(self, res, delta, gamma, out, n, rows, eps):
+        self._ok(self.lib.b200q_add_rmsnorm(res.data_ptr(), None if delta is None else delta.data_ptr(),
+                                            gamma.data_ptr(), out.data_ptr(), n, rows, eps, self._st()), "rmsnorm")
+
+    def rope_kv(self, q, k, v, batch, heads, kv_heads, hd, pos, theta, kc, vc, max_ctx):
+        self._ok(self.lib.b200q_rope_kv(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, kv_heads, hd, pos,
+                                        theta, kc.data_ptr(), vc.data_ptr(), max_ctx, self._st()), "rope_kv")
+
+    def attention(self, q, kc, vc, out, batch, heads, kv_heads, hd, ctx, max_ctx):
+        self._ok(self.lib.b200q_attention_decode(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), batch,
+                                                 heads, kv_heads, hd, ctx, max_ctx, self._st()), "attention")
+
+    def swiglu(self, g, u, out, n):
+        self._ok(self.lib.b200q_swiglu(g.data_ptr(), u.data_ptr(), out.data_ptr(), n, self._st()), "swiglu")
+
+    def all_gather(self, full, local, gbuf, batch, n_local):
+        import torch.distributed as dist
+
+        n = self.world * batch * n_local
+        if batch == 1:
+            dist.all_gather_into_tensor(full[:n], local[:n_local], group=self.group)
+            return
+        dist.all_gather_into_tensor(gbuf[:n], local[: batch * n_local], group=self.group)
+        self._ok(self.lib.b200q_unshard_rows(gbuf.data_ptr(), full.data_ptr(), self.world, batch, n_local,
+                                             self._st()), "unshard")

@@ -145,3 +145,50 @@ def test_decode_stack_matches_restatement():
         top2 = np.sort(want)[-2:]
         if top2[1] - top2[0] > 5e-3 * np.max(np.abs(want)):  # a clear winner
             assert int(np.argmax(got)) == int(np.argmax(want)), pos
+
+
+@pytest.mark.gpu
+def test_unshard_rows():
+    import torch
+    from cybel_b200 import _native
+
+    G, B, c = 4, 3, 40
+    src = torch.arange(G * B * c, dtype=torch.float32, device="cuda")
+    out = torch.empty_like(src)
+    st = torch.cuda.current_stream().cuda_stream
+    assert _native.lib().b200q_unshard_rows(src.data_ptr(), out.data_ptr(), G, B, c, st) == 0
+    want = src.cpu().numpy().reshape(G, B, c).transpose(1, 0, 2).reshape(-1)
+    assert np.array_equal(out.cpu().numpy(), want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("batch", [1, 3])
+def test_sharded_decode_one_rank_matches_restatement(batch):
+    """ShardedDecode on one GPU (world 1) with the device kernels, batched
+    glue included, against the unsharded restatement."""
+    from cybel_b200.decode import StackShape, random_layer, random_rows
+    from cybel_b200.formats import Q4_K, Q6_K
+    from cybel_b200.sharded import GpuOps, ShardedDecode, ShardPlan
+    from oracle.decode_ref import DecodeRef
+
+    shape = StackShape(layers=2, hidden=512, heads=4, kv_heads=2, ffn=768, vocab=512)
+    rng = np.random.default_rng(5)
+    layers = [random_layer(shape, rng) for _ in range(shape.layers)]
+    embed = random_rows(Q4_K, shape.vocab, shape.hidden, rng, std=1.0)
+    head = random_rows(Q6_K, shape.vocab, shape.hidden, rng)
+    out_norm = (1 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
+    model = ShardedDecode(ShardPlan(shape, 1, 0), 32, batch, layers, embed, head, out_norm, GpuOps())
+    tokens = [[3, 17, 5, 100, 7, 8], [9, 0, 511, 42, 42, 1], [1, 2, 3, 4, 5, 6]]
+    refs = [DecodeRef(shape, layers, embed, head, out_norm, 32) for _ in range(batch)]
+    for pos in range(len(tokens[0])):
+        model.tokens.copy_(torch_tokens([tokens[b][pos] for b in range(batch)]))
+        model.step(pos)
+        got = model.logits.cpu().numpy().reshape(batch, shape.vocab)
+        for b in range(batch):
+            assert _rel(got[b], refs[b].step(tokens[b][pos], pos)) <= 2e-3, (b, pos)
+
+
+def torch_tokens(vals):
+    import torch
+
+    return torch.tensor(vals, dtype=torch.int32)
