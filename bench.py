@@ -339,10 +339,11 @@ def decode_bench(dev, steps: int, warmup: int, shape_name: str = "llama3_8b", ct
 
 
 def sharded_decode_bench(dev, ws, rank, local, steps: int, warmup: int, batch: int = 1, ctx: int = 2048,
-                         shape_name: str = "llama3_70b"):
+                         shape_name: str = "llama3_70b", collective: str = "peer"):
     """Llama-3-70B-shaped Q4_K decode row-sharded over the ws ranks of this
     node (rank g holds rows [g n/ws, (g+1) n/ws) of every linear and the
-    matching heads; NCCL all-gathers of the partial outputs), `batch`
+    matching heads; all-gathers of the partial outputs by the peer-memory
+    kernel or NCCL, --collective), `batch`
     sequences at context `ctx` (KV caches prefilled with random values).
     One step is captured as a CUDA graph (collectives included) and
     replayed; time = max over ranks of the CUDA-event time. Weights: each
@@ -363,7 +364,7 @@ def sharded_decode_bench(dev, ws, rank, local, steps: int, warmup: int, batch: i
     head = D.random_rows(shape.head_qtype, shape.vocab, shape.hidden, rng, block_rows=16032)
     out_norm = (1 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
     act = _native.ACT_X16 if batch < 8 else _native.ACT_X8
-    ops = GpuOps(local, act_mode=act, world=ws)
+    ops = GpuOps(local, act_mode=act, world=ws, collective=collective, rank=rank)
     model = ShardedDecode(plan, ctx, batch, [shard_layer(layer, plan)], embed, shard_rows(head, plan, "head"),
                           out_norm, ops)
     del layer, embed, head
@@ -416,6 +417,7 @@ def sharded_decode_bench(dev, ws, rank, local, steps: int, warmup: int, batch: i
     ms = float(t[0])
     del graph
     barrier()
+    ops.close()
     wbytes = shape.token_weight_bytes()
     peak, _ = _peak_hbm()
     rec = {
@@ -428,6 +430,7 @@ def sharded_decode_bench(dev, ws, rank, local, steps: int, warmup: int, batch: i
         "weight_gbs_per_gpu": round(wbytes / ws / (ms * 1e-3) / 1e9, 1),
         "hbm_frac_per_gpu": round(wbytes / ws / (ms * 1e-3) / 1e9 / peak, 4),
         "collectives_per_step": 4 * shape.layers + 1 if ws > 1 else 0,
+        "collective": (collective if ws > 1 else None),
         "cuda_graph": graphed,
         "act_mode": "x16" if act == _native.ACT_X16 else "x8 (tile path for Q4_K)",
     }
@@ -448,7 +451,8 @@ def run_sharded_only(args, ws, rank, local):
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    rec = sharded_decode_bench(dev, ws, rank, local, args.steps, args.warmup, args.batch, args.ctx, args.decode_shape)
+    rec = sharded_decode_bench(dev, ws, rank, local, args.steps, args.warmup, args.batch, args.ctx, args.decode_shape,
+                               args.collective)
     if rank == 0:
         print(json.dumps({"impl": "ours", **rec}), flush=True)
     if ws > 1:
@@ -664,6 +668,7 @@ def main():
     ap.add_argument("--workload", default="gemv", choices=["gemv", "tile", "decode", "sharded"])
     ap.add_argument("--decode-shape", default=None, choices=["llama3_8b", "llama3_70b"])
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--collective", default="peer", choices=["peer", "nccl"])
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--tile-m", type=int, default=None)
     ap.add_argument("--tile-n", type=int, default=None)

@@ -68,6 +68,12 @@ SIGNATURES.update(
         "b200q_attention_decode": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp], _i),
         "b200q_swiglu": ([_vp, _vp, _vp, ctypes.c_longlong, _vp], _i),
         "b200q_unshard_rows": ([_vp, _vp, _i, _i, _i, _vp], _i),
+        "b200q_ipc_alloc": ([ctypes.c_longlong, ctypes.POINTER(ctypes.c_void_p), _vp], _i),
+        "b200q_ipc_open": ([_vp, ctypes.POINTER(ctypes.c_void_p)], _i),
+        "b200q_ipc_close": ([_vp], _i),
+        "b200q_ipc_free": ([_vp], _i),
+        "b200q_allgather_peer": ([_vp, _i, _i, ctypes.POINTER(ctypes.c_void_p), ctypes.c_longlong, ctypes.c_longlong,
+                                  _i, _i, _vp, _i, _vp], _i),
         "b200q_set_act_mode": ([_i], _i),
         "b200q_get_act_mode": ([], _i),
         "b200q_last_error": ([], _i),

@@ -419,6 +419,65 @@ int b200q_unshard_rows(const float* in, float* out, int shards, int rows, int co
     return rc;
 }
 
+// ---- multi-GPU: IPC-shared buffers and the peer all-gather ----------------------
+static_assert(sizeof(cudaIpcMemHandle_t) <= B200Q_IPC_HANDLE_BYTES, "IPC handle size");
+
+int b200q_ipc_alloc(long long bytes, void** dptr, void* handle) {
+    int rc = B200Q_OK;
+    if (bytes <= 0 || !dptr || !handle) rc = B200Q_EINVAL;
+    void* p = nullptr;
+    if (rc == B200Q_OK && cudaMalloc(&p, static_cast<size_t>(bytes)) != cudaSuccess) rc = B200Q_ENOMEM;
+    // zeroed (flags start at 0) before the handle can reach another process
+    if (rc == B200Q_OK && (cudaMemset(p, 0, static_cast<size_t>(bytes)) != cudaSuccess ||
+                           cudaDeviceSynchronize() != cudaSuccess))
+        rc = B200Q_ECUDA;
+    cudaIpcMemHandle_t h;
+    if (rc == B200Q_OK && cudaIpcGetMemHandle(&h, p) != cudaSuccess) rc = B200Q_ECUDA;
+    if (rc == B200Q_OK) {
+        std::memset(handle, 0, B200Q_IPC_HANDLE_BYTES);
+        std::memcpy(handle, &h, sizeof(h));
+        *dptr = p;
+    } else if (p) {
+        cudaFree(p);
+    }
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_ipc_open(const void* handle, void** dptr) {
+    int rc = (!handle || !dptr) ? B200Q_EINVAL : B200Q_OK;
+    if (rc == B200Q_OK) {
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, handle, sizeof(h));
+        if (cudaIpcOpenMemHandle(dptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) rc = B200Q_ECUDA;
+    }
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_ipc_close(void* dptr) {
+    const int rc = !dptr ? B200Q_EINVAL : (cudaIpcCloseMemHandle(dptr) == cudaSuccess ? B200Q_OK : B200Q_ECUDA);
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_ipc_free(void* dptr) {
+    const int rc = !dptr ? B200Q_EINVAL : (cudaFree(dptr) == cudaSuccess ? B200Q_OK : B200Q_ECUDA);
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_allgather_peer(const float* local, int rows, int n_local, void* const* bases, long long data_offset,
+                         long long flags_offset, int rank, int world, void* counters, int slot, void* stream) {
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    if (rc == B200Q_OK)
+        rc = launch_allgather_peer(local, rows, n_local, bases, data_offset, flags_offset, rank, world,
+                                   static_cast<uint32_t*>(counters), slot, dev, static_cast<cudaStream_t>(stream));
+    set_last_error(rc);
+    return rc;
+}
+
 int b200q_dequantize_rows(int qtype, const void* w, const int* rows, int nrows, float* out, int k, int n, void* stream) {
     const int rc = launch_dequant_rows(qtype, w, rows, nrows, out, k, n, true, static_cast<cudaStream_t>(stream));
     set_last_error(rc);

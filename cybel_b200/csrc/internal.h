@@ -83,6 +83,12 @@ int launch_attention(const float* q, const void* kc, const void* vc, float* out,
 int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaStream_t st);
 int launch_unshard_rows(const float* in, float* out, int shards, int rows, int cols, cudaStream_t st);
 
+// Peer-memory all-gather (peer.cu).
+int launch_allgather_peer(const float* local, int rows, int n_local, void* const* bases, long long data_offset,
+                          long long flags_offset, int rank, int world, uint32_t* counters, int slot, Device* dev,
+                          cudaStream_t st);
+int peer_counter_slots();
+
 bool pdl_enabled();
 void set_last_error(int status);
 

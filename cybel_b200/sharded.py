@@ -118,8 +118,9 @@ class ShardedDecode:
         # gathered vectors [B][n]; with B > 1 the all-gather lands in a
         # [G][B][n/G] buffer first and is re-laid out
         if G > 1:
-            self.a, self.o, self.f, self.d = z(B * h), z(B * h), z(B * s.ffn), z(B * h)
-            self.logits = z(B * s.vocab)
+            t = ops.gather_target
+            self.a, self.o, self.f, self.d = t("a", B * h), t("o", B * h), t("f", B * s.ffn), t("d", B * h)
+            self.logits = t("logits", B * s.vocab)
         else:  # one rank: the local vectors are the whole vectors
             self.a, self.o, self.f, self.d, self.logits = self.a_l, self.o_l, self.f_l, self.d_l, self.logits_l
         self.gbuf = z(B * max(s.ffn, s.vocab)) if (B > 1 and G > 1) else None
@@ -160,12 +161,100 @@ class ShardedDecode:
         self._gather(self.logits, self.logits_l, p.local_rows("head"))
 
 
+class _CudaView:
+    """Minimal __cuda_array_interface__ exporter, to view device memory the
+    library allocated as a torch tensor."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+
+
+class _PeerTarget:
+    """A gather slot's receive area [rows][world * n_local] in this rank's
+    IPC-shared buffer, plus the peers' mappings of their own buffers."""
+
+    def __init__(self, slot: int, own: int, bases, data_bytes: int):
+        self.slot, self.own, self.bases, self.flags_offset = slot, own, bases, data_bytes
+
+
+class PeerGather:
+    """One IPC-shared buffer per gather slot on every rank (data + a flag
+    row), opened by all peers; gathers run as b200q_allgather_peer."""
+
+    MAX_SLOTS = 16
+
+    def __init__(self, rank: int, world: int, group=None):
+        import torch
+
+        self.torch, self.rank, self.world, self.group = torch, rank, world, group
+        self.lib = _native.lib()
+        self.targets: list[_PeerTarget] = []
+        self._by_ptr: dict[int, _PeerTarget] = {}
+        self._own: list[int] = []
+        self._opened: list[int] = []
+        self.counters = torch.zeros(self.MAX_SLOTS * 16, dtype=torch.int32, device="cuda")
+
+    def target(self, n_floats: int):
+        """A new gather slot; returns its receive area as a float32 tensor
+        (a view of library-owned memory, valid until close())."""
+        import ctypes
+
+        import torch.distributed as dist
+
+        slot = len(self.targets)
+        if slot >= self.MAX_SLOTS:
+            raise ValueError("too many gather slots")
+        data = (4 * n_floats + 255) // 256 * 256
+        ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
+        _native.check(self.lib.b200q_ipc_alloc(data + 4 * 64, ctypes.byref(ptr), handle), "ipc alloc")
+        self._own.append(ptr.value)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        bases = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                bases.append(ptr.value)
+                continue
+            peer = ctypes.c_void_p()
+            buf = (ctypes.c_ubyte * 64).from_buffer_copy(h)
+            _native.check(self.lib.b200q_ipc_open(buf, ctypes.byref(peer)), "ipc open")
+            self._opened.append(peer.value)
+            bases.append(peer.value)
+        t = _PeerTarget(slot, ptr.value, (ctypes.c_void_p * self.world)(*bases), data)
+        self.targets.append(t)
+        view = self.torch.as_tensor(_CudaView(ptr.value, n_floats), device="cuda")
+        self._by_ptr[view.data_ptr()] = t
+        return view
+
+    def gather(self, full, local, rows: int, n_local: int) -> None:
+        target = self._by_ptr[full.data_ptr()]
+        st = self.torch.cuda.current_stream().cuda_stream
+        _native.check(self.lib.b200q_allgather_peer(local.data_ptr(), rows, n_local, target.bases, 0,
+                                                    target.flags_offset, self.rank, self.world,
+                                                    self.counters.data_ptr(), target.slot, st), "peer all-gather")
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (call on every rank,
+        with no gather in flight)."""
+        import torch.distributed as dist
+
+        self.torch.cuda.synchronize()
+        for p in self._opened:
+            self.lib.b200q_ipc_close(p)
+        dist.barrier(group=self.group)
+        for p in self._own:
+            self.lib.b200q_ipc_free(p)
+        self._opened, self._own = [], []
+
+
 class GpuOps:
     """ShardedDecode arithmetic on one GPU: libb200q kernels on the current
-    stream, all-gathers through torch.distributed (NCCL) on the same stream.
-    With world 1 no collective runs."""
+    stream, all-gathers on the same stream through torch.distributed (NCCL,
+    collective="nccl") or through b200q_allgather_peer over NVLink peer
+    memory (collective="peer"). With world 1 no collective runs."""
 
-    def __init__(self, device: int = 0, act_mode: int = _native.ACT_X16, group=None, world: int = 1):
+    def __init__(self, device: int = 0, act_mode: int = _native.ACT_X16, group=None, world: int = 1,
+                 collective: str = "nccl", rank: int = 0):
         import torch
 
         self.torch = torch
@@ -174,7 +263,15 @@ class GpuOps:
         self.act = act_mode
         self.group = group
         self.world = world
+        self.peer = PeerGather(rank, world, group) if (collective == "peer" and world > 1) else None
         self._keep = []  # ctypes arrays referenced by captured calls
+
+    def gather_target(self, name: str, n: int):
+        return self.peer.target(n) if self.peer else self.zeros(n)
+
+    def close(self) -> None:
+        if self.peer:
+            self.peer.close()
 
     # -- storage -------------------------------------------------------------------
     def zeros(self, n: int):
@@ -249,6 +346,9 @@ class GpuOps:
         self._ok(self.lib.b200q_swiglu(g.data_ptr(), u.data_ptr(), out.data_ptr(), n, self._st()), "swiglu")
 
     def all_gather(self, full, local, gbuf, batch, n_local):
+        if self.peer:
+            self.peer.gather(full, local, batch, n_local)
+            return
         import torch.distributed as dist
 
         n = self.world * batch * n_local

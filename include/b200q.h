@@ -246,6 +246,39 @@ B200Q_API int b200q_swiglu(const float* gate, const float* up, float* out, long 
 B200Q_API int b200q_unshard_rows(const float* in, float* out, int shards, int rows, int cols, void* stream);
 
 /* ---------------------------------------------------------------------
+ * Multi-GPU (one process per GPU of a node): buffers shared through CUDA
+ * IPC and a one-kernel all-gather over NVLink peer memory for the outputs
+ * of row-sharded linears. No reference counterpart (the reference engine
+ * runs on one host and has no collectives).
+ * ------------------------------------------------------------------- */
+
+/* Allocate `bytes` of zeroed device memory shareable with other processes;
+ * *handle (64 bytes, B200Q_IPC_HANDLE_BYTES) is passed to their
+ * b200q_ipc_open. b200q_ipc_close unmaps a peer's buffer, b200q_ipc_free
+ * frees one's own (after every peer has closed it). */
+#define B200Q_IPC_HANDLE_BYTES 64
+B200Q_API int b200q_ipc_alloc(long long bytes, void** dptr, void* handle);
+B200Q_API int b200q_ipc_open(const void* handle, void** dptr);
+B200Q_API int b200q_ipc_close(void* dptr);
+B200Q_API int b200q_ipc_free(void* dptr);
+
+/* All-gather of row-sharded outputs: this rank's rows [rows][n_local] go to
+ * columns [rank * n_local, (rank + 1) * n_local) of every rank's receive area
+ * [rows][world * n_local] at byte offset data_offset of its shared buffer
+ * (bases: host array of the world buffers as mapped here, this rank's own
+ * at index rank); each writer then release-stores a sequence number into
+ * the receiver's flag row (world uint32 at flags_offset) and the call
+ * returns on the device once all ranks' rows have arrived here (bounded
+ * wait: on timeout the device status records it, see b200q_device_status).
+ * counters: zeroed device memory of 16 uint32 per slot, private to this
+ * rank; slot: which gather (its receive area, flags and counters). Every
+ * rank issues the same gathers in the same order, and the consumers of a
+ * slot's data run before the rank's next gather. n_local % 4 == 0. */
+B200Q_API int b200q_allgather_peer(const float* local, int rows, int n_local, void* const* bases,
+                                   long long data_offset, long long flags_offset, int rank, int world,
+                                   void* counters, int slot, void* stream);
+
+/* ---------------------------------------------------------------------
  * Runtime controls.
  * ------------------------------------------------------------------- */
 B200Q_API int b200q_set_act_mode(int act_mode);       /* drop-in mode; returns previous */

@@ -23,6 +23,9 @@ class NumpyOps:
     def zeros(self, n):
         return np.zeros(n)
 
+    def gather_target(self, name, n):
+        return np.zeros(n)
+
     def vector(self, a):
         return np.asarray(a, dtype=np.float64).copy()
 
