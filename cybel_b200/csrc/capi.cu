@@ -407,6 +407,55 @@ int b200q_attention_decode(const float* q, const void* k_cache, const void* v_ca
     return rc;
 }
 
+long long b200q_xq_row_bytes(int k, int act_mode) {
+    if (k <= 0 || k % 32 || (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16)) return B200Q_EINVAL;
+    return xq_bytes_per_row(k, act_mode);
+}
+
+int b200q_add_rmsnorm_q(float* residual, const float* delta, const float* gamma, float* out, void* xq, int act_mode,
+                        int n, int rows, float eps, void* stream) {
+    const int rc = !xq ? B200Q_EINVAL
+                       : launch_add_rmsnorm(residual, delta, gamma, out, n, rows, eps,
+                                            static_cast<cudaStream_t>(stream), xq, act_mode);
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_attention_decode_q(const float* q, const void* k_cache, const void* v_cache, float* out, void* xq,
+                             int act_mode, int batch, int n_heads, int n_kv_heads, int head_dim, int ctx_len,
+                             int max_ctx, void* stream) {
+    Device* dev = nullptr;
+    int rc = !xq ? B200Q_EINVAL : current_device_state(&dev);
+    if (rc == B200Q_OK)
+        rc = launch_attention(q, k_cache, v_cache, out, batch, n_heads, n_kv_heads, head_dim, ctx_len, max_ctx, dev,
+                              static_cast<cudaStream_t>(stream), xq, act_mode);
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_swiglu_q(const float* gate, const float* up, void* xq, int act_mode, int n, void* stream) {
+    int rc = B200Q_OK;
+    if (!gate || !up || !xq || n <= 0 || (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16)) rc = B200Q_EINVAL;
+    else if (reinterpret_cast<uintptr_t>(xq) & 15u) rc = B200Q_EALIGN;
+    else rc = launch_swiglu_quantize(act_mode, gate, up, n, static_cast<uint8_t*>(xq),
+                                     static_cast<cudaStream_t>(stream), pdl_enabled());
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_matmul_xq(int qtype, int act_mode, const void* xq, const void* w, float* y, int m, int k, int n, float alpha,
+                    float beta, int flags, void* stream) {
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    if (rc == B200Q_OK && (reinterpret_cast<uintptr_t>(xq) & 15u)) rc = B200Q_EALIGN;
+    if (rc == B200Q_OK) rc = gemv_check_shape(qtype, act_mode, k, n, dev);
+    if (rc == B200Q_OK)
+        rc = gemv_from_xq(qtype, act_mode, w, static_cast<const uint8_t*>(xq), xq_bytes_per_row(k, act_mode), y, m, k,
+                          n, n, alpha, beta, nullptr, dev, static_cast<cudaStream_t>(stream), pdl_enabled(), flags);
+    set_last_error(rc);
+    return rc;
+}
+
 int b200q_swiglu(const float* gate, const float* up, float* out, long long n, void* stream) {
     const int rc = launch_swiglu(gate, up, out, n, static_cast<cudaStream_t>(stream));
     set_last_error(rc);

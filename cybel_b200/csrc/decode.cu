@@ -22,7 +22,7 @@
 
 #include <algorithm>
 
-#include "common.cuh"
+#include "gemv.cuh"
 #include "internal.h"
 
 namespace b200q {
@@ -34,16 +34,21 @@ constexpr int kAttnChunk = 128;  // cache positions per attention CTA
 constexpr int kHeadDim = 128;    // head_dim the attention kernels are built for
 constexpr int kMaxGroup = 8;     // query heads per kv head
 
-// One CTA per row of `rows` rows of n elements.
+// One CTA per row of `rows` rows of n elements. DIG > 0: the normed row is
+// also quantized (x8 / x16 codes, the GEMV's activation layout) into xq, so
+// the projections that follow read codes directly (out may then be null).
+template <int DIG>
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __restrict__ res,
                                                                    const float* __restrict__ delta,
                                                                    const float* __restrict__ gamma,
-                                                                   float* __restrict__ out, int n, float eps) {
+                                                                   float* __restrict__ out, uint8_t* __restrict__ xq,
+                                                                   int n, float eps) {
     griddep_launch_dependents();
     griddep_wait();
     res += static_cast<long long>(blockIdx.x) * n;
-    out += static_cast<long long>(blockIdx.x) * n;
+    if (out) out += static_cast<long long>(blockIdx.x) * n;
     if (delta) delta += static_cast<long long>(blockIdx.x) * n;
+    if (DIG) xq += static_cast<long long>(blockIdx.x) * xq_row_bytes(n, DIG);
     __shared__ float red[kNormThreads / 32];
     float ss = 0.0f;
     for (int i = 4 * threadIdx.x; i < n; i += 4 * kNormThreads) {
@@ -73,11 +78,22 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
     }
     __syncthreads();
     const float inv_rms = 1.0f / sqrtf(red[0] / static_cast<float>(n) + eps);
-    for (int i = 4 * threadIdx.x; i < n; i += 4 * kNormThreads) {
-        const float4 r = *reinterpret_cast<const float4*>(res + i);
-        const float4 g = *reinterpret_cast<const float4*>(gamma + i);
-        *reinterpret_cast<float4*>(out + i) =
-            make_float4(r.x * inv_rms * g.x, r.y * inv_rms * g.y, r.z * inv_rms * g.z, r.w * inv_rms * g.w);
+    // n % 128 == 0 when quantizing: a warp's 128 elements are all in range or
+    // all out of range in every pass, as quantize_quad needs.
+    const int passes = (n + 4 * kNormThreads - 1) / (4 * kNormThreads);
+    for (int pass = 0; pass < passes; ++pass) {
+        const int i = 4 * threadIdx.x + pass * 4 * kNormThreads;
+        const bool valid = i < n;
+        float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (valid) {
+            const float4 r = *reinterpret_cast<const float4*>(res + i);
+            const float4 g = *reinterpret_cast<const float4*>(gamma + i);
+            o = make_float4(r.x * inv_rms * g.x, r.y * inv_rms * g.y, r.z * inv_rms * g.z, r.w * inv_rms * g.w);
+            if (out) *reinterpret_cast<float4*>(out + i) = o;
+        }
+        if constexpr (DIG > 0) {
+            if (i - 4 * (threadIdx.x & 31) < n) quantize_quad<DIG>(o, valid, xq, n, i >> 2);  // warp-uniform
+        }
     }
 }
 
@@ -201,13 +217,42 @@ __global__ void __launch_bounds__(128) attn_chunk_kernel(const float* __restrict
     }
 }
 
+// Quantize one 32-element group held one element per lane (lane i holds
+// element e = 32 g + i of a row of k) into the quantized row at base: the
+// arithmetic of quantize_group, with amax and the code sum by shuffles.
+template <int DIG>
+__device__ __forceinline__ void quantize_lane_group(float v, uint8_t* base, int k, int e) {
+    constexpr float QMAX = DIG == 1 ? 127.0f : 32767.0f;
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float iscale = amax > 0.0f ? __fdiv_rn(QMAX, amax) : 0.0f;
+    const int c = round_half_even_small(__fmul_rn(v, iscale));
+    int sum = c;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (DIG == 1) {
+        base[e] = static_cast<uint8_t>(c & 0xFF);
+    } else {
+        base[e] = static_cast<uint8_t>((c >> 8) & 0xFF);
+        base[k + e] = static_cast<uint8_t>(c & 0xFF);
+    }
+    if ((e & 31) == 0) {
+        float* gd = reinterpret_cast<float*>(base + static_cast<long long>(k) * DIG);
+        gd[e >> 5] = amax > 0.0f ? __fdiv_rn(amax, QMAX) : 0.0f;
+        reinterpret_cast<int*>(gd + k / 32)[e >> 5] = sum;
+    }
+}
+
+// DIG > 0: the attention output row of each sequence (n_heads * head_dim
+// elements) is also quantized into xq for the o projection (out may be null).
+template <int DIG>
 __global__ void __launch_bounds__(kHeadDim) attn_combine_kernel(const float* __restrict__ part, float* __restrict__ out,
-                                                                int n_chunks) {
+                                                                uint8_t* __restrict__ xq, int n_chunks) {
     griddep_launch_dependents();
     griddep_wait();
     const int h = blockIdx.x, d = threadIdx.x, b = blockIdx.y, n_heads = gridDim.x;
     const float* rec = part + (static_cast<long long>(b) * n_heads + h) * n_chunks * kPartStride;
-    out += static_cast<long long>(b) * n_heads * kHeadDim;
     float M = -INFINITY;
     for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, rec[c * kPartStride + kHeadDim]);
     float L = 0.0f, acc = 0.0f;
@@ -216,7 +261,12 @@ __global__ void __launch_bounds__(kHeadDim) attn_combine_kernel(const float* __r
         L = fmaf(rec[c * kPartStride + kHeadDim + 1], w, L);
         acc = fmaf(rec[c * kPartStride + d], w, acc);
     }
-    out[h * kHeadDim + d] = acc / L;
+    const float v = acc / L;
+    if (out) out[static_cast<long long>(b) * n_heads * kHeadDim + h * kHeadDim + d] = v;
+    if constexpr (DIG > 0) {
+        const int k = n_heads * kHeadDim;
+        quantize_lane_group<DIG>(v, xq + static_cast<long long>(b) * xq_row_bytes(k, DIG), k, h * kHeadDim + d);
+    }
 }
 
 // out = silu(gate) * up, element-wise (the SiLU * up step of
@@ -265,14 +315,21 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 }  // namespace
 
 int launch_add_rmsnorm(float* res, const float* delta, const float* gamma, float* out, int n, int rows, float eps,
-                       cudaStream_t st) {
-    if (!res || !gamma || !out || n <= 0 || rows <= 0) return B200Q_EINVAL;
-    if (n % 4) return B200Q_ESHAPE;
-    if (!aligned16(res) || !aligned16(gamma) || !aligned16(out) || (delta && !aligned16(delta))) return B200Q_EALIGN;
+                       cudaStream_t st, void* xq, int act_mode) {
+    if (!res || !gamma || (!out && !xq) || n <= 0 || rows <= 0) return B200Q_EINVAL;
+    if (n % 4 || (xq && n % 128)) return B200Q_ESHAPE;
+    if (xq && act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
+    if (!aligned16(res) || !aligned16(gamma) || (out && !aligned16(out)) || (delta && !aligned16(delta)) ||
+        (xq && !aligned16(xq)))
+        return B200Q_EALIGN;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(rows), dim3(kNormThreads), st, attr);
-    return cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel, res, delta, gamma, out, n, eps) == cudaSuccess ? B200Q_OK
-                                                                                                    : B200Q_ECUDA;
+    uint8_t* q = static_cast<uint8_t*>(xq);
+    cudaError_t e;
+    if (!xq) e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<0>, res, delta, gamma, out, q, n, eps);
+    else if (act_mode == B200Q_ACT_X8) e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<1>, res, delta, gamma, out, q, n, eps);
+    else e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<2>, res, delta, gamma, out, q, n, eps);
+    return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
 
 int launch_rope_kv(float* q, float* k, const float* v, int batch, int n_heads, int n_kv, int hd, int pos, float theta,
@@ -291,8 +348,11 @@ int launch_rope_kv(float* q, float* k, const float* v, int batch, int n_heads, i
 }
 
 int launch_attention(const float* q, const void* kc, const void* vc, float* out, int batch, int n_heads, int n_kv,
-                     int hd, int ctx, int max_ctx, Device* dev, cudaStream_t st) {
-    if (!q || !kc || !vc || !out || batch <= 0 || n_heads <= 0 || n_kv <= 0 || ctx <= 0 || !dev) return B200Q_EINVAL;
+                     int hd, int ctx, int max_ctx, Device* dev, cudaStream_t st, void* xq, int act_mode) {
+    if (!q || !kc || !vc || (!out && !xq) || batch <= 0 || n_heads <= 0 || n_kv <= 0 || ctx <= 0 || !dev)
+        return B200Q_EINVAL;
+    if (xq && act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
+    if (xq && (reinterpret_cast<uintptr_t>(xq) & 15u)) return B200Q_EALIGN;
     if (hd != kHeadDim || n_heads % n_kv || n_heads / n_kv > kMaxGroup || ctx > max_ctx) return B200Q_ESHAPE;
     if ((reinterpret_cast<uintptr_t>(kc) & 7u) || (reinterpret_cast<uintptr_t>(vc) & 1u)) return B200Q_EALIGN;
     const int n_chunks = (ctx + kAttnChunk - 1) / kAttnChunk;
@@ -307,9 +367,13 @@ int launch_attention(const float* q, const void* kc, const void* vc, float* out,
                            1.0f / sqrtf(static_cast<float>(hd))) != cudaSuccess)
         return B200Q_ECUDA;
     cudaLaunchConfig_t cfg2 = pdl_cfg(dim3(n_heads, batch), dim3(kHeadDim), st, attr);
-    if (cudaLaunchKernelEx(&cfg2, attn_combine_kernel, static_cast<const float*>(part), out, n_chunks) != cudaSuccess)
-        return B200Q_ECUDA;
-    return B200Q_OK;
+    const float* pp = static_cast<const float*>(part);
+    uint8_t* qx = static_cast<uint8_t*>(xq);
+    cudaError_t e;
+    if (!xq) e = cudaLaunchKernelEx(&cfg2, attn_combine_kernel<0>, pp, out, qx, n_chunks);
+    else if (act_mode == B200Q_ACT_X8) e = cudaLaunchKernelEx(&cfg2, attn_combine_kernel<1>, pp, out, qx, n_chunks);
+    else e = cudaLaunchKernelEx(&cfg2, attn_combine_kernel<2>, pp, out, qx, n_chunks);
+    return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
 
 int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaStream_t st) {

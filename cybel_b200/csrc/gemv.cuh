@@ -245,18 +245,14 @@ __global__ void __launch_bounds__(128) quantize_act_kernel(const float* __restri
 // launch latency of this kernel sits between x's producer and the GEMV).
 // Writes exactly what quantize_group writes. blockDim.x must be a multiple
 // of 32.
+// Quantize elements [4 q4, 4 q4 + 4) of a row held by this thread (v) into
+// the quantized row at `base` (row of k elements). The 8 lanes holding one
+// 32-element group must be the aligned lanes 8j .. 8j+7 of the warp, and every
+// lane of the warp must call (valid == false for lanes without data; their
+// v is ignored and nothing is stored).
 template <int DIG>
-__global__ void __launch_bounds__(256) quantize_act_quads_kernel(const float* __restrict__ x, long long x_stride, int m,
-                                                                  int k, uint8_t* __restrict__ xq) {
-    griddep_launch_dependents();
-    griddep_wait();
-    const int quads = k >> 2;
-    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const bool valid = i < static_cast<long long>(m) * quads;  // groups never straddle the end
-    const int row = valid ? static_cast<int>(i / quads) : 0;
-    const int q4 = valid ? static_cast<int>(i - static_cast<long long>(row) * quads) : 0;
-    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (valid) v = __ldg(reinterpret_cast<const float4*>(x + row * x_stride) + q4);
+__device__ __forceinline__ void quantize_quad(float4 v, bool valid, uint8_t* base, int k, int q4) {
+    if (!valid) v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     constexpr float QMAX = DIG == 1 ? 127.0f : 32767.0f;
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
@@ -272,7 +268,6 @@ __global__ void __launch_bounds__(256) quantize_act_quads_kernel(const float* __
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     sum += __shfl_xor_sync(0xffffffffu, sum, 4);
     if (!valid) return;
-    uint8_t* base = xq + row * xq_row_bytes(k, DIG);
     uint32_t h, l = 0;
     if (DIG == 1) {
         h = (static_cast<uint32_t>(c0) & 0xFFu) | ((static_cast<uint32_t>(c1) & 0xFFu) << 8) |
@@ -285,11 +280,26 @@ __global__ void __launch_bounds__(256) quantize_act_quads_kernel(const float* __
     }
     reinterpret_cast<uint32_t*>(base)[q4] = h;
     if (DIG == 2) reinterpret_cast<uint32_t*>(base + k)[q4] = l;
-    if ((threadIdx.x & 7) == 0) {
+    if ((q4 & 7) == 0) {
         float* gd = reinterpret_cast<float*>(base + static_cast<long long>(k) * DIG);
         gd[q4 >> 3] = amax > 0.0f ? __fdiv_rn(amax, QMAX) : 0.0f;
         reinterpret_cast<int*>(gd + k / 32)[q4 >> 3] = sum;
     }
+}
+
+template <int DIG>
+__global__ void __launch_bounds__(256) quantize_act_quads_kernel(const float* __restrict__ x, long long x_stride, int m,
+                                                                  int k, uint8_t* __restrict__ xq) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const int quads = k >> 2;
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const bool valid = i < static_cast<long long>(m) * quads;  // groups never straddle the end
+    const int row = valid ? static_cast<int>(i / quads) : 0;
+    const int q4 = valid ? static_cast<int>(i - static_cast<long long>(row) * quads) : 0;
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (valid) v = __ldg(reinterpret_cast<const float4*>(x + row * x_stride) + q4);
+    quantize_quad<DIG>(v, valid, xq + row * xq_row_bytes(k, DIG), k, q4);
 }
 
 // One lane's run of RUN codes starting at element e (a multiple of 16) of a

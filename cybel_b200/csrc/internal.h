@@ -75,11 +75,12 @@ bool uses_tile_path(int qtype, int act_mode, int m);
 // Decode-step glue (decode.cu).
 constexpr int kScratchAttn = 6;  // attention chunk partials
 int launch_add_rmsnorm(float* res, const float* delta, const float* gamma, float* out, int n, int rows, float eps,
-                       cudaStream_t st);
+                       cudaStream_t st, void* xq = nullptr, int act_mode = 0);
 int launch_rope_kv(float* q, float* k, const float* v, int batch, int n_heads, int n_kv, int hd, int pos, float theta,
                    void* kc, void* vc, int max_ctx, cudaStream_t st);
 int launch_attention(const float* q, const void* kc, const void* vc, float* out, int batch, int n_heads, int n_kv,
-                     int hd, int ctx, int max_ctx, Device* dev, cudaStream_t st);
+                     int hd, int ctx, int max_ctx, Device* dev, cudaStream_t st, void* xq = nullptr,
+                     int act_mode = 0);
 int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaStream_t st);
 int launch_unshard_rows(const float* in, float* out, int shards, int rows, int cols, cudaStream_t st);
 

@@ -7,13 +7,14 @@ cache, the o projection with the residual add, RMSNorm, and the SwiGLU FFN
 with its residual add; then the final norm and the LM head. ``DecodeStack``
 runs that step entirely on the device through libb200q's entry points:
 
-* ``b200q_fused_matvec`` -- q/k/v sharing one quantized activation vector;
-* ``b200q_matmul_ex`` -- the o projection and the LM head;
-* ``b200q_expert_swiglu`` with beta = 1 -- gate/up, SiLU * up, down, and the
-  residual add in the down projection's epilogue;
-* ``b200q_add_rmsnorm`` / ``b200q_rope_kv`` / ``b200q_attention_decode`` --
-  the glue, with the residual add of the o projection fused into the next
-  RMSNorm;
+* ``b200q_add_rmsnorm_q`` -- RMSNorm writing the GEMV's activation codes;
+* ``b200q_matmul_xq`` -- each projection from those codes: q/k/v as one
+  matrix, o with the residual add in its epilogue (beta = 1), gate/up as one
+  matrix, down with the residual add, and the LM head;
+* ``b200q_rope_kv`` / ``b200q_attention_decode_q`` -- RoPE, the KV append and
+  attention, which also writes the o projection's codes;
+* ``b200q_swiglu_q`` -- SiLU(gate) * up, written as the down projection's
+  codes;
 
 all on one stream, so one token's step is one CUDA graph. The KV cache is
 fp16, [layer][kv_head][max_ctx][head_dim].
@@ -21,8 +22,7 @@ fp16, [layer][kv_head][max_ctx][head_dim].
 
 from __future__ import annotations
 
-import ctypes
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import numpy as np
 
@@ -107,21 +107,14 @@ def random_rows(qtype: int, n: int, k: int, rng: np.random.Generator, block_rows
     return np.ascontiguousarray(np.tile(blk, (reps, 1))[:n])
 
 
-def _vp_array(vals):
-    return (ctypes.c_void_p * len(vals))(*vals)
-
-
-def _int_array(vals):
-    return (ctypes.c_int * len(vals))(*vals)
-
-
 @dataclass
 class _Layer:
-    mats: dict[str, DeviceMatrix]
+    wqkv: DeviceMatrix      # q, k and v rows, one after the other
+    wo: DeviceMatrix
+    w_gu: DeviceMatrix      # gate rows, then up rows
+    w_down: DeviceMatrix
     attn_norm: object
     ffn_norm: object
-    qkv_w: object = field(default=None)
-    qkv_y: object = field(default=None)
 
 
 class DecodeStack:
@@ -129,6 +122,11 @@ class DecodeStack:
 
     ``layers`` holds one weight dict per layer (``random_layer`` layout); a
     shorter list is cycled, each layer still getting its own device copy.
+    On the device the q/k/v rows of a layer are stored as one matrix, and so
+    are the gate/up rows, so each is one GEMV; the norms and the attention
+    write the GEMVs' activation codes directly. A layer is ten launches:
+    norm, qkv, rope, attention (2), o (+ residual), norm, gate/up, SwiGLU,
+    down (+ residual).
     """
 
     def __init__(self, shape: StackShape, max_ctx: int, layers: list[dict[str, np.ndarray]], embed: np.ndarray,
@@ -137,42 +135,46 @@ class DecodeStack:
 
         if shape.head_dim != 128:
             raise ValueError("the attention kernels are built for head_dim 128")
+        if act_mode not in (_native.ACT_X8, _native.ACT_X16):
+            raise ValueError("DecodeStack runs the GEMV activation modes (x8 / x16)")
         self.shape = shape
         self.max_ctx = max_ctx
         self.act_mode = act_mode
         self.dev = torch.device("cuda", device)
         self.lib = _native.lib()
         f32 = dict(dtype=torch.float32, device=self.dev)
-        h, kv = shape.hidden, shape.kv_dim
+        h, kv, f, q = shape.hidden, shape.kv_dim, shape.ffn, shape.linear_qtype
         self.layers: list[_Layer] = []
+        first: list[_Layer] = []
         for i in range(shape.layers):
-            src = layers[i % len(layers)]
-            mats = {name: DeviceMatrix(shape.linear_qtype, k, n, src[name])
-                    for name, (n, k) in layer_matrix_shapes(shape).items()}
-            self.layers.append(_Layer(mats, torch.from_numpy(src["attn_norm"]).to(self.dev),
-                                      torch.from_numpy(src["ffn_norm"]).to(self.dev)))
-        self.embed = DeviceMatrix(shape.linear_qtype, h, shape.vocab, embed)
+            if i < len(layers):
+                src = layers[i]
+                lay = _Layer(
+                    DeviceMatrix(q, h, h + 2 * kv, np.concatenate([src["wq"], src["wk"], src["wv"]])),
+                    DeviceMatrix(q, h, h, src["wo"]),
+                    DeviceMatrix(q, h, 2 * f, np.concatenate([src["w_gate"], src["w_up"]])),
+                    DeviceMatrix(q, f, h, src["w_down"]),
+                    torch.from_numpy(src["attn_norm"]).to(self.dev),
+                    torch.from_numpy(src["ffn_norm"]).to(self.dev))
+                first.append(lay)
+            else:  # its own device copy of a cycled layer
+                b = first[i % len(layers)]
+                lay = _Layer(b.wqkv.clone(), b.wo.clone(), b.w_gu.clone(), b.w_down.clone(), b.attn_norm, b.ffn_norm)
+            self.layers.append(lay)
+        self.embed = DeviceMatrix(q, h, shape.vocab, embed)
         self.head = DeviceMatrix(shape.head_qtype, h, shape.vocab, head)
         self.out_norm = torch.from_numpy(out_norm).to(self.dev)
         cache_shape = (shape.layers, shape.kv_heads, max_ctx, shape.head_dim)
         self.k_cache = torch.zeros(cache_shape, dtype=torch.float16, device=self.dev)
         self.v_cache = torch.zeros(cache_shape, dtype=torch.float16, device=self.dev)
-        self.x = torch.zeros(h, **f32)       # residual stream
-        self.hn = torch.zeros(h, **f32)      # normed activations
-        self.q = torch.zeros(h, **f32)
-        self.k = torch.zeros(kv, **f32)
-        self.v = torch.zeros(kv, **f32)
-        self.attn = torch.zeros(h, **f32)
-        self.o = torch.zeros(h, **f32)
+        self.x = torch.zeros(h, **f32)             # residual stream
+        self.qkv = torch.zeros(h + 2 * kv, **f32)  # q | k | v
+        self.gu = torch.zeros(2 * f, **f32)        # gate | up
         self.logits = torch.zeros(shape.vocab, **f32)
         self.token = torch.zeros(1, dtype=torch.int32, device=self.dev)
-        qt3 = _int_array([shape.linear_qtype] * 3)
-        rows3 = _int_array([h, kv, kv])
-        ys = _vp_array([self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr()])
-        for lay in self.layers:
-            lay.qkv_w = _vp_array([lay.mats["wq"].ptr, lay.mats["wk"].ptr, lay.mats["wv"].ptr])
-            lay.qkv_y = ys
-        self._qt3, self._rows3 = qt3, rows3
+        xb = self.lib.b200q_xq_row_bytes
+        self.xq_h = torch.zeros(int(xb(h, act_mode)), dtype=torch.uint8, device=self.dev)  # codes of a hidden vector
+        self.xq_f = torch.zeros(int(xb(f, act_mode)), dtype=torch.uint8, device=self.dev)  # codes of the FFN vector
         torch.cuda.synchronize(self.dev)
 
     # -- one token ----------------------------------------------------------------
@@ -191,38 +193,43 @@ class DecodeStack:
             raise ValueError("position outside the KV cache")
         s, L, st = self.shape, self.lib, torch.cuda.current_stream(self.dev).cuda_stream
         W = _native.WEIGHTS_STATIC
-        act = self.act_mode
-        h, kv, hd = s.hidden, s.kv_dim, s.head_dim
+        act, q = self.act_mode, s.linear_qtype
+        h, kv, hd, f = s.hidden, s.kv_dim, s.head_dim, s.ffn
+        x, xq_h, xq_f = self.x.data_ptr(), self.xq_h.data_ptr(), self.xq_f.data_ptr()
+        qp = self.qkv.data_ptr()
+        kp, vp = qp + 4 * h, qp + 4 * (h + kv)
+        gp = self.gu.data_ptr()
+        up = gp + 4 * f
+        resid = 0.0 if linears_only else 1.0
         if not linears_only:
-            self._check(L.b200q_dequantize_rows(s.linear_qtype, self.embed.ptr, self.token.data_ptr(), 1,
-                                                self.x.data_ptr(), h, s.vocab, st), "embedding")
+            self._check(L.b200q_dequantize_rows(q, self.embed.ptr, self.token.data_ptr(), 1, x, h, s.vocab, st),
+                        "embedding")
         for li, lay in enumerate(self.layers):
             if not linears_only:
-                self._check(L.b200q_add_rmsnorm(self.x.data_ptr(), None, lay.attn_norm.data_ptr(), self.hn.data_ptr(),
-                                                h, 1, s.eps, st), "attn_norm")
-            self._check(L.b200q_fused_matvec(act, self.hn.data_ptr(), h, 3, lay.qkv_w, self._qt3, lay.qkv_y,
-                                             self._rows3, W, st), "qkv")
+                self._check(L.b200q_add_rmsnorm_q(x, None, lay.attn_norm.data_ptr(), None, xq_h, act, h, 1, s.eps,
+                                                  st), "attn_norm")
+            self._check(L.b200q_matmul_xq(q, act, xq_h, lay.wqkv.ptr, qp, 1, h, h + 2 * kv, 1.0, 0.0, W, st), "qkv")
             if not linears_only:
                 kc = self.k_cache[li].data_ptr()
                 vc = self.v_cache[li].data_ptr()
-                self._check(L.b200q_rope_kv(self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), 1, s.heads,
-                                            s.kv_heads, hd, pos, s.rope_theta, kc, vc, self.max_ctx, st), "rope_kv")
-                self._check(L.b200q_attention_decode(self.q.data_ptr(), kc, vc, self.attn.data_ptr(), 1, s.heads,
-                                                     s.kv_heads, hd, pos + 1, self.max_ctx, st), "attention")
-            self._check(L.b200q_matmul_ex(s.linear_qtype, act, self.attn.data_ptr(), lay.mats["wo"].ptr,
-                                          self.o.data_ptr(), 1, h, h, W, st), "o_proj")
+                self._check(L.b200q_rope_kv(qp, kp, vp, 1, s.heads, s.kv_heads, hd, pos, s.rope_theta, kc, vc,
+                                            self.max_ctx, st), "rope_kv")
+                self._check(L.b200q_attention_decode_q(qp, kc, vc, None, xq_h, act, 1, s.heads, s.kv_heads, hd,
+                                                       pos + 1, self.max_ctx, st), "attention")
+            # o projection with the residual add in its epilogue: x = Wo a + x
+            self._check(L.b200q_matmul_xq(q, act, xq_h, lay.wo.ptr, x, 1, h, h, 1.0, resid, W, st), "o_proj")
             if not linears_only:
-                self._check(L.b200q_add_rmsnorm(self.x.data_ptr(), self.o.data_ptr(), lay.ffn_norm.data_ptr(),
-                                                self.hn.data_ptr(), h, 1, s.eps, st), "ffn_norm")
-            self._check(L.b200q_expert_swiglu(act, self.hn.data_ptr(), h, lay.mats["w_gate"].ptr, s.linear_qtype,
-                                              s.ffn, lay.mats["w_up"].ptr, s.linear_qtype, lay.mats["w_down"].ptr,
-                                              s.linear_qtype, h, self.x.data_ptr(), 1.0, 1.0 if not linears_only
-                                              else 0.0, W, st), "ffn")
+                self._check(L.b200q_add_rmsnorm_q(x, None, lay.ffn_norm.data_ptr(), None, xq_h, act, h, 1, s.eps,
+                                                  st), "ffn_norm")
+            self._check(L.b200q_matmul_xq(q, act, xq_h, lay.w_gu.ptr, gp, 1, h, 2 * f, 1.0, 0.0, W, st), "gate_up")
+            if not linears_only:
+                self._check(L.b200q_swiglu_q(gp, up, xq_f, act, f, st), "swiglu")
+            self._check(L.b200q_matmul_xq(q, act, xq_f, lay.w_down.ptr, x, 1, f, h, 1.0, resid, W, st), "down")
         if not linears_only:
-            self._check(L.b200q_add_rmsnorm(self.x.data_ptr(), None, self.out_norm.data_ptr(), self.hn.data_ptr(), h,
-                                            1, s.eps, st), "out_norm")
-        self._check(L.b200q_matmul_ex(s.head_qtype, act, self.hn.data_ptr(), self.head.ptr, self.logits.data_ptr(), 1,
-                                      h, s.vocab, W, st), "lm_head")
+            self._check(L.b200q_add_rmsnorm_q(x, None, self.out_norm.data_ptr(), None, xq_h, act, h, 1, s.eps, st),
+                        "out_norm")
+        self._check(L.b200q_matmul_xq(s.head_qtype, act, xq_h, self.head.ptr, self.logits.data_ptr(), 1, h, s.vocab,
+                                      1.0, 0.0, W, st), "lm_head")
 
     def set_token(self, token: int) -> None:
         self.token.fill_(int(token))

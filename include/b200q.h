@@ -241,6 +241,26 @@ B200Q_API int b200q_attention_decode(const float* q, const void* k_cache, const 
  * QM:2380-2412, for FFNs whose gate/up and down run on different GPUs). */
 B200Q_API int b200q_swiglu(const float* gate, const float* up, float* out, long long n, void* stream);
 
+/* Quantized-activation variants: the same steps also writing their output
+ * rows as the GEMV's activation codes (act_mode B200Q_ACT_X8 / X16, row pitch
+ * b200q_xq_row_bytes(n, act_mode), 16-byte aligned), so the projection that
+ * follows starts from codes (b200q_matmul_xq) instead of quantizing first.
+ * The fp32 output pointer may be NULL. add_rmsnorm_q needs n % 128 == 0;
+ * swiglu_q quantizes one row of n. */
+B200Q_API long long b200q_xq_row_bytes(int k, int act_mode);
+B200Q_API int b200q_add_rmsnorm_q(float* residual, const float* delta, const float* gamma, float* out, void* xq,
+                                  int act_mode, int n, int rows, float eps, void* stream);
+B200Q_API int b200q_attention_decode_q(const float* q, const void* k_cache, const void* v_cache, float* out, void* xq,
+                                       int act_mode, int batch, int n_heads, int n_kv_heads, int head_dim, int ctx_len,
+                                       int max_ctx, void* stream);
+B200Q_API int b200q_swiglu_q(const float* gate, const float* up, void* xq, int act_mode, int n, void* stream);
+
+/* y = alpha * (W x) + beta * y for m activation rows given as codes written
+ * by the *_q steps above (row pitch b200q_xq_row_bytes(k, act_mode)); y rows
+ * of n floats. The computation of b200q_matmul_ex without its quantizer. */
+B200Q_API int b200q_matmul_xq(int qtype, int act_mode, const void* xq, const void* w, float* y, int m, int k, int n,
+                              float alpha, float beta, int flags, void* stream);
+
 /* out[r][s * cols + j] = in[s][r][j]: rows of a row-sharded output from the
  * all-gather of per-shard [rows][cols] blocks (identity for rows == 1). */
 B200Q_API int b200q_unshard_rows(const float* in, float* out, int shards, int rows, int cols, void* stream);

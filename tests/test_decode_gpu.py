@@ -192,3 +192,67 @@ def torch_tokens(vals):
     import torch
 
     return torch.tensor(vals, dtype=torch.int32)
+
+
+def _parse_xq(raw: np.ndarray, k: int, digits: int):
+    """hi codes, lo codes (x16), group scales and group sums of a quantized row."""
+    hi = raw[:k].view(np.int8)
+    lo = raw[k:2 * k] if digits == 2 else None
+    off = k * digits
+    d = raw[off:off + 4 * (k // 32)].view(np.float32)
+    s = raw[off + 4 * (k // 32):off + 8 * (k // 32)].view(np.int32)
+    return hi, lo, d, s
+
+
+def _check_codes(raw, x, digits):
+    from oracle import oracle as O
+
+    k = x.shape[0]
+    hi, lo, d, s = _parse_xq(raw, k, digits)
+    rh, rl, rd, rs = O.quantize_act(x, digits)
+    assert np.array_equal(hi, rh) and np.array_equal(d, rd) and np.array_equal(s, rs)
+    if digits == 2:
+        assert np.array_equal(lo, rl)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("digits", [1, 2])
+def test_quantized_outputs_of_norm_attention_swiglu(digits):
+    """The *_q glue writes exactly the codes the activation quantizer would
+    write for its fp32 output (the oracle's orc_quantize_act, bit for bit)."""
+    import torch
+    from cybel_b200 import _native
+
+    L = _native.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    rng = np.random.default_rng(digits)
+    n = 4096
+    rb = int(L.b200q_xq_row_bytes(n, digits))
+    res = torch.from_numpy(rng.standard_normal(n).astype(np.float32)).cuda()
+    gam = torch.from_numpy((1 + 0.1 * rng.standard_normal(n)).astype(np.float32)).cuda()
+    out = torch.empty(n, device="cuda")
+    xq = torch.zeros(rb, dtype=torch.uint8, device="cuda")
+    assert L.b200q_add_rmsnorm_q(res.data_ptr(), None, gam.data_ptr(), out.data_ptr(), xq.data_ptr(), digits, n, 1,
+                                 1e-5, st) == 0
+    torch.cuda.synchronize()
+    _check_codes(xq.cpu().numpy(), out.cpu().numpy(), digits)
+
+    H, KV, hd, ctx, max_ctx = 32, 8, 128, 300, 320
+    q = torch.from_numpy(rng.standard_normal(H * hd).astype(np.float32)).cuda()
+    kc = torch.from_numpy(rng.standard_normal((KV, max_ctx, hd)).astype(np.float16)).cuda()
+    vc = torch.from_numpy(rng.standard_normal((KV, max_ctx, hd)).astype(np.float16)).cuda()
+    att = torch.empty(H * hd, device="cuda")
+    assert L.b200q_attention_decode_q(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), att.data_ptr(), xq.data_ptr(),
+                                      digits, 1, H, KV, hd, ctx, max_ctx, st) == 0
+    torch.cuda.synchronize()
+    _check_codes(xq.cpu().numpy(), att.cpu().numpy(), digits)
+
+    f = 14336
+    g = torch.from_numpy(rng.standard_normal(f).astype(np.float32)).cuda()
+    u = torch.from_numpy(rng.standard_normal(f).astype(np.float32)).cuda()
+    hf = torch.empty(f, device="cuda")
+    xqf = torch.zeros(int(L.b200q_xq_row_bytes(f, digits)), dtype=torch.uint8, device="cuda")
+    assert L.b200q_swiglu(g.data_ptr(), u.data_ptr(), hf.data_ptr(), f, st) == 0
+    assert L.b200q_swiglu_q(g.data_ptr(), u.data_ptr(), xqf.data_ptr(), digits, f, st) == 0
+    torch.cuda.synchronize()
+    _check_codes(xqf.cpu().numpy(), hf.cpu().numpy(), digits)
