@@ -30,7 +30,8 @@ namespace b200q {
 namespace {
 
 constexpr int kNormThreads = 1024;
-constexpr int kAttnChunk = 128;  // cache positions per attention CTA
+constexpr int kAttnChunk = 64;   // cache positions per attention CTA
+constexpr int kAttnWarps = 8;    // warps per attention CTA
 constexpr int kHeadDim = 128;    // head_dim the attention kernels are built for
 constexpr int kMaxGroup = 8;     // query heads per kv head
 
@@ -137,14 +138,25 @@ __global__ void rope_kv_kernel(float* __restrict__ q, float* __restrict__ k, con
 // Partial record per (query head, chunk): o[kHeadDim], m, l.
 constexpr int kPartStride = kHeadDim + 2;
 
-__global__ void __launch_bounds__(128) attn_chunk_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
-                                                         const __half* __restrict__ vc, float* __restrict__ part,
-                                                         int n_heads, int n_kv, int ctx, int max_ctx, float scale) {
+// One CTA per (kv head, kAttnChunk positions, sequence), kAttnWarps warps.
+// Scores: warp w takes positions w, w + kAttnWarps, ...; a lane holds 4 of
+// the 128 dims of the K row (one 8-byte load) and the G query heads' dot
+// products are reduced across the warp. Exp-weighted V: the same position
+// split, each lane accumulating its 4 dims for the G heads in registers,
+// then a reduction over the warps through shared memory. All loads of a
+// warp's positions are issued before their arithmetic.
+__global__ void __launch_bounds__(kAttnWarps * 32) attn_chunk_kernel(const float* __restrict__ q,
+                                                                     const __half* __restrict__ kc,
+                                                                     const __half* __restrict__ vc,
+                                                                     float* __restrict__ part, int n_heads, int n_kv,
+                                                                     int ctx, int max_ctx, float scale) {
     griddep_launch_dependents();
     griddep_wait();
+    constexpr int PW = kAttnChunk / kAttnWarps;  // positions per warp
     __shared__ float qs[kMaxGroup][kHeadDim];
     __shared__ float sc[kMaxGroup][kAttnChunk];
     __shared__ float ml[kMaxGroup][2];
+    __shared__ float red[kAttnWarps][kMaxGroup * kHeadDim];
     const int kvh = blockIdx.x, c = blockIdx.y, n_chunks = gridDim.y, b = blockIdx.z;
     const int G = n_heads / n_kv;
     q += static_cast<long long>(b) * n_heads * kHeadDim;
@@ -157,23 +169,31 @@ __global__ void __launch_bounds__(128) attn_chunk_kernel(const float* __restrict
     for (int i = threadIdx.x; i < G * kHeadDim; i += blockDim.x)
         qs[i / kHeadDim][i % kHeadDim] = q[(kvh * G) * kHeadDim + i] * scale;
     __syncthreads();
-    // Scores: warp w takes positions w, w+4, ...; lane covers 4 dims.
-    const __half* kbase = kc + (static_cast<long long>(kvh) * max_ctx + p0) * kHeadDim + 4 * lane;
-    for (int p = warp; p < np; p += 4) {
-        const uint2 raw = *reinterpret_cast<const uint2*>(kbase + static_cast<long long>(p) * kHeadDim);
-        const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-        const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-        for (int g = 0; g < G; ++g) {
-            const float* qg = qs[g] + 4 * lane;
-            float d = qg[0] * k01.x + qg[1] * k01.y + qg[2] * k23.x + qg[3] * k23.y;
+    const long long row0 = static_cast<long long>(kvh) * max_ctx + p0;
+    {
+        uint2 kr[PW];
 #pragma unroll
-            for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-            if (lane == 0) sc[g][p] = d;
+        for (int j = 0; j < PW; ++j) {
+            const int p = warp + j * kAttnWarps;
+            kr[j] = p < np ? *reinterpret_cast<const uint2*>(kc + (row0 + p) * kHeadDim + 4 * lane) : make_uint2(0u, 0u);
+        }
+#pragma unroll
+        for (int j = 0; j < PW; ++j) {
+            const int p = warp + j * kAttnWarps;
+            const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&kr[j].x));
+            const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&kr[j].y));
+            for (int g = 0; g < G; ++g) {
+                const float* qg = qs[g] + 4 * lane;
+                float d = qg[0] * k01.x + qg[1] * k01.y + qg[2] * k23.x + qg[3] * k23.y;
+#pragma unroll
+                for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                if (lane == 0 && p < np) sc[g][p] = d;
+            }
         }
     }
     __syncthreads();
-    // Chunk max and exp-sum per query head (warp w takes heads w, w+4).
-    for (int g = warp; g < G; g += 4) {
+    // Chunk max and exp-sum per query head (warp w takes heads w, w + kAttnWarps).
+    for (int g = warp; g < G; g += kAttnWarps) {
         float m = -INFINITY;
         for (int p = lane; p < np; p += 32) m = fmaxf(m, sc[g][p]);
 #pragma unroll
@@ -192,27 +212,52 @@ __global__ void __launch_bounds__(128) attn_chunk_kernel(const float* __restrict
         }
     }
     __syncthreads();
-    // o[g][d] = sum_p e[g][p] * V[p][d]; thread d.
-    const int d = threadIdx.x;
-    float o[kMaxGroup];
+    // Exp-weighted V over this warp's positions; lane = 4 dims.
+    float acc[kMaxGroup][4];
 #pragma unroll
-    for (int g = 0; g < kMaxGroup; ++g) o[g] = 0.0f;
-    const __half* vbase = vc + (static_cast<long long>(kvh) * max_ctx + p0) * kHeadDim + d;
-    for (int p = 0; p < np; ++p) {
-        const float vv = __half2float(vbase[static_cast<long long>(p) * kHeadDim]);
+    for (int g = 0; g < kMaxGroup; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0f;
+    {
+        uint2 vr[PW];
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; ++g)
-            if (g < G) o[g] = fmaf(sc[g][p], vv, o[g]);
+        for (int j = 0; j < PW; ++j) {
+            const int p = warp + j * kAttnWarps;
+            vr[j] = p < np ? *reinterpret_cast<const uint2*>(vc + (row0 + p) * kHeadDim + 4 * lane) : make_uint2(0u, 0u);
+        }
+#pragma unroll
+        for (int j = 0; j < PW; ++j) {
+            const int p = warp + j * kAttnWarps;
+            if (p >= np) break;
+            const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vr[j].x));
+            const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vr[j].y));
+#pragma unroll
+            for (int g = 0; g < kMaxGroup; ++g) {
+                if (g < G) {
+                    const float e = sc[g][p];
+                    acc[g][0] = fmaf(e, v01.x, acc[g][0]);
+                    acc[g][1] = fmaf(e, v01.y, acc[g][1]);
+                    acc[g][2] = fmaf(e, v23.x, acc[g][2]);
+                    acc[g][3] = fmaf(e, v23.y, acc[g][3]);
+                }
+            }
+        }
     }
 #pragma unroll
     for (int g = 0; g < kMaxGroup; ++g) {
-        if (g < G) {
-            float* rec = part + (static_cast<long long>(kvh * G + g) * n_chunks + c) * kPartStride;
-            rec[d] = o[g];
-            if (d == 0) {
-                rec[kHeadDim] = ml[g][0];
-                rec[kHeadDim + 1] = ml[g][1];
-            }
+        if (g < G)
+            *reinterpret_cast<float4*>(&red[warp][g * kHeadDim + 4 * lane]) =
+                make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * kHeadDim; i += blockDim.x) {
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) o += red[w][i];
+        const int g = i / kHeadDim, d = i - g * kHeadDim;
+        float* rec = part + (static_cast<long long>(kvh * G + g) * n_chunks + c) * kPartStride;
+        rec[d] = o;
+        if (d == 0) {
+            rec[kHeadDim] = ml[g][0];
+            rec[kHeadDim + 1] = ml[g][1];
         }
     }
 }
@@ -251,15 +296,35 @@ __global__ void __launch_bounds__(kHeadDim) attn_combine_kernel(const float* __r
                                                                 uint8_t* __restrict__ xq, int n_chunks) {
     griddep_launch_dependents();
     griddep_wait();
+    __shared__ float wsh[kHeadDim];  // chunk weights exp(m_c - M), one tile of chunks
+    __shared__ float lsh[kHeadDim];  // l_c * weight
+    __shared__ float msh[kHeadDim / 32];
     const int h = blockIdx.x, d = threadIdx.x, b = blockIdx.y, n_heads = gridDim.x;
     const float* rec = part + (static_cast<long long>(b) * n_heads + h) * n_chunks * kPartStride;
-    float M = -INFINITY;
-    for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, rec[c * kPartStride + kHeadDim]);
+    float m = -INFINITY;
+    for (int c = d; c < n_chunks; c += kHeadDim) m = fmaxf(m, rec[c * kPartStride + kHeadDim]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((d & 31) == 0) msh[d >> 5] = m;
+    __syncthreads();
+    float M = msh[0];
+#pragma unroll
+    for (int w = 1; w < kHeadDim / 32; ++w) M = fmaxf(M, msh[w]);
     float L = 0.0f, acc = 0.0f;
-    for (int c = 0; c < n_chunks; ++c) {
-        const float w = expf(rec[c * kPartStride + kHeadDim] - M);
-        L = fmaf(rec[c * kPartStride + kHeadDim + 1], w, L);
-        acc = fmaf(rec[c * kPartStride + d], w, acc);
+    for (int c0 = 0; c0 < n_chunks; c0 += kHeadDim) {
+        const int nt = min(kHeadDim, n_chunks - c0);
+        __syncthreads();
+        if (d < nt) {
+            const float w = expf(rec[(c0 + d) * kPartStride + kHeadDim] - M);
+            wsh[d] = w;
+            lsh[d] = rec[(c0 + d) * kPartStride + kHeadDim + 1] * w;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int t = 0; t < nt; ++t) {
+            acc = fmaf(rec[(c0 + t) * kPartStride + d], wsh[t], acc);
+            L += lsh[t];
+        }
     }
     const float v = acc / L;
     if (out) out[static_cast<long long>(b) * n_heads * kHeadDim + h * kHeadDim + d] = v;
@@ -361,7 +426,7 @@ int launch_attention(const float* q, const void* kc, const void* vc, float* out,
                          static_cast<size_t>(batch) * n_heads * n_chunks * kPartStride * sizeof(float), &part);
     if (rc != B200Q_OK) return rc;
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = pdl_cfg(dim3(n_kv, n_chunks, batch), dim3(128), st, attr);
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(n_kv, n_chunks, batch), dim3(kAttnWarps * 32), st, attr);
     if (cudaLaunchKernelEx(&cfg, attn_chunk_kernel, q, static_cast<const __half*>(kc), static_cast<const __half*>(vc),
                            static_cast<float*>(part), n_heads, n_kv, ctx, max_ctx,
                            1.0f / sqrtf(static_cast<float>(hd))) != cudaSuccess)

@@ -147,18 +147,22 @@ __global__ void dequant_rows_kernel(int qtype, const uint8_t* __restrict__ w, co
 // down projection (the SiLU(gate) * up step of quantized_matmul.cpp:2380-2412).
 // ---------------------------------------------------------------------------
 template <int DIG>
-__global__ void __launch_bounds__(128) swiglu_quantize_kernel(const float* __restrict__ g, const float* __restrict__ u,
+__global__ void __launch_bounds__(256) swiglu_quantize_kernel(const float* __restrict__ g, const float* __restrict__ u,
                                                               int hidden, uint8_t* __restrict__ xq) {
     griddep_launch_dependents();
     griddep_wait();
-    const int grp = blockIdx.x * blockDim.x + threadIdx.x;
-    if (grp >= hidden / 32) return;
-    float gv[32], uv[32], v[32];
-    load_group(g + grp * 32, gv);
-    load_group(u + grp * 32, uv);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = gv[i] / (1.0f + expf(-gv[i])) * uv[i];
-    quantize_group<DIG>(v, xq, hidden, grp);
+    // four elements per thread; the 8 threads of a 32-element group quantize
+    // it together (quantize_quad); hidden % 32 == 0 keeps groups whole
+    const int q4 = blockIdx.x * blockDim.x + threadIdx.x;
+    const bool valid = q4 < hidden / 4;
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (valid) {
+        const float4 gv = __ldg(reinterpret_cast<const float4*>(g) + q4);
+        const float4 uv = __ldg(reinterpret_cast<const float4*>(u) + q4);
+        v = make_float4(gv.x / (1.0f + expf(-gv.x)) * uv.x, gv.y / (1.0f + expf(-gv.y)) * uv.y,
+                        gv.z / (1.0f + expf(-gv.z)) * uv.z, gv.w / (1.0f + expf(-gv.w)) * uv.w);
+    }
+    quantize_quad<DIG>(v, valid, xq, hidden, q4);
 }
 
 cudaLaunchConfig_t make_cfg(unsigned grid, unsigned block, cudaStream_t st, bool pdl, cudaLaunchAttribute* attr) {
@@ -212,7 +216,8 @@ int launch_swiglu_quantize(int act_mode, const float* g, const float* u, int hid
                            bool pdl) {
     if (hidden % 32) return B200Q_ESHAPE;
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(static_cast<unsigned>((hidden / 32 + 127) / 128), 128, st, pdl, attr);
+    if ((reinterpret_cast<uintptr_t>(g) & 15u) || (reinterpret_cast<uintptr_t>(u) & 15u)) return B200Q_EALIGN;
+    cudaLaunchConfig_t cfg = make_cfg(static_cast<unsigned>((hidden / 4 + 255) / 256), 256, st, pdl, attr);
     const cudaError_t e = act_mode == B200Q_ACT_X8 ? cudaLaunchKernelEx(&cfg, swiglu_quantize_kernel<1>, g, u, hidden, xq)
                                                    : cudaLaunchKernelEx(&cfg, swiglu_quantize_kernel<2>, g, u, hidden, xq);
     return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
