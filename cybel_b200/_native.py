@@ -78,7 +78,8 @@ SIGNATURES.update(
         "b200q_ipc_close": ([_vp], _i),
         "b200q_ipc_free": ([_vp], _i),
         "b200q_allgather_peer": ([_vp, _i, _i, ctypes.POINTER(ctypes.c_void_p), ctypes.c_longlong, ctypes.c_longlong,
-                                  _i, _i, _vp, _i, _vp], _i),
+                                  _i, _i, _vp, _i, _vp, _i, _vp], _i),
+        "b200q_quantize_rows": ([_i, _vp, _i, _i, _vp, _vp], _i),
         "b200q_set_act_mode": ([_i], _i),
         "b200q_get_act_mode": ([], _i),
         "b200q_last_error": ([], _i),

@@ -517,12 +517,23 @@ int b200q_ipc_free(void* dptr) {
 }
 
 int b200q_allgather_peer(const float* local, int rows, int n_local, void* const* bases, long long data_offset,
-                         long long flags_offset, int rank, int world, void* counters, int slot, void* stream) {
+                         long long flags_offset, int rank, int world, void* counters, int slot, void* xq, int act_mode,
+                         void* stream) {
     Device* dev = nullptr;
     int rc = current_device_state(&dev);
     if (rc == B200Q_OK)
         rc = launch_allgather_peer(local, rows, n_local, bases, data_offset, flags_offset, rank, world,
-                                   static_cast<uint32_t*>(counters), slot, dev, static_cast<cudaStream_t>(stream));
+                                   static_cast<uint32_t*>(counters), slot, dev, static_cast<cudaStream_t>(stream), xq,
+                                   act_mode);
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_quantize_rows(int act_mode, const float* x, int rows, int k, void* xq, void* stream) {
+    int rc = (!x || !xq || rows <= 0 || k <= 0) ? B200Q_EINVAL : B200Q_OK;
+    if (rc == B200Q_OK && (reinterpret_cast<uintptr_t>(xq) & 15u)) rc = B200Q_EALIGN;
+    if (rc == B200Q_OK) rc = launch_quantize_rows(act_mode, x, rows, k, static_cast<uint8_t*>(xq),
+                                                  static_cast<cudaStream_t>(stream), pdl_enabled());
     set_last_error(rc);
     return rc;
 }

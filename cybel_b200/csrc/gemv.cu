@@ -224,6 +224,15 @@ cudaError_t launch_quantize(const float* x, long long x_stride, int m, int k, ui
 
 }  // namespace
 
+int launch_quantize_rows(int act_mode, const float* x, int rows, int k, uint8_t* xq, cudaStream_t st, bool pdl) {
+    if (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(x) & 15u)) return B200Q_EALIGN;
+    if (k % 32) return B200Q_ESHAPE;
+    const cudaError_t e = act_mode == B200Q_ACT_X8 ? launch_quantize<1>(x, k, rows, k, xq, st, pdl)
+                                                   : launch_quantize<2>(x, k, rows, k, xq, st, pdl);
+    return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
+}
+
 int quantize_activations(int act_mode, const float* x, long long x_stride, int m, int k, Device* dev, cudaStream_t st,
                          bool pdl, int slot, const uint8_t** xq_out, long long* xq_row_out) {
     if (!x || m <= 0 || k <= 0 || !dev) return B200Q_EINVAL;

@@ -45,6 +45,8 @@ int gemv_from_xq(int qtype, int act_mode, const void* w, const uint8_t* xq, long
                  int n, long long y_stride, float alpha, float beta, int32_t* isums, Device* dev, cudaStream_t st,
                  bool pdl, int flags);
 int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev);
+// quantize_act kernel over `rows` contiguous rows of k into xq (row pitch xq_bytes_per_row).
+int launch_quantize_rows(int act_mode, const float* x, int rows, int k, uint8_t* xq, cudaStream_t st, bool pdl);
 int scratch_for(Device* dev, cudaStream_t st, int slot, size_t bytes, void** out);
 long long xq_bytes_per_row(int k, int act_mode);
 
@@ -87,7 +89,7 @@ int launch_unshard_rows(const float* in, float* out, int shards, int rows, int c
 // Peer-memory all-gather (peer.cu).
 int launch_allgather_peer(const float* local, int rows, int n_local, void* const* bases, long long data_offset,
                           long long flags_offset, int rank, int world, uint32_t* counters, int slot, Device* dev,
-                          cudaStream_t st);
+                          cudaStream_t st, void* xq = nullptr, int act_mode = 0);
 int peer_counter_slots();
 
 bool pdl_enabled();

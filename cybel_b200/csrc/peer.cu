@@ -12,13 +12,16 @@
 //    that rank's flag [slot][rank];
 //  * block 0 then waits until every other rank's flag for this slot has
 //    reached the sequence number (acquire loads, bounded by a %globaltimer
-//    limit; on timeout it records STATUS_TIMEOUT and returns).
+//    limit; on timeout it records STATUS_TIMEOUT and returns);
+//  * optionally every block waits and then quantizes a share of the gathered
+//    rows into the GEMV's activation codes, so the projection that consumes
+//    the gathered vector needs no quantizer launch of its own.
 // Sequence numbers live in a per-(slot, block) device counter each block
 // increments itself, so a CUDA graph replays them correctly. A slot's
 // receive area may be reused by the next gather on that slot once its
 // consumers have run: a rank can only write into a peer for the next use of
 // a slot after the peer has contributed to every gather in between.
-#include "common.cuh"
+#include "gemv.cuh"
 #include "internal.h"
 
 namespace b200q {
@@ -42,8 +45,10 @@ struct PeerArgs {
     long long data_offset;      // bytes: the slot's receive area in every buffer
     long long flags_offset;     // bytes: the slot's flag row in every buffer
     int rank, world, rows, n_local, slot;
+    uint8_t* xq;                // optional: gathered rows quantized here (GEMV activation codes)
 };
 
+template <int DIG>
 __global__ void __launch_bounds__(kPeerThreads) allgather_peer_kernel(const float* __restrict__ local,
                                                                       uint32_t* __restrict__ counters,
                                                                       volatile int* status, const PeerArgs a) {
@@ -72,8 +77,9 @@ __global__ void __launch_bounds__(kPeerThreads) allgather_peer_kernel(const floa
         __threadfence_system();
         st_release_sys(reinterpret_cast<uint32_t*>(a.bases[dest] + a.flags_offset) + a.rank, seq);
     }
-    if (p != 0) return;
-    // Block 0: wait for every other rank's rows of this slot.
+    if (DIG == 0 && p != 0) return;
+    // Wait for every other rank's rows of this slot (block 0 only, unless
+    // every block then quantizes a share of the gathered rows).
     if (threadIdx.x < a.world && threadIdx.x != a.rank) {
         const uint32_t* f = reinterpret_cast<const uint32_t*>(a.bases[a.rank] + a.flags_offset) + threadIdx.x;
         const uint64_t t0 = global_timer_ns();
@@ -86,14 +92,33 @@ __global__ void __launch_bounds__(kPeerThreads) allgather_peer_kernel(const floa
         }
     }
     __syncthreads();
+    if constexpr (DIG > 0) {
+        // Quantize the gathered [rows][k] into the GEMV's activation layout,
+        // four elements per thread over all blocks (k % 128 == 0, so a warp's
+        // quads are all in range or all out).
+        const int k = a.world * a.n_local;
+        const int quads = k / 4;
+        const float* full = reinterpret_cast<const float*>(a.bases[a.rank] + a.data_offset);
+        const int total = a.rows * quads;
+        for (int i = p * blockDim.x + threadIdx.x; i - static_cast<int>(threadIdx.x & 31) < total;
+             i += gridDim.x * blockDim.x) {
+            const bool valid = i < total;
+            const int r = valid ? i / quads : 0, q4 = valid ? i - r * quads : 0;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (valid) v = *reinterpret_cast<const float4*>(full + static_cast<long long>(r) * k + 4 * q4);
+            quantize_quad<DIG>(v, valid, a.xq + static_cast<long long>(r) * xq_row_bytes(k, DIG), k, q4);
+        }
+    }
 }
 
 }  // namespace
 
 int launch_allgather_peer(const float* local, int rows, int n_local, void* const* bases, long long data_offset,
                           long long flags_offset, int rank, int world, uint32_t* counters, int slot, Device* dev,
-                          cudaStream_t st) {
+                          cudaStream_t st, void* xq, int act_mode) {
     if (!local || !bases || !counters || !dev || rows <= 0 || n_local <= 0 || slot < 0) return B200Q_EINVAL;
+    if (xq && act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
+    if (xq && ((world * n_local) % 128 || (reinterpret_cast<uintptr_t>(xq) & 15u))) return B200Q_ESHAPE;
     if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world) return B200Q_EINVAL;
     if (n_local % 4 || (reinterpret_cast<uintptr_t>(local) & 15u) || (data_offset & 15) || (flags_offset & 3))
         return B200Q_EALIGN;
@@ -109,6 +134,7 @@ int launch_allgather_peer(const float* local, int rows, int n_local, void* const
     a.rows = rows;
     a.n_local = n_local;
     a.slot = slot;
+    a.xq = static_cast<uint8_t*>(xq);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(world);
     cfg.blockDim = dim3(kPeerThreads);
@@ -120,9 +146,11 @@ int launch_allgather_peer(const float* local, int rows, int n_local, void* const
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    return cudaLaunchKernelEx(&cfg, allgather_peer_kernel, local, counters, dev->status, a) == cudaSuccess
-               ? B200Q_OK
-               : B200Q_ECUDA;
+    cudaError_t e;
+    if (!xq) e = cudaLaunchKernelEx(&cfg, allgather_peer_kernel<0>, local, counters, dev->status, a);
+    else if (act_mode == B200Q_ACT_X8) e = cudaLaunchKernelEx(&cfg, allgather_peer_kernel<1>, local, counters, dev->status, a);
+    else e = cudaLaunchKernelEx(&cfg, allgather_peer_kernel<2>, local, counters, dev->status, a);
+    return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
 
 int peer_counter_slots() { return kMaxWorld; }

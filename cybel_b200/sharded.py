@@ -81,6 +81,10 @@ class ShardedDecode:
     layers: this rank's shards (``shard_layer``) of one weight dict per layer;
     a shorter list is cycled (each layer still gets its own copy); embed: the
     full packed embedding (replicated); head: this rank's rows of the LM head.
+    With batch 1 a layer's local q/k/v rows are one matrix and its local
+    gate/up rows another (one GEMV each). Norms write the GEMVs' activation
+    codes, and the gathers of the attention output and of the SwiGLU vector
+    deliver codes of the gathered rows, so no projection quantizes by itself.
     """
 
     def __init__(self, plan: ShardPlan, max_ctx: int, batch: int, layers, embed, head, out_norm, ops):
@@ -88,47 +92,60 @@ class ShardedDecode:
         self.plan, self.shape, self.ops = plan, s, ops
         self.max_ctx, self.batch = max_ctx, batch
         B, G, hd = batch, plan.world, s.head_dim
-        shapes = layer_matrix_shapes(s)
+        self.fused = batch == 1
+        h, h_l, f_l = s.hidden, s.hidden // G, s.ffn // G
+        q_l, kv_l = plan.heads * hd, plan.kv_heads * hd
+        self.q_l, self.kv_l, self.f_l = q_l, kv_l, f_l
+        qt = s.linear_qtype
         self.layers = []
-        first = {}
         for li in range(s.layers):
             src = layers[li % len(layers)]
-            lay = {}
-            for name, (_, k) in shapes.items():
-                if li >= len(layers) and hasattr(ops, "clone_matrix"):
-                    lay[name] = ops.clone_matrix(first[li % len(layers)][name])
-                else:
-                    lay[name] = ops.matrix(s.linear_qtype, k, plan.local_rows(name), src[name])
-            lay["attn_norm"] = ops.vector(src["attn_norm"])
-            lay["ffn_norm"] = ops.vector(src["ffn_norm"])
-            if li < len(layers):
-                first[li] = lay
+            if li >= len(layers) and hasattr(ops, "clone_matrix"):
+                base = self.layers[li % len(layers)]
+                lay = {k: (ops.clone_matrix(v) if k not in ("attn_norm", "ffn_norm") else v) for k, v in base.items()}
+                self.layers.append(lay)
+                continue
+            lay = {"wo": ops.matrix(qt, h, h_l, src["wo"]), "w_down": ops.matrix(qt, s.ffn, h_l, src["w_down"]),
+                   "attn_norm": ops.vector(src["attn_norm"]), "ffn_norm": ops.vector(src["ffn_norm"])}
+            if self.fused:
+                lay["wqkv"] = ops.matrix(qt, h, q_l + 2 * kv_l, np.concatenate([src["wq"], src["wk"], src["wv"]]))
+                lay["w_gu"] = ops.matrix(qt, h, 2 * f_l, np.concatenate([src["w_gate"], src["w_up"]]))
+            else:
+                for name, n in (("wq", q_l), ("wk", kv_l), ("wv", kv_l), ("w_gate", f_l), ("w_up", f_l)):
+                    lay[name] = ops.matrix(qt, h, n, src[name])
             self.layers.append(lay)
-        self.embed = ops.matrix(s.linear_qtype, s.hidden, s.vocab, embed)
-        self.head = ops.matrix(s.head_qtype, s.hidden, plan.local_rows("head"), head)
+        self.embed = ops.matrix(qt, h, s.vocab, embed)
+        self.head = ops.matrix(s.head_qtype, h, plan.local_rows("head"), head)
         self.out_norm = ops.vector(out_norm)
         self.k_cache, self.v_cache = ops.cache(s.layers, B, plan.kv_heads, max_ctx, hd)
         z = ops.zeros
-        h, h_l = s.hidden, s.hidden // G
-        q_l, kv_l, f_l = plan.heads * hd, plan.kv_heads * hd, s.ffn // G
-        self.x, self.hn = z(B * h), z(B * h)
-        self.q, self.k, self.v, self.a_l = z(B * q_l), z(B * kv_l), z(B * kv_l), z(B * q_l)
-        self.o_l, self.g_l, self.u_l, self.f_l, self.d_l = z(B * h_l), z(B * f_l), z(B * f_l), z(B * f_l), z(B * h_l)
+        self.x = z(B * h)
+        self.xq_h = ops.codes(B, h)        # codes of a hidden vector (normed, or the gathered attention)
+        self.xq_f = ops.codes(B, s.ffn)    # codes of the gathered SwiGLU vector
+        if self.fused:
+            self.qkv, self.gu = z(q_l + 2 * kv_l), z(2 * f_l)
+            self.q, self.k, self.v = self.qkv[:q_l], self.qkv[q_l:q_l + kv_l], self.qkv[q_l + kv_l:]
+            self.g_l, self.u_l = self.gu[:f_l], self.gu[f_l:]
+        else:
+            self.q, self.k, self.v = z(B * q_l), z(B * kv_l), z(B * kv_l)
+            self.g_l, self.u_l = z(B * f_l), z(B * f_l)
+        self.a_l, self.o_l, self.f_l_buf, self.d_l = z(B * q_l), z(B * h_l), z(B * f_l), z(B * h_l)
         self.logits_l = z(B * plan.local_rows("head"))
-        # gathered vectors [B][n]; with B > 1 the all-gather lands in a
-        # [G][B][n/G] buffer first and is re-laid out
         if G > 1:
             t = ops.gather_target
             self.a, self.o, self.f, self.d = t("a", B * h), t("o", B * h), t("f", B * s.ffn), t("d", B * h)
             self.logits = t("logits", B * s.vocab)
         else:  # one rank: the local vectors are the whole vectors
-            self.a, self.o, self.f, self.d, self.logits = self.a_l, self.o_l, self.f_l, self.d_l, self.logits_l
+            self.a, self.o, self.f, self.d, self.logits = self.a_l, self.o_l, self.f_l_buf, self.d_l, self.logits_l
+        # with B > 1 and NCCL, an all-gather lands in [G][B][n/G] first
         self.gbuf = z(B * max(s.ffn, s.vocab)) if (B > 1 and G > 1) else None
         self.tokens = ops.tokens(B)
 
-    def _gather(self, full, local, n_local):
+    def _gather(self, full, local, n_local, codes=None, k=None):
         if self.plan.world > 1:
-            self.ops.all_gather(full, local, self.gbuf, self.batch, n_local)
+            self.ops.all_gather(full, local, self.gbuf, self.batch, n_local, codes)
+        elif codes is not None:
+            self.ops.quantize(local, codes, self.batch, k)
 
     def step(self, pos: int) -> None:
         """Decode the tokens in ``self.tokens`` at position ``pos``; the full
@@ -140,24 +157,31 @@ class ShardedDecode:
         ops.embed(self.embed, self.tokens, self.x, B, h, s.vocab)
         delta = None
         for li, lay in enumerate(self.layers):
-            ops.add_rmsnorm(self.x, delta, lay["attn_norm"], self.hn, h, B, s.eps)
-            ops.linear3([lay["wq"], lay["wk"], lay["wv"]], self.hn, [self.q, self.k, self.v], B, h,
-                        [p.heads * hd, p.kv_heads * hd, p.kv_heads * hd])
+            ops.norm_codes(self.x, delta, lay["attn_norm"], self.xq_h, h, B, s.eps)
+            if self.fused:
+                ops.linear_codes(lay["wqkv"], self.xq_h, self.qkv, 1, h, self.q_l + 2 * self.kv_l)
+            else:
+                for name, out, n in (("wq", self.q, self.q_l), ("wk", self.k, self.kv_l), ("wv", self.v, self.kv_l)):
+                    ops.linear_codes(lay[name], self.xq_h, out, B, h, n)
             kc, vc = ops.cache_layer(self.k_cache, li), ops.cache_layer(self.v_cache, li)
             ops.rope_kv(self.q, self.k, self.v, B, p.heads, p.kv_heads, hd, pos, s.rope_theta, kc, vc, self.max_ctx)
             ops.attention(self.q, kc, vc, self.a_l, B, p.heads, p.kv_heads, hd, pos + 1, self.max_ctx)
-            self._gather(self.a, self.a_l, h // G)
-            ops.linear(lay["wo"], self.a, self.o_l, B, h, h // G)
+            self._gather(self.a, self.a_l, h // G, self.xq_h, h)
+            ops.linear_codes(lay["wo"], self.xq_h, self.o_l, B, h, h // G)
             self._gather(self.o, self.o_l, h // G)
-            ops.add_rmsnorm(self.x, self.o, lay["ffn_norm"], self.hn, h, B, s.eps)
-            ops.linear3([lay["w_gate"], lay["w_up"]], self.hn, [self.g_l, self.u_l], B, h, [s.ffn // G] * 2)
-            ops.swiglu(self.g_l, self.u_l, self.f_l, B * (s.ffn // G))
-            self._gather(self.f, self.f_l, s.ffn // G)
-            ops.linear(lay["w_down"], self.f, self.d_l, B, s.ffn, h // G)
+            ops.norm_codes(self.x, self.o, lay["ffn_norm"], self.xq_h, h, B, s.eps)
+            if self.fused:
+                ops.linear_codes(lay["w_gu"], self.xq_h, self.gu, 1, h, 2 * self.f_l)
+            else:
+                ops.linear_codes(lay["w_gate"], self.xq_h, self.g_l, B, h, self.f_l)
+                ops.linear_codes(lay["w_up"], self.xq_h, self.u_l, B, h, self.f_l)
+            ops.swiglu(self.g_l, self.u_l, self.f_l_buf, B * self.f_l)
+            self._gather(self.f, self.f_l_buf, self.f_l, self.xq_f, s.ffn)
+            ops.linear_codes(lay["w_down"], self.xq_f, self.d_l, B, s.ffn, h // G)
             self._gather(self.d, self.d_l, h // G)
             delta = self.d
-        ops.add_rmsnorm(self.x, delta, self.out_norm, self.hn, h, B, s.eps)
-        ops.linear(self.head, self.hn, self.logits_l, B, h, p.local_rows("head"))
+        ops.norm_codes(self.x, delta, self.out_norm, self.xq_h, h, B, s.eps)
+        ops.linear_codes(self.head, self.xq_h, self.logits_l, B, h, p.local_rows("head"))
         self._gather(self.logits, self.logits_l, p.local_rows("head"))
 
 
@@ -226,12 +250,14 @@ class PeerGather:
         self._by_ptr[view.data_ptr()] = t
         return view
 
-    def gather(self, full, local, rows: int, n_local: int) -> None:
+    def gather(self, full, local, rows: int, n_local: int, codes=None, act_mode: int = 0) -> None:
         target = self._by_ptr[full.data_ptr()]
         st = self.torch.cuda.current_stream().cuda_stream
         _native.check(self.lib.b200q_allgather_peer(local.data_ptr(), rows, n_local, target.bases, 0,
                                                     target.flags_offset, self.rank, self.world,
-                                                    self.counters.data_ptr(), target.slot, st), "peer all-gather")
+                                                    self.counters.data_ptr(), target.slot,
+                                                    None if codes is None else codes.data_ptr(), act_mode, st),
+                      "peer all-gather")
 
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (call on every rank,
@@ -306,33 +332,26 @@ class GpuOps:
     def _ok(self, rc, what):
         _native.check(rc, what)
 
+    def codes(self, rows: int, k: int):
+        """Buffer for `rows` rows of activation codes of length k."""
+        n = int(self.lib.b200q_xq_row_bytes(k, self.act))
+        return self.torch.zeros(rows * n, dtype=self.torch.uint8, device=self.dev)
+
     def embed(self, m, tokens, out, batch, hidden, vocab):
         self._ok(self.lib.b200q_dequantize_rows(m.qtype, m.ptr, tokens.data_ptr(), batch, out.data_ptr(), hidden,
                                                 vocab, self._st()), "embedding")
 
-    def linear(self, m, x, out, batch, k, n_rows):
-        self._ok(self.lib.b200q_matmul_ex(m.qtype, self.act, x.data_ptr(), m.ptr, out.data_ptr(), batch, k, n_rows,
-                                          _native.WEIGHTS_STATIC, self._st()), "linear")
+    def norm_codes(self, res, delta, gamma, xq, n, rows, eps):
+        self._ok(self.lib.b200q_add_rmsnorm_q(res.data_ptr(), None if delta is None else delta.data_ptr(),
+                                              gamma.data_ptr(), None, xq.data_ptr(), self.act, n, rows, eps,
+                                              self._st()), "rmsnorm")
 
-    def linear3(self, ms, x, outs, batch, k, rows):
-        if batch != 1:
-            for m, o, n in zip(ms, outs, rows):
-                self.linear(m, x, o, batch, k, n)
-            return
-        import ctypes
+    def linear_codes(self, m, xq, out, batch, k, n_rows):
+        self._ok(self.lib.b200q_matmul_xq(m.qtype, self.act, xq.data_ptr(), m.ptr, out.data_ptr(), batch, k, n_rows,
+                                          1.0, 0.0, _native.WEIGHTS_STATIC, self._st()), "linear")
 
-        c = len(ms)
-        w = (ctypes.c_void_p * c)(*[m.ptr for m in ms])
-        y = (ctypes.c_void_p * c)(*[o.data_ptr() for o in outs])
-        q = (ctypes.c_int * c)(*[m.qtype for m in ms])
-        r = (ctypes.c_int * c)(*rows)
-        self._keep.append((w, y, q, r))
-        self._ok(self.lib.b200q_fused_matvec(self.act, x.data_ptr(), k, c, w, q, y, r, _native.WEIGHTS_STATIC,
-                                             self._st()), "fused linears")
-
-    def add_rmsnorm(self, res, delta, gamma, out, n, rows, eps):
-        self._ok(self.lib.b200q_add_rmsnorm(res.data_ptr(), None if delta is None else delta.data_ptr(),
-                                            gamma.data_ptr(), out.data_ptr(), n, rows, eps, self._st()), "rmsnorm")
+    def quantize(self, x, xq, rows, k):
+        self._ok(self.lib.b200q_quantize_rows(self.act, x.data_ptr(), rows, k, xq.data_ptr(), self._st()), "quantize")
 
     def rope_kv(self, q, k, v, batch, heads, kv_heads, hd, pos, theta, kc, vc, max_ctx):
         self._ok(self.lib.b200q_rope_kv(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, kv_heads, hd, pos,
@@ -345,16 +364,20 @@ class GpuOps:
     def swiglu(self, g, u, out, n):
         self._ok(self.lib.b200q_swiglu(g.data_ptr(), u.data_ptr(), out.data_ptr(), n, self._st()), "swiglu")
 
-    def all_gather(self, full, local, gbuf, batch, n_local):
+    def all_gather(self, full, local, gbuf, batch, n_local, codes=None):
+        """full [batch][world * n_local] = every rank's local [batch][n_local];
+        with `codes`, also the activation codes of the gathered rows."""
         if self.peer:
-            self.peer.gather(full, local, batch, n_local)
+            self.peer.gather(full, local, batch, n_local, codes, self.act)
             return
         import torch.distributed as dist
 
         n = self.world * batch * n_local
         if batch == 1:
             dist.all_gather_into_tensor(full[:n], local[:n_local], group=self.group)
-            return
-        dist.all_gather_into_tensor(gbuf[:n], local[: batch * n_local], group=self.group)
-        self._ok(self.lib.b200q_unshard_rows(gbuf.data_ptr(), full.data_ptr(), self.world, batch, n_local,
-                                             self._st()), "unshard")
+        else:
+            dist.all_gather_into_tensor(gbuf[:n], local[: batch * n_local], group=self.group)
+            self._ok(self.lib.b200q_unshard_rows(gbuf.data_ptr(), full.data_ptr(), self.world, batch, n_local,
+                                                 self._st()), "unshard")
+        if codes is not None:
+            self.quantize(full, codes, batch, self.world * n_local)

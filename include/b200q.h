@@ -293,10 +293,17 @@ B200Q_API int b200q_ipc_free(void* dptr);
  * counters: zeroed device memory of 16 uint32 per slot, private to this
  * rank; slot: which gather (its receive area, flags and counters). Every
  * rank issues the same gathers in the same order, and the consumers of a
- * slot's data run before the rank's next gather. n_local % 4 == 0. */
+ * slot's data run before the rank's next gather. n_local % 4 == 0.
+ * With xq non-NULL the gathered rows are also written there as activation
+ * codes of act_mode (row pitch b200q_xq_row_bytes(world * n_local, act_mode);
+ * world * n_local % 128 == 0). */
 B200Q_API int b200q_allgather_peer(const float* local, int rows, int n_local, void* const* bases,
                                    long long data_offset, long long flags_offset, int rank, int world,
-                                   void* counters, int slot, void* stream);
+                                   void* counters, int slot, void* xq, int act_mode, void* stream);
+
+/* Activation codes of act_mode for `rows` fp32 rows of k (the quantizer the
+ * GEMV entry points run before their kernel), for b200q_matmul_xq. */
+B200Q_API int b200q_quantize_rows(int act_mode, const float* x, int rows, int k, void* xq, void* stream);
 
 /* ---------------------------------------------------------------------
  * Runtime controls.

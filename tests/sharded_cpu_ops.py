@@ -46,20 +46,23 @@ class NumpyOps:
         for b in range(batch):
             out[b * hidden:(b + 1) * hidden] = m[int(tokens[b])]
 
-    def linear(self, m, x, out, batch, k, n_rows):
-        out[: batch * n_rows] = (x[: batch * k].reshape(batch, k) @ m.T).reshape(-1)
+    def codes(self, rows, k):
+        # the restatement keeps activations in float64 (no quantization)
+        return np.zeros(rows * k)
 
-    def linear3(self, ms, x, outs, batch, k, rows):
-        for m, o, n in zip(ms, outs, rows):
-            self.linear(m, x, o, batch, k, n)
+    def quantize(self, x, xq, rows, k):
+        xq[: rows * k] = x[: rows * k]
 
-    def add_rmsnorm(self, res, delta, gamma, out, n, rows, eps):
+    def linear_codes(self, m, xq, out, batch, k, n_rows):
+        out[: batch * n_rows] = (xq[: batch * k].reshape(batch, k) @ m.T).reshape(-1)
+
+    def norm_codes(self, res, delta, gamma, xq, n, rows, eps):
         for r in range(rows):
             sl = slice(r * n, (r + 1) * n)
             if delta is not None:
                 res[sl] += delta[sl]
             x = res[sl]
-            out[sl] = x / np.sqrt(np.mean(x * x) + eps) * gamma
+            xq[sl] = x / np.sqrt(np.mean(x * x) + eps) * gamma
 
     def rope_kv(self, q, k, v, batch, heads, kv_heads, hd, pos, theta, kc, vc, max_ctx):
         p = np.arange(hd // 2)
@@ -93,7 +96,7 @@ class NumpyOps:
     def swiglu(self, g, u, out, n):
         out[:n] = g[:n] / (1.0 + np.exp(-g[:n])) * u[:n]
 
-    def all_gather(self, full, local, gbuf, batch, n_local):
+    def all_gather(self, full, local, gbuf, batch, n_local, codes=None):
         import torch
         import torch.distributed as dist
 
@@ -104,3 +107,5 @@ class NumpyOps:
             blk = t.numpy().reshape(batch, n_local)
             for b in range(batch):
                 full[b * n + g * n_local:b * n + (g + 1) * n_local] = blk[b]
+        if codes is not None:
+            codes[: batch * n] = full[: batch * n]
