@@ -601,6 +601,12 @@ def run_ours(args, ws, rank, local):
     decode = None
     if ws == 1 and not args.no_decode:
         decode = decode_bench(dev, max(10, args.steps // 2), args.warmup)
+    sharded = None
+    if not args.no_decode:
+        if ws > 1:
+            del mats, ys
+            torch.cuda.empty_cache()
+        sharded = sharded_decode_bench(dev, ws, rank, local, 10, args.warmup, 1, 2048, "llama3_70b", "peer")
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -646,6 +652,7 @@ def run_ours(args, ws, rank, local):
             "cpu_baseline": cpu,
             "tile": tile,
             "decode": decode,
+            "sharded_decode": sharded,
         }
         print(json.dumps(line), flush=True)
     if ws > 1:
