@@ -291,14 +291,19 @@ int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev) {
     return make_plan(qtype, act_mode == B200Q_ACT_X8 ? 1 : 2, k, n, 1, dev->num_sms, probe);
 }
 
-// B200Q_ACT_F16 always takes the tile path; B200Q_ACT_X8 takes it for Q4_K
-// batches of at least B200Q_TILE_MIN_M rows (default 8), where the tile
-// kernel streams W once for the whole batch and its fp16 operands are more
-// accurate than int8 activations.
-bool uses_tile_path(int qtype, int act_mode, int m) {
+// B200Q_ACT_F16 always takes the tile path (fp16 activations). Q4_K batches
+// of at least B200Q_TILE_MIN_M rows (default 8) take it too, where the tile
+// kernel streams W once for the whole batch: x8 with fp16 activations (more
+// accurate than int8 codes), x16 with the precise variant (fp16 activations
+// plus their fp16 rounding residues, within the x16 accuracy).
+int uses_tile_path(int qtype, int act_mode, int m) {
     static const int min_m = env_int("B200Q_TILE_MIN_M", 8);
-    if (act_mode == B200Q_ACT_F16) return qtype == QT_Q4_K;
-    return act_mode == B200Q_ACT_X8 && qtype == QT_Q4_K && min_m > 0 && m >= min_m;
+    if (qtype != QT_Q4_K) return 0;
+    if (act_mode == B200Q_ACT_F16) return 1;
+    if (min_m <= 0 || m < min_m) return 0;
+    if (act_mode == B200Q_ACT_X8) return 1;
+    if (act_mode == B200Q_ACT_X16) return 2;
+    return 0;
 }
 
 int launch_gemv(int qtype, int act_mode, const void* w, const float* x, float* y, int m, int k, int n,
@@ -308,11 +313,13 @@ int launch_gemv(int qtype, int act_mode, const void* w, const float* x, float* y
     if ((reinterpret_cast<uintptr_t>(w) & 15u) || (reinterpret_cast<uintptr_t>(x) & 15u) || (x_stride & 3))
         return B200Q_EALIGN;
     if (isums && m != 1) return B200Q_EINVAL;
-    if (!isums && uses_tile_path(qtype, act_mode, m)) {
-        // Batches of up to kTileMaxM activation rows per tile-kernel call.
-        for (int r0 = 0; r0 < m; r0 += kTileMaxM) {
+    const int tile = isums ? 0 : uses_tile_path(qtype, act_mode, m);
+    if (tile) {
+        // Batches of up to tile_max_rows activation rows per tile-kernel call.
+        const int step = tile_max_rows(tile == 2);
+        for (int r0 = 0; r0 < m; r0 += step) {
             const int rc = launch_tile(qtype, w, x + r0 * x_stride, x_stride, y + r0 * y_stride,
-                                       std::min(kTileMaxM, m - r0), k, n, y_stride, dev, st, pdl);
+                                       std::min(step, m - r0), k, n, y_stride, dev, st, pdl, tile == 2);
             if (rc != B200Q_OK) return rc;
         }
         return B200Q_OK;

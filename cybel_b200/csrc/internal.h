@@ -62,17 +62,22 @@ int expert_swiglu(int act_mode, const float* x, int in_dim, const void* gate, in
 // Scratch slots used by the tile path (0 = GEMV activations, 1-3 = fused FFN).
 constexpr int kScratchTileX = 4;     // fp16 activation chunks
 constexpr int kScratchTilePart = 5;  // split-K partial outputs
+constexpr int kScratchTileB2 = 7;    // per-block sub-block sums
 
-// Tile path (tcgen05, fp16 operands, fp32 accumulators) for 1..kTileMaxM
-// activation rows of a Q4_K matrix; x rows at stride x_stride, y rows at
-// y_stride. Returns a B200Q_* status.
+// Tile path (tcgen05 on fp16 operands: the exact products sc*q and the
+// fp16 activations -- plus their rounding residues when `precise` --, fp32
+// accumulators) for 1..tile_max_rows(precise) activation rows of a Q4_K
+// matrix; x rows at stride x_stride, y rows at y_stride. Returns a B200Q_*
+// status.
 constexpr int kTileMaxM = 128;
+int tile_max_rows(bool precise);
 int launch_tile(int qtype, const void* w, const float* x, long long x_stride, float* y, int m, int k, int n,
-                long long y_stride, Device* dev, cudaStream_t st, bool pdl);
-// Kernel launches one launch_tile call issues (2 or 3).
+                long long y_stride, Device* dev, cudaStream_t st, bool pdl, bool precise);
+// Kernel launches one launch_tile call issues (3 or 4).
 int tile_kernel_launches(int k, int n, long long y_stride, int num_sms);
-// Whether launch_gemv hands (qtype, act_mode, m) to the tile path.
-bool uses_tile_path(int qtype, int act_mode, int m);
+// Whether launch_gemv hands (qtype, act_mode, m) to the tile path: 0 no,
+// 1 the fp16 variant, 2 the precise variant.
+int uses_tile_path(int qtype, int act_mode, int m);
 
 // Decode-step glue (decode.cu).
 constexpr int kScratchAttn = 6;  // attention chunk partials

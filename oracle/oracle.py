@@ -202,21 +202,26 @@ def repack_q6k_lm(W: np.ndarray, k: int, n: int) -> np.ndarray:
     return dst
 
 
-def tile_matmul_f16(W: np.ndarray, qtype: int, X: np.ndarray, k: int, n: int, r0: int = 0, r1: int | None = None):
-    """Restatement of the tile path's operands: Y[m][r] for weight rows
-    [r0, r1) = sum_i fp16(w[r][i]) * fp16(x[m][i]), accumulated exactly (fp64).
-
-    w is the reference's fp32 dequantized weight (orc_dequant_rows, which
-    follows quantized_matmul.cpp:1323-1375 bit for bit) and each operand is
-    rounded once to IEEE binary16 with round-to-nearest-even (numpy's
-    float32 -> float16 conversion, subnormals included)."""
+def tile_matmul(W: np.ndarray, qtype: int, X: np.ndarray, k: int, n: int, r0: int = 0, r1: int | None = None,
+                precise: bool = False):
+    """Restatement of the tile path: Y[m][r] for weight rows [r0, r1) =
+    sum_i w[r][i] * xe[m][i], accumulated exactly (fp64), where w is the
+    reference's fp32 dequantized weight (orc_dequant_rows, which follows
+    quantized_matmul.cpp:1323-1375 bit for bit) and xe the activations the
+    tensor cores see: fp16(x) (IEEE binary16, round to nearest even, as
+    numpy's float32 -> float16 conversion), plus fp16(x - fp16(x)) when
+    `precise`. (The kernel multiplies the exact products sc*q and applies
+    d, dmin per block in fp32, which equals w within fp32 rounding.)"""
     r1 = n if r1 is None else r1
     W = np.ascontiguousarray(W, dtype=np.uint8)
     wd = np.empty((r1 - r0, k), dtype=np.float32)
     assert lib().orc_dequant_rows(_p(W), qtype, k, n, r0, r1 - r0, _p(wd)) == 1
-    w16 = wd.astype(np.float16).astype(np.float64)
-    x16 = np.atleast_2d(np.asarray(X, dtype=np.float32)).astype(np.float16).astype(np.float64)
-    return x16 @ w16.T
+    x = np.atleast_2d(np.asarray(X, dtype=np.float32))
+    hi = x.astype(np.float16)
+    xe = hi.astype(np.float64)
+    if precise:
+        xe = xe + (x - hi.astype(np.float32)).astype(np.float16).astype(np.float64)
+    return xe @ wd.astype(np.float64).T
 
 
 def normalized_error(y: np.ndarray, y_ref: np.ndarray, wnorm: np.ndarray, x: np.ndarray) -> float:

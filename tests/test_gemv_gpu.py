@@ -114,8 +114,8 @@ def test_small_batch_matmul(oracle_mod, qt, n, k, m, digits):
     X = np.random.default_rng(m).standard_normal((m, k)).astype(np.float32)
     Y = matmul_device(torch.from_numpy(X).cuda(), DeviceMatrix(qt, k, n, W), act_mode=digits).cpu().numpy()
     if qt == 12 and digits == 1 and m >= 8:
-        # x8 batches of Q4_K take the tile path (fp16 operands; tests/test_tile_gpu.py)
-        ref = O.tile_matmul_f16(W, qt, X, k, n)
+        # x8 batches of Q4_K take the tile path (fp16 activations; tests/test_tile_gpu.py)
+        ref = O.tile_matmul(W, qt, X, k, n)
         assert O.normalized_error(Y, ref, O.row_norms(W, qt, k, n), X) <= NORM_TOL
         return
     for i in range(m):
