@@ -11,24 +11,31 @@
 //           sx_j = sum_{i in j} x_i
 //
 // so the tensor cores work on exact small integers:
-//  * A = sc_j * q_i (<= 945, exact in fp16), dequantized in shared memory with
-//    one packed half2 FMA per two nibbles; B = the activations in fp16 (with
-//    the precise variant, a second pass on the fp16 rounding residue of x).
-//    One 256-element block accumulates in tensor memory as D1[row][m]
-//    (tcgen05.mma kind::f16, M = 128 rows, N = NP columns, K = 16).
+//  * A = sc_j * q_i (<= 945, exact in fp16): dequant warps place nibble pairs
+//    into fp16 with one AND-OR each and scale them with one packed FMA, then
+//    store a block's 128 rows x 256 K into tensor memory (tcgen05.st); the
+//    MMAs read A from there (kind::f16, M = 128 rows, N = NP columns,
+//    K = 16). B = the activations in fp16 from shared memory (with the
+//    precise variant, a second pass on the fp16 rounding residue of x).
 //  * A2 = mn_j (fp16, exact) against B2 = sx_j (hi and lo fp16 parts) gives
 //    D2[row][m] = sum_j mn_j sx_j with one more K = 16 MMA per block.
 //  * Epilogue warps read D1 and D2 back (tcgen05.ld) per block and
 //    accumulate d_b D1 - dmin_b D2 in fp32 registers; two tensor-memory
 //    buffers let the MMAs of block b+1 run while block b is read.
-//  * Three lanes of warp 0 stream, each with its own ring, the packed weights
-//    (2-D TMA, one 128-row x 144-byte box per block column), the prepared
-//    activation chunks and the per-block sub-block sums (1-D bulk copies);
-//    one thread of warp 1 issues the MMAs; warps 2-9 dequantize;
-//    warps 10-17 run the epilogue. Split-K across CTAs when the row tiles
-//    alone cannot fill the SMs; partials are reduced in a fixed order.
+//  * Roles have warps of their own: MMA issuers (4 at N = 16, 2 at N = 32,
+//    each a share of the block's K-steps into its own accumulator), a packed
+//    weight producer (2-D TMA, one 128-row x 144-byte box per block column),
+//    an activation producer (chunk + B2 tile per block, 1-D bulk copies, up
+//    to 6 blocks ahead), 8 dequant warps and 8 epilogue warps. Measured on
+//    B200: an M = 128, K = 16 MMA occupies the tensor core ~45 cycles at
+//    N <= 64 (~N/2 beyond), but a single issuing thread sharing its
+//    scheduler with busy warps issues one only every ~150 cycles, hence
+//    several issuers; lanes of one warp waiting on different barriers
+//    advance in lockstep, hence one warp per producer.
+//    Split-K across CTAs when the row tiles alone cannot fill the SMs;
+//    partials are reduced in a fixed order.
 //  * Every pipeline wait is bounded (status word on timeout); tensor memory
-//    is allocated and freed by warp 1 on every path. No multicast.
+//    is allocated and freed by warp 0 on every path. No multicast.
 #include <cuda.h>
 #include <cuda_fp16.h>
 
@@ -43,27 +50,38 @@ namespace b200q {
 namespace {
 
 constexpr int kTileRows = 128;     // MMA M (weight rows per CTA)
-constexpr int kChunkK = 64;        // K elements per pipeline chunk
+constexpr int kChunkK = 256;       // K elements per pipeline chunk (one block)
 constexpr int kBlockBytes = 144;   // Q4_K super-block
-constexpr int kNSW = 4;            // packed-weight slots (one 256-element block column each)
-constexpr int kNSA = 4;            // dequantized A chunk slots
-constexpr int kDeqWarps = 8;
+constexpr int kNSW = 3;            // packed-weight slots (one 256-element block column each)
 constexpr int kEpiWarps = 8;
-constexpr int kDeqThreads = kDeqWarps * 32;
-constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kThreads = (2 + kDeqWarps + kEpiWarps) * 32;
+// Dequant warps: 8, each expanding two quarters of every block row. (Sixteen
+// warps of one quarter each measured no faster: the dequant work then takes
+// more of the schedulers' issue slots from the MMA issuers.)
+__host__ __device__ constexpr int deq_warps(int) { return 8; }
+// MMA issuers: the same thread-starvation argument again. Warps 0-3 each
+// issue a share of every block's K-steps into their own accumulator (summed
+// by the epilogue in a fixed order), so four schedulers feed the tensor core:
+// 4 issuers at N = 16, 2 at N = 32, 1 beyond (longer MMAs; tensor-memory room).
+// Warps: MMA issuers 0 .. NI-1, the weight producer NI, the activation
+// producer NI+1, then the dequant and epilogue warps (any 4 consecutive warps
+// cover the 4 tensor-memory lane quarters). Each waiting role has a warp of
+// its own: lanes of one warp that wait on different barriers advance in
+// lockstep, which had tied the activation loads to the dequant warps' pace.
+__host__ __device__ constexpr int mma_issuers(int np) { return np == 16 ? 4 : (np == 32 ? 2 : 1); }
+__host__ __device__ constexpr int first_deq_warp(int np) { return mma_issuers(np) + 2; }
+__host__ __device__ constexpr int tile_threads(int np) { return (first_deq_warp(np) + deq_warps(np) + kEpiWarps) * 32; }
 constexpr int kPackedBytes = kTileRows * kBlockBytes;  // 18432
-constexpr int kABytes = kTileRows * kChunkK * 2;       // 16384
 constexpr int kA2Bytes = kTileRows * 16 * 2;           // 4096: mins tile, 128 x 16 fp16
+constexpr int kSmemLimit = 227 * 1024;
 
-// Activation bytes of one 64-element chunk: NP rows x 64 fp16, twice for
-// the precise variant (hi K-groups, then lo K-groups).
+// Activation bytes of one 256-element chunk: NP rows x 256 fp16, twice for
+// the precise variant (hi K-groups 0..31, then lo K-groups 32..63).
 __host__ __device__ constexpr int xchunk_bytes(int np, bool prec) { return np * kChunkK * 2 * (prec ? 2 : 1); }
 // Bytes of one block's B2 tile (NP rows x 16 fp16: sx hi, then sx lo).
 __host__ __device__ constexpr int b2_bytes(int np) { return np * 16 * 2; }
 
 struct TileParams {
-    const uint8_t* xc;    // [k/64][xchunk_bytes] activation chunks (UMMA K-major layout)
+    const uint8_t* xc;    // [k/256][xchunk_bytes] activation chunks (UMMA K-major layout)
     const uint8_t* b2;    // [k/256][b2_bytes] per-block sub-block sums
     float* out;           // [splits][m][n] partials, or y itself (one split, y_stride == n)
     volatile int* status;
@@ -136,15 +154,39 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Two nibble codes (bytes 2i, 2i+1 of a word of nibbles, each < 16) times a
-// sub-block scale sc as an exact half2: the bytes become the halves
-// 1024 + q (0x64 as their high byte), and fma(1024 + q, sc, -1024 sc) =
-// q * sc is exactly representable (<= 945), so the one rounding is exact.
-template <int PAIR>
-__device__ __forceinline__ uint32_t nib_pair_times(uint32_t m, __half2 sc2, __half2 off2) {
-    const uint32_t h = __byte_perm(m, 0x64646464u, PAIR == 0 ? 0x5140u : 0x5342u);
+// Nibbles in place as fp16: OR-ing 0x6400 (1024.0) into a half whose low
+// bits hold a nibble code q gives 1024 + q (bits 0-3) or 1024 + 16 q (bits
+// 4-7), exactly. One AND-OR per pair of codes; then
+//     fma(1024 + q, sc, -1024 sc) = fma(1024 + 16 q, sc / 16, -64 sc) = q sc,
+// exactly representable (<= 945, sc / 16 has 6 significant bits), so the
+// one rounding of each packed FMA is exact.
+__device__ __forceinline__ uint32_t nib_times(uint32_t h, __half2 sc2, __half2 off2) {
     const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&h), sc2, off2);
     return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+// MMA with A from tensor memory (lane = row of A, two fp16 per column) and
+// B from shared memory.
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                              uint32_t accum) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(db), "r"(idesc), "r"(accum)
+        : "memory");
+}
+
+// 32 consecutive columns of this warp's 32 lanes (one register each).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
 }
 
 __device__ __forceinline__ uint32_t tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
@@ -156,47 +198,80 @@ __device__ __forceinline__ uint32_t tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
 }
 
 // ---- the kernel -------------------------------------------------------------
-// Shared-memory map (bytes): packed slots | A chunk slots | activation
-// chunk ring (as deep as 64 KB allows, 4..16 chunks, so its loads run far
-// ahead) | per-block A2 (mins) tiles x2 | B2 tiles x2 | d/dmin per row x2 |
+// Tensor memory (512 columns): D buffers from column 0 (per buffer the
+// issuers' D1 parts then D2, NP columns each; two buffers for NP <= 64, one
+// for NP = 128), A block slots from column 256 (128 columns = 128 rows x 256
+// fp16 each).
+// Shared memory (bytes): packed slots | activation slots (chunk + B2 tile,
+// 2..6 blocks deep) | per-block A2 (mins) tiles x4 | d/dmin per row x4 |
 // barriers | tensor-memory address.
+constexpr int kNS = 2;              // A block slots in tensor memory
+constexpr int kNM = 4;              // per-block mins tile / d, dmin buffers (the epilogue releases them)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kABase = 256;    // first tensor-memory column of the A slots
+constexpr uint32_t kAColsPerChunk = kChunkK / 2;
+
 template <int NP, bool PREC>
 struct TileSmem {
     static constexpr int XB = xchunk_bytes(NP, PREC);
-    static constexpr int NSX = (64 * 1024 / XB) < 4 ? 4 : ((64 * 1024 / XB) > 16 ? 16 : (64 * 1024 / XB));
+    static constexpr int kDBufs = NP <= 64 ? 2 : 1;
+    static constexpr int kBufCols = (mma_issuers(NP) + 1) * NP;
     static constexpr int kPacked = 0;
-    static constexpr int kA = kPacked + kNSW * kPackedBytes;
-    static constexpr int kX = kA + kNSA * kABytes;
-    static constexpr int kA2 = kX + NSX * XB;
-    static constexpr int kB2 = kA2 + 2 * kA2Bytes;
-    static constexpr int kDD = kB2 + 2 * b2_bytes(NP);
-    static constexpr int kBars = kDD + 2 * kTileRows * 8;
-    static constexpr int kNumBars = 2 * kNSW + 2 * kNSA + 2 * NSX + 4 * 2;
+    static constexpr int kXSlot = XB + b2_bytes(NP);  // activation chunk, then the block's B2 tile
+    static constexpr int kFixed = kNSW * kPackedBytes + kNM * kA2Bytes + kNM * kTileRows * 8 + 1024;
+    static constexpr int NSX = ((kSmemLimit - kFixed) / kXSlot) > 6 ? 6 : ((kSmemLimit - kFixed) / kXSlot);
+    static constexpr int kX = kPacked + kNSW * kPackedBytes;  // multiple of 1024
+    static constexpr int kA2 = kX + NSX * kXSlot;
+    static constexpr int kDD = kA2 + kNM * kA2Bytes;
+    static constexpr int kBars = kDD + kNM * kTileRows * 8;
+    static constexpr int kNumBars = 2 * kNSW + 2 * kNS + 2 * NSX + 2 * 2 + 2 * kNM;  // see the kernel
     static constexpr int kTmemHolder = kBars + kNumBars * 8;
     static constexpr int kTotal = kTmemHolder + 16;
+    static_assert(NSX >= 2 && kTotal <= kSmemLimit, "tile kernel shared memory");
+    static_assert(kDBufs * kBufCols <= static_cast<int>(kABase) &&
+                  kABase + kNS * kAColsPerChunk <= kTmemCols, "tensor memory columns");
 };
 
+// Roles: lane 0 of warps 0..NI-1 issues the MMAs; warp NI lane 0 streams
+// packed block columns (2-D TMA), lane 1 the activation chunks and per-block
+// B2 tiles (bulk copies); the next 8 warps dequantize into tensor memory; the
+// last 8 warps run the epilogue.
+//
+// Slot s holds one block: A in tensor memory columns kABase + 128 s, the
+// activation chunk (and B2 tile) in shared memory. Its "full" barrier
+// completes when the dequant warps have arrived (their tensor-memory
+// stores waited for and fenced) and the activation bytes have landed: the
+// MMA issuers wait once and commit once per block (16 MMAs between them,
+// 32 with PREC); issuer 0 adds the block's mins MMA (A2 and d/dmin written
+// by the last dequant warp group).
 template <int NP, bool PREC>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(tile_threads(NP), 1)
     tile_q4k_kernel(const __grid_constant__ CUtensorMap wmap, const TileParams p) {
     using SM = TileSmem<NP, PREC>;
     extern __shared__ __align__(1024) uint8_t smem[];
     constexpr int XB = SM::XB;
-    constexpr uint32_t kTmemCols = 4 * NP;  // 2 buffers x (D1, D2); NP >= 16 -> >= 64 columns
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBars);
+    constexpr int DB = SM::kDBufs;
+    constexpr int DW = deq_warps(NP);
+    constexpr int NI = mma_issuers(NP);
+    constexpr int BC = SM::kBufCols;
+    constexpr int kProdWarp = NI;       // packed weights
+    constexpr int kXWarp = NI + 1;      // activation chunks and B2 tiles
     constexpr int NSX = SM::NSX;
+    constexpr int kFirstDeqWarp = first_deq_warp(NP);
+    constexpr int kRanges = 16 / DW;  // qs quarters per dequant thread
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBars);
     uint64_t* wfull = bars;                 // [kNSW] packed block column landed (TMA)
-    uint64_t* wempty = wfull + kNSW;        // [kNSW] dequantizers done with it
-    uint64_t* cready = wempty + kNSW;       // [kNSA] A chunk written
-    uint64_t* cfree = cready + kNSA;        // [kNSA] MMAs reading the A chunk done
-    uint64_t* xfull = cfree + kNSA;         // [NSX] activation chunk landed
-    uint64_t* xfree = xfull + NSX;          // [NSX] MMAs reading the activation chunk done
-    uint64_t* mfull = xfree + NSX;          // [2] B2 tile landed
-    uint64_t* mready = mfull + 2;           // [2] A2 tile and d/dmin written
-    uint64_t* accfull = mready + 2;         // [2] block MMAs done (D1, D2 final)
-    uint64_t* accempty = accfull + 2;       // [2] epilogue done with the buffer
+    uint64_t* wempty = wfull + kNSW;        // [kNSW] dequant warps done with it
+    uint64_t* full = wempty + kNSW;         // [kNS] A block stored in tensor memory
+    uint64_t* empty = full + kNS;           // [kNS] MMAs reading the A slot done
+    uint64_t* xfull = empty + kNS;          // [NSX] activation chunk and B2 landed
+    uint64_t* xfree = xfull + SM::NSX;      // [NSX] MMAs reading the activation slot done
+    uint64_t* mready = xfree + SM::NSX;     // [kNM] A2 and d/dmin of the block written
+    uint64_t* accfull = mready + kNM;       // [2] block MMAs done (D1, D2 final)
+    uint64_t* accempty = accfull + 2;       // [2] epilogue done with the D buffer
+    uint64_t* dfree = accempty + 2;         // [kNM] epilogue done with A2/d/dmin buffer bl % kNM
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + SM::kTmemHolder);
-    float* dd = reinterpret_cast<float*>(smem + SM::kDD);  // [2][128][2] d, dmin
+    float* dd = reinterpret_cast<float*>(smem + SM::kDD);  // [kNM][128][2] d, dmin
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row0 = blockIdx.x * kTileRows;
@@ -204,30 +279,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int b_begin = static_cast<int>(static_cast<long long>(split) * p.nblocks / p.splits);
     const int b_end = static_cast<int>(static_cast<long long>(split + 1) * p.nblocks / p.splits);
     const int nblk = b_end - b_begin;
-    const int nchunks = nblk * 4;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kNSW; ++i) {
             mbar_init(smem_addr(wfull + i), 1);
-            mbar_init(smem_addr(wempty + i), kDeqThreads);
+            mbar_init(smem_addr(wempty + i), DW);
         }
-        for (int i = 0; i < kNSA; ++i) {
-            mbar_init(smem_addr(cready + i), kDeqThreads);
-            mbar_init(smem_addr(cfree + i), 1);
+        for (int i = 0; i < kNS; ++i) {
+            mbar_init(smem_addr(full + i), DW);
+            mbar_init(smem_addr(empty + i), NI);
         }
-        for (int i = 0; i < NSX; ++i) {
+        for (int i = 0; i < SM::NSX; ++i) {
             mbar_init(smem_addr(xfull + i), 1);
-            mbar_init(smem_addr(xfree + i), 1);
+            mbar_init(smem_addr(xfree + i), NI);
         }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(smem_addr(mfull + i), 1);
-            mbar_init(smem_addr(mready + i), kTileRows);
-            mbar_init(smem_addr(accfull + i), 1);
-            mbar_init(smem_addr(accempty + i), kEpiThreads);
+            mbar_init(smem_addr(accfull + i), NI);
+            mbar_init(smem_addr(accempty + i), kEpiWarps);
+        }
+        for (int i = 0; i < kNM; ++i) {
+            mbar_init(smem_addr(mready + i), 4);
+            mbar_init(smem_addr(dfree + i), kEpiWarps);
         }
         fence_mbar_init();
     }
-    if (warp == 1) {
+    if (warp == 0) {
         tmem_alloc(smem_addr(tmem_holder), kTmemCols);
         tmem_relinquish();
     }
@@ -238,11 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     griddep_launch_dependents();
 
     bool ok = true;
-    if (warp == 0) {
-        // ---------------- producers ----------------
-        // lane 0: packed block columns; lane 1: activation chunks; lane 2: B2
-        // tiles -- independent rings, so no one waits behind another.
-        if (lane < 3) griddep_wait();  // the activation tiles come from the preceding prep kernels
+    if (warp == kProdWarp) {
+        // ---------------- packed weight producer ----------------
         if (lane == 0) {
             for (int bl = 0; bl < nblk && ok; ++bl) {
                 const int s = bl % kNSW;
@@ -252,157 +325,160 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_2d(smem_addr(smem + SM::kPacked + s * kPackedBytes), &wmap, (b_begin + bl) * kBlockBytes, row0,
                             smem_addr(wfull + s));
             }
-        } else if (lane == 1) {
-            for (int c = 0; c < nchunks && ok; ++c) {
-                const int xs = c % NSX;
-                ok = mbar_wait_bounded(smem_addr(xfree + xs), ((c / NSX) & 1) ^ 1);
-                if (!ok) break;
-                mbar_arrive_expect_tx(smem_addr(xfull + xs), XB);
-                bulk_load(smem_addr(smem + SM::kX + xs * XB), p.xc + static_cast<long long>(b_begin * 4 + c) * XB, XB,
-                          smem_addr(xfull + xs));
-            }
-        } else if (lane == 2) {
-            // B2 of block bl: its buffer is free once the epilogue of block
-            // bl - 2 is done (which follows that block's MMAs).
-            for (int bl = 0; bl < nblk && ok; ++bl) {
-                const int mb = bl & 1;
-                ok = mbar_wait_bounded(smem_addr(accempty + mb), ((bl >> 1) & 1) ^ 1);
-                if (!ok) break;
-                mbar_arrive_expect_tx(smem_addr(mfull + mb), b2_bytes(NP));
-                bulk_load(smem_addr(smem + SM::kB2 + mb * b2_bytes(NP)),
-                          p.b2 + static_cast<long long>(b_begin + bl) * b2_bytes(NP), b2_bytes(NP), smem_addr(mfull + mb));
-            }
+            if (!ok) *p.status = STATUS_TIMEOUT;
         }
-        if (!ok) *p.status = STATUS_TIMEOUT;
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
+    } else if (warp == kXWarp) {
+        // ---------------- activation producer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_f16(NP);
+            griddep_wait();  // the activation chunks and B2 tiles come from the preceding prep kernels
             for (int bl = 0; bl < nblk && ok; ++bl) {
-                const int mb = bl & 1;
-                const uint32_t d1 = tmem_base + static_cast<uint32_t>(mb * 2 * NP);
-                const uint32_t d2 = d1 + NP;
-                ok = mbar_wait_bounded(smem_addr(accempty + mb), ((bl >> 1) & 1) ^ 1);
+                const int xs = bl % NSX;
+                ok = mbar_wait_bounded(smem_addr(xfree + xs), ((bl / NSX) & 1) ^ 1);
+                if (!ok) break;
+                const uint32_t fb = smem_addr(xfull + xs);
+                const uint32_t dst = smem_addr(smem + SM::kX + xs * SM::kXSlot);
+                mbar_arrive_expect_tx(fb, SM::kXSlot);
+                bulk_load(dst, p.xc + static_cast<long long>(b_begin + bl) * XB, XB, fb);
+                bulk_load(dst + XB, p.b2 + static_cast<long long>(b_begin + bl) * b2_bytes(NP), b2_bytes(NP), fb);
+            }
+            if (!ok) *p.status = STATUS_TIMEOUT;
+        }
+    } else if (warp < NI) {
+        // ---------------- MMA issuers ----------------
+        if (lane == 0) {
+            constexpr int KS = (kChunkK / 16) / NI;  // K-steps per issuer
+            const int k0 = warp * KS;
+            constexpr uint32_t idesc = idesc_f16(NP);
+            // Descriptors of slot 0 / buffer 0; others are fixed byte offsets
+            // (>> 4 into the address field, which cannot carry: < 256 KB).
+            const uint64_t dX0 = smem_desc(smem_addr(smem + SM::kX), NP * 16, 128);
+            const uint64_t dA20 = smem_desc(smem_addr(smem + SM::kA2), kTileRows * 16, 128);
+            const uint64_t dB20 = smem_desc(smem_addr(smem + SM::kX + XB), NP * 16, 128);
+            for (int bl = 0; bl < nblk && ok; ++bl) {
+                const int mb = bl % DB, hb = bl % kNM;
+                const uint32_t d1 = tmem_base + static_cast<uint32_t>(mb * BC + warp * NP);
+                const uint32_t d2 = tmem_base + static_cast<uint32_t>(mb * BC + NI * NP);
+                ok = mbar_wait_bounded(smem_addr(accempty + mb), ((bl / DB) & 1) ^ 1);
                 if (!ok) break;
                 tc_fence_after();
-                for (int q = 0; q < 4 && ok; ++q) {
-                    const int c = bl * 4 + q;
-                    const int cs = c % kNSA, xs = c % NSX;
-                    ok = mbar_wait_bounded(smem_addr(cready + cs), (c / kNSA) & 1) &&
-                         mbar_wait_bounded(smem_addr(xfull + xs), (c / NSX) & 1);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t wa = smem_addr(smem + SM::kA + cs * kABytes);
-                    const uint32_t xa = smem_addr(smem + SM::kX + xs * XB);
+                const int s = bl % kNS, xs = bl % NSX;
+                ok = mbar_wait_bounded(smem_addr(full + s), (bl / kNS) & 1) &&
+                     mbar_wait_bounded(smem_addr(xfull + xs), (bl / NSX) & 1);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t ta = tmem_base + kABase + static_cast<uint32_t>(s) * kAColsPerChunk;
+                const uint64_t dx = dX0 + static_cast<uint64_t>((xs * SM::kXSlot) >> 4);
 #pragma unroll
-                    for (int s = 0; s < kChunkK / 16; ++s) {
-                        const uint64_t da = smem_desc(wa + s * 2 * (kTileRows * 16), kTileRows * 16, 128);
-                        const uint64_t db = smem_desc(xa + s * 2 * (NP * 16), NP * 16, 128);
-                        tc_mma_f16(d1, da, db, idesc, (q > 0 || s > 0) ? 1u : 0u);
-                        if constexpr (PREC) {  // the rounding residue of x, same A
-                            const uint64_t dl = smem_desc(xa + 8 * (NP * 16) + s * 2 * (NP * 16), NP * 16, 128);
-                            tc_mma_f16(d1, da, dl, idesc, 1u);
-                        }
-                    }
-                    tc_commit(smem_addr(cfree + cs));
-                    tc_commit(smem_addr(xfree + xs));
+                for (int i = 0; i < KS; ++i) {
+                    const int kk = k0 + i;
+                    tc_mma_f16_ts(d1, ta + 8u * kk, dx + ((kk * 2 * NP * 16) >> 4), idesc, i > 0 ? 1u : 0u);
+                    if constexpr (PREC)  // the rounding residue of x (K groups 32..63), same A
+                        tc_mma_f16_ts(d1, ta + 8u * kk, dx + (((32 + kk * 2) * NP * 16) >> 4), idesc, 1u);
                 }
-                if (!ok) break;
-                // mins: D2 = A2 (mn) x B2 (sx hi | sx lo), one K = 16 step
-                ok = mbar_wait_bounded(smem_addr(mready + mb), (bl >> 1) & 1) &&
-                     mbar_wait_bounded(smem_addr(mfull + mb), (bl >> 1) & 1);
-                if (!ok) break;
-                tc_fence_after();
-                const uint64_t da2 = smem_desc(smem_addr(smem + SM::kA2 + mb * kA2Bytes), kTileRows * 16, 128);
-                const uint64_t db2 = smem_desc(smem_addr(smem + SM::kB2 + mb * b2_bytes(NP)), NP * 16, 128);
-                tc_mma_f16(d2, da2, db2, idesc, 0u);
+                if (warp == 0)  // mins: D2 = A2 (mn) x B2 (sx hi | sx lo), one K = 16 step
+                    tc_mma_f16(d2, dA20 + ((hb * kA2Bytes) >> 4), dB20 + ((xs * SM::kXSlot) >> 4), idesc, 0u);
+                tc_commit(smem_addr(empty + s));
+                tc_commit(smem_addr(xfree + xs));
                 tc_commit(smem_addr(accfull + mb));
             }
             if (!ok) *p.status = STATUS_TIMEOUT;
         }
-    } else if (warp < 2 + kDeqWarps) {
-        // ---------------- dequantizers (warps 2..9) ----------------
-        const int dt = threadIdx.x - 64;
-        const int t = dt & (kTileRows - 1);  // tile row
-        const int h = dt >> 7;               // 0: sub-block 2q (low nibbles), 1: sub-block 2q+1 (high)
-        for (int c = 0; c < nchunks && ok; ++c) {
-            const int bl = c >> 2, q = c & 3;
-            const int s = bl % kNSW;
-            if (q == 0) {
-                ok = mbar_wait_bounded(smem_addr(wfull + s), (bl / kNSW) & 1);
-                if (!ok) break;
-            }
-            const int cs = c % kNSA;
-            ok = mbar_wait_bounded(smem_addr(cfree + cs), ((c / kNSA) & 1) ^ 1);
+    } else if (warp < kFirstDeqWarp + DW) {
+        // ---------------- dequantizers (warps NI+1 .. NI+DW) ----------------
+        // A warp reaches tensor-memory lanes 32 (warp % 4) .. + 31, so thread
+        // (t, h0) takes tile row t = 32 (warp % 4) + lane and, for each of its
+        // quarters h = h0 + u DW/4, qs bytes [32h, 32h+32) of each block:
+        // sub-block 2h (low nibbles) into slot columns 32h .. 32h+15,
+        // sub-block 2h+1 (high nibbles) into 32h+16 .. 32h+31 (two
+        // consecutive K elements per column). The last warp group also writes
+        // the block's mins tile A2 and d/dmin.
+        const int t = 32 * (warp & 3) + lane;
+        const int h0 = (warp - kFirstDeqWarp) >> 2;
+        const bool mins_group = h0 == DW / 4 - 1;
+        const uint32_t lane_addr = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+        for (int bl = 0; bl < nblk && ok; ++bl) {
+            const int s = bl % kNS, ws = bl % kNSW, hb = bl % kNM;
+            ok = mbar_wait_bounded(smem_addr(empty + s), ((bl / kNS) & 1) ^ 1) &&
+                 mbar_wait_bounded(smem_addr(wfull + ws), (bl / kNSW) & 1);
+            if (ok && mins_group) ok = mbar_wait_bounded(smem_addr(dfree + hb), ((bl / kNM) & 1) ^ 1);
+            ok = __all_sync(0xFFFFFFFFu, ok);  // warp-uniform: the tensor-memory store is warp-collective
             if (!ok) break;
             // Row t of block column bl (quantized_matmul.cpp:1323-1375 layout):
-            // d, dmin (fp16), 12 scale bytes, 128 nibble bytes; this chunk is
-            // sub-blocks 2q (low nibbles) and 2q+1 (high) of qs[32q, 32q+32).
-            const uint32_t blk = smem_addr(smem + SM::kPacked + s * kPackedBytes + t * kBlockBytes);
+            // d, dmin (fp16), 12 scale bytes, 128 nibble bytes.
+            const uint32_t blk = smem_addr(smem + SM::kPacked + ws * kPackedBytes + t * kBlockBytes);
             const uint4 hd = lds128(blk);
-            const uint4 qa = lds128(blk + 16u + 32u * q);
-            const uint4 qb = lds128(blk + 32u + 32u * q);
-            const int j = 2 * q + h;  // sub-block
-            const uint32_t sb_lo = (j < 4 ? hd.y : hd.w) >> (8 * (j & 3));
-            const uint32_t sc = j < 4 ? (sb_lo & 63u) : ((sb_lo & 15u) | ((hd.y >> (8 * (j & 3)) >> 2) & 0x30u));
-            const __half2 sc2 = __half2half2(__int2half_rn(static_cast<int>(sc)));
-            const __half2 off2 = __half2half2(__int2half_rn(-1024 * static_cast<int>(sc)));
-            const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-            const uint32_t wbase = smem_addr(smem + SM::kA + cs * kABytes) + (t >> 3) * 128 + (t & 7) * 16;
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {  // K group 4h + g: qs bytes 8g .. 8g+7 of the pair
-                const uint32_t lo = h ? (qw[2 * g] >> 4) & 0x0F0F0F0Fu : qw[2 * g] & 0x0F0F0F0Fu;
-                const uint32_t hi = h ? (qw[2 * g + 1] >> 4) & 0x0F0F0F0Fu : qw[2 * g + 1] & 0x0F0F0F0Fu;
-                const uint32_t a = wbase + (4 * h + g) * (kTileRows * 16);
-                asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a),
-                             "r"(nib_pair_times<0>(lo, sc2, off2)), "r"(nib_pair_times<1>(lo, sc2, off2)),
-                             "r"(nib_pair_times<0>(hi, sc2, off2)), "r"(nib_pair_times<1>(hi, sc2, off2))
-                             : "memory");
-            }
-            fence_proxy_async_smem();
-            mbar_arrive(smem_addr(cready + cs));
-            if (q == 3) {
-                if (h == 0) {
-                    // The block's mins tile A2 (row t: mn_0..7, twice, as fp16)
-                    // and its d / dmin, into buffer bl & 1 once the epilogue of
-                    // block bl - 2 has released it.
-                    const int mb = bl & 1;
-                    ok = mbar_wait_bounded(smem_addr(accempty + mb), ((bl >> 1) & 1) ^ 1);
-                    if (!ok) break;
-                    uint32_t mnw[4];
+            for (int u = 0; u < kRanges; ++u) {
+                const int h = h0 + u * (DW / 4);
+                const uint4 qa = lds128(blk + 16u + 32u * h);
+                const uint4 qb = lds128(blk + 32u + 32u * h);
+                const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                uint32_t r[32];
+                __half2 sc2[2], off2[2];
 #pragma unroll
-                    for (int jj = 0; jj < 8; jj += 2) {
-                        uint32_t m2[2];
-#pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            const int jx = jj + e;
-                            const uint32_t shz = 8 * (jx & 3);
-                            m2[e] = jx < 4 ? ((hd.z >> shz) & 63u)
-                                           : (((hd.w >> shz) >> 4) & 15u) | (((hd.z >> shz) >> 2) & 0x30u);
-                        }
-                        const __half2 hm = __halves2half2(__int2half_rn(static_cast<int>(m2[0])),
-                                                          __int2half_rn(static_cast<int>(m2[1])));
-                        mnw[jj / 2] = *reinterpret_cast<const uint32_t*>(&hm);
-                    }
-                    const uint32_t a2 = smem_addr(smem + SM::kA2 + mb * kA2Bytes) + (t >> 3) * 128 + (t & 7) * 16;
-#pragma unroll
-                    for (int kg = 0; kg < 2; ++kg)
-                        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a2 + kg * (kTileRows * 16)),
-                                     "r"(mnw[0]), "r"(mnw[1]), "r"(mnw[2]), "r"(mnw[3])
-                                     : "memory");
-                    dd[(mb * kTileRows + t) * 2] = half_bits_to_float(hd.x & 0xFFFFu);
-                    dd[(mb * kTileRows + t) * 2 + 1] = half_bits_to_float(hd.x >> 16);
-                    fence_proxy_async_smem();
-                    mbar_arrive(smem_addr(mready + mb));
+                for (int half = 0; half < 2; ++half) {  // sub-block j = 2h + half
+                    const int j = 2 * h + half;
+                    const uint32_t sb_lo = (j < 4 ? hd.y : hd.w) >> (8 * (j & 3));
+                    const uint32_t sc = j < 4 ? (sb_lo & 63u) : ((sb_lo & 15u) | ((hd.y >> (8 * (j & 3)) >> 2) & 0x30u));
+                    // low nibbles: (1024 + q) sc - 1024 sc; high: (1024 + 16 q) sc/16 - 64 sc
+                    sc2[half] = __float2half2_rn(half ? static_cast<float>(sc) * 0.0625f : static_cast<float>(sc));
+                    off2[half] = __float2half2_rn(-static_cast<float>(sc) * (half ? 64.0f : 1024.0f));
                 }
-                mbar_arrive(smem_addr(wempty + s));
+#pragma unroll
+                for (int w8 = 0; w8 < 8; ++w8) {  // bytes 4 w8 .. 4 w8 + 3: elements e0..e3 of both sub-blocks
+                    // Column pairs hold elements (e0, e2) and (e1, e3); the
+                    // activation chunks use the same order.
+                    const uint32_t w = qw[w8], w_8 = qw[w8] >> 8;
+                    r[2 * w8] = nib_times((w & 0x000F000Fu) | 0x64006400u, sc2[0], off2[0]);
+                    r[2 * w8 + 1] = nib_times((w_8 & 0x000F000Fu) | 0x64006400u, sc2[0], off2[0]);
+                    r[16 + 2 * w8] = nib_times((w & 0x00F000F0u) | 0x64006400u, sc2[1], off2[1]);
+                    r[16 + 2 * w8 + 1] = nib_times((w_8 & 0x00F000F0u) | 0x64006400u, sc2[1], off2[1]);
+                }
+                tmem_st32(tmem_base + lane_addr + kABase + static_cast<uint32_t>(s) * kAColsPerChunk + 32u * h, r);
+            }
+            if (mins_group) {
+                // The block's mins tile A2 (row t: mn_0..7, twice, as fp16)
+                // and its d / dmin, into buffer bl % kNM (released by the
+                // epilogue of block bl - kNM, waited for above).
+                uint32_t mnw[4];
+#pragma unroll
+                for (int jj = 0; jj < 8; jj += 2) {
+                    uint32_t m2[2];
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int jx = jj + e;
+                        const uint32_t shz = 8 * (jx & 3);
+                        m2[e] = jx < 4 ? ((hd.z >> shz) & 63u)
+                                       : (((hd.w >> shz) >> 4) & 15u) | (((hd.z >> shz) >> 2) & 0x30u);
+                    }
+                    const __half2 hm = __halves2half2(__int2half_rn(static_cast<int>(m2[0])),
+                                                      __int2half_rn(static_cast<int>(m2[1])));
+                    mnw[jj / 2] = *reinterpret_cast<const uint32_t*>(&hm);
+                }
+                const uint32_t a2 = smem_addr(smem + SM::kA2 + hb * kA2Bytes) + (t >> 3) * 128 + (t & 7) * 16;
+#pragma unroll
+                for (int kg = 0; kg < 2; ++kg)
+                    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a2 + kg * (kTileRows * 16)),
+                                 "r"(mnw[0]), "r"(mnw[1]), "r"(mnw[2]), "r"(mnw[3])
+                                 : "memory");
+                dd[(hb * kTileRows + t) * 2] = half_bits_to_float(hd.x & 0xFFFFu);
+                dd[(hb * kTileRows + t) * 2 + 1] = half_bits_to_float(hd.x >> 16);
+                fence_proxy_async_smem();
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(smem_addr(full + s));
+                mbar_arrive(smem_addr(wempty + ws));
+                if (mins_group) mbar_arrive(smem_addr(mready + hb));
             }
         }
         if (!ok) *p.status = STATUS_TIMEOUT;
     } else {
-        // ---------------- epilogue (warps 10..17) ----------------
+        // ---------------- epilogue (the last 8 warps) ----------------
         constexpr int NH = NP / 2;
-        const int ew = warp - 2 - kDeqWarps;
+        const int ew = warp - kFirstDeqWarp - DW;
         const int lane_base = 32 * (warp & 3);
         const int ch = ew >> 2;  // column half
         const int row = lane_base + lane;
@@ -410,28 +486,37 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < NH; ++i) acc[i] = 0.0f;
         for (int bl = 0; bl < nblk && ok; ++bl) {
-            const int mb = bl & 1;
-            ok = mbar_wait_bounded(smem_addr(accfull + mb), (bl >> 1) & 1) &&
-                 mbar_wait_bounded(smem_addr(mready + mb), (bl >> 1) & 1);
-            __syncwarp();
+            const int mb = bl % DB, hb = bl % kNM;
+            ok = mbar_wait_bounded(smem_addr(accfull + mb), (bl / DB) & 1) &&
+                 mbar_wait_bounded(smem_addr(mready + hb), (bl / kNM) & 1);
+            ok = __all_sync(0xFFFFFFFFu, ok);  // tcgen05.ld below is warp-collective
             if (!ok) break;
             tc_fence_after();
-            const float d = dd[(mb * kTileRows + row) * 2];
-            const float dmin = dd[(mb * kTileRows + row) * 2 + 1];
+            const float d = dd[(hb * kTileRows + row) * 2];
+            const float dmin = dd[(hb * kTileRows + row) * 2 + 1];
             const uint32_t tcol = tmem_base + (static_cast<uint32_t>(lane_base) << 16) +
-                                  static_cast<uint32_t>(mb * 2 * NP + ch * NH);
+                                  static_cast<uint32_t>(mb * BC + ch * NH);
 #pragma unroll
             for (int cc = 0; cc < NH; cc += 8) {
-                uint32_t v1[8], v2[8];
-                tmem_ld8(tcol + cc, v1);
-                tmem_ld8(tcol + NP + cc, v2);
+                uint32_t v1[NI][8], v2[8];
+#pragma unroll
+                for (int a = 0; a < NI; ++a) tmem_ld8(tcol + a * NP + cc, v1[a]);
+                tmem_ld8(tcol + NI * NP + cc, v2);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    acc[cc + i] = fmaf(d, __uint_as_float(v1[i]), fmaf(-dmin, __uint_as_float(v2[i]), acc[cc + i]));
+                for (int i = 0; i < 8; ++i) {
+                    float dsum = __uint_as_float(v1[0][i]);
+#pragma unroll
+                    for (int a = 1; a < NI; ++a) dsum += __uint_as_float(v1[a][i]);
+                    acc[cc + i] = fmaf(d, dsum, fmaf(-dmin, __uint_as_float(v2[i]), acc[cc + i]));
+                }
             }
             tc_fence_before();
-            mbar_arrive(smem_addr(accempty + mb));
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(smem_addr(accempty + mb));
+                mbar_arrive(smem_addr(dfree + hb));
+            }
         }
         if (!ok) *p.status = STATUS_TIMEOUT;
         float* dst = p.out + static_cast<long long>(split) * p.m * p.n;
@@ -443,10 +528,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     }
-    // Teardown: every warp is done with tensor memory before warp 1 frees it.
+    // Teardown: every warp is done with tensor memory before warp 0 frees it.
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == 0) {
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem_base, kTmemCols);
@@ -454,10 +539,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Activation rows (fp32, m rows of k at stride x_stride) -> fp16 chunks in
-// the UMMA K-major canonical layout: chunk c holds K elements [64c, 64c+64)
-// of NP rows (rows >= m are zero): row r, K group j (8 elements), element e
-// at byte j * NP*16 + (r / 8) * 128 + (r % 8) * 16 + 2e. With PREC the
-// rounding residues fp16(x - fp16(x)) follow as K groups 8..15.
+// the UMMA K-major canonical layout: chunk c holds K elements [256c,
+// 256c+256) of NP rows (rows >= m are zero): row r, K group j (8 elements),
+// element e at byte j * NP*16 + (r / 8) * 128 + (r % 8) * 16 + 2 pos(e), where
+// pos swaps elements 1 and 2 of each group of 4 (the order in which the
+// dequantizers pair nibbles). With PREC the rounding residues
+// fp16(x - fp16(x)) follow as K groups 32..63.
 template <int NP, bool PREC>
 __global__ void prep_x_kernel(const float* __restrict__ x, long long x_stride, int m, int k,
                               uint8_t* __restrict__ xc) {
@@ -468,13 +555,14 @@ __global__ void prep_x_kernel(const float* __restrict__ x, long long x_stride, i
     if (i >= groups) return;
     const int r = static_cast<int>(i % NP);
     const long long g8 = i / NP;  // global K group
-    const int c = static_cast<int>(g8 >> 3), j = static_cast<int>(g8 & 7);
+    const int c = static_cast<int>(g8 >> 5), j = static_cast<int>(g8 & 31);
     uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
     if (r < m) {
         const float* src = x + static_cast<long long>(r) * x_stride + g8 * 8;
         const float4 a = __ldg(reinterpret_cast<const float4*>(src));
         const float4 b = __ldg(reinterpret_cast<const float4*>(src + 4));
-        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        // K order within each group of 4 is (0, 2, 1, 3), as in the A columns.
+        const float v[8] = {a.x, a.z, a.y, a.w, b.x, b.z, b.y, b.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const __half2 hh = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
@@ -487,7 +575,7 @@ __global__ void prep_x_kernel(const float* __restrict__ x, long long x_stride, i
     }
     uint8_t* dst = xc + static_cast<long long>(c) * xchunk_bytes(NP, PREC) + j * (NP * 16) + (r >> 3) * 128 + (r & 7) * 16;
     *reinterpret_cast<uint4*>(dst) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    if constexpr (PREC) *reinterpret_cast<uint4*>(dst + 8 * (NP * 16)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    if constexpr (PREC) *reinterpret_cast<uint4*>(dst + 32 * (NP * 16)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
 }
 
 // Per block and row: the 8 sub-block sums sx_j of the fp16 activations the
@@ -641,7 +729,7 @@ int launch_np(const void* w, const float* x, long long x_stride, float* y, int m
         tp.nblocks = nblocks;
         tp.splits = splits;
         cudaLaunchConfig_t c =
-            cfg_of(dim3(tiles, splits), dim3(kThreads), TileSmem<NP, PREC>::kTotal, st, pdl, attr);
+            cfg_of(dim3(tiles, splits), dim3(tile_threads(NP)), TileSmem<NP, PREC>::kTotal, st, pdl, attr);
         if (cudaLaunchKernelEx(&c, tile_q4k_kernel<NP, PREC>, map, tp) != cudaSuccess) return B200Q_ECUDA;
     }
     if (!direct) {
