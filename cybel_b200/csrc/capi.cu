@@ -433,6 +433,18 @@ int b200q_attention_decode_q(const float* q, const void* k_cache, const void* v_
     return rc;
 }
 
+int b200q_rope_attention_decode(const float* q, const float* k, const float* v, int batch, int n_heads, int n_kv_heads,
+                                int head_dim, int pos, float theta, void* k_cache, void* v_cache, int max_ctx,
+                                float* out, void* xq, int act_mode, void* stream) {
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    if (rc == B200Q_OK)
+        rc = launch_rope_attention(q, k, v, batch, n_heads, n_kv_heads, head_dim, pos, theta, k_cache, v_cache,
+                                   max_ctx, out, xq, act_mode, dev, static_cast<cudaStream_t>(stream));
+    set_last_error(rc);
+    return rc;
+}
+
 int b200q_swiglu_q(const float* gate, const float* up, void* xq, int act_mode, int n, void* stream) {
     int rc = B200Q_OK;
     if (!gate || !up || !xq || n <= 0 || (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16)) rc = B200Q_EINVAL;

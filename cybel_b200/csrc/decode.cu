@@ -153,10 +153,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_chunk_kernel(const float
     griddep_launch_dependents();
     griddep_wait();
     constexpr int PW = kAttnChunk / kAttnWarps;  // positions per warp
-    __shared__ float qs[kMaxGroup][kHeadDim];
-    __shared__ float sc[kMaxGroup][kAttnChunk];
-    __shared__ float ml[kMaxGroup][2];
-    __shared__ float red[kAttnWarps][kMaxGroup * kHeadDim];
+    __shared__ __align__(16) float qs[kMaxGroup][kHeadDim];
+    __shared__ __align__(16) float sc[kMaxGroup][kAttnChunk];
+    __shared__ __align__(16) float ml[kMaxGroup][2];
+    __shared__ __align__(16) float red[kAttnWarps][kMaxGroup * kHeadDim];  // float4 stores
     const int kvh = blockIdx.x, c = blockIdx.y, n_chunks = gridDim.y, b = blockIdx.z;
     const int G = n_heads / n_kv;
     q += static_cast<long long>(b) * n_heads * kHeadDim;
@@ -334,6 +334,216 @@ __global__ void __launch_bounds__(kHeadDim) attn_combine_kernel(const float* __r
     }
 }
 
+// Fused decode attention for one query token per sequence (the RoPE and
+// attention stages of the reference's decode graph, model_graph.cpp:
+// 1222-1323 and the GQA attention after it, in one launch):
+//  * every CTA rotates its kv head's G query heads into shared memory
+//    (pos * theta^(-2p / head_dim), interleaved pairs), scaled by
+//    1 / sqrt(head_dim);
+//  * the CTA whose chunk holds `pos` rotates the new key and appends it and
+//    the new value to the fp16 caches before reading its chunk;
+//  * each CTA scores and weights its kAttnChunk positions like
+//    attn_chunk_kernel and writes its partial records;
+//  * the CTA that finishes last for a (kv head, sequence) -- an arrival
+//    counter, reset by that CTA -- merges the chunks (max rescaling) and
+//    writes the output rows and, with DIG > 0, their x8 / x16 codes. No CTA
+//    waits for another (threadfence-reduction pattern).
+template <int G, int DIG>
+__global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, __half* __restrict__ kc,
+    __half* __restrict__ vc, float* __restrict__ part, int* __restrict__ counters, float* __restrict__ out,
+    uint8_t* __restrict__ xq, int n_heads, int n_kv, int pos, int max_ctx, float log2_theta, float scale) {
+    griddep_launch_dependents();
+    constexpr int PW = kAttnChunk / kAttnWarps;  // positions per warp
+    constexpr int HALF = kHeadDim / 2;
+    // 16-byte aligned: qs and red are accessed as float4.
+    __shared__ __align__(16) float qs[G][kHeadDim];
+    __shared__ __align__(16) float sc[G][kAttnChunk];
+    __shared__ __align__(16) float ml[G][2];
+    __shared__ __align__(16) float red[kAttnWarps][G * kHeadDim];
+    __shared__ int is_last;
+    const int kvh = blockIdx.x, c = blockIdx.y, n_chunks = gridDim.y, b = blockIdx.z;
+    const int ctx = pos + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    q += (static_cast<long long>(b) * n_heads + kvh * G) * kHeadDim;
+    k += (static_cast<long long>(b) * n_kv + kvh) * kHeadDim;
+    v += (static_cast<long long>(b) * n_kv + kvh) * kHeadDim;
+    kc += (static_cast<long long>(b) * n_kv + kvh) * max_ctx * kHeadDim;
+    vc += (static_cast<long long>(b) * n_kv + kvh) * max_ctx * kHeadDim;
+    part += (static_cast<long long>(b) * n_heads + kvh * G) * n_chunks * kPartStride;  // records [g][chunk]
+    const int p0 = c * kAttnChunk;
+    const int np = min(kAttnChunk, ctx - p0);
+    // The cached rows before pos were written by earlier steps: load this
+    // warp's K and V rows before waiting for the preceding kernel (the
+    // projection that produces q, k, v), so the loads overlap its tail.
+    uint2 kr[PW], vr[PW];
+#pragma unroll
+    for (int j = 0; j < PW; ++j) {
+        const int p = warp + j * kAttnWarps;
+        const bool cached = p < np && p0 + p != pos;
+        const long long off = static_cast<long long>(p0 + p) * kHeadDim + 4 * lane;
+        kr[j] = cached ? *reinterpret_cast<const uint2*>(kc + off) : make_uint2(0u, 0u);
+        vr[j] = cached ? *reinterpret_cast<const uint2*>(vc + off) : make_uint2(0u, 0u);
+    }
+    griddep_wait();
+    for (int i = threadIdx.x; i < G * HALF; i += blockDim.x) {
+        const int g = i / HALF, p = i - g * HALF;
+        const float inv_freq = exp2f(-2.0f * static_cast<float>(p) / static_cast<float>(kHeadDim) * log2_theta);
+        float s, co;
+        sincosf(static_cast<float>(pos) * inv_freq, &s, &co);
+        const float x0 = q[g * kHeadDim + 2 * p], x1 = q[g * kHeadDim + 2 * p + 1];
+        const float r0 = x0 * co - x1 * s, r1 = x0 * s + x1 * co;
+        qs[g][2 * p] = r0 * scale;
+        qs[g][2 * p + 1] = r1 * scale;
+    }
+    const bool holds_pos = c == n_chunks - 1;
+    if (holds_pos) {  // this chunk holds pos: append the rotated key and the value
+        for (int i = threadIdx.x; i < HALF + kHeadDim; i += blockDim.x) {
+            if (i < HALF) {
+                const float inv_freq =
+                    exp2f(-2.0f * static_cast<float>(i) / static_cast<float>(kHeadDim) * log2_theta);
+                float s, co;
+                sincosf(static_cast<float>(pos) * inv_freq, &s, &co);
+                const float x0 = k[2 * i], x1 = k[2 * i + 1];
+                *reinterpret_cast<__half2*>(kc + static_cast<long long>(pos) * kHeadDim + 2 * i) =
+                    __floats2half2_rn(x0 * co - x1 * s, x0 * s + x1 * co);
+            } else {
+                vc[static_cast<long long>(pos) * kHeadDim + (i - HALF)] = __float2half_rn(v[i - HALF]);
+            }
+        }
+    }
+    __syncthreads();  // the appended row and the rotated queries are visible to the CTA
+    const long long pos_off = static_cast<long long>(pos) * kHeadDim + 4 * lane;  // the appended row
+    {
+#pragma unroll
+        for (int j = 0; j < PW; ++j) {
+            const int p = warp + j * kAttnWarps;
+            const uint2 kk = p0 + p == pos ? *reinterpret_cast<const uint2*>(kc + pos_off) : kr[j];
+            const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&kk.x));
+            const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&kk.y));
+            float d[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float4 qg = *reinterpret_cast<const float4*>(&qs[g][4 * lane]);
+                d[g] = qg.x * k01.x + qg.y * k01.y + qg.z * k23.x + qg.w * k23.y;
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+#pragma unroll
+                for (int g = 0; g < G; ++g) d[g] += __shfl_xor_sync(0xffffffffu, d[g], o);
+            }
+            if (p < np) {
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    if (lane == g) sc[g][p] = d[g];
+            }
+        }
+    }
+    __syncthreads();
+    for (int g = warp; g < G; g += kAttnWarps) {  // chunk max and exp-sum per query head
+        float m = -INFINITY;
+        for (int p = lane; p < np; p += 32) m = fmaxf(m, sc[g][p]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int p = lane; p < np; p += 32) {
+            const float e = expf(sc[g][p] - m);
+            sc[g][p] = e;
+            l += e;
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) {
+            ml[g][0] = m;
+            ml[g][1] = l;
+        }
+    }
+    __syncthreads();
+    float acc[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0f;
+    {
+#pragma unroll
+        for (int j = 0; j < PW; ++j) {
+            const int p = warp + j * kAttnWarps;
+            const uint2 vv = p0 + p == pos ? *reinterpret_cast<const uint2*>(vc + pos_off) : vr[j];
+            const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vv.x));
+            const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vv.y));
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float e = p < np ? sc[g][p] : 0.0f;
+                acc[g][0] = fmaf(e, v01.x, acc[g][0]);
+                acc[g][1] = fmaf(e, v01.y, acc[g][1]);
+                acc[g][2] = fmaf(e, v23.x, acc[g][2]);
+                acc[g][3] = fmaf(e, v23.y, acc[g][3]);
+            }
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+        *reinterpret_cast<float4*>(&red[warp][g * kHeadDim + 4 * lane]) =
+            make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * kHeadDim; i += blockDim.x) {
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) o += red[w][i];
+        const int g = i / kHeadDim, d = i - g * kHeadDim;
+        float* rec = part + (static_cast<long long>(g) * n_chunks + c) * kPartStride;
+        rec[d] = o;
+        if (d == 0) {
+            rec[kHeadDim] = ml[g][0];
+            rec[kHeadDim + 1] = ml[g][1];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = atomicAdd(counters + b * n_kv + kvh, 1) == n_chunks - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    // Merge: warp g < G takes query head g; lanes first read the chunks'
+    // maxima and exp-sums (lane j: chunks j, j + 32, ...), then the lanes
+    // hold 4 output dims each and sweep the chunk records, 8 loads in flight.
+    if (threadIdx.x < 32 * G) {
+        const int g = warp;
+        const float* rec = part + static_cast<long long>(g) * n_chunks * kPartStride;
+        float M = -INFINITY;
+        for (int cc = lane; cc < n_chunks; cc += 32) M = fmaxf(M, __ldcg(rec + cc * kPartStride + kHeadDim));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float L = 0.0f;
+        float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int c0 = 0; c0 < n_chunks; c0 += 32) {
+            const int cc = c0 + lane;
+            const float w_lane = cc < n_chunks ? expf(__ldcg(rec + cc * kPartStride + kHeadDim) - M) : 0.0f;
+            if (cc < n_chunks) L = fmaf(__ldcg(rec + cc * kPartStride + kHeadDim + 1), w_lane, L);
+            const int nt = min(32, n_chunks - c0);
+#pragma unroll 8
+            for (int t = 0; t < nt; ++t) {
+                const float w = __shfl_sync(0xffffffffu, w_lane, t);
+                const float* r = rec + (c0 + t) * kPartStride + 4 * lane;
+                a.x = fmaf(__ldcg(r), w, a.x);
+                a.y = fmaf(__ldcg(r + 1), w, a.y);
+                a.z = fmaf(__ldcg(r + 2), w, a.z);
+                a.w = fmaf(__ldcg(r + 3), w, a.w);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        const float4 res = make_float4(a.x / L, a.y / L, a.z / L, a.w / L);
+        const int head = kvh * G + g;
+        if (out)
+            *reinterpret_cast<float4*>(out + (static_cast<long long>(b) * n_heads + head) * kHeadDim + 4 * lane) = res;
+        if constexpr (DIG > 0) {
+            const int kk = n_heads * kHeadDim;
+            quantize_quad<DIG>(res, true, xq + static_cast<long long>(b) * xq_row_bytes(kk, DIG), kk,
+                               head * (kHeadDim / 4) + lane);
+        }
+    }
+    if (threadIdx.x == 0) counters[b * n_kv + kvh] = 0;  // ready for the next launch
+}
+
 // out = silu(gate) * up, element-wise (the SiLU * up step of
 // quantized_matmul.cpp:2380-2412, as the fused expert kernel computes it).
 __global__ void swiglu_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ out,
@@ -438,6 +648,53 @@ int launch_attention(const float* q, const void* kc, const void* vc, float* out,
     if (!xq) e = cudaLaunchKernelEx(&cfg2, attn_combine_kernel<0>, pp, out, qx, n_chunks);
     else if (act_mode == B200Q_ACT_X8) e = cudaLaunchKernelEx(&cfg2, attn_combine_kernel<1>, pp, out, qx, n_chunks);
     else e = cudaLaunchKernelEx(&cfg2, attn_combine_kernel<2>, pp, out, qx, n_chunks);
+    return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
+}
+
+int launch_rope_attention(const float* q, const float* k, const float* v, int batch, int n_heads, int n_kv, int hd,
+                          int pos, float theta, void* kc, void* vc, int max_ctx, float* out, void* xq, int act_mode,
+                          Device* dev, cudaStream_t st) {
+    if (!q || !k || !v || !kc || !vc || (!out && !xq) || batch <= 0 || n_heads <= 0 || n_kv <= 0 || max_ctx <= 0 ||
+        !dev)
+        return B200Q_EINVAL;
+    if (xq && act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
+    if (hd != kHeadDim || n_heads % n_kv || pos < 0 || pos >= max_ctx || !(theta > 0.0f)) return B200Q_ESHAPE;
+    const int G = n_heads / n_kv;
+    if (G != 1 && G != 2 && G != 4 && G != 8) return B200Q_ESHAPE;
+    if ((reinterpret_cast<uintptr_t>(kc) & 7u) || (reinterpret_cast<uintptr_t>(vc) & 7u) || (out && !aligned16(out)) ||
+        (xq && !aligned16(xq)))
+        return B200Q_EALIGN;
+    const int n_chunks = pos / kAttnChunk + 1;
+    void* part = nullptr;
+    void* cnt = nullptr;
+    bool fresh = false;
+    int rc = scratch_for(dev, st, kScratchAttn,
+                         static_cast<size_t>(batch) * n_heads * n_chunks * kPartStride * sizeof(float), &part);
+    if (rc == B200Q_OK)
+        rc = scratch_for(dev, st, kScratchAttnCnt, static_cast<size_t>(batch) * n_kv * sizeof(int), &cnt, &fresh);
+    if (rc != B200Q_OK) return rc;
+    if (fresh && cudaMemsetAsync(cnt, 0, static_cast<size_t>(batch) * n_kv * sizeof(int), st) != cudaSuccess)
+        return B200Q_ECUDA;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(n_kv, n_chunks, batch), dim3(kAttnWarps * 32), st, attr);
+    const int dig = !xq ? 0 : (act_mode == B200Q_ACT_X8 ? 1 : 2);
+    auto go = [&](auto kern) {
+        return cudaLaunchKernelEx(&cfg, kern, q, k, v, static_cast<__half*>(kc), static_cast<__half*>(vc),
+                                  static_cast<float*>(part), static_cast<int*>(cnt), out, static_cast<uint8_t*>(xq),
+                                  n_heads, n_kv, pos, max_ctx, log2f(theta), 1.0f / sqrtf(static_cast<float>(hd)));
+    };
+    cudaError_t e = cudaErrorInvalidValue;
+#define B200Q_ATTN_CASE(GG)                                                   \
+    if (G == GG) {                                                             \
+        if (dig == 0) e = go(attn_decode_kernel<GG, 0>);                       \
+        else if (dig == 1) e = go(attn_decode_kernel<GG, 1>);                  \
+        else e = go(attn_decode_kernel<GG, 2>);                                \
+    }
+    B200Q_ATTN_CASE(1)
+    B200Q_ATTN_CASE(2)
+    B200Q_ATTN_CASE(4)
+    B200Q_ATTN_CASE(8)
+#undef B200Q_ATTN_CASE
     return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
 

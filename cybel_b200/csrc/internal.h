@@ -47,7 +47,9 @@ int gemv_from_xq(int qtype, int act_mode, const void* w, const uint8_t* xq, long
 int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev);
 // quantize_act kernel over `rows` contiguous rows of k into xq (row pitch xq_bytes_per_row).
 int launch_quantize_rows(int act_mode, const float* x, int rows, int k, uint8_t* xq, cudaStream_t st, bool pdl);
-int scratch_for(Device* dev, cudaStream_t st, int slot, size_t bytes, void** out);
+// fresh (optional): set when the buffer was (re)allocated by this call; its
+// contents are then undefined.
+int scratch_for(Device* dev, cudaStream_t st, int slot, size_t bytes, void** out, bool* fresh = nullptr);
 long long xq_bytes_per_row(int k, int act_mode);
 
 int launch_repack(int dst_qtype, const void* src, void* dst, int k, int n, cudaStream_t st);
@@ -80,7 +82,8 @@ int tile_kernel_launches(int k, int n, long long y_stride, int num_sms);
 int uses_tile_path(int qtype, int act_mode, int m);
 
 // Decode-step glue (decode.cu).
-constexpr int kScratchAttn = 6;  // attention chunk partials
+constexpr int kScratchAttn = 6;     // attention chunk partials
+constexpr int kScratchAttnCnt = 8;  // fused attention arrival counters (zero between launches)
 int launch_add_rmsnorm(float* res, const float* delta, const float* gamma, float* out, int n, int rows, float eps,
                        cudaStream_t st, void* xq = nullptr, int act_mode = 0);
 int launch_rope_kv(float* q, float* k, const float* v, int batch, int n_heads, int n_kv, int hd, int pos, float theta,
@@ -88,6 +91,10 @@ int launch_rope_kv(float* q, float* k, const float* v, int batch, int n_heads, i
 int launch_attention(const float* q, const void* kc, const void* vc, float* out, int batch, int n_heads, int n_kv,
                      int hd, int ctx, int max_ctx, Device* dev, cudaStream_t st, void* xq = nullptr,
                      int act_mode = 0);
+// RoPE + KV append + attention + chunk merge in one launch (attn_decode_kernel).
+int launch_rope_attention(const float* q, const float* k, const float* v, int batch, int n_heads, int n_kv, int hd,
+                          int pos, float theta, void* kc, void* vc, int max_ctx, float* out, void* xq, int act_mode,
+                          Device* dev, cudaStream_t st);
 int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaStream_t st);
 int launch_unshard_rows(const float* in, float* out, int shards, int rows, int cols, cudaStream_t st);
 

@@ -11,8 +11,8 @@ runs that step entirely on the device through libb200q's entry points:
 * ``b200q_matmul_xq`` -- each projection from those codes: q/k/v as one
   matrix, o with the residual add in its epilogue (beta = 1), gate/up as one
   matrix, down with the residual add, and the LM head;
-* ``b200q_rope_kv`` / ``b200q_attention_decode_q`` -- RoPE, the KV append and
-  attention, which also writes the o projection's codes;
+* ``b200q_rope_attention_decode`` -- RoPE, the KV append and attention in
+  one launch, which also writes the o projection's codes;
 * ``b200q_swiglu_q`` -- SiLU(gate) * up, written as the down projection's
   codes;
 
@@ -124,9 +124,9 @@ class DecodeStack:
     shorter list is cycled, each layer still getting its own device copy.
     On the device the q/k/v rows of a layer are stored as one matrix, and so
     are the gate/up rows, so each is one GEMV; the norms and the attention
-    write the GEMVs' activation codes directly. A layer is ten launches:
-    norm, qkv, rope, attention (2), o (+ residual), norm, gate/up, SwiGLU,
-    down (+ residual).
+    write the GEMVs' activation codes directly. A layer is eight launches:
+    norm, qkv, RoPE + attention (one fused kernel), o (+ residual), norm,
+    gate/up, SwiGLU, down (+ residual).
     """
 
     def __init__(self, shape: StackShape, max_ctx: int, layers: list[dict[str, np.ndarray]], embed: np.ndarray,
@@ -212,10 +212,9 @@ class DecodeStack:
             if not linears_only:
                 kc = self.k_cache[li].data_ptr()
                 vc = self.v_cache[li].data_ptr()
-                self._check(L.b200q_rope_kv(qp, kp, vp, 1, s.heads, s.kv_heads, hd, pos, s.rope_theta, kc, vc,
-                                            self.max_ctx, st), "rope_kv")
-                self._check(L.b200q_attention_decode_q(qp, kc, vc, None, xq_h, act, 1, s.heads, s.kv_heads, hd,
-                                                       pos + 1, self.max_ctx, st), "attention")
+                self._check(L.b200q_rope_attention_decode(qp, kp, vp, 1, s.heads, s.kv_heads, hd, pos,
+                                                          s.rope_theta, kc, vc, self.max_ctx, None, xq_h, act, st),
+                            "rope_attention")
             # o projection with the residual add in its epilogue: x = Wo a + x
             self._check(L.b200q_matmul_xq(q, act, xq_h, lay.wo.ptr, x, 1, h, h, 1.0, resid, W, st), "o_proj")
             if not linears_only:

@@ -164,9 +164,13 @@ class ShardedDecode:
                 for name, out, n in (("wq", self.q, self.q_l), ("wk", self.k, self.kv_l), ("wv", self.v, self.kv_l)):
                     ops.linear_codes(lay[name], self.xq_h, out, B, h, n)
             kc, vc = ops.cache_layer(self.k_cache, li), ops.cache_layer(self.v_cache, li)
-            ops.rope_kv(self.q, self.k, self.v, B, p.heads, p.kv_heads, hd, pos, s.rope_theta, kc, vc, self.max_ctx)
-            ops.attention(self.q, kc, vc, self.a_l, B, p.heads, p.kv_heads, hd, pos + 1, self.max_ctx)
-            self._gather(self.a, self.a_l, h // G, self.xq_h, h)
+            if G > 1:  # local heads' outputs, gathered (as codes) for the o projection
+                ops.rope_attention(self.q, self.k, self.v, B, p.heads, p.kv_heads, hd, pos, s.rope_theta, kc, vc,
+                                   self.max_ctx, self.a_l, None)
+                self._gather(self.a, self.a_l, h // G, self.xq_h, h)
+            else:  # one rank: the attention writes the o projection's codes itself
+                ops.rope_attention(self.q, self.k, self.v, B, p.heads, p.kv_heads, hd, pos, s.rope_theta, kc, vc,
+                                   self.max_ctx, None, self.xq_h)
             ops.linear_codes(lay["wo"], self.xq_h, self.o_l, B, h, h // G)
             self._gather(self.o, self.o_l, h // G)
             ops.norm_codes(self.x, self.o, lay["ffn_norm"], self.xq_h, h, B, s.eps)
@@ -356,6 +360,12 @@ class GpuOps:
     def rope_kv(self, q, k, v, batch, heads, kv_heads, hd, pos, theta, kc, vc, max_ctx):
         self._ok(self.lib.b200q_rope_kv(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, kv_heads, hd, pos,
                                         theta, kc.data_ptr(), vc.data_ptr(), max_ctx, self._st()), "rope_kv")
+
+    def rope_attention(self, q, k, v, batch, heads, kv_heads, hd, pos, theta, kc, vc, max_ctx, out, xq):
+        self._ok(self.lib.b200q_rope_attention_decode(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, kv_heads, hd, pos, theta, kc.data_ptr(),
+            vc.data_ptr(), max_ctx, None if out is None else out.data_ptr(), None if xq is None else xq.data_ptr(),
+            self.act, self._st()), "rope_attention")
 
     def attention(self, q, kc, vc, out, batch, heads, kv_heads, hd, ctx, max_ctx):
         self._ok(self.lib.b200q_attention_decode(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), batch,

@@ -253,6 +253,20 @@ B200Q_API int b200q_add_rmsnorm_q(float* residual, const float* delta, const flo
 B200Q_API int b200q_attention_decode_q(const float* q, const void* k_cache, const void* v_cache, float* out, void* xq,
                                        int act_mode, int batch, int n_heads, int n_kv_heads, int head_dim, int ctx_len,
                                        int max_ctx, void* stream);
+
+/* RoPE + KV append + attention in one launch: for each of `batch` sequences
+ * at position pos, rotates q [n_heads][head_dim] and k [n_kv_heads][head_dim]
+ * (as b200q_rope_kv, without writing q and k back), appends k and v to the
+ * caches at pos, and attends over positions 0..pos (as
+ * b200q_attention_decode with ctx_len = pos + 1). out (may be NULL when xq
+ * is given) receives [batch][n_heads][head_dim]; xq (may be NULL) the codes
+ * of the same rows (act_mode B200Q_ACT_X8 / X16). head_dim == 128,
+ * n_heads / n_kv_heads in {1, 2, 4, 8}. Replaces the MG:1222-1323 RoPE and
+ * the attention after it in the decode step. */
+B200Q_API int b200q_rope_attention_decode(const float* q, const float* k, const float* v, int batch, int n_heads,
+                                          int n_kv_heads, int head_dim, int pos, float theta, void* k_cache,
+                                          void* v_cache, int max_ctx, float* out, void* xq, int act_mode,
+                                          void* stream);
 B200Q_API int b200q_swiglu_q(const float* gate, const float* up, void* xq, int act_mode, int n, void* stream);
 
 /* y = alpha * (W x) + beta * y for m activation rows given as codes written

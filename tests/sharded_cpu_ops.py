@@ -93,6 +93,14 @@ class NumpyOps:
                 e = np.exp(sc - sc.max())
                 out[(b * heads + h) * hd:(b * heads + h + 1) * hd] = (e / e.sum()) @ vc[b, h // G, :ctx]
 
+    def rope_attention(self, q, k, v, batch, heads, kv_heads, hd, pos, theta, kc, vc, max_ctx, out, xq):
+        q, k = q.copy(), k.copy()  # the fused kernel rotates without writing q and k back
+        self.rope_kv(q, k, v, batch, heads, kv_heads, hd, pos, theta, kc, vc, max_ctx)
+        o = out if out is not None else np.zeros(batch * heads * hd)
+        self.attention(q, kc, vc, o, batch, heads, kv_heads, hd, pos + 1, max_ctx)
+        if xq is not None:
+            self.quantize(o, xq, batch, heads * hd)
+
     def swiglu(self, g, u, out, n):
         out[:n] = g[:n] / (1.0 + np.exp(-g[:n])) * u[:n]
 

@@ -256,3 +256,67 @@ def test_quantized_outputs_of_norm_attention_swiglu(digits):
     assert L.b200q_swiglu_q(g.data_ptr(), u.data_ptr(), xqf.data_ptr(), digits, f, st) == 0
     torch.cuda.synchronize()
     _check_codes(xqf.cpu().numpy(), hf.cpu().numpy(), digits)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("batch,H,KV,pos", [(1, 32, 8, 2047), (1, 64, 8, 300), (2, 8, 8, 63), (3, 16, 8, 64),
+                                            (1, 8, 4, 0), (2, 4, 2, 129)])
+def test_rope_attention_fused_matches_two_step_path(batch, H, KV, pos):
+    """b200q_rope_attention_decode (one launch) against b200q_rope_kv +
+    b200q_attention_decode on copies of the same inputs: same caches (the
+    appended value row bit for bit), outputs within 1e-5 relative (fp32 merge
+    order differs), the o projection's codes those of its own output; two
+    launches in a row (the arrival counters reset themselves)."""
+    import torch
+    from cybel_b200 import _native
+
+    L = _native.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    rng = np.random.default_rng(batch * 1000 + H + pos)
+    hd, max_ctx = 128, pos + 70
+    q = torch.from_numpy(rng.standard_normal(batch * H * hd).astype(np.float32)).cuda()
+    k = torch.from_numpy(rng.standard_normal(batch * KV * hd).astype(np.float32)).cuda()
+    v = torch.from_numpy(rng.standard_normal(batch * KV * hd).astype(np.float32)).cuda()
+    kc = torch.from_numpy(rng.standard_normal((batch, KV, max_ctx, hd)).astype(np.float16)).cuda()
+    vc = torch.from_numpy(rng.standard_normal((batch, KV, max_ctx, hd)).astype(np.float16)).cuda()
+    kc2, vc2, q2, k2 = kc.clone(), vc.clone(), q.clone(), k.clone()
+    out = torch.empty(batch * H * hd, device="cuda")
+    ref = torch.empty(batch * H * hd, device="cuda")
+    xq = torch.zeros(batch * int(L.b200q_xq_row_bytes(H * hd, 2)), dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        assert L.b200q_rope_attention_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, H, KV, hd, pos, 5e5,
+                                             kc.data_ptr(), vc.data_ptr(), max_ctx, out.data_ptr(), xq.data_ptr(), 2,
+                                             st) == 0
+    assert L.b200q_rope_kv(q2.data_ptr(), k2.data_ptr(), v.data_ptr(), batch, H, KV, hd, pos, 5e5, kc2.data_ptr(),
+                           vc2.data_ptr(), max_ctx, st) == 0
+    assert L.b200q_attention_decode(q2.data_ptr(), kc2.data_ptr(), vc2.data_ptr(), ref.data_ptr(), batch, H, KV, hd,
+                                    pos + 1, max_ctx, st) == 0
+    torch.cuda.synchronize()
+    assert L.b200q_device_status(torch.cuda.current_device()) == 0
+    assert torch.equal(vc, vc2)
+    # the rotated key: the same fp32 formula in both kernels, so at most an
+    # fp16 rounding step apart if the compiler contracts them differently
+    assert torch.allclose(kc.float(), kc2.float(), rtol=1e-3, atol=1e-3)
+    got, want = out.cpu().numpy(), ref.cpu().numpy()
+    assert _rel(got, want) <= 1e-5
+    rb = int(L.b200q_xq_row_bytes(H * hd, 2))
+    codes = xq.cpu().numpy()
+    for b in range(batch):
+        _check_codes(codes[b * rb:(b + 1) * rb], got[b * H * hd:(b + 1) * H * hd], 2)
+
+
+@pytest.mark.gpu
+def test_rope_attention_rejects_bad_shapes():
+    import torch
+    from cybel_b200 import _native
+
+    L = _native.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    buf = torch.zeros(1 << 20, device="cuda")
+    p = buf.data_ptr()
+    assert L.b200q_rope_attention_decode(p, p, p, 1, 12, 4, 128, 5, 1e4, p, p, 64, p, None, 0, st) == -3  # G = 3
+    assert L.b200q_rope_attention_decode(p, p, p, 1, 8, 8, 64, 5, 1e4, p, p, 64, p, None, 0, st) == -3  # head_dim
+    assert L.b200q_rope_attention_decode(p, p, p, 1, 8, 8, 128, 64, 1e4, p, p, 64, p, None, 0, st) == -3  # pos
+    assert L.b200q_rope_attention_decode(p, p, p, 1, 8, 8, 128, 5, 1e4, p, p, 64, None, None, 0, st) == -1
+    torch.cuda.synchronize()
+    assert L.b200q_device_status(torch.cuda.current_device()) == 0
