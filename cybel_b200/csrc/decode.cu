@@ -98,6 +98,75 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
     }
 }
 
+// The same for n <= 4 * 4 * kNormThreads with the row held in registers:
+// residual, delta and gamma are loaded together once (one round trip
+// instead of a second pass over the residual after the reduction).
+constexpr int kNormRegVec = 4;  // float4 per thread
+template <int DIG>
+__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_reg_kernel(float* __restrict__ res,
+                                                                       const float* __restrict__ delta,
+                                                                       const float* __restrict__ gamma,
+                                                                       float* __restrict__ out,
+                                                                       uint8_t* __restrict__ xq, int n, float eps) {
+    griddep_launch_dependents();
+    griddep_wait();
+    res += static_cast<long long>(blockIdx.x) * n;
+    if (out) out += static_cast<long long>(blockIdx.x) * n;
+    if (delta) delta += static_cast<long long>(blockIdx.x) * n;
+    if (DIG) xq += static_cast<long long>(blockIdx.x) * xq_row_bytes(n, DIG);
+    __shared__ float red[kNormThreads / 32];
+    float4 r[kNormRegVec], g[kNormRegVec];
+#pragma unroll
+    for (int u = 0; u < kNormRegVec; ++u) {
+        const int i = 4 * (threadIdx.x + u * kNormThreads);
+        const bool valid = i < n;
+        r[u] = valid ? *reinterpret_cast<const float4*>(res + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        g[u] = valid ? *reinterpret_cast<const float4*>(gamma + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (delta && valid) {
+            const float4 d = *reinterpret_cast<const float4*>(delta + i);
+            r[u].x += d.x;
+            r[u].y += d.y;
+            r[u].z += d.z;
+            r[u].w += d.w;
+        }
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int u = 0; u < kNormRegVec; ++u) {
+        const int i = 4 * (threadIdx.x + u * kNormThreads);
+        if (delta && i < n) *reinterpret_cast<float4*>(res + i) = r[u];
+        ss = fmaf(r[u].x, r[u].x, ss);
+        ss = fmaf(r[u].y, r[u].y, ss);
+        ss = fmaf(r[u].z, r[u].z, ss);
+        ss = fmaf(r[u].w, r[u].w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < kNormThreads / 32 ? red[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float inv_rms = 1.0f / sqrtf(red[0] / static_cast<float>(n) + eps);
+#pragma unroll
+    for (int u = 0; u < kNormRegVec; ++u) {
+        const int i = 4 * (threadIdx.x + u * kNormThreads);
+        const bool valid = i < n;
+        const float4 o = valid ? make_float4(r[u].x * inv_rms * g[u].x, r[u].y * inv_rms * g[u].y,
+                                             r[u].z * inv_rms * g[u].z, r[u].w * inv_rms * g[u].w)
+                               : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (out && valid) *reinterpret_cast<float4*>(out + i) = o;
+        if constexpr (DIG > 0) {
+            // n % 128 == 0: a warp's 128 elements are all in range or all out.
+            if (i - 4 * (threadIdx.x & 31) < n) quantize_quad<DIG>(o, valid, xq, n, i >> 2);
+        }
+    }
+}
+
 // Threads [0, (n_heads + n_kv) * hd/2): one rotation pair each; threads
 // [that, + n_kv * hd): one v element each. blockIdx.y = sequence of the
 // batch (its own q/k/v rows and cache).
@@ -601,9 +670,18 @@ int launch_add_rmsnorm(float* res, const float* delta, const float* gamma, float
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(rows), dim3(kNormThreads), st, attr);
     uint8_t* q = static_cast<uint8_t*>(xq);
     cudaError_t e;
-    if (!xq) e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<0>, res, delta, gamma, out, q, n, eps);
-    else if (act_mode == B200Q_ACT_X8) e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<1>, res, delta, gamma, out, q, n, eps);
-    else e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<2>, res, delta, gamma, out, q, n, eps);
+    if (n <= 4 * kNormRegVec * kNormThreads) {
+        if (!xq) e = cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<0>, res, delta, gamma, out, q, n, eps);
+        else if (act_mode == B200Q_ACT_X8)
+            e = cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<1>, res, delta, gamma, out, q, n, eps);
+        else e = cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<2>, res, delta, gamma, out, q, n, eps);
+    } else if (!xq) {
+        e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<0>, res, delta, gamma, out, q, n, eps);
+    } else if (act_mode == B200Q_ACT_X8) {
+        e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<1>, res, delta, gamma, out, q, n, eps);
+    } else {
+        e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<2>, res, delta, gamma, out, q, n, eps);
+    }
     return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
 
