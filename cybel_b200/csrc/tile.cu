@@ -149,11 +149,6 @@ __host__ __device__ constexpr uint32_t idesc_f16(int n) {
     return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(kTileRows >> 4) << 24);
 }
 
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
-
 // Nibbles in place as fp16: OR-ing 0x6400 (1024.0) into a half whose low
 // bits hold a nibble code q gives 1024 + q (bits 0-3) or 1024 + 16 q (bits
 // 4-7), exactly. One AND-OR per pair of codes; then
@@ -330,7 +325,7 @@ __global__ void __launch_bounds__(tile_threads(NP), 1)
     } else if (warp == kXWarp) {
         // ---------------- activation producer ----------------
         if (lane == 0) {
-            griddep_wait();  // the activation chunks and B2 tiles come from the preceding prep kernels
+            griddep_wait();  // the activation chunks and B2 tiles come from the preceding prep kernel
             for (int bl = 0; bl < nblk && ok; ++bl) {
                 const int xs = bl % NSX;
                 ok = mbar_wait_bounded(smem_addr(xfree + xs), ((bl / NSX) & 1) ^ 1);
@@ -539,74 +534,62 @@ __global__ void __launch_bounds__(tile_threads(NP), 1)
 }
 
 // Activation rows (fp32, m rows of k at stride x_stride) -> fp16 chunks in
-// the UMMA K-major canonical layout: chunk c holds K elements [256c,
-// 256c+256) of NP rows (rows >= m are zero): row r, K group j (8 elements),
-// element e at byte j * NP*16 + (r / 8) * 128 + (r % 8) * 16 + 2 pos(e), where
-// pos swaps elements 1 and 2 of each group of 4 (the order in which the
-// dequantizers pair nibbles). With PREC the rounding residues
-// fp16(x - fp16(x)) follow as K groups 32..63.
+// the UMMA K-major canonical layout, and the per-block sub-block sums (B2),
+// in one pass. Chunk c holds K elements [256c, 256c+256) of NP rows (rows >=
+// m are zero): row r, K group j (8 elements), element e at byte
+// j * NP*16 + (r / 8) * 128 + (r % 8) * 16 + 2 pos(e), where pos swaps
+// elements 1 and 2 of each group of 4 (the order in which the dequantizers
+// pair nibbles). With PREC the rounding residues fp16(x - fp16(x)) follow as
+// K groups 32..63. B2 of block c, row r: K group 0 = the 8 sub-block sums
+// sx_j of the fp16 activations the MMAs see (plus the residues with PREC),
+// rounded to fp16 (hi), K group 1 = their fp16 remainders (lo).
+// Thread (c, r, j): four consecutive threads cover one 32-element sub-block
+// of row r and add their partial sums with two shuffles.
 template <int NP, bool PREC>
 __global__ void prep_x_kernel(const float* __restrict__ x, long long x_stride, int m, int k,
-                              uint8_t* __restrict__ xc) {
+                              uint8_t* __restrict__ xc, uint8_t* __restrict__ b2) {
     griddep_launch_dependents();
     griddep_wait();
-    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;  // one (K group, row)
-    const long long groups = static_cast<long long>(k / 8) * NP;
-    if (i >= groups) return;
-    const int r = static_cast<int>(i % NP);
-    const long long g8 = i / NP;  // global K group
-    const int c = static_cast<int>(g8 >> 5), j = static_cast<int>(g8 & 31);
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const long long groups = static_cast<long long>(k / 8) * NP;  // a multiple of 32 (k % 256 == 0)
+    if (i >= groups) return;                                        // whole warps
+    const int j = static_cast<int>(i & 31);                         // K group within the block
+    const int r = static_cast<int>((i >> 5) % NP);
+    const long long c = (i >> 5) / NP;                              // block / chunk
     uint32_t hw[4] = {0u, 0u, 0u, 0u}, lw[4] = {0u, 0u, 0u, 0u};
+    float part = 0.0f;
     if (r < m) {
-        const float* src = x + static_cast<long long>(r) * x_stride + g8 * 8;
+        const float* src = x + static_cast<long long>(r) * x_stride + c * 256 + j * 8;
         const float4 a = __ldg(reinterpret_cast<const float4*>(src));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(src + 4));
+        const float4 bq = __ldg(reinterpret_cast<const float4*>(src + 4));
         // K order within each group of 4 is (0, 2, 1, 3), as in the A columns.
-        const float v[8] = {a.x, a.z, a.y, a.w, b.x, b.z, b.y, b.w};
+        const float v[8] = {a.x, a.z, a.y, a.w, bq.x, bq.z, bq.y, bq.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const __half2 hh = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
             hw[e] = *reinterpret_cast<const uint32_t*>(&hh);
+            const float2 hf = __half22float2(hh);
+            part += hf.x + hf.y;
             if constexpr (PREC) {
-                const float2 hf = __half22float2(hh);
-                lw[e] = pack_h2(v[2 * e] - hf.x, v[2 * e + 1] - hf.y);
+                const __half2 ll = __floats2half2_rn(v[2 * e] - hf.x, v[2 * e + 1] - hf.y);
+                lw[e] = *reinterpret_cast<const uint32_t*>(&ll);
+                const float2 lf = __half22float2(ll);
+                part += lf.x + lf.y;
             }
         }
     }
-    uint8_t* dst = xc + static_cast<long long>(c) * xchunk_bytes(NP, PREC) + j * (NP * 16) + (r >> 3) * 128 + (r & 7) * 16;
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    uint8_t* dst = xc + c * xchunk_bytes(NP, PREC) + j * (NP * 16) + (r >> 3) * 128 + (r & 7) * 16;
     *reinterpret_cast<uint4*>(dst) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     if constexpr (PREC) *reinterpret_cast<uint4*>(dst + 32 * (NP * 16)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-}
-
-// Per block and row: the 8 sub-block sums sx_j of the fp16 activations the
-// MMAs see (fp16(x), plus the residues with PREC), summed in fp32 in element
-// order, stored as fp16 hi and lo parts: K group 0 = hi, K group 1 = lo.
-template <int NP, bool PREC>
-__global__ void prep_b2_kernel(const float* __restrict__ x, long long x_stride, int m, int k,
-                               uint8_t* __restrict__ b2) {
-    griddep_launch_dependents();
-    griddep_wait();
-    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;  // one (block, row, sub-block)
-    const long long total = static_cast<long long>(k / 256) * NP * 8;
-    if (i >= total) return;
-    const int jsb = static_cast<int>(i & 7);
-    const int r = static_cast<int>((i >> 3) % NP);
-    const long long bl = (i >> 3) / NP;
-    float sx = 0.0f;
-    if (r < m) {
-        const float* src = x + static_cast<long long>(r) * x_stride + bl * 256 + jsb * 32;
-#pragma unroll 8
-        for (int e = 0; e < 32; ++e) {
-            const float v = __ldg(src + e);
-            const float hv = __half2float(__float2half_rn(v));
-            sx += PREC ? hv + __half2float(__float2half_rn(v - hv)) : hv;
-        }
+    if ((j & 3) == 0) {
+        const __half hi = __float2half_rn(part);
+        const __half lo = __float2half_rn(part - __half2float(hi));
+        uint8_t* base = b2 + c * b2_bytes(NP) + (r >> 3) * 128 + (r & 7) * 16 + (j >> 2) * 2;
+        *reinterpret_cast<__half*>(base) = hi;
+        *reinterpret_cast<__half*>(base + NP * 16) = lo;
     }
-    const __half hi = __float2half_rn(sx);
-    const __half lo = __float2half_rn(sx - __half2float(hi));
-    uint8_t* base = b2 + bl * b2_bytes(NP) + (r >> 3) * 128 + (r & 7) * 16 + jsb * 2;
-    *reinterpret_cast<__half*>(base) = hi;
-    *reinterpret_cast<__half*>(base + NP * 16) = lo;
 }
 
 // y[m][row] = sum over splits of part[split][m][row], in split order.
@@ -709,13 +692,8 @@ int launch_np(const void* w, const float* x, long long x_stride, float* y, int m
     {
         const long long groups = static_cast<long long>(k / 8) * NP;
         cudaLaunchConfig_t c = cfg_of(dim3(static_cast<unsigned>((groups + 255) / 256)), dim3(256), 0, st, pdl, attr);
-        if (cudaLaunchKernelEx(&c, prep_x_kernel<NP, PREC>, x, x_stride, m, k, static_cast<uint8_t*>(xc)) !=
-            cudaSuccess)
-            return B200Q_ECUDA;
-        const long long sums = static_cast<long long>(nblocks) * NP * 8;
-        cudaLaunchConfig_t c2 = cfg_of(dim3(static_cast<unsigned>((sums + 255) / 256)), dim3(256), 0, st, pdl, attr);
-        if (cudaLaunchKernelEx(&c2, prep_b2_kernel<NP, PREC>, x, x_stride, m, k, static_cast<uint8_t*>(b2)) !=
-            cudaSuccess)
+        if (cudaLaunchKernelEx(&c, prep_x_kernel<NP, PREC>, x, x_stride, m, k, static_cast<uint8_t*>(xc),
+                               static_cast<uint8_t*>(b2)) != cudaSuccess)
             return B200Q_ECUDA;
     }
     {
@@ -745,7 +723,7 @@ int launch_np(const void* w, const float* x, long long x_stride, float* y, int m
 }  // namespace
 
 int tile_kernel_launches(int k, int n, long long y_stride, int num_sms) {
-    return (splits_for(k, n, num_sms) == 1 && y_stride == n) ? 3 : 4;
+    return (splits_for(k, n, num_sms) == 1 && y_stride == n) ? 2 : 3;
 }
 
 int tile_max_rows(bool precise) { return precise ? 64 : kTileMaxM; }
