@@ -179,8 +179,11 @@ class ShardedDecode:
             else:
                 ops.linear_codes(lay["w_gate"], self.xq_h, self.g_l, B, h, self.f_l)
                 ops.linear_codes(lay["w_up"], self.xq_h, self.u_l, B, h, self.f_l)
-            ops.swiglu(self.g_l, self.u_l, self.f_l_buf, B * self.f_l)
-            self._gather(self.f, self.f_l_buf, self.f_l, self.xq_f, s.ffn)
+            if G == 1 and B == 1:  # one rank: SwiGLU writes the down projection's codes itself
+                ops.swiglu_codes(self.g_l, self.u_l, self.xq_f, self.f_l)
+            else:
+                ops.swiglu(self.g_l, self.u_l, self.f_l_buf, B * self.f_l)
+                self._gather(self.f, self.f_l_buf, self.f_l, self.xq_f, s.ffn)
             ops.linear_codes(lay["w_down"], self.xq_f, self.d_l, B, s.ffn, h // G)
             self._gather(self.d, self.d_l, h // G)
             delta = self.d
@@ -370,6 +373,10 @@ class GpuOps:
     def attention(self, q, kc, vc, out, batch, heads, kv_heads, hd, ctx, max_ctx):
         self._ok(self.lib.b200q_attention_decode(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), batch,
                                                  heads, kv_heads, hd, ctx, max_ctx, self._st()), "attention")
+
+    def swiglu_codes(self, g, u, xq, n):
+        self._ok(self.lib.b200q_swiglu_q(g.data_ptr(), u.data_ptr(), xq.data_ptr(), self.act, n, self._st()),
+                 "swiglu_q")
 
     def swiglu(self, g, u, out, n):
         self._ok(self.lib.b200q_swiglu(g.data_ptr(), u.data_ptr(), out.data_ptr(), n, self._st()), "swiglu")

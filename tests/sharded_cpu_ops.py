@@ -101,6 +101,11 @@ class NumpyOps:
         if xq is not None:
             self.quantize(o, xq, batch, heads * hd)
 
+    def swiglu_codes(self, g, u, xq, n):
+        f = np.zeros(n)
+        self.swiglu(g, u, f, n)
+        self.quantize(f, xq, 1, n)
+
     def swiglu(self, g, u, out, n):
         out[:n] = g[:n] / (1.0 + np.exp(-g[:n])) * u[:n]
 
