@@ -39,10 +39,19 @@ int env_int(const char* name, int dflt) {
     return v > 0 ? v : dflt;
 }
 
-constexpr int kSmemBudget = 220 * 1024;   // ring + bookkeeping per CTA
-constexpr int kStageTargetKB = 48;        // preferred bytes per stage (KB)
+// Ring + bookkeeping per CTA (one CTA per SM; B200Q_GEMV_SMEM_KB overrides).
+constexpr int kSmemBudgetKB = 220;
+// Preferred bytes per stage (B200Q_STAGE_KB overrides). Walker groups take
+// alternate stages, so a stage is a unit of work for a group, not for all
+// warps; below ~16 KB the bulk copies in flight per SM (limited in number)
+// no longer cover the HBM latency.
+constexpr int kStageTargetKB = 32;
 constexpr int kStageMax = 96 * 1024;      // largest stage
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 48;
+// Weight bytes issued before the consumers have issued their activation
+// loads (B200Q_GEMV_PREFETCH_KB): about what HBM delivers to one SM while the
+// CTA waits for the preceding kernel.
+constexpr int kPrefetchKB = 48;
 
 struct Plan {
     GemvParams p;
@@ -51,7 +60,8 @@ struct Plan {
     int grid;
 };
 
-int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl) {
+// fq: the GEMV quantizes fp32 activations itself (transpose tiles staged too).
+int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl, bool fq = false) {
     FmtInfo f;
     if (!fmt_info(qtype, f)) return B200Q_EQTYPE;
     if (k <= 0 || n <= 0) return B200Q_EINVAL;
@@ -61,28 +71,48 @@ int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl) {
     const int S = (nb + f.blocks_per_slice - 1) / f.blocks_per_slice;
     const int max_warps = (dig == 1 && MR == 1) ? 16 : 12;  // kGemvWarps in gemv.cuh
     if (S > max_warps) return B200Q_ESHAPE;
-    const int U = MR == 1 ? 2 : 1;  // kRowsPerIter in gemv.cuh
-    // Stage = WR walkers x U rows (x4-row groups for R4); walkers are capped
-    // so a stage stays near the target size (B200Q_STAGE_KB overrides it).
+    static const int smem_budget = std::min(220, env_int("B200Q_GEMV_SMEM_KB", kSmemBudgetKB)) * 1024;
     static const int target = env_int("B200Q_STAGE_KB", kStageTargetKB) * 1024;
-    int WR = std::max(1, max_warps / S);
-    while (WR > 1 && static_cast<long long>(WR) * U * rb > target) --WR;
+    static const int prefetch = env_int("B200Q_GEMV_PREFETCH_KB", kPrefetchKB) * 1024;
+    static const int hold = env_int("B200Q_GEMV_HOLD", 2) == 1 ? 1 : 0;
+    const int U = MR == 1 ? 2 : 1;  // kRowsPerIter in gemv.cuh
+    const int walkers = std::max(1, max_warps / S);
+    const int n_quads = (n + 3) / 4;
+    const int grid = std::min(num_sms, n_quads);
+    const int rows_cta = 4 * ((n_quads + grid - 1) / grid);
+    // Rows per stage: whole U-row steps (whole 4-row groups for R4) totalling
+    // about `target` bytes, but no more than the CTA's rows.
+    int R = U * static_cast<int>(std::max<long long>(1, (target + U * rb / 2) / (U * rb)));
+    R = std::min(R, std::max(U, (rows_cta + U - 1) / U * U));
+    if (f.r4) R = (R + 3) / 4 * 4;
+    // One walker per U rows of a stage, then as many groups as that leaves.
+    const int SW = std::max(1, std::min(walkers, (R + U - 1) / U));
+    const int G = std::max(1, walkers / SW);
+    const int WR = G * SW;
     // A stage copies the 16-byte-aligned window around its rows: at most
     // rows * rb + 30 bytes; kSlotPad also covers the 4-byte over-read of the
     // unaligned word loads.
     constexpr int kSlotPad = 48;
-    int R = f.r4 ? ((WR * U + 3) / 4) * 4 : WR * U;
     if (R * rb + kSlotPad > kStageMax) {
         R = f.r4 ? 4 : std::max<int>(1, static_cast<int>((kStageMax - kSlotPad) / rb));
         if (R * rb + kSlotPad > kStageMax) return B200Q_ESHAPE;
     }
     const int stage_stride = static_cast<int>(((R * rb + kSlotPad) + 127) / 128 * 128);
-    const int n_quads = (n + 3) / 4;
-    const int grid = std::min(num_sms, n_quads);
-    const int rows_cta = 4 * ((n_quads + grid - 1) / grid);
     const int part_bytes = rows_cta * MR * S * 4;
-    int NS = std::min(kMaxStages, (kSmemBudget - part_bytes - 64) / (stage_stride + 16));
+    const int ns_fit = (smem_budget - part_bytes - 64) / (stage_stride + 16);
+    int NS = std::min(kMaxStages, ns_fit);
+    // The staged activations occupy the last bytes of the ring; only slots
+    // below them are filled before the activations are in registers. Small
+    // stages get more slots, so the ring still holds them with a slot to spare.
+    const long long x_bytes =
+        static_cast<long long>(MR) * xs_row_bytes(k, dig) + (fq ? static_cast<long long>(S * WR) * kFqWarpBytes : 0);
+    NS = static_cast<int>(
+        std::max<long long>(NS, std::min<long long>(ns_fit, (x_bytes + stage_stride - 1) / stage_stride + 1)));
     if (NS < 2) return B200Q_ESHAPE;
+    const long long ring = static_cast<long long>(NS) * stage_stride;
+    if (x_bytes > ring) return B200Q_ESHAPE;
+    const int x_off = static_cast<int>((ring - x_bytes) / 128 * 128);
+    const int PD = std::min(std::max(1, prefetch / stage_stride), x_off / stage_stride);
     GemvParams& p = pl.p;
     p = GemvParams{};
     p.row_bytes = rb;
@@ -91,20 +121,25 @@ int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl) {
     p.nb = nb;
     p.S = S;
     p.WR = WR;
+    p.G = G;
+    p.SW = SW;
     p.R = R;
     p.NS = NS;
     p.stage_stride = stage_stride;
+    p.PD = PD;
+    p.pd_hold = hold;
+    p.x_off = x_off;
     p.n_quads = n_quads;
     p.rows_cta = rows_cta;
     pl.threads = (S * WR + 1) * 32;
-    pl.smem = NS * stage_stride + 2 * NS * 8 + part_bytes + 16;
+    pl.smem = NS * stage_stride + (2 * NS + 2) * 8 + part_bytes + 16;
     pl.grid = grid;
     return B200Q_OK;
 }
 
-template <int QT, int DIG, int MR, bool DBG>
+template <int QT, int DIG, int MR, bool DBG, bool FQ>
 cudaError_t launch_kernel(const Plan& pl, cudaStream_t st, bool pdl) {
-    auto kern = gemv_kernel<QT, DIG, MR, DBG>;
+    auto kern = gemv_kernel<QT, DIG, MR, DBG, FQ>;
     // Raise the dynamic shared-memory limit once per kernel instance (the
     // attribute is per function; the largest plan is set).
     static std::mutex mu;
@@ -140,32 +175,34 @@ int max_rows_per_launch(int qtype, int dig) {
     return q4k ? 1 : 2;
 }
 
-template <int QT>
+template <int QT, bool FQ>
 cudaError_t dispatch_qt(int dig, int MR, bool dbg, const Plan& pl, cudaStream_t st, bool pdl) {
     constexpr bool q4k = QT == QT_Q4_K || QT == QT_Q4_K_R4;
-    if (dbg) return dig == 1 ? launch_kernel<QT, 1, 1, true>(pl, st, pdl) : launch_kernel<QT, 2, 1, true>(pl, st, pdl);
+    if (dbg)
+        return dig == 1 ? launch_kernel<QT, 1, 1, true, FQ>(pl, st, pdl) : launch_kernel<QT, 2, 1, true, FQ>(pl, st, pdl);
     if (dig == 1) {
         if constexpr (!q4k) {
-            if (MR == 4) return launch_kernel<QT, 1, 4, false>(pl, st, pdl);
+            if (MR == 4) return launch_kernel<QT, 1, 4, false, FQ>(pl, st, pdl);
         }
-        if (MR == 2) return launch_kernel<QT, 1, 2, false>(pl, st, pdl);
-        return launch_kernel<QT, 1, 1, false>(pl, st, pdl);
+        if (MR == 2) return launch_kernel<QT, 1, 2, false, FQ>(pl, st, pdl);
+        return launch_kernel<QT, 1, 1, false, FQ>(pl, st, pdl);
     }
     if constexpr (!q4k) {
-        if (MR == 2) return launch_kernel<QT, 2, 2, false>(pl, st, pdl);
+        if (MR == 2) return launch_kernel<QT, 2, 2, false, FQ>(pl, st, pdl);
     }
-    return launch_kernel<QT, 2, 1, false>(pl, st, pdl);
+    return launch_kernel<QT, 2, 1, false, FQ>(pl, st, pdl);
 }
 
+template <bool FQ>
 cudaError_t dispatch(int qtype, int dig, int MR, bool dbg, const Plan& pl, cudaStream_t st, bool pdl) {
     switch (qtype) {
-        case QT_Q4_K: return dispatch_qt<QT_Q4_K>(dig, MR, dbg, pl, st, pdl);
-        case QT_Q4_K_R4: return dispatch_qt<QT_Q4_K_R4>(dig, MR, dbg, pl, st, pdl);
-        case QT_Q6_K: return dispatch_qt<QT_Q6_K>(dig, MR, dbg, pl, st, pdl);
-        case QT_Q6_K_R4: return dispatch_qt<QT_Q6_K_R4>(dig, MR, dbg, pl, st, pdl);
-        case QT_Q6_K_LM: return dispatch_qt<QT_Q6_K_LM>(dig, MR, dbg, pl, st, pdl);
-        case QT_Q8_0: return dispatch_qt<QT_Q8_0>(dig, MR, dbg, pl, st, pdl);
-        case QT_Q4_0: return dispatch_qt<QT_Q4_0>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q4_K: return dispatch_qt<QT_Q4_K, FQ>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q4_K_R4: return dispatch_qt<QT_Q4_K_R4, FQ>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q6_K: return dispatch_qt<QT_Q6_K, FQ>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q6_K_R4: return dispatch_qt<QT_Q6_K_R4, FQ>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q6_K_LM: return dispatch_qt<QT_Q6_K_LM, FQ>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q8_0: return dispatch_qt<QT_Q8_0, FQ>(dig, MR, dbg, pl, st, pdl);
+        case QT_Q4_0: return dispatch_qt<QT_Q4_0, FQ>(dig, MR, dbg, pl, st, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -254,12 +291,18 @@ int quantize_activations(int act_mode, const float* x, long long x_stride, int m
     return B200Q_OK;
 }
 
-int gemv_from_xq(int qtype, int act_mode, const void* w, const uint8_t* xq, long long xq_row, float* y, int m, int k,
-                 int n, long long y_stride, float alpha, float beta, int32_t* isums, Device* dev, cudaStream_t st,
-                 bool pdl, int flags) {
-    if (!w || !xq || !y || m <= 0 || k <= 0 || n <= 0 || !dev) return B200Q_EINVAL;
+namespace {
+
+// y = alpha * (W x) + beta * y over m activation rows in chunks of at most
+// max_rows_per_launch rows: from codes (xq, quantized by a preceding kernel)
+// or, when xf is given, from fp32 rows that the GEMV quantizes itself.
+int gemv_rows(int qtype, int act_mode, const void* w, const uint8_t* xq, long long xq_row, const float* xf,
+              long long xf_stride, float* y, int m, int k, int n, long long y_stride, float alpha, float beta,
+              int32_t* isums, Device* dev, cudaStream_t st, bool pdl, int flags) {
+    if (!w || (!xq && !xf) || !y || m <= 0 || k <= 0 || n <= 0 || !dev) return B200Q_EINVAL;
     if (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
     if (reinterpret_cast<uintptr_t>(w) & 15u) return B200Q_EALIGN;
+    if (xf && ((reinterpret_cast<uintptr_t>(xf) & 15u) || (xf_stride & 3))) return B200Q_EALIGN;
     if (isums && m != 1) return B200Q_EINVAL;
     const int dig = act_mode == B200Q_ACT_X8 ? 1 : 2;
     const int mr_max = max_rows_per_launch(qtype, dig);
@@ -267,11 +310,16 @@ int gemv_from_xq(int qtype, int act_mode, const void* w, const uint8_t* xq, long
         const int left = m - m0;
         const int MR = isums ? 1 : (left >= mr_max ? mr_max : (left >= 2 && mr_max >= 2 ? 2 : 1));
         Plan pl;
-        const int rc = make_plan(qtype, dig, k, n, MR, dev->num_sms, pl);
+        const int rc = make_plan(qtype, dig, k, n, MR, dev->num_sms, pl, xf != nullptr);
         if (rc != B200Q_OK) return rc;
         pl.p.W = static_cast<const uint8_t*>(w);
-        pl.p.xq = xq + m0 * xq_row;
-        pl.p.xq_stride = xq_row;
+        if (xf) {
+            pl.p.xf = xf + m0 * xf_stride;
+            pl.p.xf_stride = xf_stride;
+        } else {
+            pl.p.xq = xq + m0 * xq_row;
+            pl.p.xq_stride = xq_row;
+        }
         pl.p.y = y + m0 * y_stride;
         pl.p.y_stride = y_stride;
         pl.p.dbg = isums;
@@ -279,11 +327,30 @@ int gemv_from_xq(int qtype, int act_mode, const void* w, const uint8_t* xq, long
         pl.p.w_static = (flags & B200Q_WEIGHTS_STATIC) ? 1 : 0;
         pl.p.alpha = alpha;
         pl.p.beta = beta;
-        const cudaError_t e = dispatch(qtype, dig, MR, isums != nullptr, pl, st, pdl);
+        const cudaError_t e = xf ? dispatch<true>(qtype, dig, MR, isums != nullptr, pl, st, pdl)
+                                 : dispatch<false>(qtype, dig, MR, isums != nullptr, pl, st, pdl);
         if (e != cudaSuccess) return B200Q_ECUDA;
         m0 += MR;
     }
     return B200Q_OK;
+}
+
+}  // namespace
+
+int gemv_from_xq(int qtype, int act_mode, const void* w, const uint8_t* xq, long long xq_row, float* y, int m, int k,
+                 int n, long long y_stride, float alpha, float beta, int32_t* isums, Device* dev, cudaStream_t st,
+                 bool pdl, int flags) {
+    if (!xq) return B200Q_EINVAL;
+    return gemv_rows(qtype, act_mode, w, xq, xq_row, nullptr, 0, y, m, k, n, y_stride, alpha, beta, isums, dev, st,
+                     pdl, flags);
+}
+
+int gemv_from_f32(int qtype, int act_mode, const void* w, const float* x, long long x_stride, float* y, int m, int k,
+                  int n, long long y_stride, float alpha, float beta, int32_t* isums, Device* dev, cudaStream_t st,
+                  bool pdl, int flags) {
+    if (!x) return B200Q_EINVAL;
+    return gemv_rows(qtype, act_mode, w, nullptr, 0, x, x_stride, y, m, k, n, y_stride, alpha, beta, isums, dev, st,
+                     pdl, flags);
 }
 
 int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev) {
@@ -329,6 +396,20 @@ int launch_gemv(int qtype, int act_mode, const void* w, const float* x, float* y
     if (act_mode == B200Q_ACT_F16) return B200Q_EQTYPE;
     int rc = gemv_check_shape(qtype, act_mode, k, n, dev);  // validate before any launch
     if (rc != B200Q_OK) return rc;
+    // One launch per chunk of rows: the GEMV quantizes x itself, unless its
+    // staging does not fit (B200Q_GEMV_FUSED_QUANT=0 selects the separate
+    // quantizer kernel).
+    static const bool fused = [] {
+        const char* e = std::getenv("B200Q_GEMV_FUSED_QUANT");
+        return !(e && e[0] == '0');
+    }();
+    Plan probe;
+    const int dig = act_mode == B200Q_ACT_X8 ? 1 : 2;
+    if (fused && make_plan(qtype, dig, k, n, 1, dev->num_sms, probe, true) == B200Q_OK &&
+        (isums || m == 1 ||
+         make_plan(qtype, dig, k, n, std::min(m, max_rows_per_launch(qtype, dig)), dev->num_sms, probe, true) == B200Q_OK))
+        return gemv_from_f32(qtype, act_mode, w, x, x_stride, y, m, k, n, y_stride, 1.0f, 0.0f, isums, dev, st, pdl,
+                             flags);
     const uint8_t* xq = nullptr;
     long long xq_row = 0;
     rc = quantize_activations(act_mode, x, x_stride, m, k, dev, st, pdl, 0, &xq, &xq_row);

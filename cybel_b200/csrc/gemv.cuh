@@ -10,13 +10,16 @@
 //    ring of shared-memory stages with 1-D bulk copies (cp.async.bulk, no
 //    multicast) that complete on mbarriers. Weights are touched once, with an
 //    L2 evict-first policy.
-//  * Activations are quantized once per call by quantize_act_kernel (per
-//    32-element group: int8 "x8", or int16 split in two byte planes "x16").
-//    Consumer warps own a fixed k-slice of the row ("slice") and walk rows;
-//    each lane loads its activation codes into registers once.
-//  * Both kernels use programmatic dependent launch: the GEMV streams its
-//    (static) weights while the quantizer runs and waits for it only before
-//    reading the codes.
+//  * Activations are quantized per 32-element group (int8 "x8", or int16
+//    split in two byte planes "x16"). The consumer warps stage them once per
+//    CTA in shared memory -- quantizing the fp32 rows themselves (FQ
+//    instances: one launch per matvec) or copying the codes a preceding
+//    kernel wrote (the decode glue kernels) -- and each lane then keeps the
+//    codes of its k-slice in registers for all its rows.
+//  * Programmatic dependent launch: the GEMV streams its first (static)
+//    weight stages while the preceding kernel runs and waits for it only
+//    before reading the activations; the rest of the ring is issued once the
+//    activation loads are out, so weight traffic does not delay them.
 //  * Per row a lane decodes its weight codes from shared memory and forms
 //    exact integer dot sums with dp4a; each group sum is scaled in fp32 by
 //    the weight and activation scales; partials are reduced per warp with
@@ -45,6 +48,8 @@ struct GemvParams {
     const uint8_t* W;      // packed weight rows (device, 16-byte aligned)
     const uint8_t* xq;     // [MR] quantized activation rows (quantize_act_kernel layout)
     long long xq_stride;   // bytes between quantized rows
+    const float* xf;       // [MR] fp32 activation rows, quantized in the kernel (FQ instances)
+    long long xf_stride;   // floats between fp32 rows
     float* y;              // [MR][y_stride] fp32 outputs
     int32_t* dbg;          // optional [n][k/G] integer group sums (MR == 1 only)
     volatile int* status;  // status word (host-mapped); kernels store STATUS_* values
@@ -53,10 +58,15 @@ struct GemvParams {
     int k, n;
     int nb;                // blocks per row
     int S;                 // slices per row (consumer warps per row)
-    int WR;                // row walkers per slice
+    int WR;                // row walkers per slice (G groups x SW)
+    int G;                 // walker groups: stage s belongs to group s % G
+    int SW;                // walkers per slice in a group; they split a stage's rows
     int R;                 // rows per stage
     int NS;                // ring stages
     int stage_stride;      // bytes between ring slots (multiple of 128)
+    int PD;                // stages issued before the activation loads are issued
+    int pd_hold;           // 1: the stages after PD wait until the activations are in registers
+    int x_off;             // ring byte offset of the staged activations (>= PD * stage_stride)
     int n_quads;           // ceil(n / 4)
     int rows_cta;          // most rows any CTA owns
     int w_static;          // weights not written by the preceding kernel: stream them before the grid dependency resolves
@@ -166,6 +176,21 @@ __device__ __forceinline__ int round_half_even_small(float v) {
 __host__ __device__ constexpr long long xq_row_bytes(int k, int dig) {
     return ((static_cast<long long>(k) * dig + (k / 32) * 8) + 15) / 16 * 16;
 }
+
+// The same row as the GEMV stages it in shared memory: each code plane has
+// 16 bytes of padding after every 256 codes, so the lanes of a warp (whose
+// runs lie 256 codes apart) read their runs without bank conflicts.
+// Plane length, byte offset of code e within a plane, and the row size:
+__host__ __device__ constexpr int xs_plane_bytes(int k) { return k + 16 * ((k + 255) / 256); }
+__host__ __device__ constexpr int xs_code_offset(int e) { return e + 16 * (e >> 8); }
+__host__ __device__ constexpr int xs_row_bytes(int k, int dig) {
+    return (dig * xs_plane_bytes(k) + (k / 32) * 8 + 15) / 16 * 16;
+}
+// Scratch of the fused quantizer: per consumer warp, 32 groups of 32 fp32
+// values at a 144-byte pitch (a transpose from coalesced loads to one group
+// per lane without bank conflicts).
+constexpr int kFqGroupPitch = 144;
+constexpr int kFqWarpBytes = 32 * kFqGroupPitch;
 
 // Quantize one 32-element group v into a quantized row at `base` (group g
 // of a row of k elements). The arithmetic is restated in the oracle as
@@ -644,15 +669,211 @@ __device__ __forceinline__ int warp_sum_lane(int i) {
     return V == 1 ? 0 : (V == 2 ? 16 * i : 16 * (i >> 1) + 8 * (i & 1));
 }
 
+// One lane's run of RUN codes starting at element e of a staged row (padded
+// layout) at shared-memory byte address `row`.
+template <int DIG, int RUN>
+__device__ __forceinline__ void load_run_smem(uint32_t row, int k, int e, XRun<DIG, RUN>& out) {
+    const uint32_t kp = static_cast<uint32_t>(xs_plane_bytes(k));
+    const uint32_t ce = static_cast<uint32_t>(xs_code_offset(e));  // a run never crosses a 256-code boundary
+#pragma unroll
+    for (int i = 0; i < RUN / 16; ++i) {
+        const uint4 v = lds128(row + ce + 16u * i);
+        out.hi[4 * i] = v.x;
+        out.hi[4 * i + 1] = v.y;
+        out.hi[4 * i + 2] = v.z;
+        out.hi[4 * i + 3] = v.w;
+    }
+    if (DIG == 2) {
+#pragma unroll
+        for (int i = 0; i < RUN / 16; ++i) {
+            const uint4 v = lds128(row + kp + ce + 16u * i);
+            out.lo[4 * i] = v.x;
+            out.lo[4 * i + 1] = v.y;
+            out.lo[4 * i + 2] = v.z;
+            out.lo[4 * i + 3] = v.w;
+        }
+    }
+    const uint32_t gd = row + kp * DIG;
+    out.d = __uint_as_float(lds32(gd + 4u * static_cast<uint32_t>(e / 32)));
+    if (RUN == 32) {
+        out.sum = static_cast<int>(lds32(gd + 4u * static_cast<uint32_t>(k / 32 + e / 32)));
+    } else {
+        int hs = 0, ls = 0;
+#pragma unroll
+        for (int w = 0; w < RUN / 4; ++w) {
+            hs = dp4a_ss(out.hi[w], 0x01010101u, hs);
+            if (DIG == 2) ls = dp4a_uu(out.lo[w], 0x01010101u, ls);
+        }
+        out.sum = DIG == 2 ? hs * 256 + ls : hs;
+    }
+    out.fsum = static_cast<float>(out.sum);
+}
+
+// Quantize one 32-element group v into the staged row at `row` (padded
+// layout, plane bytes kp): the arithmetic of quantize_group (amax,
+// iscale = QMAX / amax by IEEE division, one rounded multiply, half-even
+// codes, d = amax / QMAX), with the reductions as trees.
+template <int DIG>
+__device__ __forceinline__ void quantize_group_staged(const float (&v)[32], uint8_t* row, int k, int kp, int g) {
+    float m[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m[i] = fmaxf(fabsf(v[2 * i]), fabsf(v[2 * i + 1]));
+#pragma unroll
+    for (int w = 8; w > 0; w >>= 1) {
+#pragma unroll
+        for (int i = 0; i < w; ++i) m[i] = fmaxf(m[i], m[i + w]);
+    }
+    const float amax = m[0];
+    constexpr float QMAX = DIG == 1 ? 127.0f : 32767.0f;
+    const float iscale = amax > 0.0f ? __fdiv_rn(QMAX, amax) : 0.0f;
+    int ws[8];
+    uint32_t hw[8], lw[8];
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        uint32_t h = 0, l = 0;
+        int sw = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int q = round_half_even_small(__fmul_rn(v[4 * w + j], iscale));
+            sw += q;
+            if (DIG == 1) {
+                h |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * j);
+            } else {
+                h |= (static_cast<uint32_t>(q >> 8) & 0xFFu) << (8 * j);
+                l |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * j);
+            }
+        }
+        ws[w] = sw;
+        hw[w] = h;
+        lw[w] = l;
+    }
+    const int sum = ((ws[0] + ws[1]) + (ws[2] + ws[3])) + ((ws[4] + ws[5]) + (ws[6] + ws[7]));
+    uint4* dh = reinterpret_cast<uint4*>(row + xs_code_offset(g * 32));
+    dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+    if (DIG == 2) {
+        uint4* dl = reinterpret_cast<uint4*>(row + kp + xs_code_offset(g * 32));
+        dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+    }
+    float* gd = reinterpret_cast<float*>(row + DIG * kp);
+    gd[g] = amax > 0.0f ? __fdiv_rn(amax, QMAX) : 0.0f;
+    reinterpret_cast<int*>(gd + k / 32)[g] = sum;
+}
+
+// Stage MR activation rows in shared memory (xs, generic pointer; rows
+// xs_row bytes apart in the padded layout), using all consumer warps.
+//  * FQ: each warp takes 32 groups at a time. Its lanes load them with
+//    coalesced 16-byte loads (eight per lane), pass them through the warp's
+//    transpose tile (kFqWarpBytes at tmp_all), and then each lane quantizes
+//    one group.
+//  * Otherwise the codes a preceding kernel wrote (xq layout) are copied,
+//    four 16-byte words per thread per trip.
+// Thread 0 sets the word at `flag` once its first loads are issued: the
+// producer waits for it before releasing the bulk of the weight copies, so
+// these loads are not queued behind them.
+template <int DIG, int MR, bool FQ>
+__device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* xs, int xs_row, uint8_t* tmp_all,
+                                                  int warp, int lane, int nwarps, uint32_t flag) {
+    const int kp = xs_plane_bytes(p.k);
+    if constexpr (FQ) {
+        const int groups = p.k >> 5;
+        const int total = MR * groups;
+        float* tmp = reinterpret_cast<float*>(tmp_all + warp * kFqWarpBytes);
+        for (int gw = warp * 32; gw < total; gw += nwarps * 32) {
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int f = 32 * j + lane;  // float4 index within the warp's 32 groups
+                const int gg = gw + (f >> 3);
+                v[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (gg < total) {
+                    const int row = gg / groups, gi = gg - row * groups;
+                    v[j] = __ldg(reinterpret_cast<const float4*>(p.xf + row * p.xf_stride + gi * 32) + (f & 7));
+                }
+            }
+            if (gw == warp * 32 && warp == 0 && lane == 0) sts_volatile(flag, 1u);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int f = 32 * j + lane;
+                *reinterpret_cast<float4*>(tmp + (f >> 3) * (kFqGroupPitch / 4) + (f & 7) * 4) = v[j];
+            }
+            __syncwarp();
+            const int g = gw + lane;
+            if (g < total) {
+                float x[32];
+                const float* src = tmp + lane * (kFqGroupPitch / 4);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 f4 = *reinterpret_cast<const float4*>(src + 4 * i);
+                    x[4 * i] = f4.x;
+                    x[4 * i + 1] = f4.y;
+                    x[4 * i + 2] = f4.z;
+                    x[4 * i + 3] = f4.w;
+                }
+                const int row = g / groups, gi = g - row * groups;
+                quantize_group_staged<DIG>(x, xs + row * xs_row, p.k, kp, gi);
+            }
+            __syncwarp();
+        }
+        if (warp == 0 && lane == 0) sts_volatile(flag, 1u);
+    } else {
+        constexpr int B = 4;  // 16-byte words a thread loads per trip
+        const int nthreads = nwarps * 32, tid = warp * 32 + lane;
+        const int words = static_cast<int>(xq_row_bytes(p.k, DIG) >> 4);
+        const int code_words = (DIG * p.k) >> 4;
+        const int total = MR * words;
+        for (int i0 = tid; i0 < total; i0 += B * nthreads) {
+            uint4 v[B];
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                const int i = i0 + b * nthreads;
+                if (i < total) {
+                    const int row = i / words, w = i - row * words;
+                    v[b] = __ldg(reinterpret_cast<const uint4*>(p.xq + row * p.xq_stride) + w);
+                }
+            }
+            if (i0 == tid && tid == 0) sts_volatile(flag, 1u);
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                const int i = i0 + b * nthreads;
+                if (i < total) {
+                    const int row = i / words, w = i - row * words;
+                    int off;
+                    if (w < code_words) {
+                        const int plane = (16 * w) / p.k, e = 16 * w - plane * p.k;
+                        off = plane * kp + xs_code_offset(e);
+                    } else {
+                        off = DIG * kp + (16 * w - DIG * p.k);
+                    }
+                    *reinterpret_cast<uint4*>(xs + row * xs_row + off) = v[b];
+                }
+            }
+        }
+        if (tid == 0) sts_volatile(flag, 1u);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // The kernel: one CTA per SM streams a contiguous slab of rows through a
-// ring of NS shared-memory stages. Warp NW (the producer) issues one bulk
-// copy per stage (~32 KB, L2 evict-first); the NW consumer warps are a grid
-// of S k-slices x WR walkers, and every consumer warp takes its rows of every
-// stage (rows walker, walker + WR, ...), so all warps release each stage at
-// about the same time.
+// ring of NS shared-memory stages of R rows. Warp NW (the producer) issues
+// one bulk copy per stage (L2 evict-first; stages stay >= ~16 KB, since the
+// copies in flight per SM are limited in number). The NW consumer warps are
+// S k-slices x WR walkers, in G groups of SW walkers; stage s belongs to
+// group s % G, whose S x SW warps take their slice of its rows, U rows at a
+// time, the SW walkers of a slice interleaved.
+//
+// Start-up order: weight copies and the activation loads share the memory
+// system, so a full ring issued at CTA start would hold the activation loads
+// behind microseconds of weight traffic. The producer issues the first PD
+// stages (about what arrives while the CTA waits for the preceding kernel),
+// then waits until the consumers have issued their activation loads (a
+// shared-memory flag; a bounded wait that only delays, never fails) before
+// issuing the rest. The activations are staged in the last bytes of the ring
+// (x_off); the slots there are filled only after every consumer warp has
+// taken its codes into registers (arrivals on xbar).
 // ---------------------------------------------------------------------------
-template <int QT, int DIG, int MR, bool DBG>
+template <int QT, int DIG, int MR, bool DBG, bool FQ>
 __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(const GemvParams p) {
     using F = Fmt<QT>;
     constexpr int RUN = F::kRun;
@@ -669,7 +890,11 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(
     uint8_t* ring = smem;
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + static_cast<size_t>(p.NS) * p.stage_stride);
     uint64_t* empty = full + p.NS;
-    float* part = reinterpret_cast<float*>(empty + p.NS);  // [rows of this CTA][MR][S]
+    uint64_t* xbar = empty + p.NS;                            // activations staged: one arrival per consumer warp
+    uint32_t* xflag = reinterpret_cast<uint32_t*>(xbar + 1);  // activation loads issued
+    float* part = reinterpret_cast<float*>(xbar + 2);         // [rows of this CTA][MR][S]
+    uint8_t* xs = ring + p.x_off;                             // staged activations (padded rows)
+    uint8_t* xtmp = xs + MR * xs_row_bytes(p.k, DIG);         // fused quantizer's transpose tiles (FQ)
 
     // Contiguous slab of rows per CTA, balanced to one row (to one 4-row
     // group for the R4 layouts).
@@ -684,8 +909,10 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(
     if (tid == 0) {
         for (int i = 0; i < p.NS; ++i) {
             mbar_init(smem_addr(full + i), 1);
-            mbar_init(smem_addr(empty + i), static_cast<uint32_t>(nwarps));
+            mbar_init(smem_addr(empty + i), static_cast<uint32_t>(p.S * p.SW));
         }
+        mbar_init(smem_addr(xbar), static_cast<uint32_t>(nwarps));
+        *xflag = 0u;
         fence_mbar_init();
     }
     __syncthreads();
@@ -701,9 +928,20 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(
         if (!p.w_static) griddep_wait();
         if (lane == 0 && n_stages > 0) {
             const uint64_t pol = l2_policy_evict_first();
+            const int xs_slot = p.x_off / p.stage_stride;  // first slot the staged activations overlap
             int issued = 0;
             bool ok = true;
             for (int s = 0; s < n_stages && ok; ++s) {
+                if (s == p.PD && !p.pd_hold) {
+                    // Pacing only: proceed after ~20 us even if the flag never comes.
+                    const uint64_t t0 = global_timer_ns();
+                    while (lds_volatile(smem_addr(xflag)) == 0u && global_timer_ns() - t0 < 20000ull) {
+                    }
+                }
+                if (s == (p.pd_hold ? p.PD : xs_slot) && !mbar_wait_bounded(smem_addr(xbar), 0u)) {
+                    *p.status = STATUS_TIMEOUT;
+                    break;
+                }
                 const int slot = s % p.NS;
                 const uint32_t use = static_cast<uint32_t>(s / p.NS);
                 if (!mbar_wait_bounded(smem_addr(empty + slot), (use & 1u) ^ 1u)) {
@@ -734,34 +972,44 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(
     // ---------------- consumers ----------------
     const int slice = warp % p.S;
     const int walker = warp / p.S;
+    const int group = walker / p.SW, sub = walker - group * p.SW;
     const int t = F::lane_part(lane);
     const int blk = slice * F::kBlocksPerSlice + F::lane_block(lane);
     const bool active = blk < p.nb;
     const bool active1 = blk + 1 < p.nb;  // second block of a two-block lane
     const int blk_c = active ? blk : 0;
 
-    // The quantized activations are written by the preceding kernel.
+    // The activations (fp32 rows, or their codes) are written by the
+    // preceding kernel. Stage them once per CTA, then every lane takes its
+    // runs into registers and releases the staging bytes to the producer.
     griddep_wait();
+    const int xs_row = xs_row_bytes(p.k, DIG);
+    stage_activations<DIG, MR, FQ>(p, xs, xs_row, xtmp, warp, lane, nwarps, smem_addr(xflag));
+    fence_proxy_async_smem();
+    named_bar_sync(1, static_cast<uint32_t>(nthreads));
     X x[MR][RUNS];
     float xdd[MR][RUNS];  // group scale (with the x16 factor of in-place high nibbles folded in)
     float xsd[MR][RUNS];  // group scale * group code sum (Q4_K mins)
+    const uint32_t xs_addr = smem_addr(xs);
 #pragma unroll
     for (int m = 0; m < MR; ++m) {
 #pragma unroll
         for (int r = 0; r < RUNS; ++r) {
             const int e = F::run_start(blk_c, t, r);
-            load_run<DIG, RUN>(p.xq + m * p.xq_stride, p.k, e < p.k ? e : 0, x[m][r]);
+            load_run_smem<DIG, RUN>(xs_addr + static_cast<uint32_t>(m * xs_row), p.k, e < p.k ? e : 0, x[m][r]);
             xdd[m][r] = ((QT == QT_Q4_K || QT == QT_Q4_K_R4) && (r & 1)) ? x[m][r].d * 0.0625f : x[m][r].d;
             xsd[m][r] = x[m][r].d * x[m][r].fsum;
         }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_addr(xbar));
 
     constexpr int U = kRowsPerIter<DIG, MR>;
     constexpr int V = U * MR;
     bool ok = true;
     const uint32_t ring_base = smem_addr(ring);
     const uint32_t rb32 = static_cast<uint32_t>(p.row_bytes);
-    for (int s = 0; s < n_stages; ++s) {
+    for (int s = group; s < n_stages; s += p.G) {
         const int slot = s % p.NS;
         const uint32_t use = static_cast<uint32_t>(s / p.NS);
         const int r0 = r_begin + s * p.R;
@@ -772,7 +1020,7 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(
         }
         const uint32_t sbase = ring_base + static_cast<uint32_t>(slot) * static_cast<uint32_t>(p.stage_stride) +
                                static_cast<uint32_t>((r0 * p.row_bytes) & 15ll);
-        for (int rl0 = walker * U; rl0 < rows; rl0 += p.WR * U) {
+        for (int rl0 = sub * U; rl0 < rows; rl0 += p.SW * U) {
             float acc[U][MR];
             int isum[U][4];
 #pragma unroll

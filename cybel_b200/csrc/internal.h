@@ -44,6 +44,11 @@ int quantize_activations(int act_mode, const float* x, long long x_stride, int m
 int gemv_from_xq(int qtype, int act_mode, const void* w, const uint8_t* xq, long long xq_row, float* y, int m, int k,
                  int n, long long y_stride, float alpha, float beta, int32_t* isums, Device* dev, cudaStream_t st,
                  bool pdl, int flags);
+// The same from fp32 activation rows (x_stride floats apart, 16-byte
+// aligned), quantized inside the GEMV: one launch per chunk of rows.
+int gemv_from_f32(int qtype, int act_mode, const void* w, const float* x, long long x_stride, float* y, int m, int k,
+                  int n, long long y_stride, float alpha, float beta, int32_t* isums, Device* dev, cudaStream_t st,
+                  bool pdl, int flags);
 int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev);
 // quantize_act kernel over `rows` contiguous rows of k into xq (row pitch xq_bytes_per_row).
 int launch_quantize_rows(int act_mode, const float* x, int rows, int k, uint8_t* xq, cudaStream_t st, bool pdl);
