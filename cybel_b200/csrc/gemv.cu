@@ -105,7 +105,7 @@ int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl, b
     // below them are filled before the activations are in registers. Small
     // stages get more slots, so the ring still holds them with a slot to spare.
     const long long x_bytes =
-        static_cast<long long>(MR) * xs_row_bytes(k, dig) + (fq ? static_cast<long long>(S * WR) * kFqWarpBytes : 0);
+        static_cast<long long>(MR) * xs_row_bytes(k, dig) + (fq ? static_cast<long long>(S * WR) * kFqWarpBytes + 128 : 0);
     NS = static_cast<int>(
         std::max<long long>(NS, std::min<long long>(ns_fit, (x_bytes + stage_stride - 1) / stage_stride + 1)));
     if (NS < 2) return B200Q_ESHAPE;
@@ -298,7 +298,8 @@ namespace {
 // or, when xf is given, from fp32 rows that the GEMV quantizes itself.
 int gemv_rows(int qtype, int act_mode, const void* w, const uint8_t* xq, long long xq_row, const float* xf,
               long long xf_stride, float* y, int m, int k, int n, long long y_stride, float alpha, float beta,
-              int32_t* isums, Device* dev, cudaStream_t st, bool pdl, int flags) {
+              int32_t* isums, Device* dev, cudaStream_t st, bool pdl, int flags, const float* gamma = nullptr,
+              float eps = 0.0f) {
     if (!w || (!xq && !xf) || !y || m <= 0 || k <= 0 || n <= 0 || !dev) return B200Q_EINVAL;
     if (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
     if (reinterpret_cast<uintptr_t>(w) & 15u) return B200Q_EALIGN;
@@ -316,6 +317,12 @@ int gemv_rows(int qtype, int act_mode, const void* w, const uint8_t* xq, long lo
         if (xf) {
             pl.p.xf = xf + m0 * xf_stride;
             pl.p.xf_stride = xf_stride;
+            if (gamma) {
+                // One pass of 32 groups per consumer warp holds the whole row.
+                if (MR != 1 || k / 32 > 32 * pl.p.S * pl.p.WR) return B200Q_ESHAPE;
+                pl.p.gamma = gamma;
+                pl.p.eps = eps;
+            }
         } else {
             pl.p.xq = xq + m0 * xq_row;
             pl.p.xq_stride = xq_row;
@@ -351,6 +358,15 @@ int gemv_from_f32(int qtype, int act_mode, const void* w, const float* x, long l
     if (!x) return B200Q_EINVAL;
     return gemv_rows(qtype, act_mode, w, nullptr, 0, x, x_stride, y, m, k, n, y_stride, alpha, beta, isums, dev, st,
                      pdl, flags);
+}
+
+int gemv_norm_f32(int qtype, int act_mode, const void* w, const float* x, const float* gamma, float eps, float* y,
+                  int k, int n, float alpha, float beta, Device* dev, cudaStream_t st, bool pdl, int flags) {
+    if (!x || !gamma) return B200Q_EINVAL;
+    if (reinterpret_cast<uintptr_t>(gamma) & 15u) return B200Q_EALIGN;
+    if (!(eps >= 0.0f)) return B200Q_EINVAL;
+    return gemv_rows(qtype, act_mode, w, nullptr, 0, x, k, y, 1, k, n, n, alpha, beta, nullptr, dev, st, pdl, flags,
+                     gamma, eps);
 }
 
 int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev) {

@@ -50,6 +50,8 @@ struct GemvParams {
     long long xq_stride;   // bytes between quantized rows
     const float* xf;       // [MR] fp32 activation rows, quantized in the kernel (FQ instances)
     long long xf_stride;   // floats between fp32 rows
+    const float* gamma;    // FQ with MR == 1: RMSNorm weights; x is normalized before quantizing
+    float eps;             // RMSNorm epsilon
     float* y;              // [MR][y_stride] fp32 outputs
     int32_t* dbg;          // optional [n][k/G] integer group sums (MR == 1 only)
     volatile int* status;  // status word (host-mapped); kernels store STATUS_* values
@@ -766,7 +768,9 @@ __device__ __forceinline__ void quantize_group_staged(const float (&v)[32], uint
 //  * FQ: each warp takes 32 groups at a time. Its lanes load them with
 //    coalesced 16-byte loads (eight per lane), pass them through the warp's
 //    transpose tile (kFqWarpBytes at tmp_all), and then each lane quantizes
-//    one group.
+//    one group. With p.gamma set (one row, at most 32 groups per warp) the
+//    row is first RMS-normalized: x * (1 / sqrt(sum(x^2) / k + eps)) * gamma,
+//    the sum of squares reduced per warp into `red` and summed in warp order.
 //  * Otherwise the codes a preceding kernel wrote (xq layout) are copied,
 //    four 16-byte words per thread per trip.
 // Thread 0 sets the word at `flag` once its first loads are issued: the
@@ -774,13 +778,14 @@ __device__ __forceinline__ void quantize_group_staged(const float (&v)[32], uint
 // these loads are not queued behind them.
 template <int DIG, int MR, bool FQ>
 __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* xs, int xs_row, uint8_t* tmp_all,
-                                                  int warp, int lane, int nwarps, uint32_t flag) {
+                                                  float* red, int warp, int lane, int nwarps, uint32_t flag) {
     const int kp = xs_plane_bytes(p.k);
     if constexpr (FQ) {
         const int groups = p.k >> 5;
         const int total = MR * groups;
+        const bool norm = MR == 1 && p.gamma != nullptr;  // one pass per warp (host-checked)
         float* tmp = reinterpret_cast<float*>(tmp_all + warp * kFqWarpBytes);
-        for (int gw = warp * 32; gw < total; gw += nwarps * 32) {
+        for (int gw = warp * 32; gw < total || (norm && gw == warp * 32); gw += nwarps * 32) {
             float4 v[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -793,6 +798,36 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
                 }
             }
             if (gw == warp * 32 && warp == 0 && lane == 0) sts_volatile(flag, 1u);
+            if (norm) {
+                float4 g[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int f = 32 * j + lane;
+                    const int gg = gw + (f >> 3);
+                    g[j] = gg < total ? __ldg(reinterpret_cast<const float4*>(p.gamma + gg * 32) + (f & 7))
+                                      : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                }
+                float ss = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    ss = fmaf(v[j].x, v[j].x, ss);
+                    ss = fmaf(v[j].y, v[j].y, ss);
+                    ss = fmaf(v[j].z, v[j].z, ss);
+                    ss = fmaf(v[j].w, v[j].w, ss);
+                }
+#pragma unroll
+                for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                if (lane == 0) red[warp] = ss;
+                named_bar_sync(2, static_cast<uint32_t>(nwarps * 32));
+                float tot = 0.0f;
+                for (int w = 0; w < nwarps; ++w) tot += red[w];
+                const float inv_rms = 1.0f / sqrtf(tot / static_cast<float>(p.k) + p.eps);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    v[j] = make_float4(v[j].x * inv_rms * g[j].x, v[j].y * inv_rms * g[j].y,
+                                       v[j].z * inv_rms * g[j].z, v[j].w * inv_rms * g[j].w);
+                }
+            }
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int f = 32 * j + lane;
@@ -815,6 +850,7 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
                 quantize_group_staged<DIG>(x, xs + row * xs_row, p.k, kp, gi);
             }
             __syncwarp();
+            if (norm) break;
         }
         if (warp == 0 && lane == 0) sts_volatile(flag, 1u);
     } else {
@@ -895,6 +931,7 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(
     float* part = reinterpret_cast<float*>(xbar + 2);         // [rows of this CTA][MR][S]
     uint8_t* xs = ring + p.x_off;                             // staged activations (padded rows)
     uint8_t* xtmp = xs + MR * xs_row_bytes(p.k, DIG);         // fused quantizer's transpose tiles (FQ)
+    float* xred = reinterpret_cast<float*>(xtmp + (FQ ? nwarps * kFqWarpBytes : 0));  // per-warp sums (RMSNorm)
 
     // Contiguous slab of rows per CTA, balanced to one row (to one 4-row
     // group for the R4 layouts).
@@ -984,7 +1021,7 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(
     // runs into registers and releases the staging bytes to the producer.
     griddep_wait();
     const int xs_row = xs_row_bytes(p.k, DIG);
-    stage_activations<DIG, MR, FQ>(p, xs, xs_row, xtmp, warp, lane, nwarps, smem_addr(xflag));
+    stage_activations<DIG, MR, FQ>(p, xs, xs_row, xtmp, xred, warp, lane, nwarps, smem_addr(xflag));
     fence_proxy_async_smem();
     named_bar_sync(1, static_cast<uint32_t>(nthreads));
     X x[MR][RUNS];

@@ -49,6 +49,11 @@ int gemv_from_xq(int qtype, int act_mode, const void* w, const uint8_t* xq, long
 int gemv_from_f32(int qtype, int act_mode, const void* w, const float* x, long long x_stride, float* y, int m, int k,
                   int n, long long y_stride, float alpha, float beta, int32_t* isums, Device* dev, cudaStream_t st,
                   bool pdl, int flags);
+// y = alpha * (W rmsnorm(x) * gamma) + beta * y for one fp32 row x of k, the
+// RMSNorm computed inside the GEMV (B200Q_ESHAPE when the row is too long to
+// stage in one pass).
+int gemv_norm_f32(int qtype, int act_mode, const void* w, const float* x, const float* gamma, float eps, float* y,
+                  int k, int n, float alpha, float beta, Device* dev, cudaStream_t st, bool pdl, int flags);
 int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev);
 // quantize_act kernel over `rows` contiguous rows of k into xq (row pitch xq_bytes_per_row).
 int launch_quantize_rows(int act_mode, const float* x, int rows, int k, uint8_t* xq, cudaStream_t st, bool pdl);

@@ -7,10 +7,12 @@ cache, the o projection with the residual add, RMSNorm, and the SwiGLU FFN
 with its residual add; then the final norm and the LM head. ``DecodeStack``
 runs that step entirely on the device through libb200q's entry points:
 
-* ``b200q_add_rmsnorm_q`` -- RMSNorm writing the GEMV's activation codes;
-* ``b200q_matmul_xq`` -- each projection from those codes: q/k/v as one
-  matrix, o with the residual add in its epilogue (beta = 1), gate/up as one
-  matrix, down with the residual add, and the LM head;
+* ``b200q_matmul_norm`` -- each projection that follows an RMSNorm (q/k/v
+  as one matrix, gate/up as one matrix, the LM head), the norm computed by
+  the GEMV itself from the fp32 residual stream (``fused_norm=False`` runs
+  ``b200q_add_rmsnorm_q`` then ``b200q_matmul_xq`` instead);
+* ``b200q_matmul_xq`` -- the projections fed by codes: o with the residual
+  add in its epilogue (beta = 1) and down with the residual add;
 * ``b200q_rope_attention_decode`` -- RoPE, the KV append and attention in
   one launch, which also writes the o projection's codes;
 * ``b200q_swiglu_q`` -- SiLU(gate) * up, written as the down projection's
@@ -130,7 +132,8 @@ class DecodeStack:
     """
 
     def __init__(self, shape: StackShape, max_ctx: int, layers: list[dict[str, np.ndarray]], embed: np.ndarray,
-                 head: np.ndarray, out_norm: np.ndarray, act_mode: int = _native.ACT_X16, device: int = 0):
+                 head: np.ndarray, out_norm: np.ndarray, act_mode: int = _native.ACT_X16, device: int = 0,
+                 fused_norm: bool = True):
         import torch
 
         if shape.head_dim != 128:
@@ -140,6 +143,7 @@ class DecodeStack:
         self.shape = shape
         self.max_ctx = max_ctx
         self.act_mode = act_mode
+        self.fused_norm = fused_norm
         self.dev = torch.device("cuda", device)
         self.lib = _native.lib()
         f32 = dict(dtype=torch.float32, device=self.dev)
@@ -205,10 +209,8 @@ class DecodeStack:
             self._check(L.b200q_dequantize_rows(q, self.embed.ptr, self.token.data_ptr(), 1, x, h, s.vocab, st),
                         "embedding")
         for li, lay in enumerate(self.layers):
-            if not linears_only:
-                self._check(L.b200q_add_rmsnorm_q(x, None, lay.attn_norm.data_ptr(), None, xq_h, act, h, 1, s.eps,
-                                                  st), "attn_norm")
-            self._check(L.b200q_matmul_xq(q, act, xq_h, lay.wqkv.ptr, qp, 1, h, h + 2 * kv, 1.0, 0.0, W, st), "qkv")
+            # RMSNorm inside the q/k/v GEMV (it normalizes and quantizes x while its weights stream)
+            self._norm_matmul(q, x, lay.attn_norm, xq_h, lay.wqkv.ptr, qp, h, h + 2 * kv, "qkv", st, linears_only)
             if not linears_only:
                 kc = self.k_cache[li].data_ptr()
                 vc = self.v_cache[li].data_ptr()
@@ -217,18 +219,27 @@ class DecodeStack:
                             "rope_attention")
             # o projection with the residual add in its epilogue: x = Wo a + x
             self._check(L.b200q_matmul_xq(q, act, xq_h, lay.wo.ptr, x, 1, h, h, 1.0, resid, W, st), "o_proj")
-            if not linears_only:
-                self._check(L.b200q_add_rmsnorm_q(x, None, lay.ffn_norm.data_ptr(), None, xq_h, act, h, 1, s.eps,
-                                                  st), "ffn_norm")
-            self._check(L.b200q_matmul_xq(q, act, xq_h, lay.w_gu.ptr, gp, 1, h, 2 * f, 1.0, 0.0, W, st), "gate_up")
+            self._norm_matmul(q, x, lay.ffn_norm, xq_h, lay.w_gu.ptr, gp, h, 2 * f, "gate_up", st, linears_only)
             if not linears_only:
                 self._check(L.b200q_swiglu_q(gp, up, xq_f, act, f, st), "swiglu")
             self._check(L.b200q_matmul_xq(q, act, xq_f, lay.w_down.ptr, x, 1, f, h, 1.0, resid, W, st), "down")
+        self._norm_matmul(s.head_qtype, x, self.out_norm, xq_h, self.head.ptr, self.logits.data_ptr(), h, s.vocab,
+                          "lm_head", st, linears_only)
+
+    def _norm_matmul(self, qt, x, gamma, xq, w, y, k, n, what, st, linears_only) -> None:
+        """y = W (RMSNorm(x) * gamma): one GEMV that normalizes x itself
+        (b200q_matmul_norm), or, with fused_norm off, b200q_add_rmsnorm_q writing
+        the codes and b200q_matmul_xq reading them (linears_only keeps only the
+        GEMV of that pair)."""
+        L, s, W = self.lib, self.shape, _native.WEIGHTS_STATIC
+        if self.fused_norm:
+            self._check(L.b200q_matmul_norm(qt, self.act_mode, x, gamma.data_ptr(), s.eps, w, y, k, n, 1.0, 0.0, W, st),
+                        what)
+            return
         if not linears_only:
-            self._check(L.b200q_add_rmsnorm_q(x, None, self.out_norm.data_ptr(), None, xq_h, act, h, 1, s.eps, st),
-                        "out_norm")
-        self._check(L.b200q_matmul_xq(s.head_qtype, act, xq_h, self.head.ptr, self.logits.data_ptr(), 1, h, s.vocab,
-                                      1.0, 0.0, W, st), "lm_head")
+            self._check(L.b200q_add_rmsnorm_q(x, None, gamma.data_ptr(), None, xq, self.act_mode, k, 1, s.eps, st),
+                        what + " norm")
+        self._check(L.b200q_matmul_xq(qt, self.act_mode, xq, w, y, 1, k, n, 1.0, 0.0, W, st), what)
 
     def set_token(self, token: int) -> None:
         self.token.fill_(int(token))

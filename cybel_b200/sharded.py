@@ -87,7 +87,8 @@ class ShardedDecode:
     deliver codes of the gathered rows, so no projection quantizes by itself.
     """
 
-    def __init__(self, plan: ShardPlan, max_ctx: int, batch: int, layers, embed, head, out_norm, ops):
+    def __init__(self, plan: ShardPlan, max_ctx: int, batch: int, layers, embed, head, out_norm, ops,
+                 fuse_norm: bool | None = None):
         s = plan.shape
         self.plan, self.shape, self.ops = plan, s, ops
         self.max_ctx, self.batch = max_ctx, batch
@@ -119,7 +120,17 @@ class ShardedDecode:
         self.out_norm = ops.vector(out_norm)
         self.k_cache, self.v_cache = ops.cache(s.layers, B, plan.kv_heads, max_ctx, hd)
         z = ops.zeros
-        self.x = z(B * h)
+        # Batch 1: each RMSNorm runs inside the projection after it
+        # (ops.linear_norm), and the o / down projections add their rows into
+        # this rank's slice of the residual (beta = 1), whose slices are then
+        # all-gathered back into the full residual on every rank.
+        # fuse_norm=None takes this step on one rank; True asks for it on any
+        # number of ranks (the residual gather then runs in place).
+        if fuse_norm is None:
+            fuse_norm = G == 1
+        self.norm_fused = bool(fuse_norm) and batch == 1 and hasattr(ops, "linear_norm")
+        self.x = ops.gather_target("x", h) if (self.norm_fused and G > 1) else z(B * h)
+        self.x_l = self.x[plan.rank * h_l:(plan.rank + 1) * h_l] if self.norm_fused else None
         self.xq_h = ops.codes(B, h)        # codes of a hidden vector (normed, or the gathered attention)
         self.xq_f = ops.codes(B, s.ffn)    # codes of the gathered SwiGLU vector
         if self.fused:
@@ -150,6 +161,9 @@ class ShardedDecode:
     def step(self, pos: int) -> None:
         """Decode the tokens in ``self.tokens`` at position ``pos``; the full
         logits of every sequence land in ``self.logits`` ([batch][vocab])."""
+        if self.norm_fused:
+            self._step_norm_fused(pos)
+            return
         s, p, ops, B = self.shape, self.plan, self.ops, self.batch
         if not 0 <= pos < self.max_ctx:
             raise ValueError("position outside the KV cache")
@@ -189,6 +203,44 @@ class ShardedDecode:
             delta = self.d
         ops.norm_codes(self.x, delta, self.out_norm, self.xq_h, h, B, s.eps)
         ops.linear_codes(self.head, self.xq_h, self.logits_l, B, h, p.local_rows("head"))
+        self._gather(self.logits, self.logits_l, p.local_rows("head"))
+
+
+    def _step_norm_fused(self, pos: int) -> None:
+        """Batch-1 step: per layer the q/k/v projection with the attention
+        RMSNorm inside, attention, the o projection added into this rank's
+        residual slice, the residual gathered, the gate/up projection with the
+        FFN RMSNorm inside, SwiGLU, the down projection added into the slice,
+        the residual gathered."""
+        s, p, ops = self.shape, self.plan, self.ops
+        if not 0 <= pos < self.max_ctx:
+            raise ValueError("position outside the KV cache")
+        h, hd, G = s.hidden, s.head_dim, p.world
+        h_l = h // G
+        ops.embed(self.embed, self.tokens, self.x, 1, h, s.vocab)
+        for li, lay in enumerate(self.layers):
+            ops.linear_norm(lay["wqkv"], self.x, lay["attn_norm"], self.qkv, h, self.q_l + 2 * self.kv_l, s.eps)
+            kc, vc = ops.cache_layer(self.k_cache, li), ops.cache_layer(self.v_cache, li)
+            if G > 1:
+                ops.rope_attention(self.q, self.k, self.v, 1, p.heads, p.kv_heads, hd, pos, s.rope_theta, kc, vc,
+                                   self.max_ctx, self.a_l, None)
+                self._gather(self.a, self.a_l, h_l, self.xq_h, h)
+            else:
+                ops.rope_attention(self.q, self.k, self.v, 1, p.heads, p.kv_heads, hd, pos, s.rope_theta, kc, vc,
+                                   self.max_ctx, None, self.xq_h)
+            ops.linear_codes_add(lay["wo"], self.xq_h, self.x_l, h, h_l)
+            if G > 1:
+                self._gather(self.x, self.x_l, h_l)
+            ops.linear_norm(lay["w_gu"], self.x, lay["ffn_norm"], self.gu, h, 2 * self.f_l, s.eps)
+            if G == 1:
+                ops.swiglu_codes(self.g_l, self.u_l, self.xq_f, self.f_l)
+            else:
+                ops.swiglu(self.g_l, self.u_l, self.f_l_buf, self.f_l)
+                self._gather(self.f, self.f_l_buf, self.f_l, self.xq_f, s.ffn)
+            ops.linear_codes_add(lay["w_down"], self.xq_f, self.x_l, s.ffn, h_l)
+            if G > 1:
+                self._gather(self.x, self.x_l, h_l)
+        ops.linear_norm(self.head, self.x, self.out_norm, self.logits_l, h, p.local_rows("head"), s.eps)
         self._gather(self.logits, self.logits_l, p.local_rows("head"))
 
 
@@ -356,6 +408,17 @@ class GpuOps:
     def linear_codes(self, m, xq, out, batch, k, n_rows):
         self._ok(self.lib.b200q_matmul_xq(m.qtype, self.act, xq.data_ptr(), m.ptr, out.data_ptr(), batch, k, n_rows,
                                           1.0, 0.0, _native.WEIGHTS_STATIC, self._st()), "linear")
+
+    def linear_norm(self, m, x, gamma, out, k, n_rows, eps):
+        """out = m (RMSNorm(x) * gamma) for one row, the norm inside the GEMV."""
+        self._ok(self.lib.b200q_matmul_norm(m.qtype, self.act, x.data_ptr(), gamma.data_ptr(), eps, m.ptr,
+                                            out.data_ptr(), k, n_rows, 1.0, 0.0, _native.WEIGHTS_STATIC, self._st()),
+                 "linear+norm")
+
+    def linear_codes_add(self, m, xq, out, k, n_rows):
+        """out += m xq for one row of codes (the residual add in the epilogue)."""
+        self._ok(self.lib.b200q_matmul_xq(m.qtype, self.act, xq.data_ptr(), m.ptr, out.data_ptr(), 1, k, n_rows, 1.0,
+                                          1.0, _native.WEIGHTS_STATIC, self._st()), "linear+add")
 
     def quantize(self, x, xq, rows, k):
         self._ok(self.lib.b200q_quantize_rows(self.act, x.data_ptr(), rows, k, xq.data_ptr(), self._st()), "quantize")

@@ -275,6 +275,17 @@ B200Q_API int b200q_swiglu_q(const float* gate, const float* up, void* xq, int a
 B200Q_API int b200q_matmul_xq(int qtype, int act_mode, const void* xq, const void* w, float* y, int m, int k, int n,
                               float alpha, float beta, int flags, void* stream);
 
+/* y = alpha * (W xn) + beta * y for one fp32 row x of k, where
+ * xn = x * (1 / sqrt(sum(x^2) / k + eps)) * gamma: the RMSNorm of the decode
+ * graph (model_graph.cpp:674-697) and the projection that follows it
+ * (matvec_dispatch, model_graph.cpp:731-790) in one GEMV launch that
+ * normalizes and quantizes x while its weights stream. x and gamma 16-byte
+ * aligned; act_mode B200Q_ACT_X8 or X16; k / 32 <= 32 x the GEMV's consumer
+ * warps (B200Q_ESHAPE otherwise; every hidden size of the decode stacks
+ * fits). */
+B200Q_API int b200q_matmul_norm(int qtype, int act_mode, const float* x, const float* gamma, float eps, const void* w,
+                                float* y, int k, int n, float alpha, float beta, int flags, void* stream);
+
 /* out[r][s * cols + j] = in[s][r][j]: rows of a row-sharded output from the
  * all-gather of per-shard [rows][cols] blocks (identity for rows == 1). */
 B200Q_API int b200q_unshard_rows(const float* in, float* out, int shards, int rows, int cols, void* stream);

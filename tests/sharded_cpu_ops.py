@@ -56,6 +56,13 @@ class NumpyOps:
     def linear_codes(self, m, xq, out, batch, k, n_rows):
         out[: batch * n_rows] = (xq[: batch * k].reshape(batch, k) @ m.T).reshape(-1)
 
+    def linear_norm(self, m, x, gamma, out, k, n_rows, eps):
+        xn = x[:k] / np.sqrt(np.mean(x[:k] * x[:k]) + eps) * gamma
+        out[:n_rows] = m @ xn
+
+    def linear_codes_add(self, m, xq, out, k, n_rows):
+        out[:n_rows] += m @ xq[:k]
+
     def norm_codes(self, res, delta, gamma, xq, n, rows, eps):
         for r in range(rows):
             sl = slice(r * n, (r + 1) * n)

@@ -4,7 +4,8 @@ tests/test_sharded_multi_gpu.py through torch.distributed.run).
 Each rank holds its row slices of a two-layer stack (hidden 512, 4 query /
 2 kv heads, FFN 768, vocab 512), runs ShardedDecode with the device kernels
 and both all-gathers (NCCL, and the peer-memory kernel) for six positions at
-batch 1 and batch 3, and checks the
+batch 1 and batch 3 (batch 1 also with the RMSNorms inside the projections and
+the residual gathered in place), and checks the
 gathered logits against the unsharded float64 restatement
 (||d||_inf / ||ref||_inf <= 2e-3). Exits non-zero on a mismatch.
 """
@@ -44,10 +45,11 @@ def main() -> int:
         out_norm = (1 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
         plan = ShardPlan(shape, world, rank)
         tokens = [[3, 17, 5, 100, 7, 8], [9, 0, 511, 42, 42, 1], [1, 2, 3, 4, 5, 6]]
-        for collective, batch in (("nccl", 1), ("nccl", 3), ("peer", 1), ("peer", 3)):
+        for collective, batch, fuse in (("nccl", 1, False), ("nccl", 3, False), ("peer", 1, False), ("peer", 3, False),
+                                        ("nccl", 1, True), ("peer", 1, True)):
             ops = GpuOps(local, world=world, collective=collective, rank=rank)
             model = ShardedDecode(plan, 32, batch, [shard_layer(l, plan) for l in layers], embed,
-                                  shard_rows(head, plan, "head"), out_norm, ops)
+                                  shard_rows(head, plan, "head"), out_norm, ops, fuse_norm=fuse)
             refs = [DecodeRef(shape, layers, embed, head, out_norm, 32) for _ in range(batch)]
             for pos in range(len(tokens[0])):
                 model.tokens.copy_(torch.tensor([tokens[b][pos] for b in range(batch)], dtype=torch.int32))
@@ -57,7 +59,7 @@ def main() -> int:
                     want = refs[b].step(tokens[b][pos], pos)
                     err = np.max(np.abs(got[b] - want)) / np.max(np.abs(want))
                     if not err <= 2e-3:
-                        print(f"rank {rank} {collective} batch {batch} seq {b} pos {pos}: rel err {err:.3e}",
+                        print(f"rank {rank} {collective} batch {batch} fuse {fuse} seq {b} pos {pos}: rel err {err:.3e}",
                               flush=True)
                         bad += 1
             ops.close()

@@ -121,7 +121,8 @@ def test_attention_decode(H, KV, ctx):
 
 
 @pytest.mark.gpu
-def test_decode_stack_matches_restatement():
+@pytest.mark.parametrize("fused_norm", [True, False])
+def test_decode_stack_matches_restatement(fused_norm):
     from cybel_b200.decode import DecodeStack, StackShape, random_layer, random_rows
     from cybel_b200.formats import Q4_K, Q6_K
     from oracle.decode_ref import DecodeRef
@@ -133,7 +134,7 @@ def test_decode_stack_matches_restatement():
     head = random_rows(Q6_K, shape.vocab, shape.hidden, rng)
     out_norm = (1 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
     max_ctx = 64
-    dev = DecodeStack(shape, max_ctx, layers, embed, head, out_norm)
+    dev = DecodeStack(shape, max_ctx, layers, embed, head, out_norm, fused_norm=fused_norm)
     ref = DecodeRef(shape, layers, embed, head, out_norm, max_ctx)
     tokens = [3, 17, 5, 100, 511, 0, 42, 42, 7, 300, 64, 1]
     for pos, tok in enumerate(tokens):

@@ -248,3 +248,66 @@ def test_interleaved_strict_mode(monkeypatch, golden):
         qm.fused_expert_swiglu(x, gi, um, dm)
     monkeypatch.setenv("ANVIL_STRICT_NATIVE_QSG", "0")
     assert np.array_equal(qm.fused_expert_swiglu(x, gi, um, dm), qm.fused_expert_swiglu(x, gm, um, dm))
+
+
+@pytest.mark.parametrize("qt,n,k", [(12, 300, 4096), (14, 200, 4096), (12, 128, 8192), (8, 96, 2048)])
+@pytest.mark.parametrize("act,tol", [(2, 1e-5), (1, 1e-3)])
+def test_matmul_norm_matches_exact(oracle_mod, qt, n, k, act, tol):
+    """b200q_matmul_norm: RMSNorm(x) * gamma computed inside the GEMV, against
+    the double-precision product of the oracle's dequantized rows with the
+    norm restated in float64: x16 within the 1e-5 matvec bound; x8 within its
+    int8 activation quantization error (1e-3 of ||w_row|| * ||xn|| for these
+    inputs) and within 3e-5 of the separate GEMV given the same normalized x."""
+    import torch
+
+    from cybel_b200 import _native
+    from cybel_b200 import quantize as Q
+    from cybel_b200.quantized_matmul import DeviceMatrix
+
+    O = oracle_mod
+    rng = np.random.default_rng(qt + n + k + act)
+    W = Q.quantize(rng.normal(0.0, 0.02, size=(n, k)).astype(np.float32), qt)
+    x = (rng.standard_normal(k) * 3.0).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.5, size=k).astype(np.float32)
+    eps = 1e-5
+    xd = x.astype(np.float64)
+    xn = (xd / np.sqrt(np.mean(xd * xd) + eps) * gamma).astype(np.float32)
+    exact = O.matvec_f64(W, qt, xn, k, n)
+    dm = DeviceMatrix(qt, k, n, W)
+    xt, gt = torch.from_numpy(x).cuda(), torch.from_numpy(gamma).cuda()
+    L = _native.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    y = torch.full((n,), 0.5, dtype=torch.float32, device="cuda")
+    _native.check(L.b200q_matmul_norm(qt, act, xt.data_ptr(), gt.data_ptr(), eps, dm.ptr, y.data_ptr(), k, n, 1.0, 0.0,
+                                      _native.WEIGHTS_STATIC, st), "matmul_norm")
+    yy = y.cpu().numpy()
+    wn = O.row_norms(W, qt, k, n)
+    assert O.normalized_error(yy, exact, wn, xn) <= tol
+    if act == 1:
+        from cybel_b200.quantized_matmul import matmul_device
+
+        y_sep = matmul_device(torch.from_numpy(xn).cuda(), dm, act_mode=act).cpu().numpy()
+        assert O.normalized_error(yy, y_sep, wn, xn) <= 3e-5
+    # beta = 1 accumulates onto y (the residual form of the decode step)
+    y2 = torch.full((n,), 0.5, dtype=torch.float32, device="cuda")
+    _native.check(L.b200q_matmul_norm(qt, act, xt.data_ptr(), gt.data_ptr(), eps, dm.ptr, y2.data_ptr(), k, n, 1.0,
+                                      1.0, _native.WEIGHTS_STATIC, st), "matmul_norm beta")
+    assert O.normalized_error(y2.cpu().numpy() - 0.5, exact, wn, xn) <= tol
+
+
+def test_matmul_norm_rejects_long_rows(oracle_mod):
+    """A row too long to stage in one pass is refused (B200Q_ESHAPE), not computed."""
+    import torch
+
+    from cybel_b200 import _native
+    from cybel_b200 import quantize as Q
+    from cybel_b200.quantized_matmul import DeviceMatrix
+
+    k, n = 28672, 8
+    W = Q.quantize(np.random.default_rng(3).normal(0.0, 0.02, size=(n, k)).astype(np.float32), 12)
+    dm = DeviceMatrix(12, k, n, W)
+    x = torch.ones(k, device="cuda")
+    y = torch.zeros(n, device="cuda")
+    rc = _native.lib().b200q_matmul_norm(12, 1, x.data_ptr(), x.data_ptr(), 1e-5, dm.ptr, y.data_ptr(), k, n, 1.0, 0.0,
+                                         _native.WEIGHTS_STATIC, torch.cuda.current_stream().cuda_stream)
+    assert rc == -3

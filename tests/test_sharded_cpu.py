@@ -35,7 +35,7 @@ def _weights():
     return layers, embed, head, out_norm
 
 
-def _worker(rank, world, port, batch, q):
+def _worker(rank, world, port, batch, q, fuse=False):
     import torch.distributed as dist
 
     from cybel_b200.sharded import ShardedDecode, ShardPlan, shard_layer, shard_rows
@@ -48,7 +48,7 @@ def _worker(rank, world, port, batch, q):
         layers, embed, head, out_norm = _weights()
         plan = ShardPlan(TINY, world, rank)
         model = ShardedDecode(plan, 16, batch, [shard_layer(l, plan) for l in layers], embed,
-                              shard_rows(head, plan, "head"), out_norm, NumpyOps(world))
+                              shard_rows(head, plan, "head"), out_norm, NumpyOps(world), fuse_norm=fuse)
         outs = []
         for pos in range(len(TOKENS[0])):
             model.tokens[:] = [TOKENS[b][pos] for b in range(batch)]
@@ -65,8 +65,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("batch", [1, 3])
-def test_two_rank_sharded_decode_equals_unsharded(batch):
+@pytest.mark.parametrize("batch,fuse", [(1, False), (3, False), (1, True)])
+def test_two_rank_sharded_decode_equals_unsharded(batch, fuse):
     import multiprocessing as mp
 
     from oracle.decode_ref import DecodeRef
@@ -74,7 +74,7 @@ def test_two_rank_sharded_decode_equals_unsharded(batch):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, batch, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, batch, q, fuse)) for r in range(2)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=240) for _ in procs)
