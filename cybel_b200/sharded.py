@@ -124,10 +124,10 @@ class ShardedDecode:
         # (ops.linear_norm), and the o / down projections add their rows into
         # this rank's slice of the residual (beta = 1), whose slices are then
         # all-gathered back into the full residual on every rank.
-        # fuse_norm=None takes this step on one rank; True asks for it on any
-        # number of ranks (the residual gather then runs in place).
+        # fuse_norm (default on) applies at batch 1; with several ranks the
+        # residual gather runs in place (each rank's slice is its own input).
         if fuse_norm is None:
-            fuse_norm = G == 1
+            fuse_norm = True
         self.norm_fused = bool(fuse_norm) and batch == 1 and hasattr(ops, "linear_norm")
         self.x = ops.gather_target("x", h) if (self.norm_fused and G > 1) else z(B * h)
         self.x_l = self.x[plan.rank * h_l:(plan.rank + 1) * h_l] if self.norm_fused else None
