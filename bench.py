@@ -548,6 +548,37 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize(dev)
     launch_ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
     del graph
+    # The same chain in the other activation mode (x16 is the drop-ins'
+    # default: int16 codes, within 1e-5 of the fp32-activation product).
+    other = None
+    if ws == 1:
+        other_act = _native.ACT_X16 if act == _native.ACT_X8 else _native.ACT_X8
+
+        def step_other():
+            for i in range(C):
+                matmul_device(xt, mats[i], out=ys[i], act_mode=other_act)
+
+        with torch.cuda.stream(cap):
+            for _ in range(3):
+                step_other()
+        barrier()
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=cap):
+            step_other()
+        for _ in range(3):
+            g2.replay()
+        barrier()
+        reps = max(10, args.steps // 2)
+        e0.record(st)
+        for _ in range(reps):
+            g2.replay()
+        e1.record(st)
+        barrier()
+        ms_o = e0.elapsed_time(e1) / (reps * C)
+        gbs_o = W.nbytes / (ms_o / 1e3) / 1e9
+        other = {"act_mode": "x16" if other_act == _native.ACT_X16 else "x8", "ms_per_matvec": round(ms_o, 5),
+                 "weight_gbs": round(gbs_o, 1), "hbm_frac": round(gbs_o / _peak_hbm()[0], 4)}
+        del g2
 
     t = torch.tensor([ms_total, launch_ms], dtype=torch.float64, device=dev)
     if ws > 1:
@@ -647,6 +678,7 @@ def run_ours(args, ws, rank, local):
                 "h2d_bytes_per_step": C * K_DIM * 4,
                 "d2h_bytes_per_step": C * N_ROWS * 4,
             },
+            "other_act_mode": other,
             "gpu_launches": C * args.steps,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
