@@ -51,7 +51,7 @@ constexpr int kMaxStages = 48;
 // Weight bytes issued before the consumers have issued their activation
 // loads (B200Q_GEMV_PREFETCH_KB): about what HBM delivers to one SM while the
 // CTA waits for the preceding kernel.
-constexpr int kPrefetchKB = 48;
+constexpr int kPrefetchKB = 96;
 
 struct Plan {
     GemvParams p;
