@@ -45,6 +45,11 @@ class StackShape:
     eps: float = 1e-5
     linear_qtype: int = Q4_K
     head_qtype: int = Q6_K
+    embed_qtype: int | None = None  # token embedding rows; None: the linears' type
+
+    @property
+    def embedding_qtype(self) -> int:
+        return self.linear_qtype if self.embed_qtype is None else self.embed_qtype
 
     @property
     def head_dim(self) -> int:
@@ -165,7 +170,7 @@ class DecodeStack:
                 b = first[i % len(layers)]
                 lay = _Layer(b.wqkv.clone(), b.wo.clone(), b.w_gu.clone(), b.w_down.clone(), b.attn_norm, b.ffn_norm)
             self.layers.append(lay)
-        self.embed = DeviceMatrix(q, h, shape.vocab, embed)
+        self.embed = DeviceMatrix(shape.embedding_qtype, h, shape.vocab, embed)
         self.head = DeviceMatrix(shape.head_qtype, h, shape.vocab, head)
         self.out_norm = torch.from_numpy(out_norm).to(self.dev)
         cache_shape = (shape.layers, shape.kv_heads, max_ctx, shape.head_dim)
@@ -206,7 +211,8 @@ class DecodeStack:
         up = gp + 4 * f
         resid = 0.0 if linears_only else 1.0
         if not linears_only:
-            self._check(L.b200q_dequantize_rows(q, self.embed.ptr, self.token.data_ptr(), 1, x, h, s.vocab, st),
+            self._check(L.b200q_dequantize_rows(s.embedding_qtype, self.embed.ptr, self.token.data_ptr(), 1, x, h,
+                                                s.vocab, st),
                         "embedding")
         for li, lay in enumerate(self.layers):
             # RMSNorm inside the q/k/v GEMV (it normalizes and quantizes x while its weights stream)
@@ -240,6 +246,18 @@ class DecodeStack:
             self._check(L.b200q_add_rmsnorm_q(x, None, gamma.data_ptr(), None, xq, self.act_mode, k, 1, s.eps, st),
                         what + " norm")
         self._check(L.b200q_matmul_xq(qt, self.act_mode, xq, w, y, 1, k, n, 1.0, 0.0, W, st), what)
+
+    @classmethod
+    def from_gguf(cls, path, max_ctx: int, act_mode: int = _native.ACT_X16, device: int = 0,
+                  fused_norm: bool = True) -> "DecodeStack":
+        """A stack whose weights are the tensors of a llama-architecture GGUF
+        file (gguf_file.load_llama_stack), uploaded with their block layouts
+        unchanged."""
+        from .gguf_file import load_llama_stack
+
+        shape, layers, embed, head, out_norm = load_llama_stack(path)
+        return cls(shape, max_ctx, layers, embed, head, out_norm, act_mode=act_mode, device=device,
+                   fused_norm=fused_norm)
 
     def set_token(self, token: int) -> None:
         self.token.fill_(int(token))

@@ -115,7 +115,7 @@ class ShardedDecode:
                 for name, n in (("wq", q_l), ("wk", kv_l), ("wv", kv_l), ("w_gate", f_l), ("w_up", f_l)):
                     lay[name] = ops.matrix(qt, h, n, src[name])
             self.layers.append(lay)
-        self.embed = ops.matrix(qt, h, s.vocab, embed)
+        self.embed = ops.matrix(s.embedding_qtype, h, s.vocab, embed)
         self.head = ops.matrix(s.head_qtype, h, plan.local_rows("head"), head)
         self.out_norm = ops.vector(out_norm)
         self.k_cache, self.v_cache = ops.cache(s.layers, B, plan.kv_heads, max_ctx, hd)

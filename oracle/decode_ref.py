@@ -36,7 +36,7 @@ class DecodeRef:
             lay["attn_norm"] = src["attn_norm"].astype(np.float64)
             lay["ffn_norm"] = src["ffn_norm"].astype(np.float64)
             self.layers.append(lay)
-        self.embed = O.dequant(embed, q, h, shape.vocab).astype(np.float64)
+        self.embed = O.dequant(embed, shape.embedding_qtype, h, shape.vocab).astype(np.float64)
         self.head = O.dequant(head, shape.head_qtype, h, shape.vocab).astype(np.float64)
         self.out_norm = out_norm.astype(np.float64)
         hd = shape.head_dim
