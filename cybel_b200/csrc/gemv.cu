@@ -69,8 +69,11 @@ int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl, b
     const int nb = k / f.elems;
     const long long rb = static_cast<long long>(nb) * f.bytes;
     const int S = (nb + f.blocks_per_slice - 1) / f.blocks_per_slice;
-    const int max_warps = (dig == 1 && MR == 1) ? 16 : 12;  // kGemvWarps in gemv.cuh
+    int max_warps = (dig == 1 && MR == 1) ? 16 : 12;  // kGemvWarps in gemv.cuh
     if (S > max_warps) return B200Q_ESHAPE;
+    // B200Q_GEMV_WARPS caps the consumer warps (never below one per k-slice).
+    static const int warps_cap = env_int("B200Q_GEMV_WARPS", 0);
+    if (warps_cap > 0) max_warps = std::max(S, std::min(max_warps, warps_cap));
     static const int smem_budget = std::min(220, env_int("B200Q_GEMV_SMEM_KB", kSmemBudgetKB)) * 1024;
     static const int target = env_int("B200Q_STAGE_KB", kStageTargetKB) * 1024;
     static const int prefetch = env_int("B200Q_GEMV_PREFETCH_KB", kPrefetchKB) * 1024;
