@@ -468,6 +468,11 @@ int b200q_matmul_xq(int qtype, int act_mode, const void* xq, const void* w, floa
     return rc;
 }
 
+int b200q_gemv_plan(int qtype, int act_mode, int k, int n, int rows_per_launch, int fused_quantize, int num_sms,
+                    long long* out, int out_len) {
+    return gemv_plan_info(qtype, act_mode, k, n, rows_per_launch, fused_quantize != 0, num_sms, out, out_len);
+}
+
 int b200q_matmul_norm(int qtype, int act_mode, const float* x, const float* gamma, float eps, const void* w, float* y,
                       int k, int n, float alpha, float beta, int flags, void* stream) {
     Device* dev = nullptr;

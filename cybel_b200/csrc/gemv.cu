@@ -372,6 +372,22 @@ int gemv_norm_f32(int qtype, int act_mode, const void* w, const float* x, const 
                      gamma, eps);
 }
 
+int gemv_plan_info(int qtype, int act_mode, int k, int n, int mr, bool fq, int num_sms, long long* out, int out_len) {
+    if (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
+    if (!out || out_len < kPlanInfoFields || num_sms <= 0 || mr < 1 || mr > 4) return B200Q_EINVAL;
+    Plan pl;
+    const int dig = act_mode == B200Q_ACT_X8 ? 1 : 2;
+    const int rc = make_plan(qtype, dig, k, n, mr, num_sms, pl, fq);
+    if (rc != B200Q_OK) return rc;
+    const GemvParams& p = pl.p;
+    const long long x_bytes =
+        static_cast<long long>(mr) * xs_row_bytes(k, dig) + (fq ? static_cast<long long>(p.S * p.WR) * kFqWarpBytes + 128 : 0);
+    const long long v[kPlanInfoFields] = {pl.threads, pl.smem, pl.grid, p.S, p.WR, p.G, p.SW, p.R, p.NS,
+                                          p.stage_stride, p.PD, p.x_off, x_bytes, p.row_bytes, p.rows_cta};
+    for (int i = 0; i < kPlanInfoFields; ++i) out[i] = v[i];
+    return B200Q_OK;
+}
+
 int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev) {
     if (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
     if (k % 32) return B200Q_ESHAPE;

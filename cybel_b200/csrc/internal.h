@@ -55,6 +55,12 @@ int gemv_from_f32(int qtype, int act_mode, const void* w, const float* x, long l
 int gemv_norm_f32(int qtype, int act_mode, const void* w, const float* x, const float* gamma, float eps, float* y,
                   int k, int n, float alpha, float beta, Device* dev, cudaStream_t st, bool pdl, int flags);
 int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev);
+// The GEMV launch plan for (qtype, act_mode, k, n, mr activation rows per
+// launch, fq: quantizes fp32 x itself) on num_sms SMs, as kPlanInfoFields
+// values: threads, dynamic smem bytes, grid, S, WR, G, SW, R, NS,
+// stage_stride, PD, x_off, staged-activation bytes, row bytes, rows per CTA.
+constexpr int kPlanInfoFields = 15;
+int gemv_plan_info(int qtype, int act_mode, int k, int n, int mr, bool fq, int num_sms, long long* out, int out_len);
 // quantize_act kernel over `rows` contiguous rows of k into xq (row pitch xq_bytes_per_row).
 int launch_quantize_rows(int act_mode, const float* x, int rows, int k, uint8_t* xq, cudaStream_t st, bool pdl);
 // fresh (optional): set when the buffer was (re)allocated by this call; its

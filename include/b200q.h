@@ -286,6 +286,19 @@ B200Q_API int b200q_matmul_xq(int qtype, int act_mode, const void* xq, const voi
 B200Q_API int b200q_matmul_norm(int qtype, int act_mode, const float* x, const float* gamma, float eps, const void* w,
                                 float* y, int k, int n, float alpha, float beta, int flags, void* stream);
 
+/* The decode GEMV's launch plan for a matrix of n rows of k elements, without
+ * touching a device (no reference counterpart: a planning query for callers
+ * sizing resources and for tests). rows_per_launch: activation rows one launch
+ * carries (1-4); fused_quantize: 1 when the GEMV quantizes fp32 x itself (the
+ * matvec entry points), 0 when it reads codes (b200q_matmul_xq). Fills out[0..14]
+ * with threads per CTA, dynamic shared memory bytes, grid, k-slices, walkers
+ * per slice, walker groups, walkers per group, rows per stage, ring stages,
+ * stage stride, stages issued before the activation loads, ring offset and
+ * size of the staged activations, bytes per row, rows per CTA. Returns
+ * B200Q_OK, B200Q_ESHAPE when no plan fits, or B200Q_EINVAL. */
+B200Q_API int b200q_gemv_plan(int qtype, int act_mode, int k, int n, int rows_per_launch, int fused_quantize,
+                              int num_sms, long long* out, int out_len);
+
 /* out[r][s * cols + j] = in[s][r][j]: rows of a row-sharded output from the
  * all-gather of per-shard [rows][cols] blocks (identity for rows == 1). */
 B200Q_API int b200q_unshard_rows(const float* in, float* out, int shards, int rows, int cols, void* stream);
