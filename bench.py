@@ -121,6 +121,17 @@ class ClockSampler:
         }
 
 
+def _cpu_model() -> str:
+    """The host CPU's model name (Linux /proc/cpuinfo), or "unknown"."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def _cpu_reference_sample(W: np.ndarray, x: np.ndarray, budget_s: float = 12.0):
     """The reference's compiled simd_matvec_q4k on the host cores: GB/s."""
     from oracle import oracle as O
@@ -139,6 +150,7 @@ def _cpu_reference_sample(W: np.ndarray, x: np.ndarray, budget_s: float = 12.0):
             "unit": "GB/s",
             "cores": threads,
             "kind": "reference",
+            "cpu_model": _cpu_model(),
             "sample": f"{calls} x simd_matvec_q4k {N_ROWS}x{K_DIM} (one weight copy) in {dt:.1f} s, ANVIL_NUM_THREADS={threads}",
         }
     # Fallback: the oracle's scalar restatement, single thread.
@@ -154,6 +166,7 @@ def _cpu_reference_sample(W: np.ndarray, x: np.ndarray, budget_s: float = 12.0):
         "unit": "GB/s",
         "cores": 1,
         "kind": "port",
+        "cpu_model": _cpu_model(),
         "sample": f"{calls} x oracle matvec of {n_rows} rows of the {N_ROWS}x{K_DIM} layer in {dt:.1f} s",
     }
 
@@ -187,7 +200,7 @@ def run_reference(args, ws, rank):
         "data": "synthetic",
         "config": {"workload": f"q4k_matvec_{N_ROWS}x{K_DIM}", "copies": args.copies, "l2": "inputs > L2"},
         "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": base["cores"], "kind": base["kind"],
-                         "sample": base["sample"]},
+                         "cpu_model": base.get("cpu_model", _cpu_model()), "sample": base["sample"]},
         "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -669,6 +682,9 @@ def run_ours(args, ws, rank, local):
                 "frac": round(achieved / peak, 4),
                 "peak_source": peak_kind,
                 "traffic": _traffic_per_launch(),
+                # the reference engine's own byte counter adds the fp32 activation
+                # and output bytes to the weight bytes (model_graph.cpp:377-389)
+                "achieved_with_activation_bytes": round((wbytes + 4 * (K_DIM + N_ROWS)) / (avg_launch_ms / 1e3) / 1e9, 1),
                 "avg_launch_ms": round(avg_launch_ms, 5),
                 "isolated_launch_ms": round(launch_ms, 5),
             },
