@@ -216,11 +216,148 @@ def _peak_bf16():
     return 1590.0, "fallback"
 
 
+def _normal_w(seed: int, n: int, k: int) -> np.ndarray:
+    """N(0, 0.02) fp32 weights [n][k] from default_rng(seed)."""
+    return (np.random.default_rng(seed).standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
+
+
+def chain_time_us(dev, qt: int, W: np.ndarray, k: int, n: int, act: int, reps: int = 10,
+                  min_bytes: float = 300e6) -> float:
+    """Device time per matvec of a chain of C matvecs over C distinct resident
+    copies of W (C * bytes > 2 x L2), one fp32 x, captured as one CUDA graph
+    (PDL between launches) and replayed `reps` times after 3 warm-up replays."""
+    import torch
+
+    from cybel_b200.quantized_matmul import DeviceMatrix, matmul_device
+
+    C = max(8, int(min_bytes // W.nbytes) + 1)
+    mats = [DeviceMatrix(qt, k, n, W) for _ in range(C)]
+    x = torch.from_numpy(np.random.default_rng(1).standard_normal(k).astype(np.float32)).to(dev)
+    ys = [torch.empty(n, dtype=torch.float32, device=dev) for _ in range(C)]
+
+    def step():
+        for i in range(C):
+            matmul_device(x, mats[i], out=ys[i], act_mode=act)
+
+    cap = torch.cuda.Stream(dev)
+    with torch.cuda.stream(cap):
+        for _ in range(3):
+            step()
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=cap):
+        step()
+    for _ in range(3):
+        g.replay()
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    e0.record(st)
+    for _ in range(reps):
+        g.replay()
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / (reps * C)
+    del g, mats, ys
+    torch.cuda.empty_cache()
+    return us
+
+
+def _ref_call_time(fn, budget_s: float, min_calls: int = 2) -> tuple[float, int]:
+    """Mean seconds per call of fn() over about budget_s (after one warm-up)."""
+    fn()
+    calls, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s or calls < min_calls:
+        fn()
+        calls += 1
+    return (time.perf_counter() - t0) / calls, calls
+
+
+def _ref_threads() -> int:
+    threads = len(os.sched_getaffinity(0))
+    os.environ["ANVIL_NUM_THREADS"] = str(threads)
+    return threads
+
+
+def c1_bench(dev, no_cpu: bool = False):
+    """Q4_0 4096 x 4096 (W ~ N(0, 0.02) from default_rng(0), packed by the
+    ggml Q4_0 layout; x from default_rng(1)) in both activation modes; the
+    CPU baseline is gguf-py dequantize + a numpy fp32 product (the reference
+    engine has no Q4_0 kernel)."""
+    from cybel_b200 import _native
+    from cybel_b200 import quantize as Q
+
+    n = k = 4096
+    w = np.random.default_rng(0).normal(0.0, 0.02, size=(n, k)).astype(np.float32)
+    W = Q.quantize(w, 2)
+    peak, _ = _peak_hbm()
+    rec = {"workload": "q4_0_matvec_4096x4096", "weight_bytes": int(W.nbytes)}
+    for name, act in (("x8", _native.ACT_X8), ("x16", _native.ACT_X16)):
+        us = chain_time_us(dev, 2, W, k, n, act)
+        gbs = W.nbytes / (us * 1e-6) / 1e9
+        rec[name] = {"us_per_matvec": round(us, 2), "weight_gbs": round(gbs, 1), "hbm_frac": round(gbs / peak, 4)}
+    if not no_cpu:
+        try:
+            import gguf
+
+            x = np.random.default_rng(1).standard_normal(k).astype(np.float32)
+            qt = gguf.GGMLQuantizationType.Q4_0
+
+            def cpu():
+                return gguf.dequantize(W, qt).reshape(n, k) @ x
+
+            sec, calls = _ref_call_time(cpu, 2.0)
+            rec["cpu_baseline"] = {"value": round(W.nbytes / sec / 1e9, 3), "unit": "GB/s", "cores": 1,
+                                   "kind": "port", "cpu_model": _cpu_model(),
+                                   "sample": f"{calls} x gguf-py dequantize + numpy fp32 matvec (no reference "
+                                             f"Q4_0 kernel exists), {sec * 1e3:.1f} ms per call"}
+        except ImportError:
+            rec["cpu_baseline"] = None
+    return rec
+
+
+C2_SHAPES = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336)]  # (n, k), Llama-3-8B linears
+
+
+def c2_bench(dev, no_cpu: bool = False):
+    """Q8_0 and Q4_K matvec sweep at the Llama-3-8B linear shapes, x8 and
+    x16, with the reference's simd_matvec_* on all host cores beside each."""
+    from cybel_b200 import _native
+    from cybel_b200 import quantize as Q
+
+    peak, _ = _peak_hbm()
+    out = []
+    ref_ok = False
+    if not no_cpu:
+        from oracle import oracle as O
+
+        ref_ok = O.ref_available()
+        threads = _ref_threads()
+    for i, (n, k) in enumerate(C2_SHAPES):
+        w = _normal_w(i, n, k)
+        x = np.random.default_rng(100 + i).standard_normal(k).astype(np.float32)
+        for qt, name in ((12, "q4_k"), (8, "q8_0")):
+            W = Q.quantize(w, qt)
+            rec = {"qtype": name, "n": n, "k": k, "weight_bytes": int(W.nbytes)}
+            for mode, act in (("x8", _native.ACT_X8), ("x16", _native.ACT_X16)):
+                us = chain_time_us(dev, qt, W, k, n, act, min_bytes=270e6)
+                gbs = W.nbytes / (us * 1e-6) / 1e9
+                rec[mode] = {"us_per_matvec": round(us, 2), "weight_gbs": round(gbs, 1),
+                             "hbm_frac": round(gbs / peak, 4)}
+            if ref_ok:
+                sec, calls = _ref_call_time(lambda: O.ref_matvec(qt, W, x, k, n), 0.6)
+                rec["cpu_baseline"] = {"value": round(W.nbytes / sec / 1e9, 3), "unit": "GB/s", "cores": threads,
+                                       "kind": "reference",
+                                       "sample": f"{calls} x simd_matvec_{'q4k' if qt == 12 else 'q8_0'}"}
+            out.append(rec)
+    return out
+
+
 TILE_SHAPES = [(14336, 4096), (4096, 14336)]  # (n, k): Llama-3-8B gate/up and down
 TILE_MS = [8, 32, 128]
 
 
-def tile_bench(dev, steps: int, warmup: int, shapes=TILE_SHAPES, ms=TILE_MS, copies: int = 8):
+def tile_bench(dev, steps: int, warmup: int, shapes=TILE_SHAPES, ms=TILE_MS, copies: int = 8, no_cpu: bool = True):
     """Speculative-verify batched matmul on the tile path (tcgen05, fp16
     operands): per (shape, m), `copies` distinct resident Q4_K weight copies
     (> 2 x L2 in total) are multiplied by an m-row activation block, replayed
@@ -235,6 +372,12 @@ def tile_bench(dev, steps: int, warmup: int, shapes=TILE_SHAPES, ms=TILE_MS, cop
     peak_hbm, _ = _peak_hbm()
     peak_tc, _ = _peak_bf16()
     out = []
+    ref_ok = False
+    if not no_cpu:
+        from oracle import oracle as O
+
+        ref_ok = O.ref_available()
+        threads = _ref_threads()
     for n, k in shapes:
         rng = np.random.default_rng(n + k)
         W = Q.quantize_q4_k(rng.normal(0.0, 0.02, size=(n, k)).astype(np.float32))
@@ -269,20 +412,57 @@ def tile_bench(dev, steps: int, warmup: int, shapes=TILE_SHAPES, ms=TILE_MS, cop
             del g
             gbs = W.nbytes / (us * 1e-6) / 1e9
             tflops = 2.0 * m * n * k / (us * 1e-6) / 1e12
-            out.append({
+            rec = {
                 "n": n, "k": k, "m": m,
                 "us_per_matmul": round(us, 2),
                 "weight_gbs": round(gbs, 1),
                 "hbm_frac": round(gbs / peak_hbm, 4),
                 "tflops": round(tflops, 1),
                 "tensor_frac": round(tflops / peak_tc, 4),
-            })
+            }
+            if ref_ok:
+                Xh = X.cpu().numpy()
+                sec, calls = _ref_call_time(lambda: O.ref_matmul(12, W, Xh, k, n), 0.5)
+                rec["cpu_baseline"] = {"us_per_matmul": round(sec * 1e6, 1), "tflops": round(2.0 * m * n * k / sec / 1e12, 4),
+                                       "cores": threads, "kind": "reference",
+                                       "sample": f"{calls} x simd_matmul_q4k m={m}"}
+            out.append(rec)
         del mats
         torch.cuda.empty_cache()
     return out
 
 
-def decode_bench(dev, steps: int, warmup: int, shape_name: str = "llama3_8b", ctx: int = 2048):
+def _cpu_layer_baseline(shape, layer, head, batch: int = 1, budget_s: float = 0.6):
+    """The reference's CPU ops for one token's linears, timed per layer on all
+    host cores: the 7 matvecs of one layer (simd_matvec_*; simd_matmul_* at
+    batch > 1) times the layer count, plus the LM head. tok/s = batch / that."""
+    from cybel_b200 import decode as D
+    from oracle import oracle as O
+
+    if not O.ref_available():
+        return None
+    threads = _ref_threads()
+    q = shape.linear_qtype
+    shapes = D.layer_matrix_shapes(shape)
+    rng = np.random.default_rng(3)
+
+    def run(W, qt, k, n):
+        X = rng.standard_normal((batch, k)).astype(np.float32)
+        if batch == 1:
+            return _ref_call_time(lambda: O.ref_matvec(qt, W, X[0], k, n), budget_s / 8, 1)[0]
+        return _ref_call_time(lambda: O.ref_matmul(qt, W, X, k, n), budget_s / 8, 1)[0]
+
+    layer_s = sum(run(layer[name], q, k, n) for name, (n, k) in shapes.items())
+    head_s = run(head, shape.head_qtype, shape.hidden, shape.vocab)
+    tok_s = shape.layers * layer_s + head_s
+    return {"ms_per_step": round(tok_s * 1e3, 2), "tok_s": round(batch / tok_s, 3), "cores": threads,
+            "kind": "reference",
+            "sample": f"one layer's 7 {'simd_matvec' if batch == 1 else f'simd_matmul (m={batch})'} calls x "
+                      f"{shape.layers} layers + the LM head, {threads} threads"}
+
+
+def decode_bench(dev, steps: int, warmup: int, shape_name: str = "llama3_8b", ctx: int = 2048,
+                 no_cpu: bool = True):
     """Single-token decode of the Llama-3-8B-shaped stack at context `ctx`
     (KV cache prefilled with random values): one step = embedding, 32 layers
     of norm / qkv / rope / attention / o / norm / SwiGLU FFN, final norm and
@@ -303,6 +483,7 @@ def decode_bench(dev, steps: int, warmup: int, shape_name: str = "llama3_8b", ct
     head = D.random_rows(shape.head_qtype, shape.vocab, shape.hidden, rng, block_rows=16032)
     out_norm = (1 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
     stack = D.DecodeStack(shape, ctx, [layer], embed, head, out_norm, act_mode=2)
+    cpu = None if no_cpu else _cpu_layer_baseline(shape, layer, head)
     del layer, embed, head
     stack.k_cache.normal_()
     stack.v_cache.normal_()
@@ -345,6 +526,7 @@ def decode_bench(dev, steps: int, warmup: int, shape_name: str = "llama3_8b", ct
         "matvec_hbm_frac": round(wbytes / (res["linears"] * 1e-3) / 1e9 / peak, 4),
         "step_hbm_frac": round((wbytes + kv_bytes) / (res["step"] * 1e-3) / 1e9 / peak, 4),
         "act_mode": "x16",
+        "cpu_baseline": cpu,
     }
     del stack
     torch.cuda.empty_cache()
@@ -352,7 +534,7 @@ def decode_bench(dev, steps: int, warmup: int, shape_name: str = "llama3_8b", ct
 
 
 def sharded_decode_bench(dev, ws, rank, local, steps: int, warmup: int, batch: int = 1, ctx: int = 2048,
-                         shape_name: str = "llama3_70b", collective: str = "peer"):
+                         shape_name: str = "llama3_70b", collective: str = "peer", no_cpu: bool = True):
     """Llama-3-70B-shaped Q4_K decode row-sharded over the ws ranks of this
     node (rank g holds rows [g n/ws, (g+1) n/ws) of every linear and the
     matching heads; all-gathers of the partial outputs by the peer-memory
@@ -380,6 +562,7 @@ def sharded_decode_bench(dev, ws, rank, local, steps: int, warmup: int, batch: i
     ops = GpuOps(local, act_mode=act, world=ws, collective=collective, rank=rank)
     model = ShardedDecode(plan, ctx, batch, [shard_layer(layer, plan)], embed, shard_rows(head, plan, "head"),
                           out_norm, ops)
+    cpu = None if (no_cpu or ws > 1 or rank != 0) else _cpu_layer_baseline(shape, layer, head, batch)
     del layer, embed, head
     model.k_cache.normal_()
     model.v_cache.normal_()
@@ -445,7 +628,9 @@ def sharded_decode_bench(dev, ws, rank, local, steps: int, warmup: int, batch: i
         "collectives_per_step": 4 * shape.layers + 1 if ws > 1 else 0,
         "collective": (collective if ws > 1 else None),
         "cuda_graph": graphed,
-        "act_mode": "x16" if act == _native.ACT_X16 else "x8 (tile path for Q4_K)",
+        "act_mode": ("fp32 rows, Q4_K on the tile path (fp16 operands)" if model.tile
+                     else ("x16" if act == _native.ACT_X16 else "x8")),
+        "cpu_baseline": cpu,
     }
     if not graphed:
         rec["graph_error"] = err
@@ -637,20 +822,25 @@ def run_ours(args, ws, rank, local):
     avg_launch_ms = ms_total / (C * args.steps)
     achieved = wbytes / (avg_launch_ms / 1e3) / 1e9
     cpu = _cpu_reference_sample(W, x) if (rank == 0 and ws == 1 and not args.no_cpu) else None
+    del mats, ys
+    torch.cuda.empty_cache()
+    no_cpu = args.no_cpu or rank != 0
+    c1 = c2 = None
+    if ws == 1 and not args.no_sweep:
+        c1 = c1_bench(dev, no_cpu)
+        c2 = c2_bench(dev, no_cpu)
     tile = None
     if ws == 1 and not args.no_tile:
-        del mats, ys
-        torch.cuda.empty_cache()
-        tile = tile_bench(dev, max(10, args.steps // 2), args.warmup)
+        tile = tile_bench(dev, max(10, args.steps // 2), args.warmup, no_cpu=no_cpu)
     decode = None
     if ws == 1 and not args.no_decode:
-        decode = decode_bench(dev, max(10, args.steps // 2), args.warmup)
-    sharded = None
+        decode = decode_bench(dev, max(10, args.steps // 2), args.warmup, no_cpu=no_cpu)
+    sharded = sharded8 = None
     if not args.no_decode:
-        if ws > 1:
-            del mats, ys
-            torch.cuda.empty_cache()
-        sharded = sharded_decode_bench(dev, ws, rank, local, 10, args.warmup, 1, 2048, "llama3_70b", "peer")
+        sharded = sharded_decode_bench(dev, ws, rank, local, 10, args.warmup, 1, 2048, "llama3_70b", "peer",
+                                       no_cpu=no_cpu)
+        sharded8 = sharded_decode_bench(dev, ws, rank, local, 10, args.warmup, 8, 2048, "llama3_70b", "peer",
+                                        no_cpu=no_cpu)
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -698,9 +888,12 @@ def run_ours(args, ws, rank, local):
             "gpu_launches": C * args.steps,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "c1_q4_0": c1,
+            "c2_sweep": c2,
             "tile": tile,
             "decode": decode,
             "sharded_decode": sharded,
+            "sharded_decode_b8": sharded8,
         }
         print(json.dumps(line), flush=True)
     if ws > 1:
@@ -719,7 +912,8 @@ def main():
     ap.add_argument("--pdl", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-tile", action="store_true", help="skip the tile-path (batched matmul) summary")
-    ap.add_argument("--no-decode", action="store_true", help="skip the Llama-3-8B decode-step summary")
+    ap.add_argument("--no-decode", action="store_true", help="skip the Llama-3-8B / 70B decode-step summaries")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the Q4_0 and Q8_0/Q4_K shape-sweep records")
     ap.add_argument("--workload", default="gemv", choices=["gemv", "tile", "decode", "sharded"])
     ap.add_argument("--decode-shape", default=None, choices=["llama3_8b", "llama3_70b"])
     ap.add_argument("--batch", type=int, default=1)

@@ -63,6 +63,8 @@ SIGNATURES.update(
         "b200q_matmul_ex": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
         "b200q_matvec_isums": ([_i, _i, _vp, _vp, _vp, _vp, _i, _i, _vp], _i),
         "b200q_matvec_noalloc": ([_i, _i, _vp, _vp, _vp, _i, _i, _vp], _i),
+        "b200q_matvec_quant": ([_vp, _i, _vp, _vp, _i, _i, _vp], _i),
+        "b200q_matvec_dispatch": ([_vp, _vp, _i, _vp, _vp, _i, _i, _vp], _i),
         "b200q_add_rmsnorm": ([_vp, _vp, _vp, _vp, _i, _i, ctypes.c_float, _vp], _i),
         "b200q_rope_kv": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, ctypes.c_float, _vp, _vp, _i, _vp], _i),
         "b200q_attention_decode": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp], _i),
@@ -88,6 +90,7 @@ SIGNATURES.update(
         "b200q_last_error": ([], _i),
         "b200q_status_string": ([_i], ctypes.c_char_p),
         "b200q_device_status": ([_i], _i),
+        "b200q_set_peer_wait_ns": ([ctypes.c_longlong], ctypes.c_longlong),
         "b200q_weight_cache_clear": ([], None),
         "b200q_weight_cache_evict": ([_vp], _i),
         "b200q_weight_cache_bytes": ([], ctypes.c_longlong),
@@ -127,3 +130,17 @@ def lib() -> ctypes.CDLL:
 def check(status: int, what: str) -> None:
     if int(status) != 0:
         raise NativeError(status, what)
+
+
+STATUS_TIMEOUT = 1  # device status bit: a kernel's bounded wait gave up
+
+
+def check_device(device: int, what: str = "device status") -> None:
+    """Raise NativeError(B200Q_ETIMEOUT) if a kernel on `device` recorded a
+    wait that gave up since the last check (call after synchronizing the
+    stream the work ran on); the status is cleared by the read."""
+    v = int(lib().b200q_device_status(int(device)))
+    if v < 0:
+        raise NativeError(v, what)
+    if v & STATUS_TIMEOUT:
+        raise NativeError(-7, what)

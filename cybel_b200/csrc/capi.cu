@@ -90,6 +90,12 @@ Device* device_state(int dev, int* err) {
     return d;
 }
 
+Device* device_state_if_present(int dev) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (dev < 0 || dev >= static_cast<int>(g_devs.size())) return nullptr;
+    return g_devs[dev];
+}
+
 int current_device_state(Device** out) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess) return B200Q_ENODEV;
@@ -318,6 +324,47 @@ int b200q_matmul_ex(int qtype, int act_mode, const float* x, const void* w, floa
 int b200q_matmul(int qtype, int act_mode, const float* x, const void* w, float* y, int m, int k, int n,
                  void* stream) {
     return b200q_matmul_ex(qtype, act_mode, x, w, y, m, k, n, 0, stream);
+}
+
+// model_graph.cpp:731-747 (matvec_quant): the graph dispatches a quantized
+// linear by qtype and zero-fills y for a qtype it has no kernel for.
+int b200q_matvec_quant(const void* w_quant, int qtype, const float* x, float* y, int cols, int rows, void* stream) {
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int rc = B200Q_OK;
+    FmtInfo f;
+    if (!y || rows <= 0) {
+        rc = B200Q_EINVAL;
+    } else if (!fmt_info(qtype, f)) {
+        rc = cudaMemsetAsync(y, 0, static_cast<size_t>(rows) * sizeof(float), st) == cudaSuccess ? B200Q_OK
+                                                                                                  : B200Q_ECUDA;
+    } else {
+        Device* dev = nullptr;
+        rc = current_device_state(&dev);
+        if (rc == B200Q_OK)
+            rc = launch_gemv(qtype, act_mode_now(), w_quant, x, y, 1, cols, rows, cols, rows, nullptr, dev, st,
+                             pdl_enabled(), 0);
+    }
+    set_last_error(rc);
+    return rc;
+}
+
+// model_graph.cpp:749-760 (matvec_dispatch): fp32 weights when present, else
+// the quantized weights when qtype > 0, else a zeroed y.
+int b200q_matvec_dispatch(const float* w_f32, const void* w_quant, int qtype, const float* x, float* y, int rows,
+                          int cols, void* stream) {
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (w_f32) {
+        const int rc = launch_matvec_f32(w_f32, x, y, rows, cols, st);
+        set_last_error(rc);
+        return rc;
+    }
+    if (w_quant && qtype > 0) return b200q_matvec_quant(w_quant, qtype, x, y, cols, rows, stream);
+    int rc = B200Q_EINVAL;
+    if (y && rows > 0)
+        rc = cudaMemsetAsync(y, 0, static_cast<size_t>(rows) * sizeof(float), st) == cudaSuccess ? B200Q_OK
+                                                                                                  : B200Q_ECUDA;
+    set_last_error(rc);
+    return rc;
 }
 
 int b200q_matvec_isums(int qtype, int act_mode, const float* x, const void* w, float* y, int* isums, int k, int n,
@@ -882,13 +929,20 @@ const char* b200q_status_string(int status) {
 }
 
 int b200q_device_status(int device) {
-    int err = B200Q_OK;
-    Device* d = device_state(device, &err);
-    if (!d) return err;
-    const int v = *d->status_host;
-    *d->status_host = 0;
+    if (device < 0) return B200Q_ENODEV;
+    // Reads only what exists: the host-mapped word of the regular entry
+    // points and the word inside b200q_matvec_noalloc's fixed array; neither
+    // is created here, so this allocates nothing.
+    int v = noalloc_take_status(device);
+    if (v < 0) return v;
+    if (Device* d = device_state_if_present(device)) {
+        v |= *d->status_host;
+        *d->status_host = 0;
+    }
     return v;
 }
+
+long long b200q_set_peer_wait_ns(long long ns) { return set_peer_wait_ns(ns); }
 
 void b200q_weight_cache_clear(void) {
     std::lock_guard<std::mutex> lk(g_w_mu);

@@ -6,9 +6,9 @@
 // attention that follows), restated for one B200 so that a whole layer stack
 // runs on the device and can be captured in one CUDA graph.
 //
-//  * add_rmsnorm_kernel: one CTA per row; residual += delta, out = residual *
+//  * b200q_add_rmsnorm_kernel: one CTA per row; residual += delta, out = residual *
 //    (1 / sqrt(mean(residual^2) + eps)) * gamma (the reference's formula).
-//  * rope_kv_kernel: interleaved pairs (2p, 2p+1) rotated by pos *
+//  * b200q_rope_kv_kernel: interleaved pairs (2p, 2p+1) rotated by pos *
 //    theta^(-2p / head_dim), as the reference; the rotated k and v are
 //    written to fp16 caches [sequence][kv_head][max_ctx][head_dim].
 //  * attention: split over the context (flash-decoding): one CTA per
@@ -39,7 +39,7 @@ constexpr int kMaxGroup = 8;     // query heads per kv head
 // also quantized (x8 / x16 codes, the GEMV's activation layout) into xq, so
 // the projections that follow read codes directly (out may then be null).
 template <int DIG>
-__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __restrict__ res,
+__global__ void __launch_bounds__(kNormThreads) b200q_add_rmsnorm_kernel(float* __restrict__ res,
                                                                    const float* __restrict__ delta,
                                                                    const float* __restrict__ gamma,
                                                                    float* __restrict__ out, uint8_t* __restrict__ xq,
@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(float* __rest
 // instead of a second pass over the residual after the reduction).
 constexpr int kNormRegVec = 4;  // float4 per thread
 template <int DIG>
-__global__ void __launch_bounds__(kNormThreads) add_rmsnorm_reg_kernel(float* __restrict__ res,
+__global__ void __launch_bounds__(kNormThreads) b200q_add_rmsnorm_reg_kernel(float* __restrict__ res,
                                                                        const float* __restrict__ delta,
                                                                        const float* __restrict__ gamma,
                                                                        float* __restrict__ out,
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_reg_kernel(float* __
 // Threads [0, (n_heads + n_kv) * hd/2): one rotation pair each; threads
 // [that, + n_kv * hd): one v element each. blockIdx.y = sequence of the
 // batch (its own q/k/v rows and cache).
-__global__ void rope_kv_kernel(float* __restrict__ q, float* __restrict__ k, const float* __restrict__ v, int n_heads,
+__global__ void b200q_rope_kv_kernel(float* __restrict__ q, float* __restrict__ k, const float* __restrict__ v, int n_heads,
                                int n_kv, int hd, int pos, float log2_theta, __half* __restrict__ kc,
                                __half* __restrict__ vc, int max_ctx) {
     griddep_launch_dependents();
@@ -214,7 +214,7 @@ constexpr int kPartStride = kHeadDim + 2;
 // split, each lane accumulating its 4 dims for the G heads in registers,
 // then a reduction over the warps through shared memory. All loads of a
 // warp's positions are issued before their arithmetic.
-__global__ void __launch_bounds__(kAttnWarps * 32) attn_chunk_kernel(const float* __restrict__ q,
+__global__ void __launch_bounds__(kAttnWarps * 32) b200q_attn_chunk_kernel(const float* __restrict__ q,
                                                                      const __half* __restrict__ kc,
                                                                      const __half* __restrict__ vc,
                                                                      float* __restrict__ part, int n_heads, int n_kv,
@@ -361,7 +361,7 @@ __device__ __forceinline__ void quantize_lane_group(float v, uint8_t* base, int 
 // DIG > 0: the attention output row of each sequence (n_heads * head_dim
 // elements) is also quantized into xq for the o projection (out may be null).
 template <int DIG>
-__global__ void __launch_bounds__(kHeadDim) attn_combine_kernel(const float* __restrict__ part, float* __restrict__ out,
+__global__ void __launch_bounds__(kHeadDim) b200q_attn_combine_kernel(const float* __restrict__ part, float* __restrict__ out,
                                                                 uint8_t* __restrict__ xq, int n_chunks) {
     griddep_launch_dependents();
     griddep_wait();
@@ -412,13 +412,13 @@ __global__ void __launch_bounds__(kHeadDim) attn_combine_kernel(const float* __r
 //  * the CTA whose chunk holds `pos` rotates the new key and appends it and
 //    the new value to the fp16 caches before reading its chunk;
 //  * each CTA scores and weights its kAttnChunk positions like
-//    attn_chunk_kernel and writes its partial records;
+//    b200q_attn_chunk_kernel and writes its partial records;
 //  * the CTA that finishes last for a (kv head, sequence) -- an arrival
 //    counter, reset by that CTA -- merges the chunks (max rescaling) and
 //    writes the output rows and, with DIG > 0, their x8 / x16 codes. No CTA
 //    waits for another (threadfence-reduction pattern).
 template <int G, int DIG>
-__global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(
+__global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, __half* __restrict__ kc,
     __half* __restrict__ vc, float* __restrict__ part, int* __restrict__ counters, float* __restrict__ out,
     uint8_t* __restrict__ xq, int n_heads, int n_kv, int pos, int max_ctx, float log2_theta, float scale) {
@@ -615,7 +615,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) attn_decode_kernel(
 
 // out = silu(gate) * up, element-wise (the SiLU * up step of
 // quantized_matmul.cpp:2380-2412, as the fused expert kernel computes it).
-__global__ void swiglu_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ out,
+__global__ void b200q_swiglu_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ out,
                               long long n) {
     griddep_launch_dependents();
     griddep_wait();
@@ -627,7 +627,7 @@ __global__ void swiglu_kernel(const float* __restrict__ g, const float* __restri
 
 // out[r][s * cols + j] = in[s][r][j]: the row-major [rows][shards * cols]
 // view of an all-gather of per-shard [rows][cols] blocks.
-__global__ void unshard_rows_kernel(const float* __restrict__ in, float* __restrict__ out, int shards, int rows,
+__global__ void b200q_unshard_rows_kernel(const float* __restrict__ in, float* __restrict__ out, int shards, int rows,
                                     int cols) {
     griddep_launch_dependents();
     griddep_wait();
@@ -671,16 +671,16 @@ int launch_add_rmsnorm(float* res, const float* delta, const float* gamma, float
     uint8_t* q = static_cast<uint8_t*>(xq);
     cudaError_t e;
     if (n <= 4 * kNormRegVec * kNormThreads) {
-        if (!xq) e = cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<0>, res, delta, gamma, out, q, n, eps);
+        if (!xq) e = cudaLaunchKernelEx(&cfg, b200q_add_rmsnorm_reg_kernel<0>, res, delta, gamma, out, q, n, eps);
         else if (act_mode == B200Q_ACT_X8)
-            e = cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<1>, res, delta, gamma, out, q, n, eps);
-        else e = cudaLaunchKernelEx(&cfg, add_rmsnorm_reg_kernel<2>, res, delta, gamma, out, q, n, eps);
+            e = cudaLaunchKernelEx(&cfg, b200q_add_rmsnorm_reg_kernel<1>, res, delta, gamma, out, q, n, eps);
+        else e = cudaLaunchKernelEx(&cfg, b200q_add_rmsnorm_reg_kernel<2>, res, delta, gamma, out, q, n, eps);
     } else if (!xq) {
-        e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<0>, res, delta, gamma, out, q, n, eps);
+        e = cudaLaunchKernelEx(&cfg, b200q_add_rmsnorm_kernel<0>, res, delta, gamma, out, q, n, eps);
     } else if (act_mode == B200Q_ACT_X8) {
-        e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<1>, res, delta, gamma, out, q, n, eps);
+        e = cudaLaunchKernelEx(&cfg, b200q_add_rmsnorm_kernel<1>, res, delta, gamma, out, q, n, eps);
     } else {
-        e = cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel<2>, res, delta, gamma, out, q, n, eps);
+        e = cudaLaunchKernelEx(&cfg, b200q_add_rmsnorm_kernel<2>, res, delta, gamma, out, q, n, eps);
     }
     return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
@@ -694,7 +694,7 @@ int launch_rope_kv(float* q, float* k, const float* v, int batch, int n_heads, i
     const int threads = (n_heads + n_kv) * (hd / 2) + n_kv * hd;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_cfg(dim3((threads + 255) / 256, batch), dim3(256), st, attr);
-    return cudaLaunchKernelEx(&cfg, rope_kv_kernel, q, k, v, n_heads, n_kv, hd, pos, log2f(theta),
+    return cudaLaunchKernelEx(&cfg, b200q_rope_kv_kernel, q, k, v, n_heads, n_kv, hd, pos, log2f(theta),
                               static_cast<__half*>(kc), static_cast<__half*>(vc), max_ctx) == cudaSuccess
                ? B200Q_OK
                : B200Q_ECUDA;
@@ -715,7 +715,7 @@ int launch_attention(const float* q, const void* kc, const void* vc, float* out,
     if (rc != B200Q_OK) return rc;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(n_kv, n_chunks, batch), dim3(kAttnWarps * 32), st, attr);
-    if (cudaLaunchKernelEx(&cfg, attn_chunk_kernel, q, static_cast<const __half*>(kc), static_cast<const __half*>(vc),
+    if (cudaLaunchKernelEx(&cfg, b200q_attn_chunk_kernel, q, static_cast<const __half*>(kc), static_cast<const __half*>(vc),
                            static_cast<float*>(part), n_heads, n_kv, ctx, max_ctx,
                            1.0f / sqrtf(static_cast<float>(hd))) != cudaSuccess)
         return B200Q_ECUDA;
@@ -723,9 +723,9 @@ int launch_attention(const float* q, const void* kc, const void* vc, float* out,
     const float* pp = static_cast<const float*>(part);
     uint8_t* qx = static_cast<uint8_t*>(xq);
     cudaError_t e;
-    if (!xq) e = cudaLaunchKernelEx(&cfg2, attn_combine_kernel<0>, pp, out, qx, n_chunks);
-    else if (act_mode == B200Q_ACT_X8) e = cudaLaunchKernelEx(&cfg2, attn_combine_kernel<1>, pp, out, qx, n_chunks);
-    else e = cudaLaunchKernelEx(&cfg2, attn_combine_kernel<2>, pp, out, qx, n_chunks);
+    if (!xq) e = cudaLaunchKernelEx(&cfg2, b200q_attn_combine_kernel<0>, pp, out, qx, n_chunks);
+    else if (act_mode == B200Q_ACT_X8) e = cudaLaunchKernelEx(&cfg2, b200q_attn_combine_kernel<1>, pp, out, qx, n_chunks);
+    else e = cudaLaunchKernelEx(&cfg2, b200q_attn_combine_kernel<2>, pp, out, qx, n_chunks);
     return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
 
@@ -764,9 +764,9 @@ int launch_rope_attention(const float* q, const float* k, const float* v, int ba
     cudaError_t e = cudaErrorInvalidValue;
 #define B200Q_ATTN_CASE(GG)                                                   \
     if (G == GG) {                                                             \
-        if (dig == 0) e = go(attn_decode_kernel<GG, 0>);                       \
-        else if (dig == 1) e = go(attn_decode_kernel<GG, 1>);                  \
-        else e = go(attn_decode_kernel<GG, 2>);                                \
+        if (dig == 0) e = go(b200q_attn_decode_kernel<GG, 0>);                       \
+        else if (dig == 1) e = go(b200q_attn_decode_kernel<GG, 1>);                  \
+        else e = go(b200q_attn_decode_kernel<GG, 2>);                                \
     }
     B200Q_ATTN_CASE(1)
     B200Q_ATTN_CASE(2)
@@ -780,7 +780,7 @@ int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaS
     if (!g || !u || !out || n <= 0) return B200Q_EINVAL;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), st, attr);
-    return cudaLaunchKernelEx(&cfg, swiglu_kernel, g, u, out, n) == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
+    return cudaLaunchKernelEx(&cfg, b200q_swiglu_kernel, g, u, out, n) == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
 
 int launch_unshard_rows(const float* in, float* out, int shards, int rows, int cols, cudaStream_t st) {
@@ -788,7 +788,7 @@ int launch_unshard_rows(const float* in, float* out, int shards, int rows, int c
     const long long total = static_cast<long long>(shards) * rows * cols;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), st, attr);
-    return cudaLaunchKernelEx(&cfg, unshard_rows_kernel, in, out, shards, rows, cols) == cudaSuccess ? B200Q_OK
+    return cudaLaunchKernelEx(&cfg, b200q_unshard_rows_kernel, in, out, shards, rows, cols) == cudaSuccess ? B200Q_OK
                                                                                                   : B200Q_ECUDA;
 }
 

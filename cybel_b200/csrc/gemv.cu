@@ -58,6 +58,8 @@ struct Plan {
     int threads;
     int smem;
     int grid;
+    long long x_bytes;  // staged activations (+ the fused quantizer's tiles) at the ring's end
+    int dev = -1;       // device id the launch targets (set by the caller)
 };
 
 // fq: the GEMV quantizes fp32 activations itself (transpose tiles staged too).
@@ -134,6 +136,7 @@ int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl, b
     p.x_off = x_off;
     p.n_quads = n_quads;
     p.rows_cta = rows_cta;
+    pl.x_bytes = x_bytes;
     pl.threads = (S * WR + 1) * 32;
     pl.smem = NS * stage_stride + (2 * NS + 2) * 8 + part_bytes + 16;
     pl.grid = grid;
@@ -142,17 +145,20 @@ int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl, b
 
 template <int QT, int DIG, int MR, bool DBG, bool FQ>
 cudaError_t launch_kernel(const Plan& pl, cudaStream_t st, bool pdl) {
-    auto kern = gemv_kernel<QT, DIG, MR, DBG, FQ>;
-    // Raise the dynamic shared-memory limit once per kernel instance (the
-    // attribute is per function; the largest plan is set).
+    auto kern = b200q_gemv_kernel<QT, DIG, MR, DBG, FQ>;
+    // Raise the dynamic shared-memory limit once per kernel instance and
+    // device: the attribute belongs to the device context, so a process that
+    // drives several GPUs sets it on each (bit per device id below 64; ids
+    // beyond that set it on every launch).
     static std::mutex mu;
-    static int configured = 0;
+    static uint64_t configured = 0;
     {
         std::lock_guard<std::mutex> lk(mu);
-        if (pl.smem > configured) {
+        const uint64_t bit = (pl.dev >= 0 && pl.dev < 64) ? (1ull << pl.dev) : 0;
+        if (!bit || !(configured & bit)) {
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
             if (e != cudaSuccess) return e;
-            configured = 227 * 1024;
+            configured |= bit;
         }
     }
     cudaLaunchConfig_t cfg = {};
@@ -261,7 +267,7 @@ cudaError_t launch_quantize(const float* x, long long x_stride, int m, int k, ui
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    return cudaLaunchKernelEx(&cfg, quantize_act_quads_kernel<DIG>, x, x_stride, m, k, xq);
+    return cudaLaunchKernelEx(&cfg, b200q_quantize_act_quads_kernel<DIG>, x, x_stride, m, k, xq);
 }
 
 }  // namespace
@@ -317,6 +323,7 @@ int gemv_rows(int qtype, int act_mode, const void* w, const uint8_t* xq, long lo
         const int rc = make_plan(qtype, dig, k, n, MR, dev->num_sms, pl, xf != nullptr);
         if (rc != B200Q_OK) return rc;
         pl.p.W = static_cast<const uint8_t*>(w);
+        pl.dev = dev->id;
         if (xf) {
             pl.p.xf = xf + m0 * xf_stride;
             pl.p.xf_stride = xf_stride;
@@ -374,16 +381,19 @@ int gemv_norm_f32(int qtype, int act_mode, const void* w, const float* x, const 
 
 int gemv_plan_info(int qtype, int act_mode, int k, int n, int mr, bool fq, int num_sms, long long* out, int out_len) {
     if (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
-    if (!out || out_len < kPlanInfoFields || num_sms <= 0 || mr < 1 || mr > 4) return B200Q_EINVAL;
-    Plan pl;
+    if (!out || out_len < kPlanInfoFields || num_sms <= 0) return B200Q_EINVAL;
+    FmtInfo f;
+    if (!fmt_info(qtype, f)) return B200Q_EQTYPE;
     const int dig = act_mode == B200Q_ACT_X8 ? 1 : 2;
+    // Only the row counts a launch is ever made with: 1, 2 and (where the
+    // format's lanes carry it) 4, up to max_rows_per_launch.
+    if (mr < 1 || mr == 3 || mr > max_rows_per_launch(qtype, dig)) return B200Q_EINVAL;
+    Plan pl;
     const int rc = make_plan(qtype, dig, k, n, mr, num_sms, pl, fq);
     if (rc != B200Q_OK) return rc;
     const GemvParams& p = pl.p;
-    const long long x_bytes =
-        static_cast<long long>(mr) * xs_row_bytes(k, dig) + (fq ? static_cast<long long>(p.S * p.WR) * kFqWarpBytes + 128 : 0);
     const long long v[kPlanInfoFields] = {pl.threads, pl.smem, pl.grid, p.S, p.WR, p.G, p.SW, p.R, p.NS,
-                                          p.stage_stride, p.PD, p.x_off, x_bytes, p.row_bytes, p.rows_cta};
+                                          p.stage_stride, p.PD, p.x_off, pl.x_bytes, p.row_bytes, p.rows_cta};
     for (int i = 0; i < kPlanInfoFields; ++i) out[i] = v[i];
     return B200Q_OK;
 }

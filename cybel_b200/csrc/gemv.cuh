@@ -46,7 +46,7 @@ constexpr int kRowsPerIter = MR == 1 ? 2 : 1;
 
 struct GemvParams {
     const uint8_t* W;      // packed weight rows (device, 16-byte aligned)
-    const uint8_t* xq;     // [MR] quantized activation rows (quantize_act_kernel layout)
+    const uint8_t* xq;     // [MR] quantized activation rows (b200q_quantize_act_kernel layout)
     long long xq_stride;   // bytes between quantized rows
     const float* xf;       // [MR] fp32 activation rows, quantized in the kernel (FQ instances)
     long long xf_stride;   // floats between fp32 rows
@@ -171,7 +171,7 @@ __device__ __forceinline__ int round_half_even_small(float v) {
     return __float_as_int(t) - 0x4B400000;
 }
 
-// Activation rows quantized once per call by quantize_act_kernel, in the
+// Activation rows quantized once per call by b200q_quantize_act_kernel, in the
 // layout the GEMV lanes read: per row, k signed code bytes (x8: the code;
 // x16: its high byte), k unsigned low bytes (x16 only), k/32 fp32 group
 // scales and k/32 int32 group code sums; xq_row_bytes(k, DIG) bytes per row.
@@ -250,7 +250,7 @@ __device__ __forceinline__ void load_group(const float* p, float (&v)[32]) {
 
 // One thread per 32-element group of m activation rows.
 template <int DIG>
-__global__ void __launch_bounds__(128) quantize_act_kernel(const float* __restrict__ x, long long x_stride, int m, int k,
+__global__ void __launch_bounds__(128) b200q_quantize_act_kernel(const float* __restrict__ x, long long x_stride, int m, int k,
                                                            uint8_t* __restrict__ xq) {
     // Let the GEMV behind this kernel launch now, so it can stream its
     // weights while this grid waits for x; x may be produced by the
@@ -315,7 +315,7 @@ __device__ __forceinline__ void quantize_quad(float4 v, bool valid, uint8_t* bas
 }
 
 template <int DIG>
-__global__ void __launch_bounds__(256) quantize_act_quads_kernel(const float* __restrict__ x, long long x_stride, int m,
+__global__ void __launch_bounds__(256) b200q_quantize_act_quads_kernel(const float* __restrict__ x, long long x_stride, int m,
                                                                   int k, uint8_t* __restrict__ xq) {
     griddep_launch_dependents();
     griddep_wait();
@@ -910,7 +910,7 @@ __device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* 
 // taken its codes into registers (arrivals on xbar).
 // ---------------------------------------------------------------------------
 template <int QT, int DIG, int MR, bool DBG, bool FQ>
-__global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_kernel(const GemvParams p) {
     using F = Fmt<QT>;
     constexpr int RUN = F::kRun;
     constexpr int RUNS = F::kRuns;

@@ -71,6 +71,8 @@ long long xq_bytes_per_row(int k, int act_mode);
 int launch_repack(int dst_qtype, const void* src, void* dst, int k, int n, cudaStream_t st);
 int launch_dequant_rows(int qtype, const void* w, const int* rows, int nrows, float* out, int k, int n,
                         bool tail_canonical, cudaStream_t st);
+// y = W x for fp32 weights [rows][cols] (the graph's unquantized branch).
+int launch_matvec_f32(const float* W, const float* x, float* y, int rows, int cols, cudaStream_t st);
 int launch_swiglu_quantize(int act_mode, const float* g, const float* u, int hidden, uint8_t* xq, cudaStream_t st,
                            bool pdl);
 int expert_swiglu(int act_mode, const float* x, int in_dim, const void* gate, int gq, int hidden, const void* up, int uq,
@@ -107,7 +109,7 @@ int launch_rope_kv(float* q, float* k, const float* v, int batch, int n_heads, i
 int launch_attention(const float* q, const void* kc, const void* vc, float* out, int batch, int n_heads, int n_kv,
                      int hd, int ctx, int max_ctx, Device* dev, cudaStream_t st, void* xq = nullptr,
                      int act_mode = 0);
-// RoPE + KV append + attention + chunk merge in one launch (attn_decode_kernel).
+// RoPE + KV append + attention + chunk merge in one launch (b200q_attn_decode_kernel).
 int launch_rope_attention(const float* q, const float* k, const float* v, int batch, int n_heads, int n_kv, int hd,
                           int pos, float theta, void* kc, void* vc, int max_ctx, float* out, void* xq, int act_mode,
                           Device* dev, cudaStream_t st);
@@ -119,6 +121,15 @@ int launch_allgather_peer(const float* local, int rows, int n_local, void* const
                           long long flags_offset, int rank, int world, uint32_t* counters, int slot, Device* dev,
                           cudaStream_t st, void* xq = nullptr, int act_mode = 0);
 int peer_counter_slots();
+// Limit of the peer all-gather's wait for the other ranks' flags, in ns
+// (ns <= 0 leaves it unchanged); returns the previous limit.
+long long set_peer_wait_ns(long long ns);
+
+// Device state if it exists already (never creates it).
+Device* device_state_if_present(int dev);
+// STATUS bits recorded by b200q_matvec_noalloc's kernels on `device` since
+// the last read (0 when that entry point never ran there); cleared on read.
+int noalloc_take_status(int device);
 
 bool pdl_enabled();
 void set_last_error(int status);

@@ -81,7 +81,7 @@ cudaError_t launch_quantize_row(const float* x, int k, uint8_t* xq, cudaStream_t
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    return cudaLaunchKernelEx(&cfg, quantize_act_kernel<DIG>, x, static_cast<long long>(k), 1, k, xq);
+    return cudaLaunchKernelEx(&cfg, b200q_quantize_act_kernel<DIG>, x, static_cast<long long>(k), 1, k, xq);
 }
 
 int matvec_noalloc(int qtype, int act_mode, const float* x, const void* w, float* y, int k, int n,
@@ -107,6 +107,28 @@ int matvec_noalloc(int qtype, int act_mode, const float* x, const void* w, float
 }
 
 }  // namespace
+
+int noalloc_take_status(int device) {
+    if (device < 0 || device >= kMaxDevices) return 0;
+    uint8_t* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!g_devices[device].ready) return 0;
+        base = g_devices[device].base;
+    }
+    // A synchronous copy of the word out of the fixed array and a reset to
+    // zero (no allocation); the caller reads it after the call's stream has
+    // finished.
+    int prev = -1;
+    if (cudaGetDevice(&prev) != cudaSuccess) return B200Q_ECUDA;
+    if (prev != device && cudaSetDevice(device) != cudaSuccess) return B200Q_ECUDA;
+    int v = 0;
+    cudaError_t e = cudaMemcpy(&v, base, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && v != 0) e = cudaMemset(base, 0, sizeof(int));
+    if (prev != device) cudaSetDevice(prev);
+    return e == cudaSuccess ? v : B200Q_ECUDA;
+}
+
 }  // namespace b200q
 
 extern "C" int b200q_matvec_noalloc(int qtype, int act_mode, const float* x, const void* w, float* y, int k, int n,

@@ -16,7 +16,7 @@ namespace {
 // R4: rows grouped by 4, block-major inside a group ([g][b][r][B]); the n % 4
 // tail rows are copied canonically after the full groups. One thread per
 // output 16-bit word (block sizes are even).
-__global__ void repack_r4_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, long long words,
+__global__ void b200q_repack_r4_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, long long words,
                                  long long row_bytes, int block_bytes, int n) {
     const long long o = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (o >= words) return;
@@ -37,7 +37,7 @@ __global__ void repack_r4_kernel(const uint16_t* __restrict__ src, uint16_t* __r
 
 // Q6_K -> Q6_K_LM: 256 int8 codes (6-bit value - 32) in element order, the
 // 16 int8 scales, and d as fp32 (276 bytes per block). One warp per block.
-__global__ void repack_q6k_lm_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, long long blocks) {
+__global__ void b200q_repack_q6k_lm_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, long long blocks) {
     const long long blk = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) / 32;
     const int lane = threadIdx.x & 31;
     if (blk >= blocks) return;
@@ -125,7 +125,7 @@ __device__ float dequant_element(int qtype, const uint8_t* blk, int e) {
 // One thread per output element. `tail_canonical` selects the R4 addressing
 // of the layout (tail rows canonical, needs n) or the reference's
 // (group = row / 4 for every row; simd_dequantize_row has no n).
-__global__ void dequant_rows_kernel(int qtype, const uint8_t* __restrict__ w, const int* __restrict__ rows, int nrows,
+__global__ void b200q_dequant_rows_kernel(int qtype, const uint8_t* __restrict__ w, const int* __restrict__ rows, int nrows,
                                     float* __restrict__ out, int k, int n, int elems, int bbytes, int tail_canonical) {
     const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= static_cast<long long>(nrows) * k) return;
@@ -147,7 +147,7 @@ __global__ void dequant_rows_kernel(int qtype, const uint8_t* __restrict__ w, co
 // down projection (the SiLU(gate) * up step of quantized_matmul.cpp:2380-2412).
 // ---------------------------------------------------------------------------
 template <int DIG>
-__global__ void __launch_bounds__(256) swiglu_quantize_kernel(const float* __restrict__ g, const float* __restrict__ u,
+__global__ void __launch_bounds__(256) b200q_swiglu_quantize_kernel(const float* __restrict__ g, const float* __restrict__ u,
                                                               int hidden, uint8_t* __restrict__ xq) {
     griddep_launch_dependents();
     griddep_wait();
@@ -188,11 +188,11 @@ int launch_repack(int dst_qtype, const void* src, void* dst, int k, int n, cudaS
         const int bb = dst_qtype == QT_Q4_K_R4 ? 144 : 210;
         const long long rb = static_cast<long long>(k / 256) * bb;
         const long long words = rb * n / 2;
-        repack_r4_kernel<<<static_cast<unsigned>((words + 255) / 256), 256, 0, st>>>(
+        b200q_repack_r4_kernel<<<static_cast<unsigned>((words + 255) / 256), 256, 0, st>>>(
             static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), words, rb, bb, n);
     } else if (dst_qtype == QT_Q6_K_LM) {
         const long long blocks = static_cast<long long>(k / 256) * n;
-        repack_q6k_lm_kernel<<<static_cast<unsigned>((blocks * 32 + 255) / 256), 256, 0, st>>>(
+        b200q_repack_q6k_lm_kernel<<<static_cast<unsigned>((blocks * 32 + 255) / 256), 256, 0, st>>>(
             static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), blocks);
     } else {
         return B200Q_EQTYPE;
@@ -207,7 +207,7 @@ int launch_dequant_rows(int qtype, const void* w, const int* rows, int nrows, fl
     if (!w || !rows || !out || nrows <= 0 || k <= 0) return B200Q_EINVAL;
     if (k % f.elems) return B200Q_ESHAPE;
     const long long total = static_cast<long long>(nrows) * k;
-    dequant_rows_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(
+    b200q_dequant_rows_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, st>>>(
         qtype, static_cast<const uint8_t*>(w), rows, nrows, out, k, n, f.elems, f.bytes, tail_canonical ? 1 : 0);
     return cudaGetLastError() == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
@@ -218,8 +218,8 @@ int launch_swiglu_quantize(int act_mode, const float* g, const float* u, int hid
     cudaLaunchAttribute attr[1];
     if ((reinterpret_cast<uintptr_t>(g) & 15u) || (reinterpret_cast<uintptr_t>(u) & 15u)) return B200Q_EALIGN;
     cudaLaunchConfig_t cfg = make_cfg(static_cast<unsigned>((hidden / 4 + 255) / 256), 256, st, pdl, attr);
-    const cudaError_t e = act_mode == B200Q_ACT_X8 ? cudaLaunchKernelEx(&cfg, swiglu_quantize_kernel<1>, g, u, hidden, xq)
-                                                   : cudaLaunchKernelEx(&cfg, swiglu_quantize_kernel<2>, g, u, hidden, xq);
+    const cudaError_t e = act_mode == B200Q_ACT_X8 ? cudaLaunchKernelEx(&cfg, b200q_swiglu_quantize_kernel<1>, g, u, hidden, xq)
+                                                   : cudaLaunchKernelEx(&cfg, b200q_swiglu_quantize_kernel<2>, g, u, hidden, xq);
     return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
 
@@ -256,6 +256,49 @@ int expert_swiglu(int act_mode, const float* x, int in_dim, const void* gate, in
         rc = gemv_from_xq(dq, act_mode, down, static_cast<const uint8_t*>(hq), xq_bytes_per_row(hidden, act_mode), out,
                           1, hidden, out_dim, out_dim, alpha, beta, nullptr, dev, st, pdl, flags);
     return rc;
+}
+
+// ---------------------------------------------------------------------------
+// The graph-side dispatch of model_graph.cpp:731-790 on device pointers.
+// ---------------------------------------------------------------------------
+namespace {
+
+// y = W x for fp32 weights [rows][cols] (matvec_f32, model_graph.cpp:700-727):
+// one warp per row, coalesced 16-byte loads when the rows allow them, fp32
+// accumulation, warp-shuffle reduction.
+__global__ void __launch_bounds__(256) b200q_matvec_f32_kernel(const float* __restrict__ W, const float* __restrict__ x,
+                                                         float* __restrict__ y, int rows, int cols, int vec4) {
+    const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const float* w = W + warp * cols;
+    float acc = 0.0f;
+    if (vec4) {
+        const float4* w4 = reinterpret_cast<const float4*>(w);
+        const float4* x4 = reinterpret_cast<const float4*>(x);
+        for (int i = lane; i < cols / 4; i += 32) {
+            const float4 a = __ldg(w4 + i), b = __ldg(x4 + i);
+            acc = fmaf(a.x, b.x, acc);
+            acc = fmaf(a.y, b.y, acc);
+            acc = fmaf(a.z, b.z, acc);
+            acc = fmaf(a.w, b.w, acc);
+        }
+    } else {
+        for (int i = lane; i < cols; i += 32) acc = fmaf(__ldg(w + i), __ldg(x + i), acc);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) y[warp] = acc;
+}
+
+}  // namespace
+
+int launch_matvec_f32(const float* W, const float* x, float* y, int rows, int cols, cudaStream_t st) {
+    if (!W || !x || !y || rows <= 0 || cols <= 0) return B200Q_EINVAL;
+    const int vec4 = (cols % 4 == 0) && !(reinterpret_cast<uintptr_t>(W) & 15u) && !(reinterpret_cast<uintptr_t>(x) & 15u);
+    const long long threads = static_cast<long long>(rows) * 32;
+    b200q_matvec_f32_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, st>>>(W, x, y, rows, cols, vec4);
+    return cudaGetLastError() == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
 
 }  // namespace b200q

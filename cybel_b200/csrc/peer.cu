@@ -46,10 +46,14 @@ struct PeerArgs {
     long long flags_offset;     // bytes: the slot's flag row in every buffer
     int rank, world, rows, n_local, slot;
     uint8_t* xq;                // optional: gathered rows quantized here (GEMV activation codes)
+    unsigned long long wait_ns; // longest wait for the other ranks' flags (%globaltimer ns)
 };
 
+// Library-wide limit of the flag wait (b200q_set_peer_wait_ns).
+unsigned long long g_peer_wait_ns = kWaitTimeoutNs;
+
 template <int DIG>
-__global__ void __launch_bounds__(kPeerThreads) allgather_peer_kernel(const float* __restrict__ local,
+__global__ void __launch_bounds__(kPeerThreads) b200q_allgather_peer_kernel(const float* __restrict__ local,
                                                                       uint32_t* __restrict__ counters,
                                                                       volatile int* status, const PeerArgs a) {
     griddep_launch_dependents();
@@ -85,7 +89,7 @@ __global__ void __launch_bounds__(kPeerThreads) allgather_peer_kernel(const floa
         const uint64_t t0 = global_timer_ns();
         uint32_t polls = 0;
         while (static_cast<int32_t>(ld_acquire_sys(f) - seq) < 0) {
-            if ((++polls & 1023u) == 0 && global_timer_ns() - t0 > kWaitTimeoutNs) {
+            if ((++polls & 1023u) == 0 && global_timer_ns() - t0 > a.wait_ns) {
                 *status = STATUS_TIMEOUT;
                 break;
             }
@@ -135,6 +139,7 @@ int launch_allgather_peer(const float* local, int rows, int n_local, void* const
     a.n_local = n_local;
     a.slot = slot;
     a.xq = static_cast<uint8_t*>(xq);
+    a.wait_ns = g_peer_wait_ns;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(world);
     cfg.blockDim = dim3(kPeerThreads);
@@ -147,12 +152,18 @@ int launch_allgather_peer(const float* local, int rows, int n_local, void* const
         cfg.numAttrs = 1;
     }
     cudaError_t e;
-    if (!xq) e = cudaLaunchKernelEx(&cfg, allgather_peer_kernel<0>, local, counters, dev->status, a);
-    else if (act_mode == B200Q_ACT_X8) e = cudaLaunchKernelEx(&cfg, allgather_peer_kernel<1>, local, counters, dev->status, a);
-    else e = cudaLaunchKernelEx(&cfg, allgather_peer_kernel<2>, local, counters, dev->status, a);
+    if (!xq) e = cudaLaunchKernelEx(&cfg, b200q_allgather_peer_kernel<0>, local, counters, dev->status, a);
+    else if (act_mode == B200Q_ACT_X8) e = cudaLaunchKernelEx(&cfg, b200q_allgather_peer_kernel<1>, local, counters, dev->status, a);
+    else e = cudaLaunchKernelEx(&cfg, b200q_allgather_peer_kernel<2>, local, counters, dev->status, a);
     return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
 
 int peer_counter_slots() { return kMaxWorld; }
+
+long long set_peer_wait_ns(long long ns) {
+    const long long prev = static_cast<long long>(g_peer_wait_ns);
+    if (ns > 0) g_peer_wait_ns = static_cast<unsigned long long>(ns);
+    return prev;
+}
 
 }  // namespace b200q

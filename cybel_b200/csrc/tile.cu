@@ -241,7 +241,7 @@ struct TileSmem {
 // by the last dequant warp group).
 template <int NP, bool PREC>
 __global__ void __launch_bounds__(tile_threads(NP), 1)
-    tile_q4k_kernel(const __grid_constant__ CUtensorMap wmap, const TileParams p) {
+    b200q_tile_q4k_kernel(const __grid_constant__ CUtensorMap wmap, const TileParams p) {
     using SM = TileSmem<NP, PREC>;
     extern __shared__ __align__(1024) uint8_t smem[];
     constexpr int XB = SM::XB;
@@ -546,7 +546,7 @@ __global__ void __launch_bounds__(tile_threads(NP), 1)
 // Thread (c, r, j): four consecutive threads cover one 32-element sub-block
 // of row r and add their partial sums with two shuffles.
 template <int NP, bool PREC>
-__global__ void prep_x_kernel(const float* __restrict__ x, long long x_stride, int m, int k,
+__global__ void b200q_prep_x_kernel(const float* __restrict__ x, long long x_stride, int m, int k,
                               uint8_t* __restrict__ xc, uint8_t* __restrict__ b2) {
     griddep_launch_dependents();
     griddep_wait();
@@ -593,7 +593,7 @@ __global__ void prep_x_kernel(const float* __restrict__ x, long long x_stride, i
 }
 
 // y[m][row] = sum over splits of part[split][m][row], in split order.
-__global__ void reduce_splits_kernel(const float* __restrict__ part, float* __restrict__ y, int m, int n, int splits,
+__global__ void b200q_reduce_splits_kernel(const float* __restrict__ part, float* __restrict__ y, int m, int n, int splits,
                                      long long y_stride) {
     griddep_launch_dependents();
     griddep_wait();
@@ -645,7 +645,7 @@ int configure_tile(int dev_id) {
     std::lock_guard<std::mutex> lk(mu);
     const uint64_t bit = dev_id < 64 ? (1ull << dev_id) : 0;
     if (bit && (done & bit)) return B200Q_OK;
-    if (cudaFuncSetAttribute(tile_q4k_kernel<NP, PREC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(b200q_tile_q4k_kernel<NP, PREC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              TileSmem<NP, PREC>::kTotal) != cudaSuccess)
         return B200Q_ECUDA;
     done |= bit;
@@ -692,7 +692,7 @@ int launch_np(const void* w, const float* x, long long x_stride, float* y, int m
     {
         const long long groups = static_cast<long long>(k / 8) * NP;
         cudaLaunchConfig_t c = cfg_of(dim3(static_cast<unsigned>((groups + 255) / 256)), dim3(256), 0, st, pdl, attr);
-        if (cudaLaunchKernelEx(&c, prep_x_kernel<NP, PREC>, x, x_stride, m, k, static_cast<uint8_t*>(xc),
+        if (cudaLaunchKernelEx(&c, b200q_prep_x_kernel<NP, PREC>, x, x_stride, m, k, static_cast<uint8_t*>(xc),
                                static_cast<uint8_t*>(b2)) != cudaSuccess)
             return B200Q_ECUDA;
     }
@@ -708,12 +708,12 @@ int launch_np(const void* w, const float* x, long long x_stride, float* y, int m
         tp.splits = splits;
         cudaLaunchConfig_t c =
             cfg_of(dim3(tiles, splits), dim3(tile_threads(NP)), TileSmem<NP, PREC>::kTotal, st, pdl, attr);
-        if (cudaLaunchKernelEx(&c, tile_q4k_kernel<NP, PREC>, map, tp) != cudaSuccess) return B200Q_ECUDA;
+        if (cudaLaunchKernelEx(&c, b200q_tile_q4k_kernel<NP, PREC>, map, tp) != cudaSuccess) return B200Q_ECUDA;
     }
     if (!direct) {
         const long long total = static_cast<long long>(m) * n;
         cudaLaunchConfig_t c = cfg_of(dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, st, pdl, attr);
-        if (cudaLaunchKernelEx(&c, reduce_splits_kernel, static_cast<const float*>(part), y, m, n, splits, y_stride) !=
+        if (cudaLaunchKernelEx(&c, b200q_reduce_splits_kernel, static_cast<const float*>(part), y, m, n, splits, y_stride) !=
             cudaSuccess)
             return B200Q_ECUDA;
     }

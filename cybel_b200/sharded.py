@@ -85,15 +85,23 @@ class ShardedDecode:
     gate/up rows another (one GEMV each). Norms write the GEMVs' activation
     codes, and the gathers of the attention output and of the SwiGLU vector
     deliver codes of the gathered rows, so no projection quantizes by itself.
+    From ``TILE_MIN_BATCH`` sequences on (``tile``), the activations stay
+    fp32 and every Q4_K linear runs on the tile path (tcgen05, the weights
+    streamed once for the whole batch; other qtypes take the GEMV).
     """
 
+    TILE_MIN_BATCH = 8
+
     def __init__(self, plan: ShardPlan, max_ctx: int, batch: int, layers, embed, head, out_norm, ops,
-                 fuse_norm: bool | None = None):
+                 fuse_norm: bool | None = None, tile: bool | None = None):
         s = plan.shape
         self.plan, self.shape, self.ops = plan, s, ops
         self.max_ctx, self.batch = max_ctx, batch
         B, G, hd = batch, plan.world, s.head_dim
         self.fused = batch == 1
+        if tile is None:
+            tile = batch >= self.TILE_MIN_BATCH
+        self.tile = bool(tile) and batch > 1 and hasattr(ops, "linear_f32")
         h, h_l, f_l = s.hidden, s.hidden // G, s.ffn // G
         q_l, kv_l = plan.heads * hd, plan.kv_heads * hd
         self.q_l, self.kv_l, self.f_l = q_l, kv_l, f_l
@@ -150,6 +158,7 @@ class ShardedDecode:
             self.a, self.o, self.f, self.d, self.logits = self.a_l, self.o_l, self.f_l_buf, self.d_l, self.logits_l
         # with B > 1 and NCCL, an all-gather lands in [G][B][n/G] first
         self.gbuf = z(B * max(s.ffn, s.vocab)) if (B > 1 and G > 1) else None
+        self.xn = z(B * h) if self.tile else None  # normalized rows, fp32 (tile mode)
         self.tokens = ops.tokens(B)
 
     def _gather(self, full, local, n_local, codes=None, k=None):
@@ -163,6 +172,9 @@ class ShardedDecode:
         logits of every sequence land in ``self.logits`` ([batch][vocab])."""
         if self.norm_fused:
             self._step_norm_fused(pos)
+            return
+        if self.tile:
+            self._step_tile(pos)
             return
         s, p, ops, B = self.shape, self.plan, self.ops, self.batch
         if not 0 <= pos < self.max_ctx:
@@ -205,6 +217,39 @@ class ShardedDecode:
         ops.linear_codes(self.head, self.xq_h, self.logits_l, B, h, p.local_rows("head"))
         self._gather(self.logits, self.logits_l, p.local_rows("head"))
 
+
+    def _step_tile(self, pos: int) -> None:
+        """Batched step on fp32 activations: each norm writes fp32 rows, every
+        linear takes all ``batch`` rows at once (the tile path for Q4_K), the
+        attention writes fp32 outputs and the gathers move fp32 rows."""
+        s, p, ops, B = self.shape, self.plan, self.ops, self.batch
+        if not 0 <= pos < self.max_ctx:
+            raise ValueError("position outside the KV cache")
+        h, hd, G = s.hidden, s.head_dim, p.world
+        h_l = h // G
+        ops.embed(self.embed, self.tokens, self.x, B, h, s.vocab)
+        delta = None
+        for li, lay in enumerate(self.layers):
+            ops.norm_f32(self.x, delta, lay["attn_norm"], self.xn, h, B, s.eps)
+            for name, out, n in (("wq", self.q, self.q_l), ("wk", self.k, self.kv_l), ("wv", self.v, self.kv_l)):
+                ops.linear_f32(lay[name], self.xn, out, B, h, n)
+            kc, vc = ops.cache_layer(self.k_cache, li), ops.cache_layer(self.v_cache, li)
+            ops.rope_attention(self.q, self.k, self.v, B, p.heads, p.kv_heads, hd, pos, s.rope_theta, kc, vc,
+                               self.max_ctx, self.a_l, None)
+            self._gather(self.a, self.a_l, h_l)
+            ops.linear_f32(lay["wo"], self.a, self.o_l, B, h, h_l)
+            self._gather(self.o, self.o_l, h_l)
+            ops.norm_f32(self.x, self.o, lay["ffn_norm"], self.xn, h, B, s.eps)
+            ops.linear_f32(lay["w_gate"], self.xn, self.g_l, B, h, self.f_l)
+            ops.linear_f32(lay["w_up"], self.xn, self.u_l, B, h, self.f_l)
+            ops.swiglu(self.g_l, self.u_l, self.f_l_buf, B * self.f_l)
+            self._gather(self.f, self.f_l_buf, self.f_l)
+            ops.linear_f32(lay["w_down"], self.f, self.d_l, B, s.ffn, h_l)
+            self._gather(self.d, self.d_l, h_l)
+            delta = self.d
+        ops.norm_f32(self.x, delta, self.out_norm, self.xn, h, B, s.eps)
+        ops.linear_f32(self.head, self.xn, self.logits_l, B, h, p.local_rows("head"))
+        self._gather(self.logits, self.logits_l, p.local_rows("head"))
 
     def _step_norm_fused(self, pos: int) -> None:
         """Batch-1 step: per layer the q/k/v projection with the attention
@@ -408,6 +453,20 @@ class GpuOps:
     def linear_codes(self, m, xq, out, batch, k, n_rows):
         self._ok(self.lib.b200q_matmul_xq(m.qtype, self.act, xq.data_ptr(), m.ptr, out.data_ptr(), batch, k, n_rows,
                                           1.0, 0.0, _native.WEIGHTS_STATIC, self._st()), "linear")
+
+    def norm_f32(self, res, delta, gamma, out, n, rows, eps):
+        """res += delta (when given); out = RMSNorm(res) * gamma, fp32 rows."""
+        self._ok(self.lib.b200q_add_rmsnorm(res.data_ptr(), None if delta is None else delta.data_ptr(),
+                                            gamma.data_ptr(), out.data_ptr(), n, rows, eps, self._st()), "rmsnorm")
+
+    def linear_f32(self, m, x, out, batch, k, n_rows):
+        """out [batch][n_rows] = x [batch][k] m^T from fp32 rows: Q4_K on the
+        tile path (fp16 activations), other qtypes on the GEMV (x16)."""
+        from .formats import Q4_K
+
+        act = _native.ACT_F16 if m.qtype == Q4_K else _native.ACT_X16
+        self._ok(self.lib.b200q_matmul_ex(m.qtype, act, x.data_ptr(), m.ptr, out.data_ptr(), batch, k, n_rows,
+                                          _native.WEIGHTS_STATIC, self._st()), "linear (fp32 rows)")
 
     def linear_norm(self, m, x, gamma, out, k, n_rows, eps):
         """out = m (RMSNorm(x) * gamma) for one row, the norm inside the GEMV."""

@@ -164,6 +164,21 @@ B200Q_API int b200q_matmul_ex(int qtype, int act_mode, const float* x, const voi
 B200Q_API int b200q_matvec_isums(int qtype, int act_mode, const float* x, const void* w, float* y, int* isums, int k, int n,
                        void* stream);
 
+/* The decode graph's dispatch on device pointers, with its semantics
+ * (model_graph.cpp:731-760, "MG"):
+ * b200q_matvec_quant replaces MG:731-747 matvec_quant: y[rows] = W x for a
+ *   quantized W of `rows` rows of `cols` (argument order of MG), in the
+ *   drop-in act mode; a qtype without a kernel zero-fills y and returns
+ *   B200Q_OK, as MG does.
+ * b200q_matvec_dispatch replaces MG:749-760 matvec_dispatch: fp32 weights
+ *   [rows][cols] when w_f32 is non-NULL (MG's matvec_f32, MG:700-727),
+ *   else the quantized weights when w_quant is non-NULL and qtype > 0, else
+ *   a zeroed y. */
+B200Q_API int b200q_matvec_quant(const void* w_quant, int qtype, const float* x, float* y, int cols, int rows,
+                                 void* stream);
+B200Q_API int b200q_matvec_dispatch(const float* w_f32, const void* w_quant, int qtype, const float* x, float* y,
+                                    int rows, int cols, void* stream);
+
 /* Decode matvec (m = 1) that allocates nothing, for callers that cannot
  * allocate device memory during a call: engines whose memory pool owns HBM
  * after start-up, latency-bound decode loops that cannot absorb
@@ -177,7 +192,11 @@ B200Q_API int b200q_matvec_isums(int qtype, int act_mode, const float* x, const 
  * rounded up to 16) must fit in that size minus 256 bytes: k <= 28992 (x16)
  * or k <= 52224 (x8), else B200Q_ESCRATCH. The first call
  * on a device resolves the array's address (make it before any stream
- * capture). All calls share the array: calls that overlap on the GPU race. */
+ * capture). All calls share the array: calls that overlap on the GPU race.
+ * A kernel wait that gives up is recorded in a status word inside the same
+ * array (the call itself returns before the GPU runs it): after the call's
+ * stream has finished, b200q_device_status(device) reports it (bit 1), with
+ * a plain copy out of the array and no allocation. */
 #define B200Q_NOALLOC_SCRATCH_BYTES (64 * 1024)
 B200Q_API int b200q_matvec_noalloc(int qtype, int act_mode, const float* x, const void* w, float* y, int k, int n,
                                    void* stream);
@@ -350,7 +369,16 @@ B200Q_API int b200q_set_act_mode(int act_mode);       /* drop-in mode; returns p
 B200Q_API int b200q_get_act_mode(void);
 B200Q_API int b200q_last_error(void);                 /* last status of this host thread */
 B200Q_API const char* b200q_status_string(int status);
-B200Q_API int b200q_device_status(int device);        /* STATUS bits of a device, cleared on read */
+/* STATUS bits recorded on a device since the last read, cleared on read:
+ * bit 1 (value 1) = a kernel's bounded wait gave up (the call's results are
+ * incomplete; B200Q_ETIMEOUT in the Python layer). Covers the regular entry
+ * points and b200q_matvec_noalloc; read it after the work's stream has
+ * finished. Allocates nothing. */
+B200Q_API int b200q_device_status(int device);
+/* Longest time, in ns, that b200q_allgather_peer waits for the other ranks'
+ * rows before it records a timeout and returns (default 2 s; ns <= 0 only
+ * queries). Library-wide, read at each launch. Returns the previous limit. */
+B200Q_API long long b200q_set_peer_wait_ns(long long ns);
 B200Q_API void b200q_weight_cache_clear(void);        /* free all resident weight copies */
 B200Q_API int b200q_weight_cache_evict(const void* host_ptr); /* 1 if an entry was freed */
 B200Q_API long long b200q_weight_cache_bytes(void);   /* bytes resident */

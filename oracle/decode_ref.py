@@ -79,3 +79,72 @@ class DecodeRef:
             g, u = L["w_gate"] @ hn, L["w_up"] @ hn
             x = x + L["w_down"] @ (g / (1.0 + np.exp(-g)) * u)
         return self.head @ self._rms(x, self.out_norm)
+
+
+class DecodeRefPacked:
+    """The same decode step for `batch` sequences at one position, with the
+    linears computed straight from the packed weights (orc_matvec_f64: the
+    reference's fp32 dequantized values, double accumulation, activations
+    rounded to fp32 at each linear's input) instead of dequantized copies, so
+    full-width layers (hidden 8192, FFN 28672) fit in host memory. k/v caches
+    are [batch][layer][kv_head][max_ctx][head_dim] float64 holding fp16 values;
+    ``load_cache`` fills them from the device caches' values."""
+
+    def __init__(self, shape, layers, embed, head, out_norm, max_ctx: int, batch: int = 1):
+        self.s = shape
+        self.max_ctx = max_ctx
+        self.batch = batch
+        self.layers = [layers[i % len(layers)] for i in range(shape.layers)]
+        self.embed, self.head, self.out_norm = embed, head, out_norm.astype(np.float64)
+        hd = shape.head_dim
+        self.kc = np.zeros((batch, shape.layers, shape.kv_heads, max_ctx, hd))
+        self.vc = np.zeros_like(self.kc)
+
+    def load_cache(self, k_cache, v_cache) -> None:
+        """k_cache / v_cache: arrays [batch][layer][kv_head][ctx][hd] (any float type)."""
+        c = np.asarray(k_cache).shape[3]
+        self.kc[:, :, :, :c] = np.asarray(k_cache, dtype=np.float64)
+        self.vc[:, :, :, :c] = np.asarray(v_cache, dtype=np.float64)
+
+    def _lin(self, W, qt, X, k, n):
+        return O.matvec_f64(W, qt, np.ascontiguousarray(X, dtype=np.float32), k, n)
+
+    def _rms(self, X, g):
+        return X / np.sqrt(np.mean(X * X, axis=1, keepdims=True) + self.s.eps) * g.astype(np.float64)
+
+    def _rope(self, v, heads, pos):
+        hd = self.s.head_dim
+        p = np.arange(hd // 2)
+        ang = pos * self.s.rope_theta ** (-2.0 * p / hd)
+        c, s = np.cos(ang), np.sin(ang)
+        v = v.reshape(-1, heads, hd).copy()
+        x0, x1 = v[..., 0::2].copy(), v[..., 1::2].copy()
+        v[..., 0::2] = x0 * c - x1 * s
+        v[..., 1::2] = x0 * s + x1 * c
+        return v
+
+    def step(self, tokens, pos: int) -> np.ndarray:
+        """Logits [batch][vocab] after appending tokens[b] at position pos."""
+        s, B = self.s, self.batch
+        h, kv, f, hd, G = s.hidden, s.kv_dim, s.ffn, s.head_dim, s.heads // s.kv_heads
+        q_t = s.linear_qtype
+        X = O.dequant(self.embed, s.embedding_qtype, h, s.vocab)[np.asarray(tokens)].astype(np.float64)
+        for li, L in enumerate(self.layers):
+            hn = self._rms(X, L["attn_norm"])
+            q = self._rope(self._lin(L["wq"], q_t, hn, h, h), s.heads, pos)
+            k = self._rope(self._lin(L["wk"], q_t, hn, h, kv), s.kv_heads, pos)
+            v = self._lin(L["wv"], q_t, hn, h, kv).reshape(B, s.kv_heads, hd)
+            self.kc[:, li, :, pos] = k.astype(np.float16).astype(np.float64)
+            self.vc[:, li, :, pos] = v.astype(np.float16).astype(np.float64)
+            att = np.zeros((B, s.heads, hd))
+            for b in range(B):
+                for hh in range(s.heads):
+                    kvh = hh // G
+                    sc = self.kc[b, li, kvh, : pos + 1] @ q[b, hh] / np.sqrt(hd)
+                    e = np.exp(sc - sc.max())
+                    att[b, hh] = (e / e.sum()) @ self.vc[b, li, kvh, : pos + 1]
+            X = X + self._lin(L["wo"], q_t, att.reshape(B, -1), h, h)
+            hn = self._rms(X, L["ffn_norm"])
+            g, u = self._lin(L["w_gate"], q_t, hn, h, f), self._lin(L["w_up"], q_t, hn, h, f)
+            X = X + self._lin(L["w_down"], q_t, g / (1.0 + np.exp(-g)) * u, f, h)
+        return self._lin(self.head, s.head_qtype, self._rms(X, self.out_norm), h, s.vocab)

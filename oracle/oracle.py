@@ -51,11 +51,21 @@ _vp = ctypes.c_void_p
 _i = ctypes.c_int
 
 
+def reference_root() -> Path | None:
+    """The reference checkout the recipe compiles from: $CYBEL_REF_ROOT, else a
+    ``reference`` directory beside this repository; None when neither exists."""
+    env = os.environ.get("CYBEL_REF_ROOT")
+    cand = Path(env) if env else HERE.parent.parent / "reference"
+    return cand if (cand / "JSBuild").is_dir() else None
+
+
 def build(ref: bool = False) -> None:
-    """Compile the restatement (and, when asked and possible, the reference)."""
+    """Compile the restatement (and, when asked and the reference tree is
+    present, the reference op from its sources)."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
-    if ref:
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref"], check=True)
+    root = reference_root() if ref else None
+    if root is not None:
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF_ROOT={root}"], check=True)
 
 
 def lib() -> ctypes.CDLL:

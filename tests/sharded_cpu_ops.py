@@ -71,6 +71,12 @@ class NumpyOps:
             x = res[sl]
             xq[sl] = x / np.sqrt(np.mean(x * x) + eps) * gamma
 
+    def norm_f32(self, res, delta, gamma, out, n, rows, eps):
+        self.norm_codes(res, delta, gamma, out, n, rows, eps)
+
+    def linear_f32(self, m, x, out, batch, k, n_rows):
+        self.linear_codes(m, x, out, batch, k, n_rows)
+
     def rope_kv(self, q, k, v, batch, heads, kv_heads, hd, pos, theta, kc, vc, max_ctx):
         p = np.arange(hd // 2)
         ang = pos * theta ** (-2.0 * p / hd)

@@ -51,6 +51,55 @@ def _check(qt, act, k, n, mr, p):
     assert 0 <= p["PD"] <= p["x_off"] // p["stage_stride"]
 
 
+def _max_rows(qt, act):
+    """Activation rows one launch carries (max_rows_per_launch in gemv.cu)."""
+    q4k = qt in (12, 112)
+    if act == 1:
+        return 2 if q4k else 4
+    return 1 if q4k else 2
+
+
+def _launch_rows(qt, act):
+    return [mr for mr in (1, 2, 4) if mr <= _max_rows(qt, act)]
+
+
+def _no_plan_expected(qt, act, k, n, mr, fq):
+    """The planner's refusals (make_plan in gemv.cu), restated: more k-slices
+    than the kernel has consumer warps, one row (one 4-row group for R4) over
+    the largest stage (96 KB), or staged activations larger than the ring the
+    shared-memory budget (220 KB) leaves room for."""
+    elems, nbytes = BLOCK[qt]
+    nb = k // elems
+    rb = nb * nbytes
+    S = -(-nb // BLOCKS_PER_SLICE[qt])
+    max_warps = 16 if (act == 1 and mr == 1) else 12
+    if S > max_warps:
+        return True
+    r4 = qt in (112, 114)
+    U = 2 if mr == 1 else 1
+    walkers = max(1, max_warps // S)
+    n_quads = -(-n // 4)
+    grid = min(SMS, n_quads)
+    rows_cta = 4 * (-(-n_quads // grid))
+    R = U * max(1, (32 * 1024 + U * rb // 2) // (U * rb))
+    R = min(R, max(U, -(-rows_cta // U) * U))
+    if r4:
+        R = -(-R // 4) * 4
+    SW = max(1, min(walkers, -(-R // U)))
+    WR = max(1, walkers // SW) * SW
+    if R * rb + 48 > 96 * 1024:
+        R = 4 if r4 else max(1, (96 * 1024 - 48) // rb)
+        if R * rb + 48 > 96 * 1024:
+            return True
+    stride = -(-(R * rb + 48) // 128) * 128
+    ns_fit = (220 * 1024 - rows_cta * mr * S * 4 - 64) // (stride + 16)
+    kp = k + 16 * (-(-k // 256))
+    xs_row = -(-(act * kp + (k // 32) * 8) // 16) * 16
+    x_bytes = mr * xs_row + (S * WR * 4608 + 128 if fq else 0)
+    ns = max(min(48, ns_fit), min(ns_fit, -(-x_bytes // stride) + 1))
+    return ns < 2 or x_bytes > ns * stride
+
+
 @pytest.mark.parametrize("qt", sorted(BLOCK))
 @pytest.mark.parametrize("act", [1, 2])
 def test_plans_respect_kernel_limits(qt, act):
@@ -58,21 +107,36 @@ def test_plans_respect_kernel_limits(qt, act):
 
     lib = _native.lib()
     elems = BLOCK[qt][0]
-    ks = sorted({elems, 2 * elems, 4 * elems, 1024, 2304 if elems == 32 else 2048, 4096, 8192, 14336, 28672})
+    ks = sorted({elems, 2 * elems, 4 * elems, 1024, 2304 if elems == 32 else 2048, 4096, 8192, 14336, 28672, 57344})
     ns = [1, 3, 7, 66, 1024, 4096, 14336, 128256]
-    planned = 0
-    for k, n, mr, fq in itertools.product(ks, ns, (1, 2), (0, 1)):
+    planned = refused = 0
+    for k, n, mr, fq in itertools.product(ks, ns, _launch_rows(qt, act), (0, 1)):
         if k % elems:
             continue
         rc, p = _plan(lib, qt, act, k, n, mr, fq)
-        if rc == -3:  # no plan: only when the row needs more k-slices than the CTA has warps
-            nb = k // elems
-            assert -(-nb // BLOCKS_PER_SLICE[qt]) > (16 if (act == 1 and mr == 1) else 12) or k >= 14336, (k, n, mr)
+        if rc == -3:
+            assert _no_plan_expected(qt, act, k, n, mr, fq), (k, n, mr, fq)
+            refused += 1
             continue
         assert rc == 0, (qt, act, k, n, mr, fq, rc)
+        assert not _no_plan_expected(qt, act, k, n, mr, fq), (k, n, mr, fq)
         _check(qt, act, k, n, mr, p)
         planned += 1
     assert planned > 0
+
+
+@pytest.mark.parametrize("qt", sorted(BLOCK))
+@pytest.mark.parametrize("act", [1, 2])
+def test_plan_refuses_row_counts_never_launched(qt, act):
+    from cybel_b200 import _native
+
+    lib = _native.lib()
+    k = BLOCK[qt][0] * 8
+    for mr in (0, 3, 5):
+        assert _plan(lib, qt, act, k, 64, mr, 0)[0] == -1
+    for mr in (1, 2, 4):
+        rc = _plan(lib, qt, act, k, 64, mr, 0)[0]
+        assert rc == (0 if mr <= _max_rows(qt, act) else -1), (mr, rc)
 
 
 @pytest.mark.parametrize("act", [1, 2])

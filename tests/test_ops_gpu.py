@@ -147,12 +147,13 @@ def test_fused_qkv_matches_separate_and_reference(oracle_mod, golden):
     assert ok == 0 and np.array_equal(keep, outs["q"])
 
 
-def test_fused_quad_matches_separate(oracle_mod):
+def test_fused_quad_matches_separate_and_oracle(oracle_mod):
     from cybel_b200 import _native
     from cybel_b200 import quantized_matmul as qm
     from test_gemv_gpu import _weights
 
     O = oracle_mod
+    qm.set_act_mode("x16")
     k = 512
     mats = [(_weights(O, qt, r, k, seed=r), qt, r) for qt, r in ((12, 40), (14, 24), (112, 16), (114, 12))]
     x = np.random.default_rng(9).standard_normal(k).astype(np.float32)
@@ -163,6 +164,22 @@ def test_fused_quad_matches_separate(oracle_mod):
     assert _native.lib().simd_fused_quad_matvec_quant(_fp(x), *args, k) == 1
     for (W, qt, r), o in zip(mats, outs):
         assert np.array_equal(o, qm.matvec(x, qm.QuantizedMatrix(name="m", qtype=qt, shape=(k, r), data=W)))
+        # against the restatement of the x16 product and the exact fp32-activation product
+        wn = O.row_norms(W, qt, k, r)
+        for want in (O.matvec_q(W, qt, x, k, r, 2), O.matvec_f64(W, qt, x, k, r)):
+            assert O.normalized_error(o, want, wn, x) <= 1e-5
+            assert O.max_rel_error(o, want) <= 1e-3
+
+
+def _expert_exact(O, x, g, gq, u, uq, d, dq):
+    """Exact expert output and the 1e-5 bound's normaliser per output row:
+    ||w_down_row|| * ||h|| with h = silu(gate x) * (up x) in float64."""
+    k, hidden, out_dim = x.size, g.shape[0], d.shape[0]
+    gx = O.matvec_f64(g, gq, x, k, hidden)
+    ux = O.matvec_f64(u, uq, x, k, hidden)
+    h = gx / (1.0 + np.exp(-gx)) * ux
+    y = O.matvec_f64(d, dq, h.astype(np.float32), hidden, out_dim)
+    return y, O.row_norms(d, dq, hidden, out_dim) * np.linalg.norm(h)
 
 
 def _rel(a, b):
@@ -186,6 +203,8 @@ def test_fused_expert_swiglu_matches_reference(oracle_mod, golden):
     assert O.lib().orc_fused_expert_swiglu_f64(x.ctypes.data, x.size, g.ctypes.data, 12, hidden, u.ctypes.data, 12,
                                                d.ctypes.data, 14, out_dim, exact.ctypes.data) == 1
     assert _rel(y, exact) <= 1e-3
+    ex, scale = _expert_exact(O, x, g, 12, u, 12, d, 14)
+    assert np.max(np.abs(y - ex) / scale) <= 1e-5
 
 
 def test_fused_moe_matches_reference_and_expert_sum(oracle_mod, golden):
@@ -202,6 +221,13 @@ def test_fused_moe_matches_reference_and_expert_sum(oracle_mod, golden):
     w = golden["ffn/moe_w"]
     y = qm.fused_moe_ffn(x, w, [e[0] for e in experts], [e[1] for e in experts], [e[2] for e in experts])
     assert _rel(y, golden["ffn/moe_y"].astype(np.float64)) <= 1e-3
+    O = oracle_mod
+    exact = [_expert_exact(O, x, np.ascontiguousarray(golden[f"ffn/e{e}/gate"]), 12,
+                           np.ascontiguousarray(golden[f"ffn/e{e}/up"]), 12,
+                           np.ascontiguousarray(golden[f"ffn/e{e}/down"]), 14) for e in range(2)]
+    want = sum(float(wi) * ex for wi, (ex, _) in zip(w, exact) if wi > 0)
+    scale = sum(abs(float(wi)) * sc for wi, (_, sc) in zip(w, exact) if wi > 0)
+    assert np.max(np.abs(y - want) / scale) <= 1e-5
     expected = sum(float(wi) * qm.fused_expert_swiglu(x, *e).astype(np.float64) for wi, e in zip(w, experts))
     assert _rel(y, expected) <= 1e-5
     # non-positive weights are skipped; all skipped -> zeros (write_mode 0)

@@ -5,7 +5,8 @@ ranks (127.0.0.1); each rank owns half of every linear's rows, half of the
 heads and half of the LM head. Its gathered logits must equal the unsharded
 restatement (oracle/decode_ref.py) for every position, for one sequence and
 for a batch of three (which exercises the [rank][batch][rows] gather
-re-layout), to 1e-9 relative. Also checks the plan's row ranges and its
+re-layout) -- both on activation codes and in the batched fp32 mode whose
+linears take the tile path on the device --, to 1e-9 relative. Also checks the plan's row ranges and its
 refusal of shapes that do not divide.
 """
 
@@ -35,7 +36,7 @@ def _weights():
     return layers, embed, head, out_norm
 
 
-def _worker(rank, world, port, batch, q, fuse=False):
+def _worker(rank, world, port, batch, q, fuse=False, tile=False):
     import torch.distributed as dist
 
     from cybel_b200.sharded import ShardedDecode, ShardPlan, shard_layer, shard_rows
@@ -48,7 +49,8 @@ def _worker(rank, world, port, batch, q, fuse=False):
         layers, embed, head, out_norm = _weights()
         plan = ShardPlan(TINY, world, rank)
         model = ShardedDecode(plan, 16, batch, [shard_layer(l, plan) for l in layers], embed,
-                              shard_rows(head, plan, "head"), out_norm, NumpyOps(world), fuse_norm=fuse)
+                              shard_rows(head, plan, "head"), out_norm, NumpyOps(world), fuse_norm=fuse, tile=tile)
+        assert model.tile == tile
         outs = []
         for pos in range(len(TOKENS[0])):
             model.tokens[:] = [TOKENS[b][pos] for b in range(batch)]
@@ -65,8 +67,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("batch,fuse", [(1, False), (3, False), (1, True)])
-def test_two_rank_sharded_decode_equals_unsharded(batch, fuse):
+@pytest.mark.parametrize("batch,fuse,tile", [(1, False, False), (3, False, False), (1, True, False), (3, False, True)])
+def test_two_rank_sharded_decode_equals_unsharded(batch, fuse, tile):
     import multiprocessing as mp
 
     from oracle.decode_ref import DecodeRef
@@ -74,7 +76,7 @@ def test_two_rank_sharded_decode_equals_unsharded(batch, fuse):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, batch, q, fuse)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, batch, q, fuse, tile)) for r in range(2)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=240) for _ in procs)

@@ -2,10 +2,12 @@
 
 Called through the C ABI twice in a row with different inputs (the shared
 array keeps the first call's contents) and compared with b200q_matmul, the
-regular device entry point, on the same inputs: the same fp32 tolerances as
-the GEMV tests (max |dy| / (||w_row|| * ||x||) <= 1e-5, ||dy||_inf /
-||y||_inf <= 1e-3). Oversized requests are refused with B200Q_ESCRATCH and
-leave y untouched. The file runs last so that it also passes after the
+regular device entry point, on the same inputs, and with the oracle's
+restatement of the same activation mode: the same fp32 tolerances as the
+GEMV tests (max |dy| / (||w_row|| * ||x||) <= 1e-5, ||dy||_inf /
+||y||_inf <= 1e-3). The device status word inside the fixed array reads 0
+afterwards (b200q_device_status). Oversized requests are refused with
+B200Q_ESCRATCH and leave y untouched. The file runs last so that it also passes after the
 other tests have used the library on the same device.
 """
 
@@ -44,6 +46,7 @@ def test_noalloc_matches_matmul_two_calls(oracle_mod, qt, act, n, k):
     for x, y in zip(xs, ys):  # two calls in a row on the shared scratch
         assert L.b200q_matvec_noalloc(qt, act, x.data_ptr(), dw.data_ptr(), y.data_ptr(), k, n, st) == 0
     torch.cuda.synchronize()
+    assert L.b200q_device_status(torch.cuda.current_device()) == 0
     wn = O.row_norms(W, qt, k, n)
     for x, y in zip(xs, ys):
         ref = torch.empty(n, dtype=torch.float32, device="cuda")
@@ -53,6 +56,9 @@ def test_noalloc_matches_matmul_two_calls(oracle_mod, qt, act, n, k):
         assert np.all(np.isfinite(yv))
         assert O.normalized_error(yv, rv, wn, xv) <= NORM_TOL
         assert O.max_rel_error(yv, rv) <= REL_TOL
+        want = O.matvec_q(W, qt, xv, k, n, act)  # the oracle in the same activation mode
+        assert O.normalized_error(yv, want, wn, xv) <= NORM_TOL
+        assert O.max_rel_error(yv, want) <= REL_TOL
 
 
 def test_noalloc_rejects_oversized_request():
