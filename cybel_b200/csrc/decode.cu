@@ -745,14 +745,14 @@ int launch_rope_attention(const float* q, const float* k, const float* v, int ba
     const int n_chunks = pos / kAttnChunk + 1;
     void* part = nullptr;
     void* cnt = nullptr;
-    bool fresh = false;
     int rc = scratch_for(dev, st, kScratchAttn,
                          static_cast<size_t>(batch) * n_heads * n_chunks * kPartStride * sizeof(float), &part);
+    // Arrival counters: zero when allocated (all of the buffer, so a later
+    // call with more sequences finds its counters zero too); the merging CTA
+    // resets its counter after each launch.
     if (rc == B200Q_OK)
-        rc = scratch_for(dev, st, kScratchAttnCnt, static_cast<size_t>(batch) * n_kv * sizeof(int), &cnt, &fresh);
+        rc = scratch_for(dev, st, kScratchAttnCnt, static_cast<size_t>(batch) * n_kv * sizeof(int), &cnt, true);
     if (rc != B200Q_OK) return rc;
-    if (fresh && cudaMemsetAsync(cnt, 0, static_cast<size_t>(batch) * n_kv * sizeof(int), st) != cudaSuccess)
-        return B200Q_ECUDA;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(n_kv, n_chunks, batch), dim3(kAttnWarps * 32), st, attr);
     const int dig = !xq ? 0 : (act_mode == B200Q_ACT_X8 ? 1 : 2);

@@ -228,10 +228,9 @@ std::map<std::tuple<int, cudaStream_t, int>, Scratch> g_scratch;
 
 }  // namespace
 
-int scratch_for(Device* dev, cudaStream_t st, int slot, size_t bytes, void** out, bool* fresh) {
+int scratch_for(Device* dev, cudaStream_t st, int slot, size_t bytes, void** out, bool zero) {
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     Scratch& s = g_scratch[std::make_tuple(dev->id, st, slot)];
-    if (fresh) *fresh = false;
     if (s.bytes < bytes) {
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
@@ -245,7 +244,9 @@ int scratch_for(Device* dev, cudaStream_t st, int slot, size_t bytes, void** out
         const size_t want = std::max<size_t>(bytes, 1u << 20);
         if (cudaMalloc(&s.ptr, want) != cudaSuccess) return B200Q_ENOMEM;
         s.bytes = want;
-        if (fresh) *fresh = true;
+        // Every byte of the allocation, not just the bytes asked for: a later
+        // call may use more of it without reallocating.
+        if (zero && cudaMemsetAsync(s.ptr, 0, want, st) != cudaSuccess) return B200Q_ECUDA;
     }
     *out = s.ptr;
     return B200Q_OK;

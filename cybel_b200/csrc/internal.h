@@ -63,9 +63,9 @@ constexpr int kPlanInfoFields = 15;
 int gemv_plan_info(int qtype, int act_mode, int k, int n, int mr, bool fq, int num_sms, long long* out, int out_len);
 // quantize_act kernel over `rows` contiguous rows of k into xq (row pitch xq_bytes_per_row).
 int launch_quantize_rows(int act_mode, const float* x, int rows, int k, uint8_t* xq, cudaStream_t st, bool pdl);
-// fresh (optional): set when the buffer was (re)allocated by this call; its
-// contents are then undefined.
-int scratch_for(Device* dev, cudaStream_t st, int slot, size_t bytes, void** out, bool* fresh = nullptr);
+// zero: a buffer (re)allocated by this call is zeroed in full on the stream
+// (otherwise the contents of a new buffer are undefined).
+int scratch_for(Device* dev, cudaStream_t st, int slot, size_t bytes, void** out, bool zero = false);
 long long xq_bytes_per_row(int k, int act_mode);
 
 int launch_repack(int dst_qtype, const void* src, void* dst, int k, int n, cudaStream_t st);
