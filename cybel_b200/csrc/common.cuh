@@ -68,6 +68,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test of a phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait by polling test_wait (the thread is never suspended, so it resumes
+// as soon as the phase completes); false on timeout. For waits that are
+// usually short and on the critical path.
+__device__ __forceinline__ bool mbar_wait_spin_bounded(uint32_t bar, uint32_t parity) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1; it < kWaitMaxPolls; ++it) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((it & 63u) == 0u && global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+    }
+    return false;
+}
+
 // Wait for the phase with the given parity to complete; false on timeout.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;

@@ -39,6 +39,14 @@ int env_int(const char* name, int dflt) {
     return v > 0 ? v : dflt;
 }
 
+// The same, accepting 0.
+int env_int0(const char* name, int dflt) {
+    const char* e = std::getenv(name);
+    if (!e || !*e) return dflt;
+    const int v = std::atoi(e);
+    return v >= 0 ? v : dflt;
+}
+
 // Ring + bookkeeping per CTA (one CTA per SM; B200Q_GEMV_SMEM_KB overrides).
 constexpr int kSmemBudgetKB = 220;
 // Preferred bytes per stage (B200Q_STAGE_KB overrides). Walker groups take
@@ -48,22 +56,27 @@ constexpr int kSmemBudgetKB = 220;
 constexpr int kStageTargetKB = 32;
 constexpr int kStageMax = 96 * 1024;      // largest stage
 constexpr int kMaxStages = 48;
-// Weight bytes issued before the consumers have issued their activation
-// loads (B200Q_GEMV_PREFETCH_KB): about what HBM delivers to one SM while the
-// CTA waits for the preceding kernel.
-constexpr int kPrefetchKB = 96;
+// Weight bytes issued at CTA start, before the activations are requested
+// (B200Q_GEMV_PREFETCH_KB): about what drains while the CTA waits for the
+// preceding kernel, so that little is still queued ahead of the activation
+// copy; the rest of the ring follows that copy.
+constexpr int kPrefetchKB = 64;
 
 struct Plan {
     GemvParams p;
     int threads;
     int smem;
     int grid;
-    long long x_bytes;  // staged activations (+ the fused quantizer's tiles) at the ring's end
+    long long x_bytes;  // staged activation codes, past the ring
     int dev = -1;       // device id the launch targets (set by the caller)
 };
 
-// fq: the GEMV quantizes fp32 activations itself (transpose tiles staged too).
-int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl, bool fq = false) {
+// Rows a consumer warp carries per iteration (kRowsPerIter in gemv.cuh).
+int rows_per_iter(int MR) { return MR == 1 ? 2 : 1; }
+
+// fq: the GEMV quantizes fp32 activations itself; they (and, with norm, the
+// RMSNorm gains) are first copied into the last nx ring slots.
+int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl, bool fq = false, bool norm = false) {
     FmtInfo f;
     if (!fmt_info(qtype, f)) return B200Q_EQTYPE;
     if (k <= 0 || n <= 0) return B200Q_EINVAL;
@@ -73,14 +86,13 @@ int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl, b
     const int S = (nb + f.blocks_per_slice - 1) / f.blocks_per_slice;
     int max_warps = (dig == 1 && MR == 1) ? 16 : 12;  // kGemvWarps in gemv.cuh
     if (S > max_warps) return B200Q_ESHAPE;
-    // B200Q_GEMV_WARPS caps the consumer warps (never below one per k-slice).
+    // B200Q_GEMV_WARPS caps the warps (never below one per k-slice).
     static const int warps_cap = env_int("B200Q_GEMV_WARPS", 0);
     if (warps_cap > 0) max_warps = std::max(S, std::min(max_warps, warps_cap));
-    static const int smem_budget = std::min(220, env_int("B200Q_GEMV_SMEM_KB", kSmemBudgetKB)) * 1024;
+    static const int smem_budget = std::min(227, env_int("B200Q_GEMV_SMEM_KB", kSmemBudgetKB)) * 1024;
     static const int target = env_int("B200Q_STAGE_KB", kStageTargetKB) * 1024;
-    static const int prefetch = env_int("B200Q_GEMV_PREFETCH_KB", kPrefetchKB) * 1024;
-    static const int hold = env_int("B200Q_GEMV_HOLD", 2) == 1 ? 1 : 0;
-    const int U = MR == 1 ? 2 : 1;  // kRowsPerIter in gemv.cuh
+    static const int prefetch = env_int0("B200Q_GEMV_PREFETCH_KB", kPrefetchKB) * 1024;
+    const int U = rows_per_iter(MR);
     const int walkers = std::max(1, max_warps / S);
     const int n_quads = (n + 3) / 4;
     const int grid = std::min(num_sms, n_quads);
@@ -90,10 +102,6 @@ int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl, b
     int R = U * static_cast<int>(std::max<long long>(1, (target + U * rb / 2) / (U * rb)));
     R = std::min(R, std::max(U, (rows_cta + U - 1) / U * U));
     if (f.r4) R = (R + 3) / 4 * 4;
-    // One walker per U rows of a stage, then as many groups as that leaves.
-    const int SW = std::max(1, std::min(walkers, (R + U - 1) / U));
-    const int G = std::max(1, walkers / SW);
-    const int WR = G * SW;
     // A stage copies the 16-byte-aligned window around its rows: at most
     // rows * rb + 30 bytes; kSlotPad also covers the 4-byte over-read of the
     // unaligned word loads.
@@ -102,22 +110,27 @@ int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl, b
         R = f.r4 ? 4 : std::max<int>(1, static_cast<int>((kStageMax - kSlotPad) / rb));
         if (R * rb + kSlotPad > kStageMax) return B200Q_ESHAPE;
     }
+    // One walker per U rows of a stage, then as many groups as that leaves.
+    const int SW = std::max(1, std::min(walkers, (R + U - 1) / U));
+    int G = std::max(1, walkers / SW);
     const int stage_stride = static_cast<int>(((R * rb + kSlotPad) + 127) / 128 * 128);
     const int part_bytes = rows_cta * MR * S * 4;
-    const int ns_fit = (smem_budget - part_bytes - 64) / (stage_stride + 16);
-    int NS = std::min(kMaxStages, ns_fit);
-    // The staged activations occupy the last bytes of the ring; only slots
-    // below them are filled before the activations are in registers. Small
-    // stages get more slots, so the ring still holds them with a slot to spare.
-    const long long x_bytes =
-        static_cast<long long>(MR) * xs_row_bytes(k, dig) + (fq ? static_cast<long long>(S * WR) * kFqWarpBytes + 128 : 0);
-    NS = static_cast<int>(
-        std::max<long long>(NS, std::min<long long>(ns_fit, (x_bytes + stage_stride - 1) / stage_stride + 1)));
+    const long long x_bytes = static_cast<long long>(MR) * xs_row_bytes(k, dig);
+    // full + empty barriers per slot, x and x-done barriers, x flag, per-warp sums
+    const long long book = static_cast<long long>(kMaxStages) * 16 + 20 + kGemvMaxWarps * 4 + part_bytes + 64;
+    const long long room = smem_budget - x_bytes - book;
+    int NS = static_cast<int>(std::min<long long>(kMaxStages, room > 0 ? room / stage_stride : 0));
     if (NS < 2) return B200Q_ESHAPE;
-    const long long ring = static_cast<long long>(NS) * stage_stride;
-    if (x_bytes > ring) return B200Q_ESHAPE;
-    const int x_off = static_cast<int>((ring - x_bytes) / 128 * 128);
-    const int PD = std::min(std::max(1, prefetch / stage_stride), x_off / stage_stride);
+    // Stage s and s + NS must belong to the same walker group (each group
+    // then meets its slots' barrier phases in order): NS is a multiple of G.
+    if (NS < G) G = NS;
+    NS -= NS % G;
+    const long long fq_bytes = fq ? static_cast<long long>(MR + (norm ? 1 : 0)) * k * 4 : 0;
+    const int nx = static_cast<int>((fq_bytes + stage_stride - 1) / stage_stride);
+    if (nx > NS) return B200Q_ESHAPE;  // the fp32 rows must fit in the ring
+    const int WR = G * SW;
+    const int x_off = NS * stage_stride;
+    const int PD = std::max(0, std::min(NS, prefetch / stage_stride));
     GemvParams& p = pl.p;
     p = GemvParams{};
     p.row_bytes = rb;
@@ -132,13 +145,13 @@ int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl, b
     p.NS = NS;
     p.stage_stride = stage_stride;
     p.PD = PD;
-    p.pd_hold = hold;
     p.x_off = x_off;
+    p.nx = nx;
     p.n_quads = n_quads;
     p.rows_cta = rows_cta;
     pl.x_bytes = x_bytes;
     pl.threads = (S * WR + 1) * 32;
-    pl.smem = NS * stage_stride + (2 * NS + 2) * 8 + part_bytes + 16;
+    pl.smem = static_cast<int>(x_off + x_bytes + NS * 16 + 20 + kGemvMaxWarps * 4 + part_bytes + 16);
     pl.grid = grid;
     return B200Q_OK;
 }
@@ -321,7 +334,7 @@ int gemv_rows(int qtype, int act_mode, const void* w, const uint8_t* xq, long lo
         const int left = m - m0;
         const int MR = isums ? 1 : (left >= mr_max ? mr_max : (left >= 2 && mr_max >= 2 ? 2 : 1));
         Plan pl;
-        const int rc = make_plan(qtype, dig, k, n, MR, dev->num_sms, pl, xf != nullptr);
+        const int rc = make_plan(qtype, dig, k, n, MR, dev->num_sms, pl, xf != nullptr, gamma != nullptr);
         if (rc != B200Q_OK) return rc;
         pl.p.W = static_cast<const uint8_t*>(w);
         pl.dev = dev->id;
@@ -329,8 +342,8 @@ int gemv_rows(int qtype, int act_mode, const void* w, const uint8_t* xq, long lo
             pl.p.xf = xf + m0 * xf_stride;
             pl.p.xf_stride = xf_stride;
             if (gamma) {
-                // One pass of 32 groups per consumer warp holds the whole row.
-                if (MR != 1 || k / 32 > 32 * pl.p.S * pl.p.WR) return B200Q_ESHAPE;
+                // One group per lane covers the whole row.
+                if (MR != 1 || k > 32 * 32 * pl.p.S * pl.p.WR) return B200Q_ESHAPE;
                 pl.p.gamma = gamma;
                 pl.p.eps = eps;
             }

@@ -5,21 +5,23 @@
 // JSBuild/src/verso/Anvil/core/native/quantized_matmul.cpp:1536-2154, on the
 // same canonical (and R4 / LM) block layouts.
 //
-// Design (one persistent CTA per SM):
-//  * A producer warp streams each CTA's contiguous slab of weight rows into a
-//    ring of shared-memory stages with 1-D bulk copies (cp.async.bulk, no
-//    multicast) that complete on mbarriers. Weights are touched once, with an
-//    L2 evict-first policy.
+// Design (one persistent CTA per SM, 16 warps):
+//  * Each CTA streams its contiguous slab of weight rows into a ring of
+//    shared-memory stages with 1-D bulk copies (cp.async.bulk, no multicast)
+//    that complete on mbarriers. Weights are touched once, with an L2
+//    evict-first policy. No warp is set aside for this: thread 0 issues the
+//    first stages, and the warp that finishes a slot last refills it.
 //  * Activations are quantized per 32-element group (int8 "x8", or int16
-//    split in two byte planes "x16"). The consumer warps stage them once per
-//    CTA in shared memory -- quantizing the fp32 rows themselves (FQ
-//    instances: one launch per matvec) or copying the codes a preceding
-//    kernel wrote (the decode glue kernels) -- and each lane then keeps the
-//    codes of its k-slice in registers for all its rows.
+//    split in two byte planes "x16"). They are staged once per CTA in shared
+//    memory of their own, past the ring: FQ instances (one launch per
+//    matvec) bulk-copy the fp32 rows into ring slots and quantize them there,
+//    one group per lane; code instances copy the codes a preceding kernel
+//    wrote. Each lane then keeps the codes of its k-slice in registers for
+//    all its rows.
 //  * Programmatic dependent launch: the GEMV streams its first (static)
 //    weight stages while the preceding kernel runs and waits for it only
-//    before reading the activations; the rest of the ring is issued once the
-//    activation loads are out, so weight traffic does not delay them.
+//    before reading the activations, whose copy is requested before the rest
+//    of the ring, so the weight traffic does not delay it.
 //  * Per row a lane decodes its weight codes from shared memory and forms
 //    exact integer dot sums with dp4a; each group sum is scaled in fp32 by
 //    the weight and activation scales; partials are reduced per warp with
@@ -39,6 +41,7 @@ namespace b200q {
 // rows) take 12 consumer warps.
 template <int DIG, int MR>
 constexpr int kGemvWarps = (DIG == 1 && MR == 1) ? 16 : 12;
+constexpr int kGemvMaxWarps = 16;
 // Rows a consumer warp carries per iteration (independent chains, and the
 // loop and reduction overhead shared between them).
 template <int DIG, int MR>
@@ -66,9 +69,9 @@ struct GemvParams {
     int R;                 // rows per stage
     int NS;                // ring stages
     int stage_stride;      // bytes between ring slots (multiple of 128)
-    int PD;                // stages issued before the activation loads are issued
-    int pd_hold;           // 1: the stages after PD wait until the activations are in registers
-    int x_off;             // ring byte offset of the staged activations (>= PD * stage_stride)
+    int PD;                // stages issued at CTA start, before the activations are requested
+    int x_off;             // byte offset of the staged activation codes (just past the ring)
+    int nx;                // FQ: ring slots (at the ring's end) that first hold the fp32 rows (and gamma)
     int n_quads;           // ceil(n / 4)
     int rows_cta;          // most rows any CTA owns
     int w_static;          // weights not written by the preceding kernel: stream them before the grid dependency resolves
@@ -188,11 +191,6 @@ __host__ __device__ constexpr int xs_code_offset(int e) { return e + 16 * (e >> 
 __host__ __device__ constexpr int xs_row_bytes(int k, int dig) {
     return (dig * xs_plane_bytes(k) + (k / 32) * 8 + 15) / 16 * 16;
 }
-// Scratch of the fused quantizer: per consumer warp, 32 groups of 32 fp32
-// values at a 144-byte pitch (a transpose from coalesced loads to one group
-// per lane without bank conflicts).
-constexpr int kFqGroupPitch = 144;
-constexpr int kFqWarpBytes = 32 * kFqGroupPitch;
 
 // Quantize one 32-element group v into a quantized row at `base` (group g
 // of a row of k elements). The arithmetic is restated in the oracle as
@@ -711,203 +709,164 @@ __device__ __forceinline__ void load_run_smem(uint32_t row, int k, int e, XRun<D
     out.fsum = static_cast<float>(out.sum);
 }
 
-// Quantize one 32-element group v into the staged row at `row` (padded
-// layout, plane bytes kp): the arithmetic of quantize_group (amax,
-// iscale = QMAX / amax by IEEE division, one rounded multiply, half-even
-// codes, d = amax / QMAX), with the reductions as trees.
-template <int DIG>
-__device__ __forceinline__ void quantize_group_staged(const float (&v)[32], uint8_t* row, int k, int kp, int g) {
-    float m[16];
+// Stage MR rows of activation codes a preceding kernel wrote (xq layout) in
+// shared memory (xs, generic pointer; rows xs_row bytes apart in the padded
+// layout), using all warps, four 16-byte words per thread per trip.
+// `on_issued` runs on thread 0 once its first loads are issued (the weight
+// stages held back until then are issued behind them).
+template <int DIG, int MR, class OnIssued>
+__device__ __forceinline__ void stage_codes(const GemvParams& p, uint8_t* xs, int xs_row, int warp, int lane,
+                                            int nwarps, OnIssued on_issued) {
+    const int kp = xs_plane_bytes(p.k);
+    const int nthreads = nwarps * 32, tid = warp * 32 + lane;
+    bool first = true;
+    constexpr int B = 4;  // 16-byte words a thread loads per trip
+    const int words = static_cast<int>(xq_row_bytes(p.k, DIG) >> 4);
+    const int code_words = (DIG * p.k) >> 4;
+    const int total = MR * words;
+    for (int i0 = tid; i0 < total; i0 += B * nthreads) {
+        uint4 v[B];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) m[i] = fmaxf(fabsf(v[2 * i]), fabsf(v[2 * i + 1]));
-#pragma unroll
-    for (int w = 8; w > 0; w >>= 1) {
-#pragma unroll
-        for (int i = 0; i < w; ++i) m[i] = fmaxf(m[i], m[i + w]);
-    }
-    const float amax = m[0];
-    constexpr float QMAX = DIG == 1 ? 127.0f : 32767.0f;
-    const float iscale = amax > 0.0f ? __fdiv_rn(QMAX, amax) : 0.0f;
-    int ws[8];
-    uint32_t hw[8], lw[8];
-#pragma unroll
-    for (int w = 0; w < 8; ++w) {
-        uint32_t h = 0, l = 0;
-        int sw = 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int q = round_half_even_small(__fmul_rn(v[4 * w + j], iscale));
-            sw += q;
-            if (DIG == 1) {
-                h |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * j);
-            } else {
-                h |= (static_cast<uint32_t>(q >> 8) & 0xFFu) << (8 * j);
-                l |= (static_cast<uint32_t>(q) & 0xFFu) << (8 * j);
+        for (int b = 0; b < B; ++b) {
+            const int i = i0 + b * nthreads;
+            if (i < total) {
+                const int row = i / words, w = i - row * words;
+                v[b] = __ldg(reinterpret_cast<const uint4*>(p.xq + row * p.xq_stride) + w);
             }
         }
-        ws[w] = sw;
-        hw[w] = h;
-        lw[w] = l;
+        if (first && tid == 0) on_issued();
+        first = false;
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            const int i = i0 + b * nthreads;
+            if (i < total) {
+                const int row = i / words, w = i - row * words;
+                int off;
+                if (w < code_words) {
+                    const int plane = (16 * w) / p.k, e = 16 * w - plane * p.k;
+                    off = plane * kp + xs_code_offset(e);
+                } else {
+                    off = DIG * kp + (16 * w - DIG * p.k);
+                }
+                *reinterpret_cast<uint4*>(xs + row * xs_row + off) = v[b];
+            }
+        }
     }
-    const int sum = ((ws[0] + ws[1]) + (ws[2] + ws[3])) + ((ws[4] + ws[5]) + (ws[6] + ws[7]));
-    uint4* dh = reinterpret_cast<uint4*>(row + xs_code_offset(g * 32));
-    dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
-    if (DIG == 2) {
-        uint4* dl = reinterpret_cast<uint4*>(row + kp + xs_code_offset(g * 32));
-        dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
-    }
-    float* gd = reinterpret_cast<float*>(row + DIG * kp);
-    gd[g] = amax > 0.0f ? __fdiv_rn(amax, QMAX) : 0.0f;
-    reinterpret_cast<int*>(gd + k / 32)[g] = sum;
+    if (first && tid == 0) on_issued();
 }
 
-// Stage MR activation rows in shared memory (xs, generic pointer; rows
-// xs_row bytes apart in the padded layout), using all consumer warps.
-//  * FQ: each warp takes 32 groups at a time. Its lanes load them with
-//    coalesced 16-byte loads (eight per lane), pass them through the warp's
-//    transpose tile (kFqWarpBytes at tmp_all), and then each lane quantizes
-//    one group. With p.gamma set (one row, at most 32 groups per warp) the
-//    row is first RMS-normalized: x * (1 / sqrt(sum(x^2) / k + eps)) * gamma,
-//    the sum of squares reduced per warp into `red` and summed in warp order.
-//  * Otherwise the codes a preceding kernel wrote (xq layout) are copied,
-//    four 16-byte words per thread per trip.
-// Thread 0 sets the word at `flag` once its first loads are issued: the
-// producer waits for it before releasing the bulk of the weight copies, so
-// these loads are not queued behind them.
-template <int DIG, int MR, bool FQ>
-__device__ __forceinline__ void stage_activations(const GemvParams& p, uint8_t* xs, int xs_row, uint8_t* tmp_all,
-                                                  float* red, int warp, int lane, int nwarps, uint32_t flag) {
+// Quantize the fp32 rows staged in shared memory (xf4: MR rows of k, then
+// the RMSNorm gains when `norm`) into the padded code rows at xs, one
+// 32-element group per lane: the arithmetic of quantize_group (amax,
+// iscale = QMAX / amax by IEEE division, one rounded multiply, half-even
+// codes, d = amax / QMAX, the group's code sum), one division each per
+// group. A lane reads its group's eight float4 in an order rotated by its
+// group index and stores each code word at the matching position, so the
+// lanes of a quarter-warp (groups 128 B apart) use different banks. With
+// `norm` (one row, one group per lane covering it -- host-checked) the row
+// is first scaled by 1 / sqrt(sum(x^2) / k + eps) and by the gains, the sum
+// of squares reduced per warp into `red` and summed in warp order.
+template <int DIG, int MR>
+__device__ __forceinline__ void quantize_staged_rows(const GemvParams& p, const float4* xf4, bool norm, uint8_t* xs,
+                                                     int xs_row, float* red, int warp, int lane, int nwarps) {
+    const int nthreads = nwarps * 32;
     const int kp = xs_plane_bytes(p.k);
-    if constexpr (FQ) {
-        const int groups = p.k >> 5;
-        const int total = MR * groups;
-        const bool norm = MR == 1 && p.gamma != nullptr;  // one pass per warp (host-checked)
-        float* tmp = reinterpret_cast<float*>(tmp_all + warp * kFqWarpBytes);
-        for (int gw = warp * 32; gw < total || (norm && gw == warp * 32); gw += nwarps * 32) {
-            float4 v[8];
+    const int groups = p.k >> 5;
+    const int total_g = MR * groups;
+    constexpr float QMAX = DIG == 1 ? 127.0f : 32767.0f;
+    for (int g0 = warp * 32; g0 < total_g || (norm && g0 == warp * 32); g0 += nthreads) {
+        const int g = g0 + lane;
+        const bool valid = g < total_g;
+        float4 f[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int f = 32 * j + lane;  // float4 index within the warp's 32 groups
-                const int gg = gw + (f >> 3);
-                v[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (gg < total) {
-                    const int row = gg / groups, gi = gg - row * groups;
-                    v[j] = __ldg(reinterpret_cast<const float4*>(p.xf + row * p.xf_stride + gi * 32) + (f & 7));
-                }
-            }
-            if (gw == warp * 32 && warp == 0 && lane == 0) sts_volatile(flag, 1u);
-            if (norm) {
-                float4 g[8];
+        for (int i = 0; i < 8; ++i)
+            f[i] = valid ? xf4[g * 8 + ((i + g) & 7)] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (norm) {
+            float ss = 0.0f;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int f = 32 * j + lane;
-                    const int gg = gw + (f >> 3);
-                    g[j] = gg < total ? __ldg(reinterpret_cast<const float4*>(p.gamma + gg * 32) + (f & 7))
-                                      : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                }
-                float ss = 0.0f;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    ss = fmaf(v[j].x, v[j].x, ss);
-                    ss = fmaf(v[j].y, v[j].y, ss);
-                    ss = fmaf(v[j].z, v[j].z, ss);
-                    ss = fmaf(v[j].w, v[j].w, ss);
-                }
-#pragma unroll
-                for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-                if (lane == 0) red[warp] = ss;
-                named_bar_sync(2, static_cast<uint32_t>(nwarps * 32));
-                float tot = 0.0f;
-                for (int w = 0; w < nwarps; ++w) tot += red[w];
-                const float inv_rms = 1.0f / sqrtf(tot / static_cast<float>(p.k) + p.eps);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    v[j] = make_float4(v[j].x * inv_rms * g[j].x, v[j].y * inv_rms * g[j].y,
-                                       v[j].z * inv_rms * g[j].z, v[j].w * inv_rms * g[j].w);
-                }
+            for (int i = 0; i < 8; ++i) {
+                ss = fmaf(f[i].x, f[i].x, ss);
+                ss = fmaf(f[i].y, f[i].y, ss);
+                ss = fmaf(f[i].z, f[i].z, ss);
+                ss = fmaf(f[i].w, f[i].w, ss);
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int f = 32 * j + lane;
-                *reinterpret_cast<float4*>(tmp + (f >> 3) * (kFqGroupPitch / 4) + (f & 7) * 4) = v[j];
-            }
-            __syncwarp();
-            const int g = gw + lane;
-            if (g < total) {
-                float x[32];
-                const float* src = tmp + lane * (kFqGroupPitch / 4);
+            for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) red[warp] = ss;
+            named_bar_sync(2, static_cast<uint32_t>(nthreads));
+            float tot = 0.0f;
+            for (int w = 0; w < nwarps; ++w) tot += red[w];
+            const float inv_rms = 1.0f / sqrtf(tot / static_cast<float>(p.k) + p.eps);
+            if (valid) {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    const float4 f4 = *reinterpret_cast<const float4*>(src + 4 * i);
-                    x[4 * i] = f4.x;
-                    x[4 * i + 1] = f4.y;
-                    x[4 * i + 2] = f4.z;
-                    x[4 * i + 3] = f4.w;
-                }
-                const int row = g / groups, gi = g - row * groups;
-                quantize_group_staged<DIG>(x, xs + row * xs_row, p.k, kp, gi);
-            }
-            __syncwarp();
-            if (norm) break;
-        }
-        if (warp == 0 && lane == 0) sts_volatile(flag, 1u);
-    } else {
-        constexpr int B = 4;  // 16-byte words a thread loads per trip
-        const int nthreads = nwarps * 32, tid = warp * 32 + lane;
-        const int words = static_cast<int>(xq_row_bytes(p.k, DIG) >> 4);
-        const int code_words = (DIG * p.k) >> 4;
-        const int total = MR * words;
-        for (int i0 = tid; i0 < total; i0 += B * nthreads) {
-            uint4 v[B];
-#pragma unroll
-            for (int b = 0; b < B; ++b) {
-                const int i = i0 + b * nthreads;
-                if (i < total) {
-                    const int row = i / words, w = i - row * words;
-                    v[b] = __ldg(reinterpret_cast<const uint4*>(p.xq + row * p.xq_stride) + w);
-                }
-            }
-            if (i0 == tid && tid == 0) sts_volatile(flag, 1u);
-#pragma unroll
-            for (int b = 0; b < B; ++b) {
-                const int i = i0 + b * nthreads;
-                if (i < total) {
-                    const int row = i / words, w = i - row * words;
-                    int off;
-                    if (w < code_words) {
-                        const int plane = (16 * w) / p.k, e = 16 * w - plane * p.k;
-                        off = plane * kp + xs_code_offset(e);
-                    } else {
-                        off = DIG * kp + (16 * w - DIG * p.k);
-                    }
-                    *reinterpret_cast<uint4*>(xs + row * xs_row + off) = v[b];
+                    const float4 gm = xf4[total_g * 8 + g * 8 + ((i + g) & 7)];
+                    f[i] = make_float4(f[i].x * inv_rms * gm.x, f[i].y * inv_rms * gm.y, f[i].z * inv_rms * gm.z,
+                                       f[i].w * inv_rms * gm.w);
                 }
             }
         }
-        if (tid == 0) sts_volatile(flag, 1u);
+        if (valid) {
+            float m4[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                m4[i] = fmaxf(fmaxf(fabsf(f[i].x), fabsf(f[i].y)), fmaxf(fabsf(f[i].z), fabsf(f[i].w)));
+            const float amax = fmaxf(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])),
+                                     fmaxf(fmaxf(m4[4], m4[5]), fmaxf(m4[6], m4[7])));
+            const float iscale = amax > 0.0f ? __fdiv_rn(QMAX, amax) : 0.0f;
+            const int row = g / groups, gi = g - row * groups;
+            uint8_t* xrow = xs + row * xs_row;
+            int ws[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int c0 = round_half_even_small(__fmul_rn(f[i].x, iscale));
+                const int c1 = round_half_even_small(__fmul_rn(f[i].y, iscale));
+                const int c2 = round_half_even_small(__fmul_rn(f[i].z, iscale));
+                const int c3 = round_half_even_small(__fmul_rn(f[i].w, iscale));
+                ws[i] = (c0 + c1) + (c2 + c3);
+                const int off = xs_code_offset(gi * 32) + 4 * ((i + g) & 7);
+                if (DIG == 1) {
+                    *reinterpret_cast<uint32_t*>(xrow + off) =
+                        __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
+                } else {
+                    *reinterpret_cast<uint32_t*>(xrow + off) =
+                        __byte_perm(__byte_perm(c0, c1, 0x0051), __byte_perm(c2, c3, 0x0051), 0x5410);
+                    *reinterpret_cast<uint32_t*>(xrow + kp + off) =
+                        __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
+                }
+            }
+            float* gd = reinterpret_cast<float*>(xrow + DIG * kp);
+            gd[gi] = amax > 0.0f ? __fdiv_rn(amax, QMAX) : 0.0f;
+            reinterpret_cast<int*>(gd + groups)[gi] =
+                ((ws[0] + ws[1]) + (ws[2] + ws[3])) + ((ws[4] + ws[5]) + (ws[6] + ws[7]));
+        }
+        if (norm) break;
     }
 }
 
 // ---------------------------------------------------------------------------
 // The kernel: one CTA per SM streams a contiguous slab of rows through a
-// ring of NS shared-memory stages of R rows. Warp NW (the producer) issues
-// one bulk copy per stage (L2 evict-first; stages stay >= ~16 KB, since the
-// copies in flight per SM are limited in number). The NW consumer warps are
-// S k-slices x WR walkers, in G groups of SW walkers; stage s belongs to
-// group s % G, whose S x SW warps take their slice of its rows, U rows at a
-// time, the SW walkers of a slice interleaved.
+// ring of NS shared-memory stages of R rows (1-D bulk copies, L2
+// evict-first, no multicast; stages stay >= ~16 KB, since the copies in
+// flight per SM are limited in number). Warp NW (the producer) issues every
+// copy. The NW consumer warps are S k-slices x WR walkers, in G groups of SW
+// walkers; stage s belongs to group s % G, whose S x SW warps take their
+// slice of its rows, U rows at a time, the SW walkers of a slice
+// interleaved, and release it with one arrival each on the slot's empty
+// barrier.
 //
-// Start-up order: weight copies and the activation loads share the memory
-// system, so a full ring issued at CTA start would hold the activation loads
-// behind microseconds of weight traffic. The producer issues the first PD
-// stages (about what arrives while the CTA waits for the preceding kernel),
-// then waits until the consumers have issued their activation loads (a
-// shared-memory flag; a bounded wait that only delays, never fails) before
-// issuing the rest. The activations are staged in the last bytes of the ring
-// (x_off); the slots there are filled only after every consumer warp has
-// taken its codes into registers (arrivals on xbar).
+// The order of the requests is chosen for the memory system, whose queues
+// serve them roughly in order (a request waits behind the bytes requested
+// before it): the producer issues PD weight stages at CTA start (before the
+// grid dependency resolves, when the weights are static), then -- once the
+// activations may be read -- their copy first and the rest of the ring
+// behind it. FQ instances bring the fp32 rows (and the RMSNorm gains) in
+// with one bulk copy per row into the last nx ring slots; the consumers
+// quantize them there into the codes area (which has its own bytes past the
+// ring) and hand the slots back to the producer (xdone). Code instances copy
+// the codes with plain loads; the producer issues the ring's remaining
+// stages once thread 0 has issued its loads (a shared-memory flag; a bounded
+// wait that only paces, never fails).
 // ---------------------------------------------------------------------------
 template <int QT, int DIG, int MR, bool DBG, bool FQ>
 __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_kernel(const GemvParams p) {
@@ -923,15 +882,19 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_k
     const int nwarps = p.S * p.WR;
     const int nthreads = nwarps * 32;
 
+    // Layout: ring | staged activation codes | full barriers | empty
+    // barriers | x barrier | x-done barrier | x-loads flag | per-warp sums
+    // (RMSNorm) | slice partials.
     uint8_t* ring = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(ring + static_cast<size_t>(p.NS) * p.stage_stride);
+    uint8_t* xs = smem + p.x_off;
+    const int xs_row = xs_row_bytes(p.k, DIG);
+    uint64_t* full = reinterpret_cast<uint64_t*>(xs + MR * xs_row);
     uint64_t* empty = full + p.NS;
-    uint64_t* xbar = empty + p.NS;                            // activations staged: one arrival per consumer warp
-    uint32_t* xflag = reinterpret_cast<uint32_t*>(xbar + 1);  // activation loads issued
-    float* part = reinterpret_cast<float*>(xbar + 2);         // [rows of this CTA][MR][S]
-    uint8_t* xs = ring + p.x_off;                             // staged activations (padded rows)
-    uint8_t* xtmp = xs + MR * xs_row_bytes(p.k, DIG);         // fused quantizer's transpose tiles (FQ)
-    float* xred = reinterpret_cast<float*>(xtmp + (FQ ? nwarps * kFqWarpBytes : 0));  // per-warp sums (RMSNorm)
+    uint64_t* xbar = empty + p.NS;
+    uint64_t* xdone = xbar + 1;
+    uint32_t* xflag = reinterpret_cast<uint32_t*>(xdone + 1);
+    float* red = reinterpret_cast<float*>(xflag + 1);
+    float* part = red + kGemvMaxWarps;  // [rows of this CTA][MR][S]
 
     // Contiguous slab of rows per CTA, balanced to one row (to one 4-row
     // group for the R4 layouts).
@@ -942,13 +905,17 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_k
     const int r_begin = u0 * unit;
     const int r_end = min(u1 * unit, p.n);
     const int n_stages = r_end > r_begin ? (r_end - r_begin + p.R - 1) / p.R : 0;
+    const int free_slots = p.NS - (FQ ? p.nx : 0);  // slots the weights have before the activations are staged
+    const bool norm = FQ && MR == 1 && p.gamma != nullptr;
+    float* xf_s = reinterpret_cast<float*>(ring + static_cast<size_t>(free_slots) * p.stage_stride);  // FQ fp32 rows
 
     if (tid == 0) {
         for (int i = 0; i < p.NS; ++i) {
             mbar_init(smem_addr(full + i), 1);
             mbar_init(smem_addr(empty + i), static_cast<uint32_t>(p.S * p.SW));
         }
-        mbar_init(smem_addr(xbar), static_cast<uint32_t>(nwarps));
+        mbar_init(smem_addr(xbar), 1);
+        mbar_init(smem_addr(xdone), static_cast<uint32_t>(nwarps));
         *xflag = 0u;
         fence_mbar_init();
     }
@@ -960,34 +927,13 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_k
 
     if (warp == nwarps) {
         // ---------------- producer ----------------
-        // Weights may stream before the preceding kernel finishes only when
-        // the caller declared them static.
-        if (!p.w_static) griddep_wait();
         if (lane == 0 && n_stages > 0) {
             const uint64_t pol = l2_policy_evict_first();
-            const int xs_slot = p.x_off / p.stage_stride;  // first slot the staged activations overlap
-            int issued = 0;
-            bool ok = true;
-            for (int s = 0; s < n_stages && ok; ++s) {
-                if (s == p.PD && !p.pd_hold) {
-                    // Pacing only: proceed after ~20 us even if the flag never comes.
-                    const uint64_t t0 = global_timer_ns();
-                    while (lds_volatile(smem_addr(xflag)) == 0u && global_timer_ns() - t0 < 20000ull) {
-                    }
-                }
-                if (s == (p.pd_hold ? p.PD : xs_slot) && !mbar_wait_bounded(smem_addr(xbar), 0u)) {
-                    *p.status = STATUS_TIMEOUT;
-                    break;
-                }
+            // Stage s into its slot: the 16-byte-aligned window around the
+            // stage's rows (consumers add (r0 * row_bytes) & 15 to find the
+            // first row).
+            auto issue = [&](int s) {
                 const int slot = s % p.NS;
-                const uint32_t use = static_cast<uint32_t>(s / p.NS);
-                if (!mbar_wait_bounded(smem_addr(empty + slot), (use & 1u) ^ 1u)) {
-                    *p.status = STATUS_TIMEOUT;
-                    ok = false;
-                    break;
-                }
-                // Copy the 16-byte-aligned window around the stage's rows;
-                // consumers add (r0 * row_bytes) & 15 to find the first row.
                 const int r0 = r_begin + s * p.R;
                 const int rows = min(p.R, r_end - r0);
                 const long long b0 = (r0 * p.row_bytes) & ~15ll;
@@ -996,17 +942,80 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_k
                 const uint32_t fb = smem_addr(full + slot);
                 mbar_arrive_expect_tx(fb, bytes);
                 bulk_g2s(smem_addr(ring + static_cast<size_t>(slot) * p.stage_stride), p.W + b0, bytes, fb, pol);
+            };
+            const uint32_t x_bytes = static_cast<uint32_t>(MR * p.k * 4);
+            const uint32_t g_bytes = norm ? static_cast<uint32_t>(p.k * 4) : 0u;
+            const int first_batch = min(n_stages, min(p.PD, free_slots));
+            const int pre_fill = min(n_stages, free_slots);
+            const int ring_fill = min(n_stages, p.NS);
+            auto start = [&]() {
+                for (int s = 0; s < first_batch; ++s) issue(s);
+                if (FQ) {
+                    mbar_arrive_expect_tx(smem_addr(xbar), x_bytes + g_bytes);
+                    if (norm) bulk_g2s(smem_addr(xf_s + MR * p.k), p.gamma, g_bytes, smem_addr(xbar), pol);
+                }
+            };
+            // Weights (and gains) may stream before the preceding kernel
+            // finishes only when the caller declared them static.
+            if (p.w_static) start();
+            griddep_wait();
+            if (!p.w_static) start();
+            bool ok = true;
+            if (FQ) {
+                for (int m = 0; m < MR; ++m)
+                    bulk_g2s(smem_addr(xf_s + m * p.k), p.xf + m * p.xf_stride, static_cast<uint32_t>(p.k * 4),
+                             smem_addr(xbar), pol);
+                for (int s = first_batch; s < pre_fill; ++s) issue(s);
+                // The fp32 slots return once every consumer warp has quantized.
+                ok = mbar_wait_bounded(smem_addr(xdone), 0u);
+                if (ok)
+                    for (int s = pre_fill; s < ring_fill; ++s) issue(s);
+            } else {
+                // Pacing only: proceed after ~20 us even if the flag never comes.
+                const uint64_t t0 = global_timer_ns();
+                while (lds_volatile(smem_addr(xflag)) == 0u && global_timer_ns() - t0 < 20000ull) {
+                }
+                for (int s = first_batch; s < ring_fill; ++s) issue(s);
+            }
+            int issued = ok ? ring_fill : first_batch;
+            for (int s = ring_fill; s < n_stages && ok; ++s) {
+                const int slot = s % p.NS;
+                if (!mbar_wait_bounded(smem_addr(empty + slot), static_cast<uint32_t>(((s / p.NS) - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                issue(s);
                 issued = s + 1;
             }
+            if (!ok) *p.status = STATUS_TIMEOUT;
             // Do not let the CTA retire with copies in flight: wait (bounded)
             // for the last stages issued.
             for (int s = max(0, issued - p.NS); s < issued; ++s)
                 (void)mbar_wait_bounded(smem_addr(full + s % p.NS), static_cast<uint32_t>((s / p.NS) & 1));
+            if (FQ) (void)mbar_wait_bounded(smem_addr(xbar), 0u);
         }
         return;
     }
 
     // ---------------- consumers ----------------
+    // The activations (fp32 rows, or their codes) are written by the
+    // preceding kernel. Stage them once per CTA, then every lane takes its
+    // runs into registers.
+    griddep_wait();
+    if constexpr (FQ) {
+        if (!mbar_wait_spin_bounded(smem_addr(xbar), 0u) && tid == 0) *p.status = STATUS_TIMEOUT;
+        quantize_staged_rows<DIG, MR>(p, reinterpret_cast<const float4*>(xf_s), norm, xs, xs_row, red, warp, lane,
+                                      nwarps);
+        // The fp32 slots go back to the weights: order this thread's reads of
+        // them before the bulk copies that overwrite them.
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(xdone));
+    } else {
+        stage_codes<DIG, MR>(p, xs, xs_row, warp, lane, nwarps, [&]() { sts_volatile(smem_addr(xflag), 1u); });
+    }
+    named_bar_sync(1, static_cast<uint32_t>(nthreads));
+
     const int slice = warp % p.S;
     const int walker = warp / p.S;
     const int group = walker / p.SW, sub = walker - group * p.SW;
@@ -1016,14 +1025,6 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_k
     const bool active1 = blk + 1 < p.nb;  // second block of a two-block lane
     const int blk_c = active ? blk : 0;
 
-    // The activations (fp32 rows, or their codes) are written by the
-    // preceding kernel. Stage them once per CTA, then every lane takes its
-    // runs into registers and releases the staging bytes to the producer.
-    griddep_wait();
-    const int xs_row = xs_row_bytes(p.k, DIG);
-    stage_activations<DIG, MR, FQ>(p, xs, xs_row, xtmp, xred, warp, lane, nwarps, smem_addr(xflag));
-    fence_proxy_async_smem();
-    named_bar_sync(1, static_cast<uint32_t>(nthreads));
     X x[MR][RUNS];
     float xdd[MR][RUNS];  // group scale (with the x16 factor of in-place high nibbles folded in)
     float xsd[MR][RUNS];  // group scale * group code sum (Q4_K mins)
@@ -1038,8 +1039,6 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_k
             xsd[m][r] = x[m][r].d * x[m][r].fsum;
         }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_addr(xbar));
 
     constexpr int U = kRowsPerIter<DIG, MR>;
     constexpr int V = U * MR;
@@ -1051,7 +1050,7 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_k
         const uint32_t use = static_cast<uint32_t>(s / p.NS);
         const int r0 = r_begin + s * p.R;
         const int rows = min(p.R, r_end - r0);
-        if (ok && !mbar_wait_bounded(smem_addr(full + slot), use & 1u)) {
+        if (ok && !mbar_wait_spin_bounded(smem_addr(full + slot), use & 1u)) {
             if (lane == 0) *p.status = STATUS_TIMEOUT;
             ok = false;
         }
@@ -1117,9 +1116,9 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_k
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_addr(empty + slot));
     }
-    // One barrier for the consumers: sum the slice partials of every row in a
-    // fixed order and write y (zeros for rows a timed-out wait skipped are
-    // flagged through the status word).
+    // One barrier for the consumers: sum the slice partials of every row in
+    // a fixed order and write y (rows a timed-out wait skipped are flagged
+    // through the status word).
     named_bar_sync(1, static_cast<uint32_t>(nthreads));
     for (int i = tid; i < (r_end - r_begin) * MR; i += nthreads) {
         const int rl = i / MR, m = i % MR;

@@ -2,8 +2,10 @@
 sweep of formats, activation modes and shapes, without a GPU:
 
 * every plan the kernel may be launched with fits the kernel's launch bounds
-  and the shared memory of an SM, covers every row, and keeps the staged
-  activations inside the ring above the slots filled before them;
+  and the shared memory of an SM, covers every row, keeps the staged
+  activation codes in bytes of their own past the ring, and has a ring whose
+  slot count is a multiple of the walker groups;
+* the planner refuses exactly the shapes its rule refuses;
 * every Llama-3-8B / 70B shape of the benchmark configurations has a plan, in
   both activation modes, from codes and from fp32 x.
 """
@@ -28,27 +30,39 @@ def _plan(lib, qt, act, k, n, mr, fq):
     return rc, dict(zip(FIELDS, list(out)))
 
 
+def _rows_per_iter(qt, act, mr):
+    """Rows a consumer warp carries per iteration (kRowsPerIter in gemv.cuh)."""
+    return 2 if mr == 1 else 1
+
+
+def _max_warps(act, mr):
+    """Consumer warps of the kernel instance (kGemvWarps in gemv.cuh)."""
+    return 16 if (act == 1 and mr == 1) else 12
+
+
 def _check(qt, act, k, n, mr, p):
     elems, nbytes = BLOCK[qt]
     nb = k // elems
     rb = nb * nbytes
-    max_warps = 16 if (act == 1 and mr == 1) else 12
     assert p["row_bytes"] == rb
     assert p["S"] == -(-nb // BLOCKS_PER_SLICE[qt])
-    assert p["G"] * p["SW"] == p["WR"] and p["S"] * p["WR"] <= max_warps
-    assert p["threads"] == (p["S"] * p["WR"] + 1) * 32
+    assert p["G"] * p["SW"] == p["WR"] and p["S"] * p["WR"] <= _max_warps(act, mr)
+    assert p["threads"] == (p["S"] * p["WR"] + 1) * 32  # consumer warps and the producer warp
     assert p["grid"] == min(SMS, -(-n // 4))
     assert p["rows_cta"] * p["grid"] >= n
     assert p["R"] >= 1 and (qt not in (112, 114) or p["R"] % 4 == 0)
     # a stage holds the 16-byte-aligned window around its rows plus the
     # 4-byte over-read of the unaligned word loads
     assert p["stage_stride"] % 128 == 0 and p["stage_stride"] >= p["R"] * rb + 34
-    assert p["NS"] >= 2
+    # stage s and s + NS belong to the same walker group
+    assert p["NS"] >= 2 and p["NS"] % p["G"] == 0
     ring = p["NS"] * p["stage_stride"]
-    assert p["smem"] >= ring and p["smem"] <= 220 * 1024
-    # staged activations at the ring's end, above every slot filled before them
-    assert p["x_off"] % 128 == 0 and p["x_off"] + p["x_bytes"] <= ring
-    assert 0 <= p["PD"] <= p["x_off"] // p["stage_stride"]
+    # the staged activation codes have their own bytes past the ring
+    assert p["x_off"] == ring
+    kp = k + 16 * (-(-k // 256))
+    assert p["x_bytes"] == mr * (-(-(act * kp + (k // 32) * 8) // 16) * 16)
+    assert p["smem"] >= ring + p["x_bytes"] + p["NS"] * 16 and p["smem"] <= 220 * 1024
+    assert 0 <= p["PD"] <= p["NS"]
 
 
 def _max_rows(qt, act):
@@ -65,19 +79,18 @@ def _launch_rows(qt, act):
 
 def _no_plan_expected(qt, act, k, n, mr, fq):
     """The planner's refusals (make_plan in gemv.cu), restated: more k-slices
-    than the kernel has consumer warps, one row (one 4-row group for R4) over
-    the largest stage (96 KB), or staged activations larger than the ring the
-    shared-memory budget (220 KB) leaves room for."""
+    than the kernel has consumer warps, one row (one 4-row group for R4) over the
+    largest stage (96 KB), fewer than two stages left in the shared-memory
+    budget (220 KB) beside the staged activation codes, or (fq) fp32 rows
+    larger than the ring they are first copied into."""
     elems, nbytes = BLOCK[qt]
     nb = k // elems
     rb = nb * nbytes
     S = -(-nb // BLOCKS_PER_SLICE[qt])
-    max_warps = 16 if (act == 1 and mr == 1) else 12
-    if S > max_warps:
+    if S > _max_warps(act, mr):
         return True
     r4 = qt in (112, 114)
-    U = 2 if mr == 1 else 1
-    walkers = max(1, max_warps // S)
+    U = _rows_per_iter(qt, act, mr)
     n_quads = -(-n // 4)
     grid = min(SMS, n_quads)
     rows_cta = 4 * (-(-n_quads // grid))
@@ -85,19 +98,23 @@ def _no_plan_expected(qt, act, k, n, mr, fq):
     R = min(R, max(U, -(-rows_cta // U) * U))
     if r4:
         R = -(-R // 4) * 4
-    SW = max(1, min(walkers, -(-R // U)))
-    WR = max(1, walkers // SW) * SW
     if R * rb + 48 > 96 * 1024:
         R = 4 if r4 else max(1, (96 * 1024 - 48) // rb)
         if R * rb + 48 > 96 * 1024:
             return True
     stride = -(-(R * rb + 48) // 128) * 128
-    ns_fit = (220 * 1024 - rows_cta * mr * S * 4 - 64) // (stride + 16)
     kp = k + 16 * (-(-k // 256))
-    xs_row = -(-(act * kp + (k // 32) * 8) // 16) * 16
-    x_bytes = mr * xs_row + (S * WR * 4608 + 128 if fq else 0)
-    ns = max(min(48, ns_fit), min(ns_fit, -(-x_bytes // stride) + 1))
-    return ns < 2 or x_bytes > ns * stride
+    x_bytes = mr * (-(-(act * kp + (k // 32) * 8) // 16) * 16)
+    room = 220 * 1024 - x_bytes - (48 * 16 + 20 + 16 * 4 + rows_cta * mr * S * 4 + 64)
+    NS = min(48, room // stride if room > 0 else 0)
+    if NS < 2:
+        return True
+    walkers = max(1, _max_warps(act, mr) // S)
+    SW = max(1, min(walkers, -(-R // U)))
+    G = min(max(1, walkers // SW), NS)
+    NS -= NS % G
+    nx = -(-(mr * k * 4) // stride) if fq else 0
+    return nx > NS
 
 
 @pytest.mark.parametrize("qt", sorted(BLOCK))
