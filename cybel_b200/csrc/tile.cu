@@ -200,10 +200,15 @@ __device__ __forceinline__ uint32_t tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
 // Shared memory (bytes): packed slots | activation slots (chunk + B2 tile,
 // 2..6 blocks deep) | per-block A2 (mins) tiles x4 | d/dmin per row x4 |
 // barriers | tensor-memory address.
-constexpr int kNS = 2;              // A block slots in tensor memory
+// A block slots in tensor memory: three where the accumulators leave room
+// (N = 16 with at most two issuers: 96 columns of accumulators), else two.
+// (Measured at N = 16: two issuers and three slots ran slower than four
+// issuers and two slots, so the latter is used.)
+__host__ __device__ constexpr int a_slots(int np) { return (np == 16 && mma_issuers(np) <= 2) ? 3 : 2; }
 constexpr int kNM = 4;              // per-block mins tile / d, dmin buffers (the epilogue releases them)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kABase = 256;    // first tensor-memory column of the A slots
+// First tensor-memory column of the A slots.
+__host__ __device__ constexpr uint32_t a_base(int np) { return a_slots(np) == 3 ? 128u : 256u; }
 constexpr uint32_t kAColsPerChunk = kChunkK / 2;
 
 template <int NP, bool PREC>
@@ -219,12 +224,14 @@ struct TileSmem {
     static constexpr int kA2 = kX + NSX * kXSlot;
     static constexpr int kDD = kA2 + kNM * kA2Bytes;
     static constexpr int kBars = kDD + kNM * kTileRows * 8;
+    static constexpr int kNS = a_slots(NP);
+    static constexpr uint32_t kABase = a_base(NP);
     static constexpr int kNumBars = 2 * kNSW + 2 * kNS + 2 * NSX + 2 * 2 + 2 * kNM;  // see the kernel
     static constexpr int kTmemHolder = kBars + kNumBars * 8;
     static constexpr int kTotal = kTmemHolder + 16;
     static_assert(NSX >= 2 && kTotal <= kSmemLimit, "tile kernel shared memory");
-    static_assert(kDBufs * kBufCols <= static_cast<int>(kABase) &&
-                  kABase + kNS * kAColsPerChunk <= kTmemCols, "tensor memory columns");
+    static_assert(kDBufs * kBufCols <= static_cast<int>(a_base(NP)) &&
+                  a_base(NP) + a_slots(NP) * kAColsPerChunk <= kTmemCols, "tensor memory columns");
 };
 
 // Roles: lane 0 of warps 0..NI-1 issues the MMAs; warp NI lane 0 streams
@@ -254,6 +261,8 @@ __global__ void __launch_bounds__(tile_threads(NP), 1)
     constexpr int NSX = SM::NSX;
     constexpr int kFirstDeqWarp = first_deq_warp(NP);
     constexpr int kRanges = 16 / DW;  // qs quarters per dequant thread
+    constexpr int kNS = SM::kNS;
+    constexpr uint32_t kABase = SM::kABase;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBars);
     uint64_t* wfull = bars;                 // [kNSW] packed block column landed (TMA)
     uint64_t* wempty = wfull + kNSW;        // [kNSW] dequant warps done with it
@@ -402,13 +411,22 @@ __global__ void __launch_bounds__(tile_threads(NP), 1)
             // d, dmin (fp16), 12 scale bytes, 128 nibble bytes.
             const uint32_t blk = smem_addr(smem + SM::kPacked + ws * kPackedBytes + t * kBlockBytes);
             const uint4 hd = lds128(blk);
+            // Both quarters' bytes first, then their fp16 products, then the
+            // tensor-memory stores, so the quarters' load and arithmetic
+            // latencies overlap.
+            uint32_t qw[kRanges][8];
 #pragma unroll
             for (int u = 0; u < kRanges; ++u) {
                 const int h = h0 + u * (DW / 4);
                 const uint4 qa = lds128(blk + 16u + 32u * h);
                 const uint4 qb = lds128(blk + 32u + 32u * h);
-                const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-                uint32_t r[32];
+                qw[u][0] = qa.x; qw[u][1] = qa.y; qw[u][2] = qa.z; qw[u][3] = qa.w;
+                qw[u][4] = qb.x; qw[u][5] = qb.y; qw[u][6] = qb.z; qw[u][7] = qb.w;
+            }
+            uint32_t r[kRanges][32];
+#pragma unroll
+            for (int u = 0; u < kRanges; ++u) {
+                const int h = h0 + u * (DW / 4);
                 __half2 sc2[2], off2[2];
 #pragma unroll
                 for (int half = 0; half < 2; ++half) {  // sub-block j = 2h + half
@@ -423,13 +441,17 @@ __global__ void __launch_bounds__(tile_threads(NP), 1)
                 for (int w8 = 0; w8 < 8; ++w8) {  // bytes 4 w8 .. 4 w8 + 3: elements e0..e3 of both sub-blocks
                     // Column pairs hold elements (e0, e2) and (e1, e3); the
                     // activation chunks use the same order.
-                    const uint32_t w = qw[w8], w_8 = qw[w8] >> 8;
-                    r[2 * w8] = nib_times((w & 0x000F000Fu) | 0x64006400u, sc2[0], off2[0]);
-                    r[2 * w8 + 1] = nib_times((w_8 & 0x000F000Fu) | 0x64006400u, sc2[0], off2[0]);
-                    r[16 + 2 * w8] = nib_times((w & 0x00F000F0u) | 0x64006400u, sc2[1], off2[1]);
-                    r[16 + 2 * w8 + 1] = nib_times((w_8 & 0x00F000F0u) | 0x64006400u, sc2[1], off2[1]);
+                    const uint32_t w = qw[u][w8], w_8 = qw[u][w8] >> 8;
+                    r[u][2 * w8] = nib_times((w & 0x000F000Fu) | 0x64006400u, sc2[0], off2[0]);
+                    r[u][2 * w8 + 1] = nib_times((w_8 & 0x000F000Fu) | 0x64006400u, sc2[0], off2[0]);
+                    r[u][16 + 2 * w8] = nib_times((w & 0x00F000F0u) | 0x64006400u, sc2[1], off2[1]);
+                    r[u][16 + 2 * w8 + 1] = nib_times((w_8 & 0x00F000F0u) | 0x64006400u, sc2[1], off2[1]);
                 }
-                tmem_st32(tmem_base + lane_addr + kABase + static_cast<uint32_t>(s) * kAColsPerChunk + 32u * h, r);
+            }
+#pragma unroll
+            for (int u = 0; u < kRanges; ++u) {
+                const int h = h0 + u * (DW / 4);
+                tmem_st32(tmem_base + lane_addr + kABase + static_cast<uint32_t>(s) * kAColsPerChunk + 32u * h, r[u]);
             }
             if (mins_group) {
                 // The block's mins tile A2 (row t: mn_0..7, twice, as fp16)
