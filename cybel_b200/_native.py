@@ -29,6 +29,7 @@ STATUS = {
     -8: "no usable sm_100 device",
     -9: "scratch must grow during stream capture",
     -10: "request larger than the fixed no-alloc scratch",
+    -11: "page table entry names no page or one outside the pool",
 }
 
 # Every symbol include/b200q.h declares: (name, argtypes, restype).
@@ -74,6 +75,8 @@ SIGNATURES.update(
         "b200q_add_rmsnorm_q": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, ctypes.c_float, _vp], _i),
         "b200q_attention_decode_q": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp], _i),
         "b200q_rope_attention_decode": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, _i, _vp, _vp, _i, _vp], _i),
+        "b200q_rope_attention_decode_paged": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _vp, _vp, _vp, _vp, _i, _i,
+                                               _vp, _i, _vp, _vp, _i, _vp], _i),
         "b200q_swiglu_q": ([_vp, _vp, _vp, _i, _i, _vp], _i),
         "b200q_matmul_xq": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _i, _vp], _i),
         "b200q_matmul_norm": ([_i, _i, _vp, _vp, _f, _vp, _vp, _i, _i, _f, _f, _i, _vp], _i),
@@ -133,14 +136,19 @@ def check(status: int, what: str) -> None:
 
 
 STATUS_TIMEOUT = 1  # device status bit: a kernel's bounded wait gave up
+STATUS_BAD_PAGE = 2  # device status bit: a paged cache's table named no page or one outside the pool
+KV_F16, KV_Q8 = 0, 1  # paged KV storage modes
 
 
 def check_device(device: int, what: str = "device status") -> None:
     """Raise NativeError(B200Q_ETIMEOUT) if a kernel on `device` recorded a
-    wait that gave up since the last check (call after synchronizing the
+    wait that gave up since the last check, NativeError(B200Q_EPAGE) if a
+    paged attention met a bad page-table entry (call after synchronizing the
     stream the work ran on); the status is cleared by the read."""
     v = int(lib().b200q_device_status(int(device)))
     if v < 0:
         raise NativeError(v, what)
     if v & STATUS_TIMEOUT:
         raise NativeError(-7, what)
+    if v & STATUS_BAD_PAGE:
+        raise NativeError(-11, what)

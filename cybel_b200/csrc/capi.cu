@@ -492,6 +492,21 @@ int b200q_rope_attention_decode(const float* q, const float* k, const float* v, 
     return rc;
 }
 
+int b200q_rope_attention_decode_paged(const float* q, const float* k, const float* v, int batch, int n_heads,
+                                      int n_kv_heads, int head_dim, int pos, float theta, int kv_mode, void* k_pages,
+                                      void* v_pages, float* k_scales, float* v_scales, int n_slots, int page_size,
+                                      const int* page_table, int pages_per_seq, float* out, void* xq, int act_mode,
+                                      void* stream) {
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    if (rc == B200Q_OK)
+        rc = launch_rope_attention_paged(q, k, v, batch, n_heads, n_kv_heads, head_dim, pos, theta, kv_mode, k_pages,
+                                         v_pages, k_scales, v_scales, n_slots, page_size, page_table, pages_per_seq,
+                                         out, xq, act_mode, dev, static_cast<cudaStream_t>(stream));
+    set_last_error(rc);
+    return rc;
+}
+
 int b200q_swiglu_q(const float* gate, const float* up, void* xq, int act_mode, int n, void* stream) {
     int rc = B200Q_OK;
     if (!gate || !up || !xq || n <= 0 || (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16)) rc = B200Q_EINVAL;
@@ -924,6 +939,7 @@ const char* b200q_status_string(int status) {
         case B200Q_ENODEV: return "no usable sm_100 device";
         case B200Q_ECAPTURE: return "scratch must grow during stream capture";
         case B200Q_ESCRATCH: return "request larger than the fixed no-alloc scratch";
+        case B200Q_EPAGE: return "page table entry names no page or one outside the pool";
         default: return "unknown status";
     }
 }

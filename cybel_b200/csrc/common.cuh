@@ -19,6 +19,7 @@ constexpr int QT_Q6_K_LM = 214;
 
 // Device status word bits (set by kernels, read by the host).
 constexpr int STATUS_TIMEOUT = 1;   // a bounded wait gave up
+constexpr int STATUS_BAD_PAGE = 2;  // a page table named no page (or one past the pool) for a needed row
 
 // Longest a kernel waits on one pipeline barrier before it records
 // STATUS_TIMEOUT and stops consuming (ns of %globaltimer).

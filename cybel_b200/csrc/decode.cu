@@ -22,6 +22,8 @@
 
 #include <algorithm>
 
+#include <type_traits>
+
 #include "gemv.cuh"
 #include "internal.h"
 
@@ -403,6 +405,94 @@ __global__ void __launch_bounds__(kHeadDim) b200q_attn_combine_kernel(const floa
     }
 }
 
+// Where a sequence's cached keys and values live (template KVM):
+//  * KV_CONTIG: fp16 [seq][kv_head][max_ctx][head_dim] (one contiguous cache);
+//  * KV_PAGED: fp16 pages of `page` positions, [slot][kv_head][page][head_dim],
+//    the slot of each of a sequence's pages taken from its page table
+//    (model_graph.cpp:1413-1449 keeps pages of 4096 tokens per layer);
+//  * KV_PAGED_Q8: the same pages holding int8 codes plus one fp32 scale per
+//    (slot, kv head, position): the reference's q8 KV mode
+//    (model_graph.cpp:507-513, 1539-1576): scale = amax / 127 (1 / 127 for an
+//    all-zero row), code = clamp(round(x * (1 / scale)), -127, 127).
+constexpr int KV_CONTIG = 0, KV_PAGED = 1, KV_PAGED_Q8 = 2;
+
+struct KvArgs {
+    void* k;              // cache or page pool (fp16, or int8 codes for Q8)
+    void* v;
+    float* ks;            // Q8: scale pools [slot][kv_head][page]
+    float* vs;
+    const int* table;     // paged: [seq][pages_per_seq] slot of each page, -1 = none
+    int pages_per_seq;
+    int page;             // positions per page
+    int n_slots;          // pages in the pool
+    int max_ctx;          // contiguous: positions per sequence
+    volatile int* status; // STATUS_BAD_PAGE is recorded here
+};
+
+// Element offset of (sequence b, kv head h, position p) in the caches (the
+// offset / kHeadDim indexes the Q8 scales), or -1 where the page table names
+// no page: the reference scores such a position -1e9 and skips its value
+// (model_graph.cpp:1790-1795, 1896-1897); a slot past the pool is treated
+// the same and recorded as STATUS_BAD_PAGE.
+template <int KVM>
+__device__ __forceinline__ long long kv_row(const KvArgs& a, int b, int h, int n_kv, int p) {
+    if constexpr (KVM == KV_CONTIG) {
+        return ((static_cast<long long>(b) * n_kv + h) * a.max_ctx + p) * kHeadDim;
+    } else {
+        const int slot = __ldg(a.table + static_cast<long long>(b) * a.pages_per_seq + p / a.page);
+        if (slot < 0 || slot >= a.n_slots) {
+            if (slot >= a.n_slots) *a.status = STATUS_BAD_PAGE;
+            return -1;
+        }
+        return ((static_cast<long long>(slot) * n_kv + h) * a.page + (p % a.page)) * kHeadDim;
+    }
+}
+
+constexpr float kMaskedScore = -1e9f;  // the reference's score for a position without a page
+
+// One lane's four cached elements of a row (raw) and their values.
+template <int KVM>
+struct KvLane {
+    using Raw = typename std::conditional<KVM == KV_PAGED_Q8, uint32_t, uint2>::type;
+    __device__ static Raw load(const void* base, long long row, int lane) {
+        if constexpr (KVM == KV_PAGED_Q8)
+            return *reinterpret_cast<const uint32_t*>(static_cast<const int8_t*>(base) + row + 4 * lane);
+        else
+            return *reinterpret_cast<const uint2*>(static_cast<const __half*>(base) + row + 4 * lane);
+    }
+    // fp16: the values; Q8: the codes (the scale is applied by the caller,
+    // to the dot product for keys and to the softmax weight for values, as
+    // model_graph.cpp:1790-1812 and 1894-1915 do).
+    __device__ static float4 value(Raw r) {
+        if constexpr (KVM == KV_PAGED_Q8) {
+            return make_float4(static_cast<float>(static_cast<int8_t>(r & 0xFFu)),
+                               static_cast<float>(static_cast<int8_t>((r >> 8) & 0xFFu)),
+                               static_cast<float>(static_cast<int8_t>((r >> 16) & 0xFFu)),
+                               static_cast<float>(static_cast<int8_t>(r >> 24)));
+        } else {
+            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+            return make_float4(a.x, a.y, b.x, b.y);
+        }
+    }
+};
+
+// Q8 codes of four values of a 128-element row held by the 32 lanes of a
+// warp (lane l: elements 4l .. 4l+3), and the row's scale (lane 0 stores it).
+__device__ __forceinline__ void q8_row_store(float4 x, int8_t* dst, float* scale_dst, int lane) {
+    float amax = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : __fdiv_rn(1.0f, 127.0f);
+    const float inv = __fdiv_rn(1.0f, scale);
+    auto code = [&](float e) {
+        const int c = static_cast<int>(roundf(__fmul_rn(e, inv)));
+        return static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(max(-127, min(127, c)))));
+    };
+    *reinterpret_cast<uint32_t*>(dst + 4 * lane) = code(x.x) | (code(x.y) << 8) | (code(x.z) << 16) | (code(x.w) << 24);
+    if (lane == 0) *scale_dst = scale;
+}
+
 // Fused decode attention for one query token per sequence (the RoPE and
 // attention stages of the reference's decode graph, model_graph.cpp:
 // 1222-1323 and the GQA attention after it, in one launch):
@@ -410,19 +500,23 @@ __global__ void __launch_bounds__(kHeadDim) b200q_attn_combine_kernel(const floa
 //    (pos * theta^(-2p / head_dim), interleaved pairs), scaled by
 //    1 / sqrt(head_dim);
 //  * the CTA whose chunk holds `pos` rotates the new key and appends it and
-//    the new value to the fp16 caches before reading its chunk;
+//    the new value to the caches (fp16, or Q8 codes and scales) before
+//    reading its chunk;
 //  * each CTA scores and weights its kAttnChunk positions like
 //    b200q_attn_chunk_kernel and writes its partial records;
 //  * the CTA that finishes last for a (kv head, sequence) -- an arrival
 //    counter, reset by that CTA -- merges the chunks (max rescaling) and
 //    writes the output rows and, with DIG > 0, their x8 / x16 codes. No CTA
 //    waits for another (threadfence-reduction pattern).
-template <int G, int DIG>
+template <int G, int DIG, int KVM>
 __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
-    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, __half* __restrict__ kc,
-    __half* __restrict__ vc, float* __restrict__ part, int* __restrict__ counters, float* __restrict__ out,
-    uint8_t* __restrict__ xq, int n_heads, int n_kv, int pos, int max_ctx, float log2_theta, float scale) {
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, const KvArgs kv,
+    float* __restrict__ part, int* __restrict__ counters, float* __restrict__ out, uint8_t* __restrict__ xq,
+    int n_heads, int n_kv, int pos, float log2_theta, float scale) {
     griddep_launch_dependents();
+    using KL = KvLane<KVM>;
+    using Raw = typename KL::Raw;
+    constexpr bool Q8 = KVM == KV_PAGED_Q8;
     constexpr int PW = kAttnChunk / kAttnWarps;  // positions per warp
     constexpr int HALF = kHeadDim / 2;
     // 16-byte aligned: qs and red are accessed as float4.
@@ -437,22 +531,32 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
     q += (static_cast<long long>(b) * n_heads + kvh * G) * kHeadDim;
     k += (static_cast<long long>(b) * n_kv + kvh) * kHeadDim;
     v += (static_cast<long long>(b) * n_kv + kvh) * kHeadDim;
-    kc += (static_cast<long long>(b) * n_kv + kvh) * max_ctx * kHeadDim;
-    vc += (static_cast<long long>(b) * n_kv + kvh) * max_ctx * kHeadDim;
     part += (static_cast<long long>(b) * n_heads + kvh * G) * n_chunks * kPartStride;  // records [g][chunk]
     const int p0 = c * kAttnChunk;
     const int np = min(kAttnChunk, ctx - p0);
     // The cached rows before pos were written by earlier steps: load this
     // warp's K and V rows before waiting for the preceding kernel (the
     // projection that produces q, k, v), so the loads overlap its tail.
-    uint2 kr[PW], vr[PW];
+    Raw kr[PW], vr[PW];
+    float ksc[PW], vsc[PW];
+    uint32_t live = 0;  // bit j: this warp's position j has a cached row
 #pragma unroll
     for (int j = 0; j < PW; ++j) {
         const int p = warp + j * kAttnWarps;
         const bool cached = p < np && p0 + p != pos;
-        const long long off = static_cast<long long>(p0 + p) * kHeadDim + 4 * lane;
-        kr[j] = cached ? *reinterpret_cast<const uint2*>(kc + off) : make_uint2(0u, 0u);
-        vr[j] = cached ? *reinterpret_cast<const uint2*>(vc + off) : make_uint2(0u, 0u);
+        kr[j] = Raw{};
+        vr[j] = Raw{};
+        ksc[j] = vsc[j] = 0.0f;
+        const long long row = cached ? kv_row<KVM>(kv, b, kvh, n_kv, p0 + p) : -1;
+        if (row >= 0) {
+            live |= 1u << j;
+            kr[j] = KL::load(kv.k, row, lane);
+            vr[j] = KL::load(kv.v, row, lane);
+            if constexpr (Q8) {
+                ksc[j] = kv.ks[row / kHeadDim];
+                vsc[j] = kv.vs[row / kHeadDim];
+            }
+        }
     }
     griddep_wait();
     for (int i = threadIdx.x; i < G * HALF; i += blockDim.x) {
@@ -466,40 +570,79 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
         qs[g][2 * p + 1] = r1 * scale;
     }
     const bool holds_pos = c == n_chunks - 1;
-    if (holds_pos) {  // this chunk holds pos: append the rotated key and the value
-        for (int i = threadIdx.x; i < HALF + kHeadDim; i += blockDim.x) {
-            if (i < HALF) {
-                const float inv_freq =
-                    exp2f(-2.0f * static_cast<float>(i) / static_cast<float>(kHeadDim) * log2_theta);
-                float s, co;
-                sincosf(static_cast<float>(pos) * inv_freq, &s, &co);
-                const float x0 = k[2 * i], x1 = k[2 * i + 1];
-                *reinterpret_cast<__half2*>(kc + static_cast<long long>(pos) * kHeadDim + 2 * i) =
-                    __floats2half2_rn(x0 * co - x1 * s, x0 * s + x1 * co);
-            } else {
-                vc[static_cast<long long>(pos) * kHeadDim + (i - HALF)] = __float2half_rn(v[i - HALF]);
+    const long long prow = holds_pos ? kv_row<KVM>(kv, b, kvh, n_kv, pos) : -1;  // the appended row
+    if (holds_pos && prow < 0 && threadIdx.x == 0) *kv.status = STATUS_BAD_PAGE;  // no page to append to
+    if (prow >= 0) {  // this chunk holds pos: append the rotated key and the value
+        if constexpr (Q8) {
+            // warp 0: the rotated key; warp 1: the value (lane l: elements 4l .. 4l+3)
+            if (warp < 2) {
+                float4 x;
+                if (warp == 0) {
+                    float e[4];
+#pragma unroll
+                    for (int t = 0; t < 2; ++t) {
+                        const int i = 2 * lane + t;  // pair i: elements 2i, 2i+1
+                        const float inv_freq =
+                            exp2f(-2.0f * static_cast<float>(i) / static_cast<float>(kHeadDim) * log2_theta);
+                        float sn, co;
+                        sincosf(static_cast<float>(pos) * inv_freq, &sn, &co);
+                        const float x0 = k[2 * i], x1 = k[2 * i + 1];
+                        e[2 * t] = x0 * co - x1 * sn;
+                        e[2 * t + 1] = x0 * sn + x1 * co;
+                    }
+                    x = make_float4(e[0], e[1], e[2], e[3]);
+                    q8_row_store(x, static_cast<int8_t*>(kv.k) + prow, kv.ks + prow / kHeadDim, lane);
+                } else {
+                    x = *reinterpret_cast<const float4*>(v + 4 * lane);
+                    q8_row_store(x, static_cast<int8_t*>(kv.v) + prow, kv.vs + prow / kHeadDim, lane);
+                }
+            }
+        } else {
+            __half* kc = static_cast<__half*>(kv.k);
+            __half* vc = static_cast<__half*>(kv.v);
+            for (int i = threadIdx.x; i < HALF + kHeadDim; i += blockDim.x) {
+                if (i < HALF) {
+                    const float inv_freq =
+                        exp2f(-2.0f * static_cast<float>(i) / static_cast<float>(kHeadDim) * log2_theta);
+                    float s, co;
+                    sincosf(static_cast<float>(pos) * inv_freq, &s, &co);
+                    const float x0 = k[2 * i], x1 = k[2 * i + 1];
+                    *reinterpret_cast<__half2*>(kc + prow + 2 * i) =
+                        __floats2half2_rn(x0 * co - x1 * s, x0 * s + x1 * co);
+                } else {
+                    vc[prow + (i - HALF)] = __float2half_rn(v[i - HALF]);
+                }
             }
         }
     }
     __syncthreads();  // the appended row and the rotated queries are visible to the CTA
-    const long long pos_off = static_cast<long long>(pos) * kHeadDim + 4 * lane;  // the appended row
     {
 #pragma unroll
         for (int j = 0; j < PW; ++j) {
             const int p = warp + j * kAttnWarps;
-            const uint2 kk = p0 + p == pos ? *reinterpret_cast<const uint2*>(kc + pos_off) : kr[j];
-            const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&kk.x));
-            const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&kk.y));
+            const bool appended = p0 + p == pos;
+            const bool ok = appended ? prow >= 0 : ((live >> j) & 1u) != 0;
+            const Raw kk = appended && ok ? KL::load(kv.k, prow, lane) : kr[j];
+            const float4 kf = KL::value(kk);
             float d[G];
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 const float4 qg = *reinterpret_cast<const float4*>(&qs[g][4 * lane]);
-                d[g] = qg.x * k01.x + qg.y * k01.y + qg.z * k23.x + qg.w * k23.y;
+                d[g] = qg.x * kf.x + qg.y * kf.y + qg.z * kf.z + qg.w * kf.w;
             }
 #pragma unroll
             for (int o = 16; o; o >>= 1) {
 #pragma unroll
                 for (int g = 0; g < G; ++g) d[g] += __shfl_xor_sync(0xffffffffu, d[g], o);
+            }
+            if constexpr (Q8) {
+                const float ks = appended && ok ? kv.ks[prow / kHeadDim] : ksc[j];
+#pragma unroll
+                for (int g = 0; g < G; ++g) d[g] *= ks;
+            }
+            if (!ok) {
+#pragma unroll
+                for (int g = 0; g < G; ++g) d[g] = kMaskedScore;
             }
             if (p < np) {
 #pragma unroll
@@ -535,16 +678,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
 #pragma unroll
         for (int j = 0; j < PW; ++j) {
             const int p = warp + j * kAttnWarps;
-            const uint2 vv = p0 + p == pos ? *reinterpret_cast<const uint2*>(vc + pos_off) : vr[j];
-            const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vv.x));
-            const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vv.y));
+            const bool appended = p0 + p == pos;
+            const bool ok = appended ? prow >= 0 : ((live >> j) & 1u) != 0;
+            const Raw vv = appended && ok ? KL::load(kv.v, prow, lane) : vr[j];  // zero without a row
+            float vsv = 1.0f;
+            if constexpr (Q8) vsv = appended && ok ? kv.vs[prow / kHeadDim] : vsc[j];
+            const float4 vf = KL::value(vv);
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-                const float e = p < np ? sc[g][p] : 0.0f;
-                acc[g][0] = fmaf(e, v01.x, acc[g][0]);
-                acc[g][1] = fmaf(e, v01.y, acc[g][1]);
-                acc[g][2] = fmaf(e, v23.x, acc[g][2]);
-                acc[g][3] = fmaf(e, v23.y, acc[g][3]);
+                float e = p < np ? sc[g][p] : 0.0f;
+                if constexpr (Q8) e *= vsv;
+                acc[g][0] = fmaf(e, vf.x, acc[g][0]);
+                acc[g][1] = fmaf(e, vf.y, acc[g][1]);
+                acc[g][2] = fmaf(e, vf.z, acc[g][2]);
+                acc[g][3] = fmaf(e, vf.w, acc[g][3]);
             }
         }
     }
@@ -729,19 +876,19 @@ int launch_attention(const float* q, const void* kc, const void* vc, float* out,
     return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
 }
 
-int launch_rope_attention(const float* q, const float* k, const float* v, int batch, int n_heads, int n_kv, int hd,
-                          int pos, float theta, void* kc, void* vc, int max_ctx, float* out, void* xq, int act_mode,
-                          Device* dev, cudaStream_t st) {
-    if (!q || !k || !v || !kc || !vc || (!out && !xq) || batch <= 0 || n_heads <= 0 || n_kv <= 0 || max_ctx <= 0 ||
-        !dev)
-        return B200Q_EINVAL;
+namespace {
+
+// Shared by the contiguous and paged entry points: checks the head shapes and
+// outputs, takes the scratch, and launches b200q_attn_decode_kernel<G, DIG, KVM>.
+int launch_attention(int kvm, const KvArgs& kv, const float* q, const float* k, const float* v, int batch,
+                     int n_heads, int n_kv, int hd, int pos, float theta, float* out, void* xq, int act_mode,
+                     Device* dev, cudaStream_t st) {
+    if (!q || !k || !v || (!out && !xq) || batch <= 0 || n_heads <= 0 || n_kv <= 0 || !dev) return B200Q_EINVAL;
     if (xq && act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
-    if (hd != kHeadDim || n_heads % n_kv || pos < 0 || pos >= max_ctx || !(theta > 0.0f)) return B200Q_ESHAPE;
+    if (hd != kHeadDim || n_heads % n_kv || pos < 0 || !(theta > 0.0f)) return B200Q_ESHAPE;
     const int G = n_heads / n_kv;
     if (G != 1 && G != 2 && G != 4 && G != 8) return B200Q_ESHAPE;
-    if ((reinterpret_cast<uintptr_t>(kc) & 7u) || (reinterpret_cast<uintptr_t>(vc) & 7u) || (out && !aligned16(out)) ||
-        (xq && !aligned16(xq)))
-        return B200Q_EALIGN;
+    if ((out && !aligned16(out)) || (xq && !aligned16(xq))) return B200Q_EALIGN;
     const int n_chunks = pos / kAttnChunk + 1;
     void* part = nullptr;
     void* cnt = nullptr;
@@ -753,27 +900,76 @@ int launch_rope_attention(const float* q, const float* k, const float* v, int ba
     if (rc == B200Q_OK)
         rc = scratch_for(dev, st, kScratchAttnCnt, static_cast<size_t>(batch) * n_kv * sizeof(int), &cnt, true);
     if (rc != B200Q_OK) return rc;
+    KvArgs a = kv;
+    a.status = dev->status;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(n_kv, n_chunks, batch), dim3(kAttnWarps * 32), st, attr);
     const int dig = !xq ? 0 : (act_mode == B200Q_ACT_X8 ? 1 : 2);
     auto go = [&](auto kern) {
-        return cudaLaunchKernelEx(&cfg, kern, q, k, v, static_cast<__half*>(kc), static_cast<__half*>(vc),
-                                  static_cast<float*>(part), static_cast<int*>(cnt), out, static_cast<uint8_t*>(xq),
-                                  n_heads, n_kv, pos, max_ctx, log2f(theta), 1.0f / sqrtf(static_cast<float>(hd)));
+        return cudaLaunchKernelEx(&cfg, kern, q, k, v, a, static_cast<float*>(part), static_cast<int*>(cnt), out,
+                                  static_cast<uint8_t*>(xq), n_heads, n_kv, pos, log2f(theta),
+                                  1.0f / sqrtf(static_cast<float>(hd)));
     };
     cudaError_t e = cudaErrorInvalidValue;
-#define B200Q_ATTN_CASE(GG)                                                   \
-    if (G == GG) {                                                             \
-        if (dig == 0) e = go(b200q_attn_decode_kernel<GG, 0>);                       \
-        else if (dig == 1) e = go(b200q_attn_decode_kernel<GG, 1>);                  \
-        else e = go(b200q_attn_decode_kernel<GG, 2>);                                \
+#define B200Q_ATTN_KVM(GG, DD)                                                          \
+    if (kvm == KV_CONTIG) e = go(b200q_attn_decode_kernel<GG, DD, KV_CONTIG>);            \
+    else if (kvm == KV_PAGED) e = go(b200q_attn_decode_kernel<GG, DD, KV_PAGED>);         \
+    else e = go(b200q_attn_decode_kernel<GG, DD, KV_PAGED_Q8>);
+#define B200Q_ATTN_CASE(GG)                  \
+    if (G == GG) {                           \
+        if (dig == 0) { B200Q_ATTN_KVM(GG, 0) } \
+        else if (dig == 1) { B200Q_ATTN_KVM(GG, 1) } \
+        else { B200Q_ATTN_KVM(GG, 2) }          \
     }
     B200Q_ATTN_CASE(1)
     B200Q_ATTN_CASE(2)
     B200Q_ATTN_CASE(4)
     B200Q_ATTN_CASE(8)
 #undef B200Q_ATTN_CASE
+#undef B200Q_ATTN_KVM
     return e == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
+}
+
+}  // namespace
+
+int launch_rope_attention(const float* q, const float* k, const float* v, int batch, int n_heads, int n_kv, int hd,
+                          int pos, float theta, void* kc, void* vc, int max_ctx, float* out, void* xq, int act_mode,
+                          Device* dev, cudaStream_t st) {
+    if (!kc || !vc || max_ctx <= 0) return B200Q_EINVAL;
+    if (pos >= max_ctx) return B200Q_ESHAPE;
+    if ((reinterpret_cast<uintptr_t>(kc) & 7u) || (reinterpret_cast<uintptr_t>(vc) & 7u)) return B200Q_EALIGN;
+    KvArgs kv{};
+    kv.k = kc;
+    kv.v = vc;
+    kv.max_ctx = max_ctx;
+    return launch_attention(KV_CONTIG, kv, q, k, v, batch, n_heads, n_kv, hd, pos, theta, out, xq, act_mode, dev, st);
+}
+
+int launch_rope_attention_paged(const float* q, const float* k, const float* v, int batch, int n_heads, int n_kv,
+                                int hd, int pos, float theta, int kv_mode, void* k_pages, void* v_pages,
+                                float* k_scales, float* v_scales, int n_slots, int page_size, const int* page_table,
+                                int pages_per_seq, float* out, void* xq, int act_mode, Device* dev, cudaStream_t st) {
+    const bool q8 = kv_mode == B200Q_KV_Q8;
+    if ((kv_mode != B200Q_KV_F16 && !q8) || !k_pages || !v_pages || !page_table || n_slots <= 0 || page_size <= 0 ||
+        pages_per_seq <= 0 || (q8 && (!k_scales || !v_scales)))
+        return B200Q_EINVAL;
+    if (static_cast<long long>(pos) >= static_cast<long long>(pages_per_seq) * page_size) return B200Q_ESHAPE;
+    const uintptr_t row_align = q8 ? 3u : 7u;  // int8 rows read 4 bytes a lane, fp16 rows 8
+    if ((reinterpret_cast<uintptr_t>(k_pages) & row_align) || (reinterpret_cast<uintptr_t>(v_pages) & row_align) ||
+        (reinterpret_cast<uintptr_t>(page_table) & 3u) ||
+        (q8 && ((reinterpret_cast<uintptr_t>(k_scales) & 3u) || (reinterpret_cast<uintptr_t>(v_scales) & 3u))))
+        return B200Q_EALIGN;
+    KvArgs kv{};
+    kv.k = k_pages;
+    kv.v = v_pages;
+    kv.ks = k_scales;
+    kv.vs = v_scales;
+    kv.table = page_table;
+    kv.pages_per_seq = pages_per_seq;
+    kv.page = page_size;
+    kv.n_slots = n_slots;
+    return launch_attention(q8 ? KV_PAGED_Q8 : KV_PAGED, kv, q, k, v, batch, n_heads, n_kv, hd, pos, theta, out, xq,
+                            act_mode, dev, st);
 }
 
 int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaStream_t st) {

@@ -19,7 +19,8 @@ runs that step entirely on the device through libb200q's entry points:
   codes;
 
 all on one stream, so one token's step is one CUDA graph. The KV cache is
-fp16, [layer][kv_head][max_ctx][head_dim].
+fp16, [layer][kv_head][max_ctx][head_dim], or the reference's paged store
+(kv_cache.PagedKVCache: fp16 or Q8 pages, ``b200q_rope_attention_decode_paged``).
 """
 
 from __future__ import annotations
@@ -138,9 +139,29 @@ class DecodeStack:
 
     def __init__(self, shape: StackShape, max_ctx: int, layers: list[dict[str, np.ndarray]], embed: np.ndarray,
                  head: np.ndarray, out_norm: np.ndarray, act_mode: int = _native.ACT_X16, device: int = 0,
-                 fused_norm: bool = True):
+                 fused_norm: bool = True, repack: "RepackPolicy | None" = None, architecture: str = "llama",
+                 kv: str | None = None, page_size: int | None = None):
+        """``repack`` picks each weight's decode layout as the reference does
+        when it registers a graph's weights (repack_policy.RepackPolicy; by
+        default from the ANVIL_* environment switches for `architecture`).
+
+        ``kv`` picks the KV cache: "contiguous" (fp16 [layer][kv_head][max_ctx]
+        [head_dim]), "paged" (fp16 pages) or "q8" (the reference's Q8 pages);
+        by default "q8" when ANVIL_KV_QUANT asks for it (kv_cache.q8_from_env),
+        else "contiguous". Pages hold ``page_size`` positions (default
+        kv_cache.KV_PAGE_SIZE)."""
         import torch
 
+        from .kv_cache import KV_PAGE_SIZE, PagedKVCache, q8_from_env
+        from .repack_policy import RepackPolicy, apply
+
+        if kv is None:
+            kv = "q8" if q8_from_env() else "contiguous"
+        if kv not in ("contiguous", "paged", "q8"):
+            raise ValueError(f"unknown KV cache kind {kv!r}")
+        self.kv = kv
+
+        policy = RepackPolicy.from_env(architecture) if repack is None else repack
         if shape.head_dim != 128:
             raise ValueError("the attention kernels are built for head_dim 128")
         if act_mode not in (_native.ACT_X8, _native.ACT_X16):
@@ -159,10 +180,10 @@ class DecodeStack:
             if i < len(layers):
                 src = layers[i]
                 lay = _Layer(
-                    DeviceMatrix(q, h, h + 2 * kv, np.concatenate([src["wq"], src["wk"], src["wv"]])),
-                    DeviceMatrix(q, h, h, src["wo"]),
-                    DeviceMatrix(q, h, 2 * f, np.concatenate([src["w_gate"], src["w_up"]])),
-                    DeviceMatrix(q, f, h, src["w_down"]),
+                    apply(policy, DeviceMatrix(q, h, h + 2 * kv, np.concatenate([src["wq"], src["wk"], src["wv"]]))),
+                    apply(policy, DeviceMatrix(q, h, h, src["wo"])),
+                    apply(policy, DeviceMatrix(q, h, 2 * f, np.concatenate([src["w_gate"], src["w_up"]]))),
+                    apply(policy, DeviceMatrix(q, f, h, src["w_down"])),
                     torch.from_numpy(src["attn_norm"]).to(self.dev),
                     torch.from_numpy(src["ffn_norm"]).to(self.dev))
                 first.append(lay)
@@ -171,11 +192,17 @@ class DecodeStack:
                 lay = _Layer(b.wqkv.clone(), b.wo.clone(), b.w_gu.clone(), b.w_down.clone(), b.attn_norm, b.ffn_norm)
             self.layers.append(lay)
         self.embed = DeviceMatrix(shape.embedding_qtype, h, shape.vocab, embed)
-        self.head = DeviceMatrix(shape.head_qtype, h, shape.vocab, head)
+        self.head = apply(policy, DeviceMatrix(shape.head_qtype, h, shape.vocab, head), lm_head=True)
         self.out_norm = torch.from_numpy(out_norm).to(self.dev)
-        cache_shape = (shape.layers, shape.kv_heads, max_ctx, shape.head_dim)
-        self.k_cache = torch.zeros(cache_shape, dtype=torch.float16, device=self.dev)
-        self.v_cache = torch.zeros(cache_shape, dtype=torch.float16, device=self.dev)
+        if self.kv == "contiguous":
+            cache_shape = (shape.layers, shape.kv_heads, max_ctx, shape.head_dim)
+            self.k_cache = torch.zeros(cache_shape, dtype=torch.float16, device=self.dev)
+            self.v_cache = torch.zeros(cache_shape, dtype=torch.float16, device=self.dev)
+            self.kv_cache = None
+        else:
+            self.k_cache = self.v_cache = None
+            self.kv_cache = PagedKVCache(shape.layers, shape.kv_heads, max_ctx, batch=1,
+                                         page_size=page_size or KV_PAGE_SIZE, q8=self.kv == "q8", device=device)
         self.x = torch.zeros(h, **f32)             # residual stream
         self.qkv = torch.zeros(h + 2 * kv, **f32)  # q | k | v
         self.gu = torch.zeros(2 * f, **f32)        # gate | up
@@ -200,9 +227,11 @@ class DecodeStack:
 
         if not 0 <= pos < self.max_ctx:
             raise ValueError("position outside the KV cache")
+        if self.kv_cache is not None and not linears_only:
+            self.kv_cache.ensure(pos)  # the page of pos (a table copy only when it is new)
         s, L, st = self.shape, self.lib, torch.cuda.current_stream(self.dev).cuda_stream
         W = _native.WEIGHTS_STATIC
-        act, q = self.act_mode, s.linear_qtype
+        act = self.act_mode
         h, kv, hd, f = s.hidden, s.kv_dim, s.head_dim, s.ffn
         x, xq_h, xq_f = self.x.data_ptr(), self.xq_h.data_ptr(), self.xq_f.data_ptr()
         qp = self.qkv.data_ptr()
@@ -216,20 +245,25 @@ class DecodeStack:
                         "embedding")
         for li, lay in enumerate(self.layers):
             # RMSNorm inside the q/k/v GEMV (it normalizes and quantizes x while its weights stream)
-            self._norm_matmul(q, x, lay.attn_norm, xq_h, lay.wqkv.ptr, qp, h, h + 2 * kv, "qkv", st, linears_only)
-            if not linears_only:
+            self._norm_matmul(lay.wqkv.qtype, x, lay.attn_norm, xq_h, lay.wqkv.ptr, qp, h, h + 2 * kv, "qkv", st,
+                              linears_only)
+            if not linears_only and self.kv_cache is not None:
+                self.kv_cache.attention(li, qp, kp, vp, pos, s.heads, s.rope_theta, None, xq_h, act, st)
+            elif not linears_only:
                 kc = self.k_cache[li].data_ptr()
                 vc = self.v_cache[li].data_ptr()
                 self._check(L.b200q_rope_attention_decode(qp, kp, vp, 1, s.heads, s.kv_heads, hd, pos,
                                                           s.rope_theta, kc, vc, self.max_ctx, None, xq_h, act, st),
                             "rope_attention")
             # o projection with the residual add in its epilogue: x = Wo a + x
-            self._check(L.b200q_matmul_xq(q, act, xq_h, lay.wo.ptr, x, 1, h, h, 1.0, resid, W, st), "o_proj")
-            self._norm_matmul(q, x, lay.ffn_norm, xq_h, lay.w_gu.ptr, gp, h, 2 * f, "gate_up", st, linears_only)
+            self._check(L.b200q_matmul_xq(lay.wo.qtype, act, xq_h, lay.wo.ptr, x, 1, h, h, 1.0, resid, W, st), "o_proj")
+            self._norm_matmul(lay.w_gu.qtype, x, lay.ffn_norm, xq_h, lay.w_gu.ptr, gp, h, 2 * f, "gate_up", st,
+                              linears_only)
             if not linears_only:
                 self._check(L.b200q_swiglu_q(gp, up, xq_f, act, f, st), "swiglu")
-            self._check(L.b200q_matmul_xq(q, act, xq_f, lay.w_down.ptr, x, 1, f, h, 1.0, resid, W, st), "down")
-        self._norm_matmul(s.head_qtype, x, self.out_norm, xq_h, self.head.ptr, self.logits.data_ptr(), h, s.vocab,
+            self._check(L.b200q_matmul_xq(lay.w_down.qtype, act, xq_f, lay.w_down.ptr, x, 1, f, h, 1.0, resid, W, st),
+                        "down")
+        self._norm_matmul(self.head.qtype, x, self.out_norm, xq_h, self.head.ptr, self.logits.data_ptr(), h, s.vocab,
                           "lm_head", st, linears_only)
 
     def _norm_matmul(self, qt, x, gamma, xq, w, y, k, n, what, st, linears_only) -> None:
@@ -251,13 +285,15 @@ class DecodeStack:
     def from_gguf(cls, path, max_ctx: int, act_mode: int = _native.ACT_X16, device: int = 0,
                   fused_norm: bool = True) -> "DecodeStack":
         """A stack whose weights are the tensors of a llama-architecture GGUF
-        file (gguf_file.load_llama_stack), uploaded with their block layouts
-        unchanged."""
-        from .gguf_file import load_llama_stack
+        file (gguf_file.load_llama_stack), uploaded as the file stores them
+        and then given the decode layouts the repack policy picks for the
+        file's architecture (repack_policy.RepackPolicy.from_env)."""
+        from .gguf_file import GGUFFile, load_llama_stack
 
         shape, layers, embed, head, out_norm = load_llama_stack(path)
+        arch = str(GGUFFile(path).metadata.get("general.architecture", "llama"))
         return cls(shape, max_ctx, layers, embed, head, out_norm, act_mode=act_mode, device=device,
-                   fused_norm=fused_norm)
+                   fused_norm=fused_norm, architecture=arch)
 
     def set_token(self, token: int) -> None:
         self.token.fill_(int(token))

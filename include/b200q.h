@@ -62,6 +62,10 @@ extern "C" {
 #define B200Q_ACT_X16 2
 #define B200Q_ACT_F16 3
 
+/* KV storage of b200q_rope_attention_decode_paged */
+#define B200Q_KV_F16 0         /* fp16 pages */
+#define B200Q_KV_Q8 1          /* int8 pages + one fp32 scale per (position, kv head) */
+
 /* status codes */
 #define B200Q_OK 0
 #define B200Q_EINVAL (-1)      /* null pointer, non-positive size */
@@ -74,6 +78,7 @@ extern "C" {
 #define B200Q_ENODEV (-8)      /* no usable sm_100 device */
 #define B200Q_ECAPTURE (-9)    /* scratch must grow while the stream is being captured */
 #define B200Q_ESCRATCH (-10)   /* request larger than b200q_matvec_noalloc's fixed scratch */
+#define B200Q_EPAGE (-11)      /* a paged cache's table named no page, or one outside its pool */
 
 /* ---------------------------------------------------------------------
  * 1. Drop-in entry points (host pointers), reference signatures.
@@ -286,6 +291,31 @@ B200Q_API int b200q_rope_attention_decode(const float* q, const float* k, const 
                                           int n_kv_heads, int head_dim, int pos, float theta, void* k_cache,
                                           void* v_cache, int max_ctx, float* out, void* xq, int act_mode,
                                           void* stream);
+
+/* The same over a paged KV cache: the reference's PagedKVStore
+ * (model_graph.cpp:1413-1576: pages of page_size positions, allocated per
+ * (layer, page) when a position is first written) and its attention
+ * (fused_gqa_attention_decode_paged, model_graph.cpp:1686-1930). One pool of
+ * n_slots pages per cache: k_pages / v_pages [n_slots][n_kv_heads][page_size]
+ * [head_dim] of fp16 (kv_mode B200Q_KV_F16) or int8 codes (B200Q_KV_Q8, the
+ * reference's ANVIL_KV_QUANT=q8 mode, model_graph.cpp:507-513) with
+ * k_scales / v_scales [n_slots][n_kv_heads][page_size] fp32 (NULL for fp16).
+ * page_table [batch][pages_per_seq] int32 gives the slot of each page of
+ * each sequence, -1 for a page not allocated: a position there scores -1e9
+ * and adds no value, as in the reference. The caller assigns the slot of
+ * pos's page before the call. A Q8 append stores, per kv head,
+ * scale = amax / 127 (1 / 127 for an all-zero row) and
+ * code = clamp(round(x * (1 / scale)), -127, 127); scores are
+ * dot(q, codes) * scale and values enter as softmax weight * scale * codes,
+ * as the reference computes them. A slot outside [0, n_slots) in the table,
+ * or no page at pos, is recorded as device status bit 2 (value 2) and the
+ * position is masked. pos < pages_per_seq * page_size; pools 8-byte (fp16)
+ * or 4-byte (Q8) aligned. */
+B200Q_API int b200q_rope_attention_decode_paged(const float* q, const float* k, const float* v, int batch,
+                                                int n_heads, int n_kv_heads, int head_dim, int pos, float theta,
+                                                int kv_mode, void* k_pages, void* v_pages, float* k_scales,
+                                                float* v_scales, int n_slots, int page_size, const int* page_table,
+                                                int pages_per_seq, float* out, void* xq, int act_mode, void* stream);
 B200Q_API int b200q_swiglu_q(const float* gate, const float* up, void* xq, int act_mode, int n, void* stream);
 
 /* y = alpha * (W x) + beta * y for m activation rows given as codes written
@@ -371,7 +401,10 @@ B200Q_API int b200q_last_error(void);                 /* last status of this hos
 B200Q_API const char* b200q_status_string(int status);
 /* STATUS bits recorded on a device since the last read, cleared on read:
  * bit 1 (value 1) = a kernel's bounded wait gave up (the call's results are
- * incomplete; B200Q_ETIMEOUT in the Python layer). Covers the regular entry
+ * incomplete; B200Q_ETIMEOUT in the Python layer).
+ * bit 2 (value 2) = a paged attention call met a page-table entry outside
+ * its pool, or no page at the appended position (those positions were
+ * masked). Covers the regular entry
  * points and b200q_matvec_noalloc; read it after the work's stream has
  * finished. Allocates nothing. */
 B200Q_API int b200q_device_status(int device);

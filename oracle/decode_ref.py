@@ -9,7 +9,9 @@ kv head h / (heads / kv_heads)), the o projection and residual add, RMSNorm,
 the SwiGLU FFN (silu(gate) * up, down) and residual add, the final norm and
 the LM head. Weights are the reference's fp32 dequantized values
 (orc_dequant_rows); arithmetic is float64, except that cached k and v are
-rounded to fp16 as the device cache stores them.
+rounded to fp16 as the device cache stores them, or (DecodeRef with kv_q8)
+stored as the reference's Q8 KV rows (PagedKVStore::write,
+model_graph.cpp:1545-1573).
 
 Only the tests import this module.
 """
@@ -21,10 +23,23 @@ import numpy as np
 from . import oracle as O
 
 
+def _stored(rows, q8: bool) -> np.ndarray:
+    """KV rows as the cache holds them: fp16 values, or Q8 codes * scale."""
+    if not q8:
+        return rows.astype(np.float16).astype(np.float64)
+    from .paged_kv_ref import q8_rows
+
+    codes, scales = q8_rows(rows.astype(np.float32))
+    return codes.astype(np.float64) * scales[..., None].astype(np.float64)
+
+
 class DecodeRef:
-    def __init__(self, shape, layers, embed, head, out_norm, max_ctx: int):
+    def __init__(self, shape, layers, embed, head, out_norm, max_ctx: int, kv_q8: bool = False):
+        """kv_q8: the cache holds the reference's Q8 rows (codes * scale, the
+        quantizer of oracle/paged_kv_ref.py) instead of fp16 values."""
         self.s = shape
         self.max_ctx = max_ctx
+        self.kv_q8 = kv_q8
         h, kv, f = shape.hidden, shape.kv_dim, shape.ffn
         q = shape.linear_qtype
         dims = {"wq": (h, h), "wk": (kv, h), "wv": (kv, h), "wo": (h, h), "w_gate": (f, h), "w_up": (f, h),
@@ -66,8 +81,8 @@ class DecodeRef:
             q = self._rope(L["wq"] @ hn, s.heads, pos)
             k = self._rope(L["wk"] @ hn, s.kv_heads, pos)
             v = (L["wv"] @ hn).reshape(s.kv_heads, hd)
-            self.kc[li, :, pos] = k.astype(np.float16).astype(np.float64)
-            self.vc[li, :, pos] = v.astype(np.float16).astype(np.float64)
+            self.kc[li, :, pos] = _stored(k, self.kv_q8)
+            self.vc[li, :, pos] = _stored(v, self.kv_q8)
             att = np.zeros((s.heads, hd))
             for hh in range(s.heads):
                 kvh = hh // G

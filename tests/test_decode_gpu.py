@@ -120,11 +120,22 @@ def test_attention_decode(H, KV, ctx):
     assert _rel(out.cpu().numpy().reshape(H, hd), ref) <= 1e-4
 
 
+LAYOUTS = {
+    "canonical": {"ANVIL_LM_HEAD_PACKED": "0"},
+    "default": {},  # the reference's defaults for llama: the Q6_K head as Q6_K_R4
+    "r4_lm": {"ANVIL_Q4K_R4": "1", "ANVIL_LM_HEAD_Q6K_LM": "1"},  # Q4_K_R4 linears, Q6_K_LM head
+}
+
+
 @pytest.mark.gpu
+@pytest.mark.parametrize("layout", sorted(LAYOUTS))
 @pytest.mark.parametrize("fused_norm", [True, False])
-def test_decode_stack_matches_restatement(fused_norm):
+def test_decode_stack_matches_restatement(fused_norm, layout):
+    """Logits of 12 tokens against the float64 restatement, with the weights
+    in each decode layout the registration policy can pick."""
     from cybel_b200.decode import DecodeStack, StackShape, random_layer, random_rows
-    from cybel_b200.formats import Q4_K, Q6_K
+    from cybel_b200.formats import Q4_K, Q4_K_R4, Q6_K, Q6_K_LM, Q6_K_R4
+    from cybel_b200.repack_policy import RepackPolicy
     from oracle.decode_ref import DecodeRef
 
     shape = StackShape(layers=2, hidden=512, heads=4, kv_heads=2, ffn=768, vocab=512)
@@ -134,7 +145,12 @@ def test_decode_stack_matches_restatement(fused_norm):
     head = random_rows(Q6_K, shape.vocab, shape.hidden, rng)
     out_norm = (1 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
     max_ctx = 64
-    dev = DecodeStack(shape, max_ctx, layers, embed, head, out_norm, fused_norm=fused_norm)
+    policy = RepackPolicy.from_env("llama", env=LAYOUTS[layout])
+    dev = DecodeStack(shape, max_ctx, layers, embed, head, out_norm, fused_norm=fused_norm, repack=policy,
+                      kv="contiguous")
+    assert dev.kv_cache is None and dev.k_cache is not None
+    want_q = {"canonical": (Q4_K, Q6_K), "default": (Q4_K, Q6_K_R4), "r4_lm": (Q4_K_R4, Q6_K_LM)}[layout]
+    assert (dev.layers[0].wqkv.qtype, dev.head.qtype) == want_q
     ref = DecodeRef(shape, layers, embed, head, out_norm, max_ctx)
     tokens = [3, 17, 5, 100, 511, 0, 42, 42, 7, 300, 64, 1]
     for pos, tok in enumerate(tokens):
@@ -146,6 +162,35 @@ def test_decode_stack_matches_restatement(fused_norm):
         top2 = np.sort(want)[-2:]
         if top2[1] - top2[0] > 5e-3 * np.max(np.abs(want)):  # a clear winner
             assert int(np.argmax(got)) == int(np.argmax(want)), pos
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kv", ["paged", "q8"])
+def test_decode_stack_paged_cache(kv):
+    """The stack over the paged caches (8-position pages, so the 12 tokens
+    cross a page boundary) against the restatement with the same cache
+    storage: fp16 rows, or the reference's Q8 rows (ANVIL_KV_QUANT)."""
+    from cybel_b200.decode import DecodeStack, StackShape, random_layer, random_rows
+    from cybel_b200.formats import Q4_K, Q6_K
+    from cybel_b200.repack_policy import RepackPolicy
+    from oracle.decode_ref import DecodeRef
+
+    shape = StackShape(layers=2, hidden=512, heads=4, kv_heads=2, ffn=768, vocab=512)
+    rng = np.random.default_rng(8)
+    layers = [random_layer(shape, rng) for _ in range(shape.layers)]
+    embed = random_rows(Q4_K, shape.vocab, shape.hidden, rng, std=1.0)
+    head = random_rows(Q6_K, shape.vocab, shape.hidden, rng)
+    out_norm = (1 + 0.1 * rng.standard_normal(shape.hidden)).astype(np.float32)
+    dev = DecodeStack(shape, 64, layers, embed, head, out_norm, repack=RepackPolicy.canonical(), kv=kv, page_size=8)
+    ref = DecodeRef(shape, layers, embed, head, out_norm, 64, kv_q8=kv == "q8")
+    tokens = [3, 17, 5, 100, 511, 0, 42, 42, 7, 300, 64, 1]
+    for pos, tok in enumerate(tokens):
+        dev.set_token(tok)
+        dev.step(pos)
+        got = dev.logits.cpu().numpy()
+        assert _rel(got, ref.step(tok, pos)) <= 2e-3, pos
+    assert dev.k_cache is None and dev.kv_cache.q8 == (kv == "q8")
+    assert dev.kv_cache.pages_in_use == shape.layers * 2
 
 
 @pytest.mark.gpu
