@@ -75,8 +75,10 @@ SIGNATURES.update(
         "b200q_add_rmsnorm_q": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, ctypes.c_float, _vp], _i),
         "b200q_attention_decode_q": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp], _i),
         "b200q_rope_attention_decode": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, _i, _vp, _vp, _i, _vp], _i),
-        "b200q_rope_attention_decode_paged": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _vp, _vp, _vp, _vp, _i, _i,
-                                               _vp, _i, _vp, _vp, _i, _vp], _i),
+        "b200q_rope_attention_decode_paged": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i, _vp, _vp, _vp, _vp, _i,
+                                               _i, _vp, _i, _vp, _vp, _i, _vp], _i),
+        "b200q_rope_attention_decode_tokens": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _i, _vp, _vp, _i,
+                                                _vp], _i),
         "b200q_swiglu_q": ([_vp, _vp, _vp, _i, _i, _vp], _i),
         "b200q_matmul_xq": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _i, _vp], _i),
         "b200q_matmul_norm": ([_i, _i, _vp, _vp, _f, _vp, _vp, _i, _i, _f, _f, _i, _vp], _i),

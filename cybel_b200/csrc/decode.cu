@@ -478,8 +478,9 @@ struct KvLane {
 };
 
 // Q8 codes of four values of a 128-element row held by the 32 lanes of a
-// warp (lane l: elements 4l .. 4l+3), and the row's scale (lane 0 stores it).
-__device__ __forceinline__ void q8_row_store(float4 x, int8_t* dst, float* scale_dst, int lane) {
+// warp (lane l: elements 4l .. 4l+3), packed little-endian, and the row's
+// scale in *scale.
+__device__ __forceinline__ uint32_t q8_row_codes(float4 x, float* scale_out) {
     float amax = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
 #pragma unroll
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -489,22 +490,62 @@ __device__ __forceinline__ void q8_row_store(float4 x, int8_t* dst, float* scale
         const int c = static_cast<int>(roundf(__fmul_rn(e, inv)));
         return static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(max(-127, min(127, c)))));
     };
-    *reinterpret_cast<uint32_t*>(dst + 4 * lane) = code(x.x) | (code(x.y) << 8) | (code(x.z) << 16) | (code(x.w) << 24);
-    if (lane == 0) *scale_dst = scale;
+    *scale_out = scale;
+    return code(x.x) | (code(x.y) << 8) | (code(x.z) << 16) | (code(x.w) << 24);
 }
 
-// Fused decode attention for one query token per sequence (the RoPE and
-// attention stages of the reference's decode graph, model_graph.cpp:
-// 1222-1323 and the GQA attention after it, in one launch):
-//  * every CTA rotates its kv head's G query heads into shared memory
-//    (pos * theta^(-2p / head_dim), interleaved pairs), scaled by
-//    1 / sqrt(head_dim);
-//  * the CTA whose chunk holds `pos` rotates the new key and appends it and
-//    the new value to the caches (fp16, or Q8 codes and scales) before
-//    reading its chunk;
+// Pair i (elements 2i, 2i+1) of a head rotated to position pos
+// (apply_rope_with_dim, model_graph.cpp:1222-1323: angle pos * theta^(-2i / d)).
+// Explicitly rounded products and sums, so every caller gets the same bits.
+__device__ __forceinline__ float2 rope_pair(float x0, float x1, int pos, int i, float log2_theta) {
+    const float inv_freq = exp2f(-2.0f * static_cast<float>(i) / static_cast<float>(kHeadDim) * log2_theta);
+    float s, c;
+    sincosf(static_cast<float>(pos) * inv_freq, &s, &c);
+    return make_float2(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)), __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c)));
+}
+
+// Lane l's elements 4l .. 4l+3 of key row `kin` rotated to position pos.
+__device__ __forceinline__ float4 rope_lane(const float* kin, int pos, int lane, float log2_theta) {
+    const float4 x = *reinterpret_cast<const float4*>(kin + 4 * lane);
+    const float2 a = rope_pair(x.x, x.y, pos, 2 * lane, log2_theta);
+    const float2 b = rope_pair(x.z, x.w, pos, 2 * lane + 1, log2_theta);
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// A lane's four elements in the cache's storage form (fp16 pairs, or Q8
+// codes with the row scale in *scale).
+template <int KVM>
+__device__ __forceinline__ typename KvLane<KVM>::Raw to_stored(float4 x, float* scale) {
+    if constexpr (KVM == KV_PAGED_Q8) {
+        return q8_row_codes(x, scale);
+    } else {
+        const __half2 a = __floats2half2_rn(x.x, x.y), b = __floats2half2_rn(x.z, x.w);
+        uint2 r;
+        r.x = *reinterpret_cast<const uint32_t*>(&a);
+        r.y = *reinterpret_cast<const uint32_t*>(&b);
+        *scale = 1.0f;
+        return r;
+    }
+}
+
+// Fused decode attention (the RoPE and attention stages of the reference's
+// decode graph, model_graph.cpp:1222-1323 and the GQA attention after it,
+// in one launch). blockIdx.z = s * n_tok + t: token t of sequence s, at
+// position pos + t. n_tok = 1 is the ordinary decode step of a batch of
+// sequences; n_tok > 1 runs several consecutive tokens of each sequence
+// (the rows a speculative verify feeds through the stack in one pass), each
+// attending causally over the cache and the tokens before it.
+//  * every CTA rotates its kv head's G query heads into shared memory,
+//    scaled by 1 / sqrt(head_dim);
+//  * the CTA whose chunk holds its token's position appends the rotated key
+//    and the value there (fp16, or Q8 codes and scales);
+//  * positions written by this launch (pos .. pos + t) are not read back
+//    from the cache: each CTA forms those rows from the q/k/v inputs in the
+//    cache's storage form, bit-identical to what is stored; older positions
+//    are loaded before the wait on the preceding kernel;
 //  * each CTA scores and weights its kAttnChunk positions like
 //    b200q_attn_chunk_kernel and writes its partial records;
-//  * the CTA that finishes last for a (kv head, sequence) -- an arrival
+//  * the CTA that finishes last for a (kv head, token) -- an arrival
 //    counter, reset by that CTA -- merges the chunks (max rescaling) and
 //    writes the output rows and, with DIG > 0, their x8 / x16 codes. No CTA
 //    waits for another (threadfence-reduction pattern).
@@ -512,7 +553,7 @@ template <int G, int DIG, int KVM>
 __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, const KvArgs kv,
     float* __restrict__ part, int* __restrict__ counters, float* __restrict__ out, uint8_t* __restrict__ xq,
-    int n_heads, int n_kv, int pos, float log2_theta, float scale) {
+    int n_heads, int n_kv, int pos, int n_tok, float log2_theta, float scale) {
     griddep_launch_dependents();
     using KL = KvLane<KVM>;
     using Raw = typename KL::Raw;
@@ -525,29 +566,33 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
     __shared__ __align__(16) float ml[G][2];
     __shared__ __align__(16) float red[kAttnWarps][G * kHeadDim];
     __shared__ int is_last;
-    const int kvh = blockIdx.x, c = blockIdx.y, n_chunks = gridDim.y, b = blockIdx.z;
-    const int ctx = pos + 1;
+    const int kvh = blockIdx.x, c = blockIdx.y, b = blockIdx.z;  // b: the (sequence, token) row
+    const int seq = b / n_tok, tok = b - seq * n_tok;
+    const int my_pos = pos + tok;
+    const int n_chunks = my_pos / kAttnChunk + 1;  // this token's chunks (gridDim.y covers the last token)
+    if (c >= n_chunks) return;
+    const int ctx = my_pos + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* k_seq = k + (static_cast<long long>(seq) * n_tok * n_kv + kvh) * kHeadDim;  // token 0's k row
+    const float* v_seq = v + (static_cast<long long>(seq) * n_tok * n_kv + kvh) * kHeadDim;
+    const long long tok_stride = static_cast<long long>(n_kv) * kHeadDim;
     q += (static_cast<long long>(b) * n_heads + kvh * G) * kHeadDim;
-    k += (static_cast<long long>(b) * n_kv + kvh) * kHeadDim;
-    v += (static_cast<long long>(b) * n_kv + kvh) * kHeadDim;
-    part += (static_cast<long long>(b) * n_heads + kvh * G) * n_chunks * kPartStride;  // records [g][chunk]
+    part += (static_cast<long long>(b) * n_heads + kvh * G) * gridDim.y * kPartStride;  // records [g][chunk]
     const int p0 = c * kAttnChunk;
     const int np = min(kAttnChunk, ctx - p0);
-    // The cached rows before pos were written by earlier steps: load this
-    // warp's K and V rows before waiting for the preceding kernel (the
-    // projection that produces q, k, v), so the loads overlap its tail.
+    // Rows before pos were written by earlier steps: load this warp's K and
+    // V rows before waiting for the preceding kernel (the projection that
+    // produces q, k, v), so the loads overlap its tail.
     Raw kr[PW], vr[PW];
     float ksc[PW], vsc[PW];
-    uint32_t live = 0;  // bit j: this warp's position j has a cached row
+    uint32_t live = 0;  // bit j: this warp's position j has a row
 #pragma unroll
     for (int j = 0; j < PW; ++j) {
         const int p = warp + j * kAttnWarps;
-        const bool cached = p < np && p0 + p != pos;
         kr[j] = Raw{};
         vr[j] = Raw{};
         ksc[j] = vsc[j] = 0.0f;
-        const long long row = cached ? kv_row<KVM>(kv, b, kvh, n_kv, p0 + p) : -1;
+        const long long row = p < np && p0 + p < pos ? kv_row<KVM>(kv, seq, kvh, n_kv, p0 + p) : -1;
         if (row >= 0) {
             live |= 1u << j;
             kr[j] = KL::load(kv.k, row, lane);
@@ -561,69 +606,47 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
     griddep_wait();
     for (int i = threadIdx.x; i < G * HALF; i += blockDim.x) {
         const int g = i / HALF, p = i - g * HALF;
-        const float inv_freq = exp2f(-2.0f * static_cast<float>(p) / static_cast<float>(kHeadDim) * log2_theta);
-        float s, co;
-        sincosf(static_cast<float>(pos) * inv_freq, &s, &co);
-        const float x0 = q[g * kHeadDim + 2 * p], x1 = q[g * kHeadDim + 2 * p + 1];
-        const float r0 = x0 * co - x1 * s, r1 = x0 * s + x1 * co;
-        qs[g][2 * p] = r0 * scale;
-        qs[g][2 * p + 1] = r1 * scale;
+        const float2 r = rope_pair(q[g * kHeadDim + 2 * p], q[g * kHeadDim + 2 * p + 1], my_pos, p, log2_theta);
+        qs[g][2 * p] = r.x * scale;
+        qs[g][2 * p + 1] = r.y * scale;
     }
-    const bool holds_pos = c == n_chunks - 1;
-    const long long prow = holds_pos ? kv_row<KVM>(kv, b, kvh, n_kv, pos) : -1;  // the appended row
-    if (holds_pos && prow < 0 && threadIdx.x == 0) *kv.status = STATUS_BAD_PAGE;  // no page to append to
-    if (prow >= 0) {  // this chunk holds pos: append the rotated key and the value
-        if constexpr (Q8) {
-            // warp 0: the rotated key; warp 1: the value (lane l: elements 4l .. 4l+3)
-            if (warp < 2) {
-                float4 x;
-                if (warp == 0) {
-                    float e[4];
+    // This launch's own positions (pos .. my_pos): rows from the inputs.
 #pragma unroll
-                    for (int t = 0; t < 2; ++t) {
-                        const int i = 2 * lane + t;  // pair i: elements 2i, 2i+1
-                        const float inv_freq =
-                            exp2f(-2.0f * static_cast<float>(i) / static_cast<float>(kHeadDim) * log2_theta);
-                        float sn, co;
-                        sincosf(static_cast<float>(pos) * inv_freq, &sn, &co);
-                        const float x0 = k[2 * i], x1 = k[2 * i + 1];
-                        e[2 * t] = x0 * co - x1 * sn;
-                        e[2 * t + 1] = x0 * sn + x1 * co;
-                    }
-                    x = make_float4(e[0], e[1], e[2], e[3]);
-                    q8_row_store(x, static_cast<int8_t*>(kv.k) + prow, kv.ks + prow / kHeadDim, lane);
-                } else {
-                    x = *reinterpret_cast<const float4*>(v + 4 * lane);
-                    q8_row_store(x, static_cast<int8_t*>(kv.v) + prow, kv.vs + prow / kHeadDim, lane);
-                }
-            }
-        } else {
-            __half* kc = static_cast<__half*>(kv.k);
-            __half* vc = static_cast<__half*>(kv.v);
-            for (int i = threadIdx.x; i < HALF + kHeadDim; i += blockDim.x) {
-                if (i < HALF) {
-                    const float inv_freq =
-                        exp2f(-2.0f * static_cast<float>(i) / static_cast<float>(kHeadDim) * log2_theta);
-                    float s, co;
-                    sincosf(static_cast<float>(pos) * inv_freq, &s, &co);
-                    const float x0 = k[2 * i], x1 = k[2 * i + 1];
-                    *reinterpret_cast<__half2*>(kc + prow + 2 * i) =
-                        __floats2half2_rn(x0 * co - x1 * s, x0 * s + x1 * co);
-                } else {
-                    vc[prow + (i - HALF)] = __float2half_rn(v[i - HALF]);
-                }
+    for (int j = 0; j < PW; ++j) {
+        const int p = warp + j * kAttnWarps;
+        const int pp = p0 + p;
+        if (p < np && pp >= pos && kv_row<KVM>(kv, seq, kvh, n_kv, pp) >= 0) {  // warp-uniform
+            const long long t = pp - pos;
+            kr[j] = to_stored<KVM>(rope_lane(k_seq + t * tok_stride, pp, lane, log2_theta), &ksc[j]);
+            vr[j] = to_stored<KVM>(*reinterpret_cast<const float4*>(v_seq + t * tok_stride + 4 * lane), &vsc[j]);
+            live |= 1u << j;
+        }
+    }
+    if (c == n_chunks - 1) {  // this chunk holds my_pos: append its rotated key and value
+        const long long prow = kv_row<KVM>(kv, seq, kvh, n_kv, my_pos);
+        if (prow < 0) {
+            if (threadIdx.x == 0) *kv.status = STATUS_BAD_PAGE;  // no page to append to
+        } else if (warp < 2) {  // warp 0: the key, warp 1: the value (lane l: elements 4l .. 4l+3)
+            const float* src = (warp == 0 ? k_seq : v_seq) + tok * tok_stride;
+            const float4 x = warp == 0 ? rope_lane(src, my_pos, lane, log2_theta)
+                                       : *reinterpret_cast<const float4*>(src + 4 * lane);
+            float sc_row;
+            const Raw r = to_stored<KVM>(x, &sc_row);
+            if constexpr (Q8) {
+                *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(warp == 0 ? kv.k : kv.v) + prow + 4 * lane) = r;
+                if (lane == 0) (warp == 0 ? kv.ks : kv.vs)[prow / kHeadDim] = sc_row;
+            } else {
+                *reinterpret_cast<uint2*>(static_cast<__half*>(warp == 0 ? kv.k : kv.v) + prow + 4 * lane) = r;
             }
         }
     }
-    __syncthreads();  // the appended row and the rotated queries are visible to the CTA
+    __syncthreads();  // the rotated queries are visible to the CTA
     {
 #pragma unroll
         for (int j = 0; j < PW; ++j) {
             const int p = warp + j * kAttnWarps;
-            const bool appended = p0 + p == pos;
-            const bool ok = appended ? prow >= 0 : ((live >> j) & 1u) != 0;
-            const Raw kk = appended && ok ? KL::load(kv.k, prow, lane) : kr[j];
-            const float4 kf = KL::value(kk);
+            const bool ok = ((live >> j) & 1u) != 0;
+            const float4 kf = KL::value(kr[j]);
             float d[G];
 #pragma unroll
             for (int g = 0; g < G; ++g) {
@@ -636,9 +659,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
                 for (int g = 0; g < G; ++g) d[g] += __shfl_xor_sync(0xffffffffu, d[g], o);
             }
             if constexpr (Q8) {
-                const float ks = appended && ok ? kv.ks[prow / kHeadDim] : ksc[j];
 #pragma unroll
-                for (int g = 0; g < G; ++g) d[g] *= ks;
+                for (int g = 0; g < G; ++g) d[g] *= ksc[j];
             }
             if (!ok) {
 #pragma unroll
@@ -678,16 +700,11 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
 #pragma unroll
         for (int j = 0; j < PW; ++j) {
             const int p = warp + j * kAttnWarps;
-            const bool appended = p0 + p == pos;
-            const bool ok = appended ? prow >= 0 : ((live >> j) & 1u) != 0;
-            const Raw vv = appended && ok ? KL::load(kv.v, prow, lane) : vr[j];  // zero without a row
-            float vsv = 1.0f;
-            if constexpr (Q8) vsv = appended && ok ? kv.vs[prow / kHeadDim] : vsc[j];
-            const float4 vf = KL::value(vv);
+            const float4 vf = KL::value(vr[j]);  // zero without a row
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 float e = p < np ? sc[g][p] : 0.0f;
-                if constexpr (Q8) e *= vsv;
+                if constexpr (Q8) e *= vsc[j];
                 acc[g][0] = fmaf(e, vf.x, acc[g][0]);
                 acc[g][1] = fmaf(e, vf.y, acc[g][1]);
                 acc[g][2] = fmaf(e, vf.z, acc[g][2]);
@@ -881,33 +898,37 @@ namespace {
 // Shared by the contiguous and paged entry points: checks the head shapes and
 // outputs, takes the scratch, and launches b200q_attn_decode_kernel<G, DIG, KVM>.
 int launch_attention(int kvm, const KvArgs& kv, const float* q, const float* k, const float* v, int batch,
-                     int n_heads, int n_kv, int hd, int pos, float theta, float* out, void* xq, int act_mode,
-                     Device* dev, cudaStream_t st) {
-    if (!q || !k || !v || (!out && !xq) || batch <= 0 || n_heads <= 0 || n_kv <= 0 || !dev) return B200Q_EINVAL;
+                     int n_tok, int n_heads, int n_kv, int hd, int pos, float theta, float* out, void* xq,
+                     int act_mode, Device* dev, cudaStream_t st) {
+    if (!q || !k || !v || (!out && !xq) || batch <= 0 || n_tok <= 0 || n_heads <= 0 || n_kv <= 0 || !dev)
+        return B200Q_EINVAL;
     if (xq && act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
     if (hd != kHeadDim || n_heads % n_kv || pos < 0 || !(theta > 0.0f)) return B200Q_ESHAPE;
+    const long long rows = static_cast<long long>(batch) * n_tok;
+    if (rows > 65535) return B200Q_ESHAPE;
     const int G = n_heads / n_kv;
     if (G != 1 && G != 2 && G != 4 && G != 8) return B200Q_ESHAPE;
-    if ((out && !aligned16(out)) || (xq && !aligned16(xq))) return B200Q_EALIGN;
-    const int n_chunks = pos / kAttnChunk + 1;
+    if ((out && !aligned16(out)) || (xq && !aligned16(xq)) || !aligned16(k) || !aligned16(v)) return B200Q_EALIGN;
+    const int n_chunks = (pos + n_tok - 1) / kAttnChunk + 1;  // the last token's
     void* part = nullptr;
     void* cnt = nullptr;
     int rc = scratch_for(dev, st, kScratchAttn,
-                         static_cast<size_t>(batch) * n_heads * n_chunks * kPartStride * sizeof(float), &part);
+                         static_cast<size_t>(rows) * n_heads * n_chunks * kPartStride * sizeof(float), &part);
     // Arrival counters: zero when allocated (all of the buffer, so a later
-    // call with more sequences finds its counters zero too); the merging CTA
+    // call with more rows finds its counters zero too); the merging CTA
     // resets its counter after each launch.
     if (rc == B200Q_OK)
-        rc = scratch_for(dev, st, kScratchAttnCnt, static_cast<size_t>(batch) * n_kv * sizeof(int), &cnt, true);
+        rc = scratch_for(dev, st, kScratchAttnCnt, static_cast<size_t>(rows) * n_kv * sizeof(int), &cnt, true);
     if (rc != B200Q_OK) return rc;
     KvArgs a = kv;
     a.status = dev->status;
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = pdl_cfg(dim3(n_kv, n_chunks, batch), dim3(kAttnWarps * 32), st, attr);
+    cudaLaunchConfig_t cfg =
+        pdl_cfg(dim3(n_kv, n_chunks, static_cast<unsigned>(rows)), dim3(kAttnWarps * 32), st, attr);
     const int dig = !xq ? 0 : (act_mode == B200Q_ACT_X8 ? 1 : 2);
     auto go = [&](auto kern) {
         return cudaLaunchKernelEx(&cfg, kern, q, k, v, a, static_cast<float*>(part), static_cast<int*>(cnt), out,
-                                  static_cast<uint8_t*>(xq), n_heads, n_kv, pos, log2f(theta),
+                                  static_cast<uint8_t*>(xq), n_heads, n_kv, pos, n_tok, log2f(theta),
                                   1.0f / sqrtf(static_cast<float>(hd)));
     };
     cudaError_t e = cudaErrorInvalidValue;
@@ -932,28 +953,29 @@ int launch_attention(int kvm, const KvArgs& kv, const float* q, const float* k, 
 
 }  // namespace
 
-int launch_rope_attention(const float* q, const float* k, const float* v, int batch, int n_heads, int n_kv, int hd,
-                          int pos, float theta, void* kc, void* vc, int max_ctx, float* out, void* xq, int act_mode,
-                          Device* dev, cudaStream_t st) {
-    if (!kc || !vc || max_ctx <= 0) return B200Q_EINVAL;
-    if (pos >= max_ctx) return B200Q_ESHAPE;
+int launch_rope_attention(const float* q, const float* k, const float* v, int batch, int n_tok, int n_heads, int n_kv,
+                          int hd, int pos, float theta, void* kc, void* vc, int max_ctx, float* out, void* xq,
+                          int act_mode, Device* dev, cudaStream_t st) {
+    if (!kc || !vc || max_ctx <= 0 || n_tok <= 0) return B200Q_EINVAL;
+    if (static_cast<long long>(pos) + n_tok > max_ctx) return B200Q_ESHAPE;
     if ((reinterpret_cast<uintptr_t>(kc) & 7u) || (reinterpret_cast<uintptr_t>(vc) & 7u)) return B200Q_EALIGN;
     KvArgs kv{};
     kv.k = kc;
     kv.v = vc;
     kv.max_ctx = max_ctx;
-    return launch_attention(KV_CONTIG, kv, q, k, v, batch, n_heads, n_kv, hd, pos, theta, out, xq, act_mode, dev, st);
+    return launch_attention(KV_CONTIG, kv, q, k, v, batch, n_tok, n_heads, n_kv, hd, pos, theta, out, xq, act_mode,
+                            dev, st);
 }
 
-int launch_rope_attention_paged(const float* q, const float* k, const float* v, int batch, int n_heads, int n_kv,
-                                int hd, int pos, float theta, int kv_mode, void* k_pages, void* v_pages,
+int launch_rope_attention_paged(const float* q, const float* k, const float* v, int batch, int n_tok, int n_heads,
+                                int n_kv, int hd, int pos, float theta, int kv_mode, void* k_pages, void* v_pages,
                                 float* k_scales, float* v_scales, int n_slots, int page_size, const int* page_table,
                                 int pages_per_seq, float* out, void* xq, int act_mode, Device* dev, cudaStream_t st) {
     const bool q8 = kv_mode == B200Q_KV_Q8;
     if ((kv_mode != B200Q_KV_F16 && !q8) || !k_pages || !v_pages || !page_table || n_slots <= 0 || page_size <= 0 ||
-        pages_per_seq <= 0 || (q8 && (!k_scales || !v_scales)))
+        pages_per_seq <= 0 || n_tok <= 0 || (q8 && (!k_scales || !v_scales)))
         return B200Q_EINVAL;
-    if (static_cast<long long>(pos) >= static_cast<long long>(pages_per_seq) * page_size) return B200Q_ESHAPE;
+    if (static_cast<long long>(pos) + n_tok > static_cast<long long>(pages_per_seq) * page_size) return B200Q_ESHAPE;
     const uintptr_t row_align = q8 ? 3u : 7u;  // int8 rows read 4 bytes a lane, fp16 rows 8
     if ((reinterpret_cast<uintptr_t>(k_pages) & row_align) || (reinterpret_cast<uintptr_t>(v_pages) & row_align) ||
         (reinterpret_cast<uintptr_t>(page_table) & 3u) ||
@@ -968,8 +990,8 @@ int launch_rope_attention_paged(const float* q, const float* k, const float* v, 
     kv.pages_per_seq = pages_per_seq;
     kv.page = page_size;
     kv.n_slots = n_slots;
-    return launch_attention(q8 ? KV_PAGED_Q8 : KV_PAGED, kv, q, k, v, batch, n_heads, n_kv, hd, pos, theta, out, xq,
-                            act_mode, dev, st);
+    return launch_attention(q8 ? KV_PAGED_Q8 : KV_PAGED, kv, q, k, v, batch, n_tok, n_heads, n_kv, hd, pos, theta, out,
+                            xq, act_mode, dev, st);
 }
 
 int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaStream_t st) {

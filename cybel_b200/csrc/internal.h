@@ -109,13 +109,15 @@ int launch_rope_kv(float* q, float* k, const float* v, int batch, int n_heads, i
 int launch_attention(const float* q, const void* kc, const void* vc, float* out, int batch, int n_heads, int n_kv,
                      int hd, int ctx, int max_ctx, Device* dev, cudaStream_t st, void* xq = nullptr,
                      int act_mode = 0);
-// RoPE + KV append + attention + chunk merge in one launch (b200q_attn_decode_kernel).
-int launch_rope_attention(const float* q, const float* k, const float* v, int batch, int n_heads, int n_kv, int hd,
-                          int pos, float theta, void* kc, void* vc, int max_ctx, float* out, void* xq, int act_mode,
-                          Device* dev, cudaStream_t st);
+// RoPE + KV append + attention + chunk merge in one launch (b200q_attn_decode_kernel)
+// for n_tok consecutive tokens (positions pos .. pos + n_tok - 1) of each of
+// `batch` sequences.
+int launch_rope_attention(const float* q, const float* k, const float* v, int batch, int n_tok, int n_heads, int n_kv,
+                          int hd, int pos, float theta, void* kc, void* vc, int max_ctx, float* out, void* xq,
+                          int act_mode, Device* dev, cudaStream_t st);
 // The same over a paged cache (b200q_rope_attention_decode_paged).
-int launch_rope_attention_paged(const float* q, const float* k, const float* v, int batch, int n_heads, int n_kv,
-                                int hd, int pos, float theta, int kv_mode, void* k_pages, void* v_pages,
+int launch_rope_attention_paged(const float* q, const float* k, const float* v, int batch, int n_tok, int n_heads,
+                                int n_kv, int hd, int pos, float theta, int kv_mode, void* k_pages, void* v_pages,
                                 float* k_scales, float* v_scales, int n_slots, int page_size, const int* page_table,
                                 int pages_per_seq, float* out, void* xq, int act_mode, Device* dev, cudaStream_t st);
 int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaStream_t st);

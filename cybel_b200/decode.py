@@ -30,7 +30,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _native
-from .formats import Q4_K, Q6_K
+from .formats import Q4_K, Q6_K, row_bytes
 from .quantized_matmul import DeviceMatrix
 
 
@@ -297,3 +297,84 @@ class DecodeStack:
 
     def set_token(self, token: int) -> None:
         self.token.fill_(int(token))
+
+    # -- several tokens in one pass ---------------------------------------------
+    def _verify_buffers(self, m: int) -> dict:
+        import torch
+
+        bufs = self._vbufs.get(m) if hasattr(self, "_vbufs") else None
+        if bufs is None:
+            s = self.shape
+            h, kv, f = s.hidden, s.kv_dim, s.ffn
+            z = (lambda *shape: torch.zeros(shape, dtype=torch.float32, device=self.dev))
+            bufs = dict(x=z(m, h), hn=z(m, h), q=z(m, h), k=z(m, kv), v=z(m, kv), att=z(m, h), o=z(m, h),
+                        g=z(m, f), u=z(m, f), sw=z(m, f), d=z(m, h), logits=z(m, s.vocab),
+                        tok=torch.zeros(m, dtype=torch.int32, device=self.dev))
+            self._vbufs = getattr(self, "_vbufs", {})
+            self._vbufs[m] = bufs
+        return bufs
+
+    def verify(self, tokens, pos0: int):
+        """Feed len(tokens) tokens at positions pos0, pos0 + 1, ... through
+        the stack in ONE pass and return their next-token logits, a device
+        tensor [m][vocab] (row j: the logits after tokens[j]).
+
+        This is the batched form of the reference's speculative verify, which
+        asks the engine for the logits of each drafted prefix in turn
+        (cpu_speculative_decode.py:740-769): every quantized linear runs once
+        over the m rows (b200q_matmul_ex: the GEMV below 8 rows, the tcgen05
+        tile kernel for Q4_K from 8 rows), and one attention launch per layer
+        appends the m keys/values and attends causally
+        (b200q_rope_attention_decode_tokens / the paged form). The cache then
+        holds all m tokens; positions past the accepted prefix are simply
+        written again by the next step before anything reads them."""
+        import torch
+
+        m = len(tokens)
+        if m <= 0:
+            raise ValueError("no tokens to verify")
+        if pos0 < 0 or pos0 + m > self.max_ctx:
+            raise ValueError("positions outside the KV cache")
+        s, L = self.shape, self.lib
+        st = torch.cuda.current_stream(self.dev).cuda_stream
+        act, W = self.act_mode, _native.WEIGHTS_STATIC
+        h, kv, hd, f = s.hidden, s.kv_dim, s.head_dim, s.ffn
+        B = self._verify_buffers(m)
+        B["tok"].copy_(torch.tensor([int(t) for t in tokens], dtype=torch.int32))
+        if self.kv_cache is not None:
+            self.kv_cache.ensure(pos0, pos0 + m - 1)
+        P = {name: t.data_ptr() for name, t in B.items()}
+
+        def lin(mat, row0, n, x, y, k):
+            ptr = mat.ptr + row0 * row_bytes(mat.qtype, k)
+            self._check(L.b200q_matmul_ex(mat.qtype, act, x, ptr, y, m, k, n, W, st), "verify linear")
+
+        self._check(L.b200q_dequantize_rows(s.embedding_qtype, self.embed.ptr, P["tok"], m, P["x"], h, s.vocab, st),
+                    "embedding")
+        delta = None
+        for li, lay in enumerate(self.layers):
+            self._check(L.b200q_add_rmsnorm(P["x"], delta, lay.attn_norm.data_ptr(), P["hn"], h, m, s.eps, st),
+                        "attn norm")
+            lin(lay.wqkv, 0, h, P["hn"], P["q"], h)
+            lin(lay.wqkv, h, kv, P["hn"], P["k"], h)
+            lin(lay.wqkv, h + kv, kv, P["hn"], P["v"], h)
+            if self.kv_cache is not None:
+                self.kv_cache.attention(li, P["q"], P["k"], P["v"], pos0, s.heads, s.rope_theta, P["att"], None, 0, st,
+                                        n_tokens=m)
+            else:
+                self._check(L.b200q_rope_attention_decode_tokens(
+                    P["q"], P["k"], P["v"], 1, m, s.heads, s.kv_heads, hd, pos0, s.rope_theta,
+                    self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), self.max_ctx, P["att"], None, 0, st),
+                    "verify attention")
+            lin(lay.wo, 0, h, P["att"], P["o"], h)
+            self._check(L.b200q_add_rmsnorm(P["x"], P["o"], lay.ffn_norm.data_ptr(), P["hn"], h, m, s.eps, st),
+                        "ffn norm")
+            lin(lay.w_gu, 0, f, P["hn"], P["g"], h)
+            lin(lay.w_gu, f, f, P["hn"], P["u"], h)
+            self._check(L.b200q_swiglu(P["g"], P["u"], P["sw"], m * f, st), "swiglu")
+            lin(lay.w_down, 0, h, P["sw"], P["d"], f)
+            delta = P["d"]
+        self._check(L.b200q_add_rmsnorm(P["x"], delta, self.out_norm.data_ptr(), P["hn"], h, m, s.eps, st),
+                    "output norm")
+        lin(self.head, 0, s.vocab, P["hn"], P["logits"], h)
+        return B["logits"]

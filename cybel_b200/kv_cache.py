@@ -162,17 +162,19 @@ class PagedKVCache:
         return self.table.data_ptr() + 4 * layer * self.batch * self.pages_per_seq
 
     def attention(self, layer: int, q: int, k: int, v: int, pos: int, n_heads: int, theta: float, out: int | None,
-                  xq: int | None, act_mode: int, stream: int) -> None:
-        """RoPE + append at pos + attention over 0..pos for every sequence of
-        layer `layer` (device pointers; q [batch][n_heads][128], k and v
-        [batch][kv_heads][128]); the page of pos must have been ensured."""
+                  xq: int | None, act_mode: int, stream: int, n_tokens: int = 1) -> None:
+        """RoPE + append + attention of layer `layer` for n_tokens
+        consecutive tokens of every sequence, token t at pos + t attending
+        over 0..pos + t (device pointers; q [batch][n_tokens][n_heads][128], k
+        and v [batch][n_tokens][kv_heads][128]); the pages of those positions
+        must have been ensured."""
         if self.dev.type != "cuda":
             raise RuntimeError("the paged attention runs on a CUDA device")
         L = _native.lib()
         ks = self.ks.data_ptr() if self.q8 else None
         vs = self.vs.data_ptr() if self.q8 else None
         _native.check(L.b200q_rope_attention_decode_paged(
-            q, k, v, self.batch, n_heads, self.kv_heads, self.head_dim, pos, theta, self.kv_mode, self.k.data_ptr(),
+            q, k, v, self.batch, n_tokens, n_heads, self.kv_heads, self.head_dim, pos, theta, self.kv_mode, self.k.data_ptr(),
             self.v.data_ptr(), ks, vs, self.n_slots, self.page_size, self.table_ptr(layer), self.pages_per_seq, out,
             xq, act_mode, stream), "paged attention")
 

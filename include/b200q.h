@@ -292,6 +292,19 @@ B200Q_API int b200q_rope_attention_decode(const float* q, const float* k, const 
                                           void* v_cache, int max_ctx, float* out, void* xq, int act_mode,
                                           void* stream);
 
+/* The same for n_tokens consecutive tokens of each sequence: q, k, v and the
+ * outputs hold batch x n_tokens rows (sequence-major), token t of a sequence
+ * sits at position pos0 + t, is appended there, and attends causally over
+ * positions 0 .. pos0 + t (the cache and the tokens before it in this call).
+ * One launch for the rows a speculative verify feeds through the stack at
+ * once, in place of n_tokens single-token steps (the sequential verify loop
+ * of cpu_speculative_decode.py:740-769). k and v 16-byte aligned;
+ * pos0 + n_tokens <= max_ctx. */
+B200Q_API int b200q_rope_attention_decode_tokens(const float* q, const float* k, const float* v, int batch,
+                                                 int n_tokens, int n_heads, int n_kv_heads, int head_dim, int pos0,
+                                                 float theta, void* k_cache, void* v_cache, int max_ctx, float* out,
+                                                 void* xq, int act_mode, void* stream);
+
 /* The same over a paged KV cache: the reference's PagedKVStore
  * (model_graph.cpp:1413-1576: pages of page_size positions, allocated per
  * (layer, page) when a position is first written) and its attention
@@ -309,13 +322,16 @@ B200Q_API int b200q_rope_attention_decode(const float* q, const float* k, const 
  * dot(q, codes) * scale and values enter as softmax weight * scale * codes,
  * as the reference computes them. A slot outside [0, n_slots) in the table,
  * or no page at pos, is recorded as device status bit 2 (value 2) and the
- * position is masked. pos < pages_per_seq * page_size; pools 8-byte (fp16)
- * or 4-byte (Q8) aligned. */
+ * position is masked. pos + n_tokens <= pages_per_seq * page_size; pools 8-byte (fp16)
+ * or 4-byte (Q8) aligned. n_tokens consecutive tokens per sequence as in
+ * b200q_rope_attention_decode_tokens (1 for a decode step); the pages of
+ * pos .. pos + n_tokens - 1 assigned before the call. */
 B200Q_API int b200q_rope_attention_decode_paged(const float* q, const float* k, const float* v, int batch,
-                                                int n_heads, int n_kv_heads, int head_dim, int pos, float theta,
-                                                int kv_mode, void* k_pages, void* v_pages, float* k_scales,
-                                                float* v_scales, int n_slots, int page_size, const int* page_table,
-                                                int pages_per_seq, float* out, void* xq, int act_mode, void* stream);
+                                                int n_tokens, int n_heads, int n_kv_heads, int head_dim, int pos,
+                                                float theta, int kv_mode, void* k_pages, void* v_pages,
+                                                float* k_scales, float* v_scales, int n_slots, int page_size,
+                                                const int* page_table, int pages_per_seq, float* out, void* xq,
+                                                int act_mode, void* stream);
 B200Q_API int b200q_swiglu_q(const float* gate, const float* up, void* xq, int act_mode, int n, void* stream);
 
 /* y = alpha * (W x) + beta * y for m activation rows given as codes written

@@ -11,8 +11,8 @@ restatement of the reference's PagedKVStore and its attention
   the rows the device stored (theta = 1, so rotation angles are exact
   integers and the fp32 rotation adds only rounding).
 * fp16 pages with a permuted page table against the contiguous-cache kernel
-  on the same rows: outputs, activation codes and the appended rows
-  bit-identical.
+  on the same rows, one token and three consecutive tokens per sequence:
+  outputs, activation codes and the appended rows bit-identical.
 * A page missing from the table and a slot past the pool: those positions
   are masked as the reference masks a position without a page (score -1e9,
   no value), the call records STATUS_BAD_PAGE (NativeError -11 from
@@ -87,8 +87,9 @@ def test_q8_steps_against_restatement(H, KV):
             assert _rel(outs[pos][b], want) <= 1e-4, (b, pos)
 
 
+@pytest.mark.parametrize("n_tok", [1, 3])
 @pytest.mark.parametrize("H,KV,act", [(32, 8, 2), (64, 8, 1), (16, 16, 0)])
-def test_f16_pages_match_contiguous_cache(H, KV, act):
+def test_f16_pages_match_contiguous_cache(H, KV, act, n_tok):
     import torch
 
     from cybel_b200 import _native
@@ -109,21 +110,27 @@ def test_f16_pages_match_contiguous_cache(H, KV, act):
             cache.v[slot] = contig_v[b, :, pg * P:(pg + 1) * P]
     cache.table.copy_(torch.from_numpy(cache.table_host))
     cache._free = []
-    q = torch.from_numpy(rng.standard_normal((B, H, HD)).astype(np.float32)).cuda()
-    k = torch.from_numpy(rng.standard_normal((B, KV, HD)).astype(np.float32)).cuda()
-    v = torch.from_numpy(rng.standard_normal((B, KV, HD)).astype(np.float32)).cuda()
+    q = torch.from_numpy(rng.standard_normal((B, n_tok, H, HD)).astype(np.float32)).cuda()
+    k = torch.from_numpy(rng.standard_normal((B, n_tok, KV, HD)).astype(np.float32)).cuda()
+    v = torch.from_numpy(rng.standard_normal((B, n_tok, KV, HD)).astype(np.float32)).cuda()
     xb = int(L.b200q_xq_row_bytes(H * HD, act)) if act else 16
     outs, xqs = [], []
     for paged in (False, True):
-        out = torch.empty((B, H, HD), device="cuda")
-        xq = torch.zeros((B, xb), dtype=torch.uint8, device="cuda")
+        out = torch.empty((B, n_tok, H, HD), device="cuda")
+        xq = torch.zeros((B, n_tok, xb), dtype=torch.uint8, device="cuda")
         xp = xq.data_ptr() if act else None
         if paged:
-            cache.attention(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos, H, theta, out.data_ptr(), xp, act, _st())
-        else:
+            cache.attention(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos, H, theta, out.data_ptr(), xp, act, _st(),
+                            n_tokens=n_tok)
+        elif n_tok == 1:
             _native.check(L.b200q_rope_attention_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, H, KV, HD, pos,
                                                         theta, contig_k.data_ptr(), contig_v.data_ptr(), max_ctx,
                                                         out.data_ptr(), xp, act, _st()), "contiguous")
+        else:
+            _native.check(L.b200q_rope_attention_decode_tokens(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, n_tok, H,
+                                                               KV, HD, pos, theta, contig_k.data_ptr(),
+                                                               contig_v.data_ptr(), max_ctx, out.data_ptr(), xp, act,
+                                                               _st()), "contiguous tokens")
         torch.cuda.synchronize()
         outs.append(out.cpu().numpy())
         xqs.append(xq.cpu().numpy())
@@ -132,9 +139,9 @@ def test_f16_pages_match_contiguous_cache(H, KV, act):
     assert np.array_equal(xqs[0], xqs[1])
     for b in range(B):
         for h in range(KV):
-            kc, vc, _, _ = cache.rows(0, b, h, pos, pos + 1)
-            assert np.array_equal(kc[0], contig_k[b, h, pos].cpu().numpy())
-            assert np.array_equal(vc[0], contig_v[b, h, pos].cpu().numpy())
+            kc, vc, _, _ = cache.rows(0, b, h, pos, pos + n_tok)
+            assert np.array_equal(kc, contig_k[b, h, pos:pos + n_tok].cpu().numpy())
+            assert np.array_equal(vc, contig_v[b, h, pos:pos + n_tok].cpu().numpy())
 
 
 def test_missing_and_bad_pages_are_masked_and_reported():
@@ -201,7 +208,7 @@ def test_paged_entry_rejects_bad_arguments():
 
     def call(**over):
         a = dict(args, **over)
-        return L.b200q_rope_attention_decode_paged(a["q"], a["k"], a["v"], a["batch"], a["H"], a["KV"], a["hd"],
+        return L.b200q_rope_attention_decode_paged(a["q"], a["k"], a["v"], a["batch"], 1, a["H"], a["KV"], a["hd"],
                                                    a["pos"], a["theta"], a["mode"], a["kp"], a["vp"], a["ks"],
                                                    a["vs"], a["n_slots"], a["page"], a["table"], a["pps"], a["out"],
                                                    a["xq"], a["act"], st)
