@@ -207,7 +207,7 @@ __global__ void b200q_rope_kv_kernel(float* __restrict__ q, float* __restrict__ 
 }
 
 // Partial record per (query head, chunk): o[kHeadDim], m, l.
-constexpr int kPartStride = kHeadDim + 2;
+constexpr int kPartStride = kHeadDim + 4;  // numerators, max, sum, pad: 16-byte records
 
 // One CTA per (kv head, kAttnChunk positions, sequence), kAttnWarps warps.
 // Scores: warp w takes positions w, w + kAttnWarps, ...; a lane holds 4 of
@@ -560,12 +560,30 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
     constexpr bool Q8 = KVM == KV_PAGED_Q8;
     constexpr int PW = kAttnChunk / kAttnWarps;  // positions per warp
     constexpr int HALF = kHeadDim / 2;
-    // 16-byte aligned: qs and red are accessed as float4.
-    __shared__ __align__(16) float qs[G][kHeadDim];
+    // Keys are scored position-major: lane l of a warp takes position slot
+    // l / 4 of the warp's PW positions over the quarter l % 4 of the head
+    // dimension (QD elements, KW 32-bit words of stored form), so a dot
+    // product needs two shuffle levels instead of five. Values stay
+    // dimension-major (lane l: elements 4l .. 4l+3 of each of the PW rows).
+    static_assert(PW * 4 == 32, "one position slot per four lanes");
+    constexpr int QD = kHeadDim / 4;
+    constexpr int KW = Q8 ? QD / 4 : QD / 2;         // words per lane quarter: 8 (Q8) or 16 (fp16)
+    constexpr int ROWW = Q8 ? kHeadDim / 4 : kHeadDim / 2;  // words per stored row
+    constexpr int QPAD = QD + 4;  // query quarters padded so the 4 quarters fall on distinct banks
+    // 16-byte aligned: qs, red and the staged rows are accessed as float4 / uint4.
+    __shared__ __align__(16) float qs[G][4][QPAD];
     __shared__ __align__(16) float sc[G][kAttnChunk];
     __shared__ __align__(16) float ml[G][2];
-    __shared__ __align__(16) float red[kAttnWarps][G * kHeadDim];
+    // red (after the PV phase) shares its storage with the key rows this
+    // launch writes (read in the score phase only).
+    constexpr int kRedBytes = kAttnWarps * G * kHeadDim * 4;
+    constexpr int kFreshBytes = kAttnChunk * ROWW * 4;
+    __shared__ __align__(16) unsigned char shared_rows[kRedBytes > kFreshBytes ? kRedBytes : kFreshBytes];
+    __shared__ float fresh_ks[kAttnChunk];
+    __shared__ float merge_l[kAttnWarps];
     __shared__ int is_last;
+    float (*red)[G * kHeadDim] = reinterpret_cast<float (*)[G * kHeadDim]>(shared_rows);
+    uint32_t (*fresh_k)[ROWW] = reinterpret_cast<uint32_t (*)[ROWW]>(shared_rows);
     const int kvh = blockIdx.x, c = blockIdx.y, b = blockIdx.z;  // b: the (sequence, token) row
     const int seq = b / n_tok, tok = b - seq * n_tok;
     const int my_pos = pos + tok;
@@ -580,46 +598,66 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
     part += (static_cast<long long>(b) * n_heads + kvh * G) * gridDim.y * kPartStride;  // records [g][chunk]
     const int p0 = c * kAttnChunk;
     const int np = min(kAttnChunk, ctx - p0);
-    // Rows before pos were written by earlier steps: load this warp's K and
-    // V rows before waiting for the preceding kernel (the projection that
-    // produces q, k, v), so the loads overlap its tail.
-    Raw kr[PW], vr[PW];
-    float ksc[PW], vsc[PW];
-    uint32_t live = 0;  // bit j: this warp's position j has a row
+    const int kp = warp + (lane >> 2) * kAttnWarps;  // this lane's key position in the chunk
+    const int qd = lane & 3;                          // and its quarter of the head dimension
+    // Rows before pos were written by earlier steps: load them before
+    // waiting for the preceding kernel (the projection that produces q, k,
+    // v), so the loads overlap its tail.
+    uint4 kq[KW / 4];
+    float kscale = 0.0f;
+    bool k_live = false;
+#pragma unroll
+    for (int w = 0; w < KW / 4; ++w) kq[w] = make_uint4(0u, 0u, 0u, 0u);
+    {
+        const long long row = kp < np && p0 + kp < pos ? kv_row<KVM>(kv, seq, kvh, n_kv, p0 + kp) : -1;
+        if (row >= 0) {
+            const uint4* src = reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(kv.k) +
+                                                              (row + qd * QD) * (Q8 ? 1 : 2));
+#pragma unroll
+            for (int w = 0; w < KW / 4; ++w) kq[w] = src[w];
+            if constexpr (Q8) kscale = kv.ks[row / kHeadDim];
+            k_live = true;
+        }
+    }
+    Raw vr[PW];
+    float vsc[PW];
+    uint32_t v_live = 0;  // bit j: this warp's position j has a value row
 #pragma unroll
     for (int j = 0; j < PW; ++j) {
         const int p = warp + j * kAttnWarps;
-        kr[j] = Raw{};
         vr[j] = Raw{};
-        ksc[j] = vsc[j] = 0.0f;
+        vsc[j] = 0.0f;
         const long long row = p < np && p0 + p < pos ? kv_row<KVM>(kv, seq, kvh, n_kv, p0 + p) : -1;
         if (row >= 0) {
-            live |= 1u << j;
-            kr[j] = KL::load(kv.k, row, lane);
+            v_live |= 1u << j;
             vr[j] = KL::load(kv.v, row, lane);
-            if constexpr (Q8) {
-                ksc[j] = kv.ks[row / kHeadDim];
-                vsc[j] = kv.vs[row / kHeadDim];
-            }
+            if constexpr (Q8) vsc[j] = kv.vs[row / kHeadDim];
         }
     }
     griddep_wait();
     for (int i = threadIdx.x; i < G * HALF; i += blockDim.x) {
         const int g = i / HALF, p = i - g * HALF;
         const float2 r = rope_pair(q[g * kHeadDim + 2 * p], q[g * kHeadDim + 2 * p + 1], my_pos, p, log2_theta);
-        qs[g][2 * p] = r.x * scale;
-        qs[g][2 * p + 1] = r.y * scale;
+        const int e = 2 * p;
+        qs[g][e / QD][e % QD] = r.x * scale;
+        qs[g][e / QD][e % QD + 1] = r.y * scale;
     }
-    // This launch's own positions (pos .. my_pos): rows from the inputs.
+    // This launch's own positions (pos .. my_pos): rows formed from the
+    // inputs in the cache's storage form (bit-identical to what is stored);
+    // keys staged in shared memory for the position-major score phase.
 #pragma unroll
     for (int j = 0; j < PW; ++j) {
         const int p = warp + j * kAttnWarps;
         const int pp = p0 + p;
         if (p < np && pp >= pos && kv_row<KVM>(kv, seq, kvh, n_kv, pp) >= 0) {  // warp-uniform
             const long long t = pp - pos;
-            kr[j] = to_stored<KVM>(rope_lane(k_seq + t * tok_stride, pp, lane, log2_theta), &ksc[j]);
+            float ks;
+            const Raw kr = to_stored<KVM>(rope_lane(k_seq + t * tok_stride, pp, lane, log2_theta), &ks);
+            if constexpr (Q8) fresh_k[p][lane] = kr;
+            else *reinterpret_cast<uint2*>(&fresh_k[p][2 * lane]) = kr;
+            if (lane == 0) fresh_ks[p] = ks;
             vr[j] = to_stored<KVM>(*reinterpret_cast<const float4*>(v_seq + t * tok_stride + 4 * lane), &vsc[j]);
-            live |= 1u << j;
+            v_live |= 1u << j;
         }
     }
     if (c == n_chunks - 1) {  // this chunk holds my_pos: append its rotated key and value
@@ -640,37 +678,50 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
             }
         }
     }
-    __syncthreads();  // the rotated queries are visible to the CTA
+    __syncthreads();  // the rotated queries and the staged key rows are visible to the CTA
     {
+        if (kp < np && p0 + kp >= pos && kv_row<KVM>(kv, seq, kvh, n_kv, p0 + kp) >= 0) {
+            const uint4* src = reinterpret_cast<const uint4*>(&fresh_k[kp][qd * KW]);
 #pragma unroll
-        for (int j = 0; j < PW; ++j) {
-            const int p = warp + j * kAttnWarps;
-            const bool ok = ((live >> j) & 1u) != 0;
-            const float4 kf = KL::value(kr[j]);
-            float d[G];
+            for (int w = 0; w < KW / 4; ++w) kq[w] = src[w];
+            kscale = fresh_ks[kp];
+            k_live = true;
+        }
+        const uint32_t* kw = reinterpret_cast<const uint32_t*>(kq);
+        float d[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) d[g] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < QD / 4; ++i) {  // elements 4i .. 4i+3 of the quarter
+            float4 x;
+            if constexpr (Q8) {
+                const uint32_t r = kw[i];
+                x = make_float4(static_cast<float>(static_cast<int8_t>(r & 0xFFu)),
+                                static_cast<float>(static_cast<int8_t>((r >> 8) & 0xFFu)),
+                                static_cast<float>(static_cast<int8_t>((r >> 16) & 0xFFu)),
+                                static_cast<float>(static_cast<int8_t>(r >> 24)));
+            } else {
+                const uint32_t r0 = kw[2 * i], r1 = kw[2 * i + 1];
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r0));
+                const float2 bb = __half22float2(*reinterpret_cast<const __half2*>(&r1));
+                x = make_float4(a.x, a.y, bb.x, bb.y);
+            }
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-                const float4 qg = *reinterpret_cast<const float4*>(&qs[g][4 * lane]);
-                d[g] = qg.x * kf.x + qg.y * kf.y + qg.z * kf.z + qg.w * kf.w;
+                const float4 qg = *reinterpret_cast<const float4*>(&qs[g][qd][4 * i]);
+                d[g] = fmaf(qg.x, x.x, fmaf(qg.y, x.y, fmaf(qg.z, x.z, fmaf(qg.w, x.w, d[g]))));
             }
+        }
 #pragma unroll
-            for (int o = 16; o; o >>= 1) {
+        for (int g = 0; g < G; ++g) {
+            d[g] += __shfl_xor_sync(0xffffffffu, d[g], 1);
+            d[g] += __shfl_xor_sync(0xffffffffu, d[g], 2);
+            if constexpr (Q8) d[g] *= kscale;
+            if (!k_live) d[g] = kMaskedScore;
+        }
+        if (qd == 0 && kp < np) {
 #pragma unroll
-                for (int g = 0; g < G; ++g) d[g] += __shfl_xor_sync(0xffffffffu, d[g], o);
-            }
-            if constexpr (Q8) {
-#pragma unroll
-                for (int g = 0; g < G; ++g) d[g] *= ksc[j];
-            }
-            if (!ok) {
-#pragma unroll
-                for (int g = 0; g < G; ++g) d[g] = kMaskedScore;
-            }
-            if (p < np) {
-#pragma unroll
-                for (int g = 0; g < G; ++g)
-                    if (lane == g) sc[g][p] = d[g];
-            }
+            for (int g = 0; g < G; ++g) sc[g][kp] = d[g];
         }
     }
     __syncthreads();
@@ -729,17 +780,22 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
             rec[kHeadDim + 1] = ml[g][1];
         }
     }
-    __threadfence();
+    // Release the records (the barrier orders the CTA's stores before the
+    // fence of the thread that publishes them), then count the arrival.
     __syncthreads();
-    if (threadIdx.x == 0) is_last = atomicAdd(counters + b * n_kv + kvh, 1) == n_chunks - 1;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        is_last = atomicAdd(counters + b * n_kv + kvh, 1) == n_chunks - 1;
+    }
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    // Merge: warp g < G takes query head g; lanes first read the chunks'
-    // maxima and exp-sums (lane j: chunks j, j + 32, ...), then the lanes
-    // hold 4 output dims each and sweep the chunk records, 8 loads in flight.
-    if (threadIdx.x < 32 * G) {
-        const int g = warp;
+    // Merge: S = kAttnWarps / G warps per query head g, warp s of a head
+    // taking chunks s, s + S, ...; each lane holds 4 output dims. All warps
+    // first find the heads' maximum over the chunks' maxima.
+    {
+        constexpr int S = kAttnWarps / G;
+        const int g = warp % G, s = warp / G;
         const float* rec = part + static_cast<long long>(g) * n_chunks * kPartStride;
         float M = -INFINITY;
         for (int cc = lane; cc < n_chunks; cc += 32) M = fmaxf(M, __ldcg(rec + cc * kPartStride + kHeadDim));
@@ -747,31 +803,44 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
         for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         float L = 0.0f;
         float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        for (int c0 = 0; c0 < n_chunks; c0 += 32) {
-            const int cc = c0 + lane;
-            const float w_lane = cc < n_chunks ? expf(__ldcg(rec + cc * kPartStride + kHeadDim) - M) : 0.0f;
-            if (cc < n_chunks) L = fmaf(__ldcg(rec + cc * kPartStride + kHeadDim + 1), w_lane, L);
-            const int nt = min(32, n_chunks - c0);
 #pragma unroll 8
-            for (int t = 0; t < nt; ++t) {
-                const float w = __shfl_sync(0xffffffffu, w_lane, t);
-                const float* r = rec + (c0 + t) * kPartStride + 4 * lane;
-                a.x = fmaf(__ldcg(r), w, a.x);
-                a.y = fmaf(__ldcg(r + 1), w, a.y);
-                a.z = fmaf(__ldcg(r + 2), w, a.z);
-                a.w = fmaf(__ldcg(r + 3), w, a.w);
+        for (int cc = s; cc < n_chunks; cc += S) {
+            const float* r = rec + cc * kPartStride;
+            const float w = expf(__ldcg(r + kHeadDim) - M);
+            L = fmaf(__ldcg(r + kHeadDim + 1), w, L);
+            const float4 x = __ldcg(reinterpret_cast<const float4*>(r + 4 * lane));
+            a.x = fmaf(x.x, w, a.x);
+            a.y = fmaf(x.y, w, a.y);
+            a.z = fmaf(x.z, w, a.z);
+            a.w = fmaf(x.w, w, a.w);
+        }
+        if constexpr (S > 1) {
+            *reinterpret_cast<float4*>(&red[warp][4 * lane]) = a;
+            if (lane == 0) merge_l[warp] = L;
+            __syncthreads();
+            if (s == 0) {
+#pragma unroll
+                for (int t = 1; t < S; ++t) {
+                    const float4 y = *reinterpret_cast<const float4*>(&red[warp + t * G][4 * lane]);
+                    a.x += y.x;
+                    a.y += y.y;
+                    a.z += y.z;
+                    a.w += y.w;
+                    L += merge_l[warp + t * G];
+                }
             }
         }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-        const float4 res = make_float4(a.x / L, a.y / L, a.z / L, a.w / L);
-        const int head = kvh * G + g;
-        if (out)
-            *reinterpret_cast<float4*>(out + (static_cast<long long>(b) * n_heads + head) * kHeadDim + 4 * lane) = res;
-        if constexpr (DIG > 0) {
-            const int kk = n_heads * kHeadDim;
-            quantize_quad<DIG>(res, true, xq + static_cast<long long>(b) * xq_row_bytes(kk, DIG), kk,
-                               head * (kHeadDim / 4) + lane);
+        if (s == 0) {
+            const float4 res = make_float4(a.x / L, a.y / L, a.z / L, a.w / L);
+            const int head = kvh * G + g;
+            if (out)
+                *reinterpret_cast<float4*>(out + (static_cast<long long>(b) * n_heads + head) * kHeadDim + 4 * lane) =
+                    res;
+            if constexpr (DIG > 0) {
+                const int kk = n_heads * kHeadDim;
+                quantize_quad<DIG>(res, true, xq + static_cast<long long>(b) * xq_row_bytes(kk, DIG), kk,
+                                   head * (kHeadDim / 4) + lane);
+            }
         }
     }
     if (threadIdx.x == 0) counters[b * n_kv + kvh] = 0;  // ready for the next launch
@@ -958,7 +1027,7 @@ int launch_rope_attention(const float* q, const float* k, const float* v, int ba
                           int act_mode, Device* dev, cudaStream_t st) {
     if (!kc || !vc || max_ctx <= 0 || n_tok <= 0) return B200Q_EINVAL;
     if (static_cast<long long>(pos) + n_tok > max_ctx) return B200Q_ESHAPE;
-    if ((reinterpret_cast<uintptr_t>(kc) & 7u) || (reinterpret_cast<uintptr_t>(vc) & 7u)) return B200Q_EALIGN;
+    if (!aligned16(kc) || !aligned16(vc)) return B200Q_EALIGN;  // key rows are read 16 bytes a lane
     KvArgs kv{};
     kv.k = kc;
     kv.v = vc;
@@ -976,8 +1045,7 @@ int launch_rope_attention_paged(const float* q, const float* k, const float* v, 
         pages_per_seq <= 0 || n_tok <= 0 || (q8 && (!k_scales || !v_scales)))
         return B200Q_EINVAL;
     if (static_cast<long long>(pos) + n_tok > static_cast<long long>(pages_per_seq) * page_size) return B200Q_ESHAPE;
-    const uintptr_t row_align = q8 ? 3u : 7u;  // int8 rows read 4 bytes a lane, fp16 rows 8
-    if ((reinterpret_cast<uintptr_t>(k_pages) & row_align) || (reinterpret_cast<uintptr_t>(v_pages) & row_align) ||
+    if (!aligned16(k_pages) || !aligned16(v_pages) ||  // key rows are read 16 bytes a lane
         (reinterpret_cast<uintptr_t>(page_table) & 3u) ||
         (q8 && ((reinterpret_cast<uintptr_t>(k_scales) & 3u) || (reinterpret_cast<uintptr_t>(v_scales) & 3u))))
         return B200Q_EALIGN;

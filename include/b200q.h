@@ -285,8 +285,9 @@ B200Q_API int b200q_attention_decode_q(const float* q, const void* k_cache, cons
  * b200q_attention_decode with ctx_len = pos + 1). out (may be NULL when xq
  * is given) receives [batch][n_heads][head_dim]; xq (may be NULL) the codes
  * of the same rows (act_mode B200Q_ACT_X8 / X16). head_dim == 128,
- * n_heads / n_kv_heads in {1, 2, 4, 8}. Replaces the MG:1222-1323 RoPE and
- * the attention after it in the decode step. */
+ * n_heads / n_kv_heads in {1, 2, 4, 8}; q, k, v, the caches, out and xq
+ * 16-byte aligned. Replaces the MG:1222-1323 RoPE and the attention after it
+ * in the decode step. */
 B200Q_API int b200q_rope_attention_decode(const float* q, const float* k, const float* v, int batch, int n_heads,
                                           int n_kv_heads, int head_dim, int pos, float theta, void* k_cache,
                                           void* v_cache, int max_ctx, float* out, void* xq, int act_mode,
@@ -322,8 +323,8 @@ B200Q_API int b200q_rope_attention_decode_tokens(const float* q, const float* k,
  * dot(q, codes) * scale and values enter as softmax weight * scale * codes,
  * as the reference computes them. A slot outside [0, n_slots) in the table,
  * or no page at pos, is recorded as device status bit 2 (value 2) and the
- * position is masked. pos + n_tokens <= pages_per_seq * page_size; pools 8-byte (fp16)
- * or 4-byte (Q8) aligned. n_tokens consecutive tokens per sequence as in
+ * position is masked. pos + n_tokens <= pages_per_seq * page_size; pools 16-byte
+ * aligned. n_tokens consecutive tokens per sequence as in
  * b200q_rope_attention_decode_tokens (1 for a decode step); the pages of
  * pos .. pos + n_tokens - 1 assigned before the call. */
 B200Q_API int b200q_rope_attention_decode_paged(const float* q, const float* k, const float* v, int batch,
