@@ -572,8 +572,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
     constexpr int QPAD = QD + 4;  // query quarters padded so the 4 quarters fall on distinct banks
     // 16-byte aligned: qs, red and the staged rows are accessed as float4 / uint4.
     __shared__ __align__(16) float qs[G][4][QPAD];
-    __shared__ __align__(16) float sc[G][kAttnChunk];
-    __shared__ __align__(16) float ml[G][2];
+    __shared__ float ml[kAttnWarps][G][2];  // per warp and head: max, exp-sum
     // red (after the PV phase) shares its storage with the key rows this
     // launch writes (read in the score phase only).
     constexpr int kRedBytes = kAttnWarps * G * kHeadDim * 4;
@@ -679,6 +678,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
         }
     }
     __syncthreads();  // the rotated queries and the staged key rows are visible to the CTA
+    // Scores: lane group l / 4 holds the G dot products of its position;
+    // positions past the context score -inf (excluded), positions without a
+    // page kMaskedScore (counted, as in the reference).
+    float d[G];
     {
         if (kp < np && p0 + kp >= pos && kv_row<KVM>(kv, seq, kvh, n_kv, p0 + kp) >= 0) {
             const uint4* src = reinterpret_cast<const uint4*>(&fresh_k[kp][qd * KW]);
@@ -688,7 +691,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
             k_live = true;
         }
         const uint32_t* kw = reinterpret_cast<const uint32_t*>(kq);
-        float d[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) d[g] = 0.0f;
 #pragma unroll
@@ -718,49 +720,47 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
             d[g] += __shfl_xor_sync(0xffffffffu, d[g], 2);
             if constexpr (Q8) d[g] *= kscale;
             if (!k_live) d[g] = kMaskedScore;
-        }
-        if (qd == 0 && kp < np) {
-#pragma unroll
-            for (int g = 0; g < G; ++g) sc[g][kp] = d[g];
+            if (kp >= np) d[g] = -INFINITY;
         }
     }
-    __syncthreads();
-    for (int g = warp; g < G; g += kAttnWarps) {  // chunk max and exp-sum per query head
-        float m = -INFINITY;
-        for (int p = lane; p < np; p += 32) m = fmaxf(m, sc[g][p]);
+    // Chunk softmax: each warp's maximum over its PW positions (lane groups
+    // differ in lane bits 2..4), one barrier, the chunk maximum from the
+    // warps' maxima; then each warp's exp-weighted values.
 #pragma unroll
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float l = 0.0f;
-        for (int p = lane; p < np; p += 32) {
-            const float e = expf(sc[g][p] - m);
-            sc[g][p] = e;
-            l += e;
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        if (lane == 0) {
-            ml[g][0] = m;
-            ml[g][1] = l;
-        }
+    for (int g = 0; g < G; ++g) {
+        float m = d[g];
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        if (lane == 0) ml[warp][g][0] = m;  // -inf only when none of the warp's positions is in the context
     }
     __syncthreads();
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        float m = ml[0][g][0];  // the chunk maximum (position 0 of a chunk is always in the context)
+#pragma unroll
+        for (int w = 1; w < kAttnWarps; ++w) m = fmaxf(m, ml[w][g][0]);
+        d[g] = d[g] == -INFINITY ? 0.0f : expf(d[g] - m);
+        float l = d[g];
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        if (lane == 0) ml[warp][g][1] = l;
+    }
     float acc[G][4];
 #pragma unroll
     for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0f;
-    {
 #pragma unroll
-        for (int j = 0; j < PW; ++j) {
-            const int p = warp + j * kAttnWarps;
-            const float4 vf = KL::value(vr[j]);  // zero without a row
+    for (int j = 0; j < PW; ++j) {
+        const float4 vf = KL::value(vr[j]);  // zero without a row
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float e = p < np ? sc[g][p] : 0.0f;
-                if constexpr (Q8) e *= vsc[j];
-                acc[g][0] = fmaf(e, vf.x, acc[g][0]);
-                acc[g][1] = fmaf(e, vf.y, acc[g][1]);
-                acc[g][2] = fmaf(e, vf.z, acc[g][2]);
-                acc[g][3] = fmaf(e, vf.w, acc[g][3]);
-            }
+        for (int g = 0; g < G; ++g) {
+            float e = __shfl_sync(0xffffffffu, d[g], 4 * j);  // slot j's weight
+            if constexpr (Q8) e *= vsc[j];
+            acc[g][0] = fmaf(e, vf.x, acc[g][0]);
+            acc[g][1] = fmaf(e, vf.y, acc[g][1]);
+            acc[g][2] = fmaf(e, vf.z, acc[g][2]);
+            acc[g][3] = fmaf(e, vf.w, acc[g][3]);
         }
     }
 #pragma unroll
@@ -768,51 +768,86 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
         *reinterpret_cast<float4*>(&red[warp][g * kHeadDim + 4 * lane]) =
             make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
     __syncthreads();
+    // The chunk's record per query head: the warps' sums.
     for (int i = threadIdx.x; i < G * kHeadDim; i += blockDim.x) {
+        const int g = i / kHeadDim, dd = i - g * kHeadDim;
         float o = 0.0f;
 #pragma unroll
         for (int w = 0; w < kAttnWarps; ++w) o += red[w][i];
-        const int g = i / kHeadDim, d = i - g * kHeadDim;
         float* rec = part + (static_cast<long long>(g) * n_chunks + c) * kPartStride;
-        rec[d] = o;
-        if (d == 0) {
-            rec[kHeadDim] = ml[g][0];
-            rec[kHeadDim + 1] = ml[g][1];
+        rec[dd] = o;
+        if (dd == 0) {
+            float m = ml[0][g][0], l = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kAttnWarps; ++w) {
+                m = fmaxf(m, ml[w][g][0]);
+                l += ml[w][g][1];
+            }
+            rec[kHeadDim] = m;
+            rec[kHeadDim + 1] = l;
         }
     }
     // Release the records (the barrier orders the CTA's stores before the
-    // fence of the thread that publishes them), then count the arrival.
+    // releasing atomic of thread 0) and count the arrival; the last CTA's
+    // thread 0 acquires the other CTAs' records the same way.
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
-        is_last = atomicAdd(counters + b * n_kv + kvh, 1) == n_chunks - 1;
+        int prev;
+        asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;"
+                     : "=r"(prev)
+                     : "l"(counters + b * n_kv + kvh)
+                     : "memory");
+        is_last = prev == n_chunks - 1;
     }
     __syncthreads();
     if (!is_last) return;
-    __threadfence();
     // Merge: S = kAttnWarps / G warps per query head g, warp s of a head
-    // taking chunks s, s + S, ...; each lane holds 4 output dims. All warps
-    // first find the heads' maximum over the chunks' maxima.
+    // taking chunks s, s + S, ...; each lane holds 4 output dims. The first
+    // 16 of a warp's records are loaded together with the chunk maxima.
     {
         constexpr int S = kAttnWarps / G;
+        constexpr int B8 = 16;
         const int g = warp % G, s = warp / G;
         const float* rec = part + static_cast<long long>(g) * n_chunks * kPartStride;
+        float4 x[B8];
+        float2 mlc[B8];
+#pragma unroll
+        for (int t = 0; t < B8; ++t) {
+            const int cc = s + t * S;
+            x[t] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            mlc[t] = make_float2(-INFINITY, 0.0f);
+            if (cc < n_chunks) {
+                const float* r = rec + cc * kPartStride;
+                x[t] = __ldcg(reinterpret_cast<const float4*>(r + 4 * lane));
+                mlc[t] = __ldcg(reinterpret_cast<const float2*>(r + kHeadDim));
+            }
+        }
         float M = -INFINITY;
         for (int cc = lane; cc < n_chunks; cc += 32) M = fmaxf(M, __ldcg(rec + cc * kPartStride + kHeadDim));
 #pragma unroll
         for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         float L = 0.0f;
         float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int t = 0; t < B8; ++t) {
+            const float w = mlc[t].x == -INFINITY ? 0.0f : expf(mlc[t].x - M);
+            L = fmaf(mlc[t].y, w, L);
+            a.x = fmaf(x[t].x, w, a.x);
+            a.y = fmaf(x[t].y, w, a.y);
+            a.z = fmaf(x[t].z, w, a.z);
+            a.w = fmaf(x[t].w, w, a.w);
+        }
 #pragma unroll 8
-        for (int cc = s; cc < n_chunks; cc += S) {
+        for (int cc = s + B8 * S; cc < n_chunks; cc += S) {
             const float* r = rec + cc * kPartStride;
-            const float w = expf(__ldcg(r + kHeadDim) - M);
-            L = fmaf(__ldcg(r + kHeadDim + 1), w, L);
-            const float4 x = __ldcg(reinterpret_cast<const float4*>(r + 4 * lane));
-            a.x = fmaf(x.x, w, a.x);
-            a.y = fmaf(x.y, w, a.y);
-            a.z = fmaf(x.z, w, a.z);
-            a.w = fmaf(x.w, w, a.w);
+            const float2 m2 = __ldcg(reinterpret_cast<const float2*>(r + kHeadDim));
+            const float4 y = __ldcg(reinterpret_cast<const float4*>(r + 4 * lane));
+            const float w = expf(m2.x - M);
+            L = fmaf(m2.y, w, L);
+            a.x = fmaf(y.x, w, a.x);
+            a.y = fmaf(y.y, w, a.y);
+            a.z = fmaf(y.z, w, a.z);
+            a.w = fmaf(y.w, w, a.w);
         }
         if constexpr (S > 1) {
             *reinterpret_cast<float4*>(&red[warp][4 * lane]) = a;
