@@ -511,6 +511,36 @@ def decode_bench(dev, steps: int, warmup: int, shape_name: str = "llama3_8b", ct
         torch.cuda.synchronize(dev)
         res[name] = e0.elapsed_time(e1) / steps
         del g
+    # Batched speculative verify (DecodeStack.verify): m drafted tokens in one
+    # pass over the weights (m-row linears: GEMV below 8 rows, tcgen05 tile
+    # kernel from 8), against m single-token steps.
+    verify = []
+    for m in (4, 8):
+        toks = torch.full((m,), 128000 % shape.vocab, dtype=torch.int32, device=dev)
+        pos0 = ctx - m
+        cap = torch.cuda.Stream(dev)
+        with torch.cuda.stream(cap):
+            for _ in range(max(3, warmup)):
+                stack.verify(toks, pos0)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            stack.verify(toks, pos0)
+        for _ in range(3):
+            g.replay()
+        st = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record(st)
+        for _ in range(steps):
+            g.replay()
+        e1.record(st)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / steps
+        del g
+        verify.append({"m": m, "ms_per_pass": round(ms, 4), "ms_as_single_steps": round(m * res["step"], 4),
+                       "tokens_checked_per_s": round(m * 1e3 / ms, 1),
+                       "speedup_vs_single_steps": round(m * res["step"] / ms, 2)})
     peak, _ = _peak_hbm()
     wbytes = shape.token_weight_bytes()
     kv_bytes = 2 * shape.layers * shape.kv_heads * ctx * shape.head_dim * 2
@@ -526,10 +556,82 @@ def decode_bench(dev, steps: int, warmup: int, shape_name: str = "llama3_8b", ct
         "matvec_hbm_frac": round(wbytes / (res["linears"] * 1e-3) / 1e9 / peak, 4),
         "step_hbm_frac": round((wbytes + kv_bytes) / (res["step"] * 1e-3) / 1e9 / peak, 4),
         "act_mode": "x16",
+        "verify": verify,
         "cpu_baseline": cpu,
     }
     del stack
     torch.cuda.empty_cache()
+    return out
+
+
+def attention_bench(dev, steps: int, warmup: int, ctx: int = 2048):
+    """The fused RoPE + KV-append + attention launch of the Llama-3-8B step
+    (32 query / 8 kv heads, head_dim 128, batch 1) at context `ctx`, over
+    the contiguous fp16 cache and the Q8 paged cache: 32 launches (one cache
+    per layer, 32 x the KV bytes > L2) chained with PDL in one CUDA graph.
+    Algorithmic bytes per launch: the cached K and V rows read
+    (2 x 8 x ctx x 128 x 2 B fp16; 1 B + 4 B scale per row in Q8)."""
+    import torch
+
+    from cybel_b200 import _native
+    from cybel_b200.kv_cache import PagedKVCache
+
+    L = _native.lib()
+    H, KV, HD, layers, pos = 32, 8, 128, 32, ctx - 1
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(H * HD, device=dev, generator=g)
+    k = torch.randn(KV * HD, device=dev, generator=g)
+    v = torch.randn(KV * HD, device=dev, generator=g)
+    xq = torch.zeros(int(L.b200q_xq_row_bytes(H * HD, _native.ACT_X16)), dtype=torch.uint8, device=dev)
+    peak, _ = _peak_hbm()
+    out = []
+    for kind in ("fp16_contiguous", "q8_paged"):
+        if kind == "fp16_contiguous":
+            kc = torch.randn((layers, KV, ctx, HD), device=dev, generator=g).half()
+            vc = torch.randn((layers, KV, ctx, HD), device=dev, generator=g).half()
+
+            def launch(i, st):
+                _native.check(L.b200q_rope_attention_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, H, KV, HD,
+                                                            pos, 5e5, kc[i].data_ptr(), vc[i].data_ptr(), ctx, None,
+                                                            xq.data_ptr(), _native.ACT_X16, st), "attention")
+            kv_bytes = 2 * KV * ctx * HD * 2
+        else:
+            cache = PagedKVCache(layers, KV, ctx, batch=1, q8=True, device=dev.index or 0)
+            cache.ensure(0, pos)
+            cache.k.copy_(torch.randint(-127, 128, cache.k.shape, device=dev, generator=g, dtype=torch.int32))
+            cache.v.copy_(torch.randint(-127, 128, cache.v.shape, device=dev, generator=g, dtype=torch.int32))
+            cache.ks.fill_(0.01)
+            cache.vs.fill_(0.01)
+
+            def launch(i, st):
+                cache.attention(i, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos, H, 5e5, None, xq.data_ptr(),
+                                _native.ACT_X16, st)
+            kv_bytes = 2 * KV * ctx * (HD + 4)
+        cap = torch.cuda.Stream(dev)
+        with torch.cuda.stream(cap):
+            for _ in range(max(1, warmup)):
+                for i in range(layers):
+                    launch(i, cap.cuda_stream)
+        torch.cuda.synchronize(dev)
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=cap):
+            for i in range(layers):
+                launch(i, cap.cuda_stream)
+        for _ in range(3):
+            gr.replay()
+        st = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record(st)
+        for _ in range(steps):
+            gr.replay()
+        e1.record(st)
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1e3 / (steps * layers)
+        _native.check_device(dev.index or 0, "attention bench")
+        del gr
+        out.append({"cache": kind, "ctx": ctx, "us_per_launch": round(us, 2), "kv_bytes_per_launch": kv_bytes,
+                    "kv_gbs": round(kv_bytes / us / 1e3, 1), "hbm_frac": round(kv_bytes / us / 1e3 / peak, 4)})
     return out
 
 
@@ -666,6 +768,17 @@ def run_decode_only(args, ws, rank, local):
     rec = decode_bench(dev, args.steps, args.warmup, args.decode_shape, args.ctx)
     if rank == 0:
         print(json.dumps({"impl": "ours", **rec}), flush=True)
+
+
+def run_attention_only(args, ws, rank, local):
+    """`--workload attention`: the fused decode attention alone, one JSON line."""
+    import torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    recs = attention_bench(dev, args.steps, args.warmup, ctx=args.ctx)
+    if rank == 0:
+        print(json.dumps({"workload": "llama3_8b_decode_attention", "impl": "ours", "cases": recs}), flush=True)
 
 
 def run_tile_only(args, ws, rank, local):
@@ -832,9 +945,10 @@ def run_ours(args, ws, rank, local):
     tile = None
     if ws == 1 and not args.no_tile:
         tile = tile_bench(dev, max(10, args.steps // 2), args.warmup, no_cpu=no_cpu)
-    decode = None
+    decode = attention = None
     if ws == 1 and not args.no_decode:
         decode = decode_bench(dev, max(10, args.steps // 2), args.warmup, no_cpu=no_cpu)
+        attention = attention_bench(dev, max(10, args.steps // 2), args.warmup)
     sharded = sharded8 = None
     if not args.no_decode:
         sharded = sharded_decode_bench(dev, ws, rank, local, 10, args.warmup, 1, 2048, "llama3_70b", "peer",
@@ -892,6 +1006,7 @@ def run_ours(args, ws, rank, local):
             "c2_sweep": c2,
             "tile": tile,
             "decode": decode,
+            "attention": attention,
             "sharded_decode": sharded,
             "sharded_decode_b8": sharded8,
         }
@@ -914,7 +1029,7 @@ def main():
     ap.add_argument("--no-tile", action="store_true", help="skip the tile-path (batched matmul) summary")
     ap.add_argument("--no-decode", action="store_true", help="skip the Llama-3-8B / 70B decode-step summaries")
     ap.add_argument("--no-sweep", action="store_true", help="skip the Q4_0 and Q8_0/Q4_K shape-sweep records")
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "tile", "decode", "sharded"])
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "tile", "decode", "sharded", "attention"])
     ap.add_argument("--decode-shape", default=None, choices=["llama3_8b", "llama3_70b"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--collective", default="peer", choices=["peer", "nccl"])
@@ -939,6 +1054,9 @@ def main():
     if args.workload == "sharded":
         args.decode_shape = args.decode_shape or "llama3_70b"
         run_sharded_only(args, ws, rank, local)
+        return
+    if args.workload == "attention":
+        run_attention_only(args, ws, rank, local)
         return
     run_ours(args, ws, rank, local)
 

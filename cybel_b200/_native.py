@@ -16,6 +16,7 @@ ACT_X8 = 1
 ACT_X16 = 2
 ACT_F16 = 3  # tile path (tcgen05, fp16 operands), Q4_K, device entry points
 WEIGHTS_STATIC = 1
+TILE_FROM_2 = 2  # Q4_K batches of 2-7 rows on the tile kernel too
 
 STATUS = {
     0: "ok",

@@ -424,11 +424,12 @@ int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev) {
 // kernel streams W once for the whole batch: x8 with fp16 activations (more
 // accurate than int8 codes), x16 with the precise variant (fp16 activations
 // plus their fp16 rounding residues, within the x16 accuracy).
-int uses_tile_path(int qtype, int act_mode, int m) {
+int uses_tile_path(int qtype, int act_mode, int m, int flags) {
     static const int min_m = env_int("B200Q_TILE_MIN_M", 8);
     if (qtype != QT_Q4_K) return 0;
     if (act_mode == B200Q_ACT_F16) return 1;
-    if (min_m <= 0 || m < min_m) return 0;
+    const int from = (flags & B200Q_TILE_FROM_2) ? 2 : min_m;
+    if (from <= 0 || m < from) return 0;
     if (act_mode == B200Q_ACT_X8) return 1;
     if (act_mode == B200Q_ACT_X16) return 2;
     return 0;
@@ -441,7 +442,7 @@ int launch_gemv(int qtype, int act_mode, const void* w, const float* x, float* y
     if ((reinterpret_cast<uintptr_t>(w) & 15u) || (reinterpret_cast<uintptr_t>(x) & 15u) || (x_stride & 3))
         return B200Q_EALIGN;
     if (isums && m != 1) return B200Q_EINVAL;
-    const int tile = isums ? 0 : uses_tile_path(qtype, act_mode, m);
+    const int tile = isums ? 0 : uses_tile_path(qtype, act_mode, m, flags);
     if (tile) {
         // Batches of up to tile_max_rows activation rows per tile-kernel call.
         const int step = tile_max_rows(tile == 2);

@@ -95,9 +95,9 @@ int launch_tile(int qtype, const void* w, const float* x, long long x_stride, fl
                 long long y_stride, Device* dev, cudaStream_t st, bool pdl, bool precise);
 // Kernel launches one launch_tile call issues (3 or 4).
 int tile_kernel_launches(int k, int n, long long y_stride, int num_sms);
-// Whether launch_gemv hands (qtype, act_mode, m) to the tile path: 0 no,
-// 1 the fp16 variant, 2 the precise variant.
-int uses_tile_path(int qtype, int act_mode, int m);
+// Whether launch_gemv hands (qtype, act_mode, m, flags) to the tile path:
+// 0 no, 1 the fp16 variant, 2 the precise variant.
+int uses_tile_path(int qtype, int act_mode, int m, int flags);
 
 // Decode-step glue (decode.cu).
 constexpr int kScratchAttn = 6;     // attention chunk partials

@@ -322,8 +322,9 @@ class DecodeStack:
         This is the batched form of the reference's speculative verify, which
         asks the engine for the logits of each drafted prefix in turn
         (cpu_speculative_decode.py:740-769): every quantized linear runs once
-        over the m rows (b200q_matmul_ex: the GEMV below 8 rows, the tcgen05
-        tile kernel for Q4_K from 8 rows), and one attention launch per layer
+        over the m rows (b200q_matmul_ex with B200Q_TILE_FROM_2: the tcgen05
+        tile kernel for Q4_K from 2 rows, the GEMV for the other qtypes),
+        and one attention launch per layer
         appends the m keys/values and attends causally
         (b200q_rope_attention_decode_tokens / the paged form). The cache then
         holds all m tokens; positions past the accepted prefix are simply
@@ -337,10 +338,13 @@ class DecodeStack:
             raise ValueError("positions outside the KV cache")
         s, L = self.shape, self.lib
         st = torch.cuda.current_stream(self.dev).cuda_stream
-        act, W = self.act_mode, _native.WEIGHTS_STATIC
+        act, W = self.act_mode, _native.WEIGHTS_STATIC | _native.TILE_FROM_2
         h, kv, hd, f = s.hidden, s.kv_dim, s.head_dim, s.ffn
         B = self._verify_buffers(m)
-        B["tok"].copy_(torch.tensor([int(t) for t in tokens], dtype=torch.int32))
+        if isinstance(tokens, torch.Tensor) and tokens.is_cuda:  # already on the device (graph capture)
+            B["tok"].copy_(tokens.to(torch.int32))
+        else:
+            B["tok"].copy_(torch.tensor([int(t) for t in tokens], dtype=torch.int32))
         if self.kv_cache is not None:
             self.kv_cache.ensure(pos0, pos0 + m - 1)
         P = {name: t.data_ptr() for name, t in B.items()}

@@ -158,6 +158,11 @@ B200Q_API int b200q_matmul(int qtype, int act_mode, const float* x, const void* 
  * then starts streaming weights while the preceding kernel drains, and only
  * waits for it before reading x and writing y. */
 #define B200Q_WEIGHTS_STATIC 1
+/* B200Q_TILE_FROM_2: Q4_K batches of 2 to 7 rows also take the tile kernel
+ * (by default only 8 rows and more do; below that each launch of the GEMV
+ * carries at most 2 rows in x8 and 1 in x16, so the weights stream once per
+ * 1-2 rows). The batched speculative verify sets it. */
+#define B200Q_TILE_FROM_2 2
 B200Q_API int b200q_matmul_ex(int qtype, int act_mode, const float* x, const void* w, float* y, int m, int k, int n,
                               int flags, void* stream);
 

@@ -1,6 +1,6 @@
 """Batched speculative verify on the device: ``DecodeStack.verify`` (m draft
-tokens in one pass: m-row linears -- the GEMV below 8 rows, the tcgen05 tile
-kernel from 8 rows -- and one causal multi-token attention launch per layer)
+tokens in one pass: m-row linears -- the tcgen05 tile kernel for Q4_K from 2
+rows, the GEMV for the Q6_K head -- and one causal multi-token attention launch per layer)
 against the float64 restatement stepping the same tokens one at a time
 (oracle/decode_ref.py): every row's logits within max |d| / max |ref| <=
 2e-3, for the contiguous fp16 cache and the Q8 paged cache, and a decode

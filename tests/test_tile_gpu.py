@@ -166,3 +166,32 @@ def test_precise_tile_for_x16_batches(oracle_mod, n, k, m):
     exact = O.matvec_f64(W, 12, X, k, n)
     assert O.normalized_error(Y, exact, wn, X) <= NORM_TOL
     assert O.max_rel_error(Y, exact) <= REL_TOL
+
+
+@pytest.mark.parametrize("act", [ACT_X16, ACT_X8])
+@pytest.mark.parametrize("n,k,m", [(300, 2048, 2), (1000, 1536, 3), (4096, 1024, 5), (130, 512, 7)])
+def test_tile_from_two_rows(oracle_mod, n, k, m, act):
+    """B200Q_TILE_FROM_2 sends Q4_K batches of 2-7 rows to the tile kernel
+    (precise variant in x16, fp16 variant in x8), as the batched speculative
+    verify does: the same bounds as the >= 8-row batches."""
+    import torch
+
+    from cybel_b200 import _native
+
+    O = oracle_mod
+    W = _q4k(n, k, seed=n + k + m)
+    X = np.random.default_rng(5 * m + n).standard_normal((m, k)).astype(np.float32)
+    w = torch.from_numpy(W).cuda()
+    x = torch.from_numpy(X).cuda()
+    y = torch.empty((m, n), device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    _native.check(_native.lib().b200q_matmul_ex(12, act, x.data_ptr(), w.data_ptr(), y.data_ptr(), m, k, n,
+                                                _native.TILE_FROM_2, st), "matmul_ex")
+    torch.cuda.synchronize()
+    Y = y.cpu().numpy()
+    wn = O.row_norms(W, 12, k, n)
+    precise = act == ACT_X16
+    assert O.normalized_error(Y, O.tile_matmul(W, 12, X, k, n, precise=precise), wn, X) <= NORM_TOL
+    exact = O.matvec_f64(W, 12, X, k, n)
+    assert O.normalized_error(Y, exact, wn, X) <= (NORM_TOL if precise else TILE_VS_FP32)
+    assert O.max_rel_error(Y, exact) <= REL_TOL
