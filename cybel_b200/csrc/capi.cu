@@ -241,7 +241,25 @@ int act_mode_now() {
     return g_act_mode;
 }
 
-// Host-pointer matmul through the device: the body of every drop-in.
+// The device address of page-locked host memory allocated or registered
+// through CUDA (cudaHostAlloc / cudaMallocHost / cudaHostRegister), else
+// nullptr. Only such memory qualifies: ordinary pageable memory is refused
+// by cudaHostGetFlags even where the device could reach it otherwise.
+void* mapped_host(const void* p) {
+    unsigned int flags = 0;
+    void* d = nullptr;
+    if (cudaHostGetFlags(&flags, const_cast<void*>(p)) != cudaSuccess ||
+        cudaHostGetDevicePointer(&d, const_cast<void*>(p), 0) != cudaSuccess) {
+        cudaGetLastError();  // clear: p is not CUDA page-locked memory
+        return nullptr;
+    }
+    return d;
+}
+
+// Host-pointer matmul through the device: the body of every drop-in. x and
+// y in page-locked host memory are read and written in place by the GPU
+// (a staging kernel for x, the GEMV's own stores for y); pageable buffers go
+// through DMA copies to and from device staging.
 int dropin(int qtype, const float* x, const void* w, float* y, int m, int k, int n) {
     if (!x || !w || !y || m <= 0 || k <= 0 || n <= 0) return B200Q_EINVAL;
     const long long rb = row_bytes_of(qtype, k);
@@ -257,15 +275,22 @@ int dropin(int qtype, const float* x, const void* w, float* y, int m, int k, int
     if (rc != B200Q_OK) return rc;
     rc = ensure_cap(&s->dx, &s->xcap, static_cast<size_t>(m) * k);
     if (rc == B200Q_OK) rc = ensure_cap(&s->dy, &s->ycap, static_cast<size_t>(m) * n);
+    const int act = act_mode_now();
+    const float* x_mapped = static_cast<const float*>(mapped_host(x));
+    // y straight to host memory only on the GEMV route (the tile path's
+    // epilogue and split-K reduction stay on device memory)
+    float* y_mapped = uses_tile_path(qtype, act, m, 0) ? nullptr : static_cast<float*>(mapped_host(y));
     if (rc == B200Q_OK) {
         *dev->status_host = 0;
-        if (cudaMemcpyAsync(s->dx, x, sizeof(float) * m * k, cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
+        if (x_mapped)
+            rc = launch_stage_host_rows(x_mapped, s->dx, static_cast<long long>(m) * k, s->stream);
+        else if (cudaMemcpyAsync(s->dx, x, sizeof(float) * m * k, cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
             rc = B200Q_ECUDA;
     }
     if (rc == B200Q_OK)
-        rc = launch_gemv(qtype, act_mode_now(), dw, s->dx, s->dy, m, k, n, k, n, nullptr, dev, s->stream, pdl_enabled(),
-                         B200Q_WEIGHTS_STATIC);
-    if (rc == B200Q_OK) {
+        rc = launch_gemv(qtype, act, dw, s->dx, y_mapped ? y_mapped : s->dy, m, k, n, k, n, nullptr, dev, s->stream,
+                         pdl_enabled(), B200Q_WEIGHTS_STATIC);
+    if (rc == B200Q_OK && !y_mapped) {
         if (cudaMemcpyAsync(y, s->dy, sizeof(float) * m * n, cudaMemcpyDeviceToHost, s->stream) != cudaSuccess)
             rc = B200Q_ECUDA;
     }

@@ -121,6 +121,10 @@ int launch_rope_attention_paged(const float* q, const float* k, const float* v, 
                                 float* k_scales, float* v_scales, int n_slots, int page_size, const int* page_table,
                                 int pages_per_seq, float* out, void* xq, int act_mode, Device* dev, cudaStream_t st);
 int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaStream_t st);
+// dst[0..n) = src[0..n) from page-locked host memory mapped into the device
+// (src_mapped: its device address), by a kernel that lets a PDL-launched
+// GEMV behind it start streaming weights (ops.cu).
+int launch_stage_host_rows(const float* src_mapped, float* dst, long long n, cudaStream_t st);
 int launch_unshard_rows(const float* in, float* out, int shards, int rows, int cols, cudaStream_t st);
 
 // Peer-memory all-gather (peer.cu).

@@ -293,6 +293,37 @@ __global__ void __launch_bounds__(256) b200q_matvec_f32_kernel(const float* __re
 
 }  // namespace
 
+namespace {
+
+// dst[0..n) = src[0..n) where src is page-locked host memory mapped into the
+// device's address space: the drop-ins' activation upload without a DMA
+// copy (whose setup costs several microseconds). Launched without the
+// programmatic-launch attribute, so all earlier work on the stream is done;
+// it lets the GEMV launched behind it start at once, which streams its
+// first weight stages while these PCIe reads are in flight and waits for
+// this grid before it reads dst.
+__global__ void b200q_stage_host_rows_kernel(const float* __restrict__ src, float* __restrict__ dst, long long n,
+                                             int vec4) {
+    griddep_launch_dependents();
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (vec4) {
+        if (i < n / 4) reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+    } else if (i < n) {
+        dst[i] = src[i];
+    }
+}
+
+}  // namespace
+
+int launch_stage_host_rows(const float* src_mapped, float* dst, long long n, cudaStream_t st) {
+    if (!src_mapped || !dst || n <= 0) return B200Q_EINVAL;
+    const int vec4 = (n % 4 == 0) && !(reinterpret_cast<uintptr_t>(src_mapped) & 15u) &&
+                     !(reinterpret_cast<uintptr_t>(dst) & 15u);
+    const long long items = vec4 ? n / 4 : n;
+    b200q_stage_host_rows_kernel<<<static_cast<unsigned>((items + 255) / 256), 256, 0, st>>>(src_mapped, dst, n, vec4);
+    return cudaGetLastError() == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
+}
+
 int launch_matvec_f32(const float* W, const float* x, float* y, int rows, int cols, cudaStream_t st) {
     if (!W || !x || !y || rows <= 0 || cols <= 0) return B200Q_EINVAL;
     const int vec4 = (cols % 4 == 0) && !(reinterpret_cast<uintptr_t>(W) & 15u) && !(reinterpret_cast<uintptr_t>(x) & 15u);
