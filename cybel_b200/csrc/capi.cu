@@ -6,6 +6,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
 #include <vector>
 
@@ -256,6 +257,57 @@ void* mapped_host(const void* p) {
     return d;
 }
 
+// Drop-in calls on page-locked buffers replay a CUDA graph of their two
+// launches (staging kernel, GEMV): one launch call instead of two on the
+// host's critical path. Keyed by everything the graph bakes in; a key is
+// captured the second time it is seen (the first call sizes the scratch on
+// the direct path). B200Q_DROPIN_GRAPHS=0 disables.
+using GraphKey = std::tuple<int, int, int, int, int, int, const void*, const void*, const void*, void*>;
+thread_local std::map<GraphKey, cudaGraphExec_t> t_graphs;
+thread_local std::map<GraphKey, int> t_graph_seen;
+constexpr size_t kMaxDropinGraphs = 512;
+
+bool dropin_graphs_enabled() {
+    static const bool on = env_flag("B200Q_DROPIN_GRAPHS", true);
+    return on;
+}
+
+// Launch (or capture and launch) the staged drop-in; returns false when the
+// caller should take the direct path instead.
+bool dropin_graph_launch(const GraphKey& key, Staging* s, int qtype, int act, const void* dw, const float* x_mapped,
+                         float* y_mapped, int m, int k, int n, Device* dev, int* rc) {
+    auto it = t_graphs.find(key);
+    if (it == t_graphs.end()) {
+        if (++t_graph_seen[key] < 2) return false;
+        if (t_graphs.size() >= kMaxDropinGraphs) {
+            for (auto& kv : t_graphs) cudaGraphExecDestroy(kv.second);
+            t_graphs.clear();
+            t_graph_seen.clear();
+        }
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        int r = launch_stage_host_rows(x_mapped, s->dx, static_cast<long long>(m) * k, s->stream);
+        if (r == B200Q_OK)
+            r = launch_gemv(qtype, act, dw, s->dx, y_mapped, m, k, n, k, n, nullptr, dev, s->stream, pdl_enabled(),
+                            B200Q_WEIGHTS_STATIC);
+        const bool ended = cudaStreamEndCapture(s->stream, &g) == cudaSuccess;
+        cudaGraphExec_t ex = nullptr;
+        if (r == B200Q_OK && ended && g && cudaGraphInstantiate(&ex, g, 0) != cudaSuccess) ex = nullptr;
+        if (g) cudaGraphDestroy(g);
+        if (!ex) {
+            cudaGetLastError();
+            t_graph_seen[key] = -1000000;  // this key stays on the direct path
+            return false;
+        }
+        it = t_graphs.emplace(key, ex).first;
+    }
+    *rc = cudaGraphLaunch(it->second, s->stream) == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
+    return true;
+}
+
 // Host-pointer matmul through the device: the body of every drop-in. x and
 // y in page-locked host memory are read and written in place by the GPU
 // (a staging kernel for x, the GEMV's own stores for y); pageable buffers go
@@ -280,14 +332,22 @@ int dropin(int qtype, const float* x, const void* w, float* y, int m, int k, int
     // y straight to host memory only on the GEMV route (the tile path's
     // epilogue and split-K reduction stay on device memory)
     float* y_mapped = uses_tile_path(qtype, act, m, 0) ? nullptr : static_cast<float*>(mapped_host(y));
+    bool launched = false;
     if (rc == B200Q_OK) {
         *dev->status_host = 0;
-        if (x_mapped)
-            rc = launch_stage_host_rows(x_mapped, s->dx, static_cast<long long>(m) * k, s->stream);
-        else if (cudaMemcpyAsync(s->dx, x, sizeof(float) * m * k, cudaMemcpyHostToDevice, s->stream) != cudaSuccess)
-            rc = B200Q_ECUDA;
+        if (x_mapped && y_mapped && !temporary && dropin_graphs_enabled()) {
+            const GraphKey key(dev->id, qtype, act, m, k, n, dw, x_mapped, s->dx, y_mapped);
+            launched = dropin_graph_launch(key, s, qtype, act, dw, x_mapped, y_mapped, m, k, n, dev, &rc);
+        }
+        if (!launched) {
+            if (x_mapped)
+                rc = launch_stage_host_rows(x_mapped, s->dx, static_cast<long long>(m) * k, s->stream);
+            else if (cudaMemcpyAsync(s->dx, x, sizeof(float) * m * k, cudaMemcpyHostToDevice, s->stream) !=
+                     cudaSuccess)
+                rc = B200Q_ECUDA;
+        }
     }
-    if (rc == B200Q_OK)
+    if (rc == B200Q_OK && !launched)
         rc = launch_gemv(qtype, act, dw, s->dx, y_mapped ? y_mapped : s->dy, m, k, n, k, n, nullptr, dev, s->stream,
                          pdl_enabled(), B200Q_WEIGHTS_STATIC);
     if (rc == B200Q_OK && !y_mapped) {
