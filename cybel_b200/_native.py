@@ -83,6 +83,7 @@ SIGNATURES.update(
         "b200q_swiglu_q": ([_vp, _vp, _vp, _i, _i, _vp], _i),
         "b200q_matmul_xq": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _i, _vp], _i),
         "b200q_matmul_norm": ([_i, _i, _vp, _vp, _f, _vp, _vp, _i, _i, _f, _f, _i, _vp], _i),
+        "b200q_matmul_swiglu": ([_i, _i, _vp, _vp, _vp, _vp, _i, _i, _f, _f, _i, _vp], _i),
         "b200q_gemv_plan": ([_i, _i, _i, _i, _i, _i, _i, ctypes.POINTER(ctypes.c_longlong), _i], _i),
         "b200q_ipc_alloc": ([ctypes.c_longlong, ctypes.POINTER(ctypes.c_void_p), _vp], _i),
         "b200q_ipc_open": ([_vp, ctypes.POINTER(ctypes.c_void_p)], _i),

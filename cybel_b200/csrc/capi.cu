@@ -645,6 +645,19 @@ int b200q_matmul_norm(int qtype, int act_mode, const float* x, const float* gamm
     return rc;
 }
 
+int b200q_matmul_swiglu(int qtype, int act_mode, const float* gate, const float* up, const void* w, float* y, int k,
+                        int n, float alpha, float beta, int flags, void* stream) {
+    Device* dev = nullptr;
+    int rc = current_device_state(&dev);
+    if (rc == B200Q_OK && (reinterpret_cast<uintptr_t>(gate) & 15u)) rc = B200Q_EALIGN;
+    if (rc == B200Q_OK) rc = gemv_check_shape(qtype, act_mode, k, n, dev);
+    if (rc == B200Q_OK)
+        rc = gemv_swiglu_f32(qtype, act_mode, w, gate, up, y, k, n, alpha, beta, dev, static_cast<cudaStream_t>(stream),
+                             pdl_enabled(), flags);
+    set_last_error(rc);
+    return rc;
+}
+
 int b200q_swiglu(const float* gate, const float* up, float* out, long long n, void* stream) {
     const int rc = launch_swiglu(gate, up, out, n, static_cast<cudaStream_t>(stream));
     set_last_error(rc);

@@ -322,7 +322,7 @@ namespace {
 int gemv_rows(int qtype, int act_mode, const void* w, const uint8_t* xq, long long xq_row, const float* xf,
               long long xf_stride, float* y, int m, int k, int n, long long y_stride, float alpha, float beta,
               int32_t* isums, Device* dev, cudaStream_t st, bool pdl, int flags, const float* gamma = nullptr,
-              float eps = 0.0f) {
+              float eps = 0.0f, const float* xu = nullptr) {
     if (!w || (!xq && !xf) || !y || m <= 0 || k <= 0 || n <= 0 || !dev) return B200Q_EINVAL;
     if (act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
     if (reinterpret_cast<uintptr_t>(w) & 15u) return B200Q_EALIGN;
@@ -334,7 +334,8 @@ int gemv_rows(int qtype, int act_mode, const void* w, const uint8_t* xq, long lo
         const int left = m - m0;
         const int MR = isums ? 1 : (left >= mr_max ? mr_max : (left >= 2 && mr_max >= 2 ? 2 : 1));
         Plan pl;
-        const int rc = make_plan(qtype, dig, k, n, MR, dev->num_sms, pl, xf != nullptr, gamma != nullptr);
+        // (the planner's extra fp32 row holds the RMSNorm gains or the up row)
+        const int rc = make_plan(qtype, dig, k, n, MR, dev->num_sms, pl, xf != nullptr, gamma != nullptr || xu != nullptr);
         if (rc != B200Q_OK) return rc;
         pl.p.W = static_cast<const uint8_t*>(w);
         pl.dev = dev->id;
@@ -346,6 +347,10 @@ int gemv_rows(int qtype, int act_mode, const void* w, const uint8_t* xq, long lo
                 if (MR != 1 || k > 32 * 32 * pl.p.S * pl.p.WR) return B200Q_ESHAPE;
                 pl.p.gamma = gamma;
                 pl.p.eps = eps;
+            }
+            if (xu) {
+                if (MR != 1 || gamma) return B200Q_EINVAL;
+                pl.p.xu = xu;
             }
         } else {
             pl.p.xq = xq + m0 * xq_row;
@@ -391,6 +396,14 @@ int gemv_norm_f32(int qtype, int act_mode, const void* w, const float* x, const 
     if (!(eps >= 0.0f)) return B200Q_EINVAL;
     return gemv_rows(qtype, act_mode, w, nullptr, 0, x, k, y, 1, k, n, n, alpha, beta, nullptr, dev, st, pdl, flags,
                      gamma, eps);
+}
+
+int gemv_swiglu_f32(int qtype, int act_mode, const void* w, const float* gate, const float* up, float* y, int k, int n,
+                    float alpha, float beta, Device* dev, cudaStream_t st, bool pdl, int flags) {
+    if (!gate || !up) return B200Q_EINVAL;
+    if (reinterpret_cast<uintptr_t>(up) & 15u) return B200Q_EALIGN;
+    return gemv_rows(qtype, act_mode, w, nullptr, 0, gate, k, y, 1, k, n, n, alpha, beta, nullptr, dev, st, pdl, flags,
+                     nullptr, 0.0f, up);
 }
 
 int gemv_plan_info(int qtype, int act_mode, int k, int n, int mr, bool fq, int num_sms, long long* out, int out_len) {

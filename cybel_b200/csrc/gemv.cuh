@@ -54,6 +54,7 @@ struct GemvParams {
     const float* xf;       // [MR] fp32 activation rows, quantized in the kernel (FQ instances)
     long long xf_stride;   // floats between fp32 rows
     const float* gamma;    // FQ with MR == 1: RMSNorm weights; x is normalized before quantizing
+    const float* xu;       // FQ with MR == 1: up row; silu(x) * xu is quantized (SwiGLU inside the GEMV)
     float eps;             // RMSNorm epsilon
     float* y;              // [MR][y_stride] fp32 outputs
     int32_t* dbg;          // optional [n][k/G] integer group sums (MR == 1 only)
@@ -756,7 +757,8 @@ __device__ __forceinline__ void stage_codes(const GemvParams& p, uint8_t* xs, in
 }
 
 // Quantize the fp32 rows staged in shared memory (xf4: MR rows of k, then
-// the RMSNorm gains when `norm`) into the padded code rows at xs, one
+// the RMSNorm gains when `norm`, or the up row when `swiglu`) into the
+// padded code rows at xs, one
 // 32-element group per lane: the arithmetic of quantize_group (amax,
 // iscale = QMAX / amax by IEEE division, one rounded multiply, half-even
 // codes, d = amax / QMAX, the group's code sum), one division each per
@@ -767,8 +769,9 @@ __device__ __forceinline__ void stage_codes(const GemvParams& p, uint8_t* xs, in
 // is first scaled by 1 / sqrt(sum(x^2) / k + eps) and by the gains, the sum
 // of squares reduced per warp into `red` and summed in warp order.
 template <int DIG, int MR>
-__device__ __forceinline__ void quantize_staged_rows(const GemvParams& p, const float4* xf4, bool norm, uint8_t* xs,
-                                                     int xs_row, float* red, int warp, int lane, int nwarps) {
+__device__ __forceinline__ void quantize_staged_rows(const GemvParams& p, const float4* xf4, bool norm, bool swiglu,
+                                                     uint8_t* xs, int xs_row, float* red, int warp, int lane,
+                                                     int nwarps) {
     const int nthreads = nwarps * 32;
     const int kp = xs_plane_bytes(p.k);
     const int groups = p.k >> 5;
@@ -804,6 +807,14 @@ __device__ __forceinline__ void quantize_staged_rows(const GemvParams& p, const 
                     f[i] = make_float4(f[i].x * inv_rms * gm.x, f[i].y * inv_rms * gm.y, f[i].z * inv_rms * gm.z,
                                        f[i].w * inv_rms * gm.w);
                 }
+            }
+        }
+        if (swiglu && valid) {  // silu(gate) * up, as b200q_swiglu_quantize_kernel forms it
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float4 u = xf4[total_g * 8 + g * 8 + ((i + g) & 7)];
+                f[i] = make_float4(f[i].x / (1.0f + expf(-f[i].x)) * u.x, f[i].y / (1.0f + expf(-f[i].y)) * u.y,
+                                   f[i].z / (1.0f + expf(-f[i].z)) * u.z, f[i].w / (1.0f + expf(-f[i].w)) * u.w);
             }
         }
         if (valid) {
@@ -907,6 +918,7 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_k
     const int n_stages = r_end > r_begin ? (r_end - r_begin + p.R - 1) / p.R : 0;
     const int free_slots = p.NS - (FQ ? p.nx : 0);  // slots the weights have before the activations are staged
     const bool norm = FQ && MR == 1 && p.gamma != nullptr;
+    const bool swiglu = FQ && MR == 1 && p.xu != nullptr;  // never together with norm (host-checked)
     float* xf_s = reinterpret_cast<float*>(ring + static_cast<size_t>(free_slots) * p.stage_stride);  // FQ fp32 rows
 
     if (tid == 0) {
@@ -944,7 +956,7 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_k
                 bulk_g2s(smem_addr(ring + static_cast<size_t>(slot) * p.stage_stride), p.W + b0, bytes, fb, pol);
             };
             const uint32_t x_bytes = static_cast<uint32_t>(MR * p.k * 4);
-            const uint32_t g_bytes = norm ? static_cast<uint32_t>(p.k * 4) : 0u;
+            const uint32_t g_bytes = (norm || swiglu) ? static_cast<uint32_t>(p.k * 4) : 0u;
             const int first_batch = min(n_stages, min(p.PD, free_slots));
             const int pre_fill = min(n_stages, free_slots);
             const int ring_fill = min(n_stages, p.NS);
@@ -965,6 +977,8 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_k
                 for (int m = 0; m < MR; ++m)
                     bulk_g2s(smem_addr(xf_s + m * p.k), p.xf + m * p.xf_stride, static_cast<uint32_t>(p.k * 4),
                              smem_addr(xbar), pol);
+                if (swiglu)  // the up row, written by the preceding kernel like x
+                    bulk_g2s(smem_addr(xf_s + MR * p.k), p.xu, g_bytes, smem_addr(xbar), pol);
                 for (int s = first_batch; s < pre_fill; ++s) issue(s);
                 // The fp32 slots return once every consumer warp has quantized.
                 ok = mbar_wait_bounded(smem_addr(xdone), 0u);
@@ -1004,8 +1018,8 @@ __global__ void __launch_bounds__(kGemvWarps<DIG, MR> * 32 + 32, 1) b200q_gemv_k
     griddep_wait();
     if constexpr (FQ) {
         if (!mbar_wait_spin_bounded(smem_addr(xbar), 0u) && tid == 0) *p.status = STATUS_TIMEOUT;
-        quantize_staged_rows<DIG, MR>(p, reinterpret_cast<const float4*>(xf_s), norm, xs, xs_row, red, warp, lane,
-                                      nwarps);
+        quantize_staged_rows<DIG, MR>(p, reinterpret_cast<const float4*>(xf_s), norm, swiglu, xs, xs_row, red, warp,
+                                      lane, nwarps);
         // The fp32 slots go back to the weights: order this thread's reads of
         // them before the bulk copies that overwrite them.
         fence_proxy_async_smem();

@@ -54,6 +54,11 @@ int gemv_from_f32(int qtype, int act_mode, const void* w, const float* x, long l
 // stage in one pass).
 int gemv_norm_f32(int qtype, int act_mode, const void* w, const float* x, const float* gamma, float eps, float* y,
                   int k, int n, float alpha, float beta, Device* dev, cudaStream_t st, bool pdl, int flags);
+// y = alpha * (W (silu(gate) * up)) + beta * y for one row: the SwiGLU step
+// inside the down projection's GEMV (gate and up staged and combined in
+// shared memory before quantizing).
+int gemv_swiglu_f32(int qtype, int act_mode, const void* w, const float* gate, const float* up, float* y, int k, int n,
+                    float alpha, float beta, Device* dev, cudaStream_t st, bool pdl, int flags);
 int gemv_check_shape(int qtype, int act_mode, int k, int n, Device* dev);
 // The GEMV launch plan for (qtype, act_mode, k, n, mr activation rows per
 // launch, fq: quantizes fp32 x itself) on num_sms SMs, as kPlanInfoFields

@@ -11,12 +11,14 @@ runs that step entirely on the device through libb200q's entry points:
   as one matrix, gate/up as one matrix, the LM head), the norm computed by
   the GEMV itself from the fp32 residual stream (``fused_norm=False`` runs
   ``b200q_add_rmsnorm_q`` then ``b200q_matmul_xq`` instead);
-* ``b200q_matmul_xq`` -- the projections fed by codes: o with the residual
-  add in its epilogue (beta = 1) and down with the residual add;
+* ``b200q_matmul_xq`` -- the o projection fed by the attention's codes, with
+  the residual add in its epilogue (beta = 1);
 * ``b200q_rope_attention_decode`` -- RoPE, the KV append and attention in
   one launch, which also writes the o projection's codes;
 * ``b200q_swiglu_q`` -- SiLU(gate) * up, written as the down projection's
-  codes;
+  codes, and ``b200q_matmul_xq`` -- the down projection with the residual
+  add (``fused_swiglu=True`` runs both inside one GEMV,
+  ``b200q_matmul_swiglu``);
 
 all on one stream, so one token's step is one CUDA graph. The KV cache is
 fp16, [layer][kv_head][max_ctx][head_dim], or the reference's paged store
@@ -131,16 +133,17 @@ class DecodeStack:
     ``layers`` holds one weight dict per layer (``random_layer`` layout); a
     shorter list is cycled, each layer still getting its own device copy.
     On the device the q/k/v rows of a layer are stored as one matrix, and so
-    are the gate/up rows, so each is one GEMV; the norms and the attention
-    write the GEMVs' activation codes directly. A layer is eight launches:
-    norm, qkv, RoPE + attention (one fused kernel), o (+ residual), norm,
-    gate/up, SwiGLU, down (+ residual).
+    are the gate/up rows, so each is one GEMV. A layer is six launches: qkv
+    (RMSNorm inside), RoPE + KV append + attention (writing the o
+    projection's codes), o (+ residual), gate/up (RMSNorm inside), SwiGLU
+    (writing the down projection's codes), down (+ residual); five with
+    ``fused_swiglu``, eight with ``fused_norm=False``.
     """
 
     def __init__(self, shape: StackShape, max_ctx: int, layers: list[dict[str, np.ndarray]], embed: np.ndarray,
                  head: np.ndarray, out_norm: np.ndarray, act_mode: int = _native.ACT_X16, device: int = 0,
                  fused_norm: bool = True, repack: "RepackPolicy | None" = None, architecture: str = "llama",
-                 kv: str | None = None, page_size: int | None = None):
+                 kv: str | None = None, page_size: int | None = None, fused_swiglu: bool = False):
         """``repack`` picks each weight's decode layout as the reference does
         when it registers a graph's weights (repack_policy.RepackPolicy; by
         default from the ANVIL_* environment switches for `architecture`).
@@ -149,7 +152,13 @@ class DecodeStack:
         [head_dim]), "paged" (fp16 pages) or "q8" (the reference's Q8 pages);
         by default "q8" when ANVIL_KV_QUANT asks for it (kv_cache.q8_from_env),
         else "contiguous". Pages hold ``page_size`` positions (default
-        kv_cache.KV_PAGE_SIZE)."""
+        kv_cache.KV_PAGE_SIZE).
+
+        ``fused_swiglu`` forms SiLU(gate) * up inside the down projection's
+        GEMV (``b200q_matmul_swiglu``, one launch fewer per layer) instead of
+        ``b200q_swiglu_q`` + ``b200q_matmul_xq``; off by default, because
+        staging the two fp32 rows in every CTA of the down GEMV costs more
+        than the launch it saves on the Llama-3-8B shape."""
         import torch
 
         from .kv_cache import KV_PAGE_SIZE, PagedKVCache, q8_from_env
@@ -170,6 +179,7 @@ class DecodeStack:
         self.max_ctx = max_ctx
         self.act_mode = act_mode
         self.fused_norm = fused_norm
+        self.fused_swiglu = fused_swiglu
         self.dev = torch.device("cuda", device)
         self.lib = _native.lib()
         f32 = dict(dtype=torch.float32, device=self.dev)
@@ -259,10 +269,15 @@ class DecodeStack:
             self._check(L.b200q_matmul_xq(lay.wo.qtype, act, xq_h, lay.wo.ptr, x, 1, h, h, 1.0, resid, W, st), "o_proj")
             self._norm_matmul(lay.w_gu.qtype, x, lay.ffn_norm, xq_h, lay.w_gu.ptr, gp, h, 2 * f, "gate_up", st,
                               linears_only)
-            if not linears_only:
-                self._check(L.b200q_swiglu_q(gp, up, xq_f, act, f, st), "swiglu")
-            self._check(L.b200q_matmul_xq(lay.w_down.qtype, act, xq_f, lay.w_down.ptr, x, 1, f, h, 1.0, resid, W, st),
-                        "down")
+            if self.fused_swiglu and not linears_only:
+                # SiLU(gate) * up formed and quantized inside the down GEMV, with the residual add
+                self._check(L.b200q_matmul_swiglu(lay.w_down.qtype, act, gp, up, lay.w_down.ptr, x, f, h, 1.0, resid,
+                                                  W, st), "swiglu+down")
+            else:
+                if not linears_only:
+                    self._check(L.b200q_swiglu_q(gp, up, xq_f, act, f, st), "swiglu")
+                self._check(L.b200q_matmul_xq(lay.w_down.qtype, act, xq_f, lay.w_down.ptr, x, 1, f, h, 1.0, resid, W,
+                                              st), "down")
         self._norm_matmul(self.head.qtype, x, self.out_norm, xq_h, self.head.ptr, self.logits.data_ptr(), h, s.vocab,
                           "lm_head", st, linears_only)
 

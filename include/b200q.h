@@ -357,6 +357,14 @@ B200Q_API int b200q_matmul_xq(int qtype, int act_mode, const void* xq, const voi
 B200Q_API int b200q_matmul_norm(int qtype, int act_mode, const float* x, const float* gamma, float eps, const void* w,
                                 float* y, int k, int n, float alpha, float beta, int flags, void* stream);
 
+/* y = alpha * (W h) + beta * y with h = silu(gate) * up, element-wise, for
+ * one row of k: the SiLU * up step of the decode layer (QM:2380-2412, as
+ * b200q_swiglu_q forms it) inside the down projection's GEMV, which stages
+ * gate and up (written by the preceding gate/up projection) and quantizes h
+ * itself. gate and up 16-byte aligned; act_mode B200Q_ACT_X8 or X16. */
+B200Q_API int b200q_matmul_swiglu(int qtype, int act_mode, const float* gate, const float* up, const void* w, float* y,
+                                  int k, int n, float alpha, float beta, int flags, void* stream);
+
 /* The decode GEMV's launch plan for a matrix of n rows of k elements, without
  * touching a device (no reference counterpart: a planning query for callers
  * sizing resources and for tests). rows_per_launch: activation rows one launch

@@ -129,8 +129,8 @@ LAYOUTS = {
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("layout", sorted(LAYOUTS))
-@pytest.mark.parametrize("fused_norm", [True, False])
-def test_decode_stack_matches_restatement(fused_norm, layout):
+@pytest.mark.parametrize("fused_norm,fused_swiglu", [(True, False), (False, False), (True, True)])
+def test_decode_stack_matches_restatement(fused_norm, fused_swiglu, layout):
     """Logits of 12 tokens against the float64 restatement, with the weights
     in each decode layout the registration policy can pick."""
     from cybel_b200.decode import DecodeStack, StackShape, random_layer, random_rows
@@ -147,7 +147,7 @@ def test_decode_stack_matches_restatement(fused_norm, layout):
     max_ctx = 64
     policy = RepackPolicy.from_env("llama", env=LAYOUTS[layout])
     dev = DecodeStack(shape, max_ctx, layers, embed, head, out_norm, fused_norm=fused_norm, repack=policy,
-                      kv="contiguous")
+                      kv="contiguous", fused_swiglu=fused_swiglu)
     assert dev.kv_cache is None and dev.k_cache is not None
     want_q = {"canonical": (Q4_K, Q6_K), "default": (Q4_K, Q6_K_R4), "r4_lm": (Q4_K_R4, Q6_K_LM)}[layout]
     assert (dev.layers[0].wqkv.qtype, dev.head.qtype) == want_q

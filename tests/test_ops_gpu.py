@@ -337,3 +337,45 @@ def test_matmul_norm_rejects_long_rows(oracle_mod):
     rc = _native.lib().b200q_matmul_norm(12, 1, x.data_ptr(), x.data_ptr(), 1e-5, dm.ptr, y.data_ptr(), k, n, 1.0, 0.0,
                                          _native.WEIGHTS_STATIC, torch.cuda.current_stream().cuda_stream)
     assert rc == -3
+
+
+@pytest.mark.parametrize("qt,n,k", [(12, 4096, 14336), (12, 300, 768), (14, 256, 2048), (8, 96, 4096)])
+@pytest.mark.parametrize("act", [2, 1])
+def test_matmul_swiglu_equals_swiglu_then_gemv(oracle_mod, qt, n, k, act):
+    """b200q_matmul_swiglu (SiLU(gate) * up formed and quantized inside the
+    down projection's GEMV) against the two-launch form it replaces,
+    b200q_swiglu_q + b200q_matmul_xq: the same codes, so the same outputs bit
+    for bit, with and without the residual (beta = 1); and (x16) within 1e-5
+    of the exact product with the float64 SwiGLU vector."""
+    import torch
+
+    from cybel_b200 import _native
+    from cybel_b200 import quantize as Q
+    from cybel_b200.quantized_matmul import DeviceMatrix
+
+    O = oracle_mod
+    rng = np.random.default_rng(qt + n + k + act)
+    W = Q.quantize(rng.normal(0.0, 0.02, size=(n, k)).astype(np.float32), qt)
+    g = (rng.standard_normal(k) * 2.0).astype(np.float32)
+    u = rng.standard_normal(k).astype(np.float32)
+    dm = DeviceMatrix(qt, k, n, W)
+    gt, ut = torch.from_numpy(g).cuda(), torch.from_numpy(u).cuda()
+    L = _native.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    W_ = _native.WEIGHTS_STATIC
+    for beta in (0.0, 1.0):
+        y1 = torch.full((n,), 0.25, dtype=torch.float32, device="cuda")
+        y2 = y1.clone()
+        _native.check(L.b200q_matmul_swiglu(qt, act, gt.data_ptr(), ut.data_ptr(), dm.ptr, y1.data_ptr(), k, n, 1.0,
+                                            beta, W_, st), "matmul_swiglu")
+        xq = torch.zeros(int(L.b200q_xq_row_bytes(k, act)), dtype=torch.uint8, device="cuda")
+        _native.check(L.b200q_swiglu_q(gt.data_ptr(), ut.data_ptr(), xq.data_ptr(), act, k, st), "swiglu_q")
+        _native.check(L.b200q_matmul_xq(qt, act, xq.data_ptr(), dm.ptr, y2.data_ptr(), 1, k, n, 1.0, beta, W_, st),
+                      "matmul_xq")
+        torch.cuda.synchronize()
+        assert np.array_equal(y1.cpu().numpy(), y2.cpu().numpy()), beta
+    if act == 2:
+        gd = g.astype(np.float64)
+        h = (gd / (1.0 + np.exp(-gd)) * u).astype(np.float32)
+        wn = O.row_norms(W, qt, k, n)
+        assert O.normalized_error(y1.cpu().numpy() - 0.25, O.matvec_f64(W, qt, h, k, n), wn, h) <= 1e-5
