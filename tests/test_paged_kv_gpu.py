@@ -221,3 +221,54 @@ def test_paged_entry_rejects_bad_arguments():
     assert call(kp=p + 2) == -4          # Q8 pools 4-byte aligned
     assert call(mode=_native.KV_F16, ks=None, vs=None, kp=p + 4) == -4  # fp16 pools 8-byte aligned
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("n_tok", [3, 5])
+def test_q8_multi_token_pages_not_aligned_to_chunks(n_tok):
+    """Several tokens per sequence in one call over Q8 pages of 48 positions
+    (pages and 64-position attention chunks cross each other): each token
+    attends causally over the cache and the tokens before it; the rows the
+    call appends are the restated quantizer's codes (values bit-exact) and
+    every token's output matches the restated attention over the stored
+    rows, within 1e-4 of max |ref|."""
+    import torch
+
+    from cybel_b200 import _native
+    from cybel_b200.kv_cache import PagedKVCache
+    from oracle.paged_kv_ref import PagedKVStoreRef, q8_rows, rope
+
+    B, H, KV, P, theta = 2, 16, 4, 48, 1.0
+    pos0 = 90  # the call covers positions 90 .. 90 + n_tok - 1 (pages 1 and 2, chunk 1)
+    cache = PagedKVCache(layers=1, kv_heads=KV, max_seq=192, batch=B, page_size=P, q8=True)
+    rng = np.random.default_rng(40 + n_tok)
+    out1 = torch.empty((B, H, HD), device="cuda")
+    for pos in range(pos0):  # single-token steps fill the cache
+        q = torch.from_numpy(rng.standard_normal((B, H, HD)).astype(np.float32)).cuda()
+        k = torch.from_numpy(rng.standard_normal((B, KV, HD)).astype(np.float32)).cuda()
+        v = torch.from_numpy(rng.standard_normal((B, KV, HD)).astype(np.float32)).cuda()
+        cache.ensure(pos)
+        cache.attention(0, q.data_ptr(), k.data_ptr(), v.data_ptr(), pos, H, theta, out1.data_ptr(), None, 0, _st())
+    q = rng.standard_normal((B, n_tok, H, HD)).astype(np.float32)
+    k = rng.standard_normal((B, n_tok, KV, HD)).astype(np.float32)
+    v = rng.standard_normal((B, n_tok, KV, HD)).astype(np.float32)
+    qt, kt, vt = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    out = torch.empty((B, n_tok, H, HD), device="cuda")
+    cache.ensure(pos0, pos0 + n_tok - 1)
+    cache.attention(0, qt.data_ptr(), kt.data_ptr(), vt.data_ptr(), pos0, H, theta, out.data_ptr(), None, 0, _st(),
+                    n_tokens=n_tok)
+    torch.cuda.synchronize()
+    _native.check_device(0)
+    got = out.cpu().numpy()
+    last = pos0 + n_tok
+    for b in range(B):
+        rows = [cache.rows(0, b, h, 0, last) for h in range(KV)]
+        for h in range(KV):
+            want_v, want_vs = q8_rows(v[b, :, h])
+            assert np.array_equal(rows[h][1][pos0:], want_v) and np.array_equal(rows[h][3][pos0:], want_vs)
+        ref = PagedKVStoreRef(1, KV, HD, 192, P, q8=True)
+        for p in range(last):
+            ref.set_row(0, p, np.stack([r[0][p] for r in rows]), np.stack([r[1][p] for r in rows]),
+                        np.stack([r[2][p] for r in rows]), np.stack([r[3][p] for r in rows]))
+        for t in range(n_tok):
+            want = ref.attention(0, rope(q[b, t], pos0 + t, theta), pos0 + t + 1)
+            assert _rel(got[b, t], want) <= 1e-4, (b, t)
