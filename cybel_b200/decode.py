@@ -180,6 +180,7 @@ class DecodeStack:
         self.act_mode = act_mode
         self.fused_norm = fused_norm
         self.fused_swiglu = fused_swiglu
+        self._vbufs: dict = {}  # verify-pass buffers per row count
         self.dev = torch.device("cuda", device)
         self.lib = _native.lib()
         f32 = dict(dtype=torch.float32, device=self.dev)
@@ -317,7 +318,7 @@ class DecodeStack:
     def _verify_buffers(self, m: int) -> dict:
         import torch
 
-        bufs = self._vbufs.get(m) if hasattr(self, "_vbufs") else None
+        bufs = self._vbufs.get(m)
         if bufs is None:
             s = self.shape
             h, kv, f = s.hidden, s.kv_dim, s.ffn
@@ -325,7 +326,6 @@ class DecodeStack:
             bufs = dict(x=z(m, h), hn=z(m, h), q=z(m, h), k=z(m, kv), v=z(m, kv), att=z(m, h), o=z(m, h),
                         g=z(m, f), u=z(m, f), sw=z(m, f), d=z(m, h), logits=z(m, s.vocab),
                         tok=torch.zeros(m, dtype=torch.int32, device=self.dev))
-            self._vbufs = getattr(self, "_vbufs", {})
             self._vbufs[m] = bufs
         return bufs
 

@@ -132,6 +132,23 @@ class PagedKVCache:
                 self.table_host[li, b, p] = self._free.pop()
         self.table.copy_(torch.from_numpy(self.table_host))
 
+    def assign(self, layer: int, seq: int, page: int, slot: int) -> None:
+        """Place page `page` of sequence `seq` in layer `layer` at pool slot
+        `slot` (for callers that choose placement themselves, e.g. pages
+        shared between sequences); the table reaches the device with
+        ``sync_table``."""
+        if not 0 <= slot < self.n_slots:
+            raise ValueError("slot outside the pool")
+        if slot in self._free:
+            self._free.remove(slot)
+        self.table_host[layer, seq, page] = slot
+
+    def sync_table(self) -> None:
+        """Copy the host page table to the device (current stream)."""
+        import torch
+
+        self.table.copy_(torch.from_numpy(self.table_host))
+
     def reset(self) -> None:
         """Drop every page (graph_reset, model_graph.cpp:5191-5193)."""
         import torch

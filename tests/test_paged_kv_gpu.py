@@ -105,11 +105,11 @@ def test_f16_pages_match_contiguous_cache(H, KV, act, n_tok):
     for b in range(B):
         for pg in range(cache.pages_per_seq):
             slot = int(perm[b * cache.pages_per_seq + pg])
-            cache.table_host[0, b, pg] = slot
+            cache.assign(0, b, pg, slot)
             cache.k[slot] = contig_k[b, :, pg * P:(pg + 1) * P]
             cache.v[slot] = contig_v[b, :, pg * P:(pg + 1) * P]
-    cache.table.copy_(torch.from_numpy(cache.table_host))
-    cache._free = []
+    cache.sync_table()
+    assert cache.pages_in_use == cache.n_slots
     q = torch.from_numpy(rng.standard_normal((B, n_tok, H, HD)).astype(np.float32)).cuda()
     k = torch.from_numpy(rng.standard_normal((B, n_tok, KV, HD)).astype(np.float32)).cuda()
     v = torch.from_numpy(rng.standard_normal((B, n_tok, KV, HD)).astype(np.float32)).cuda()

@@ -94,3 +94,9 @@ def test_page_bookkeeping_on_host():
     c.restore(snap)
     assert int(c.k[0].abs().max()) == 0 and c.pages_in_use == 8
     assert np.array_equal(c.table.numpy(), c.table_host)
+    free = [s for s in range(9) if s not in set(c.table_host[c.table_host >= 0].tolist())][0]
+    c.assign(1, 0, 2, free)  # caller-chosen placement takes the slot off the free list
+    c.sync_table()
+    assert c.pages_in_use == 9 and int(c.table[1, 0, 2]) == free
+    with pytest.raises(MemoryError):
+        c.ensure(32)
