@@ -278,6 +278,7 @@ bool dropin_graph_launch(const GraphKey& key, Staging* s, int qtype, int act, co
                          float* y_mapped, int m, int k, int n, Device* dev, int* rc) {
     auto it = t_graphs.find(key);
     if (it == t_graphs.end()) {
+        if (t_graph_seen.size() >= 8 * kMaxDropinGraphs) t_graph_seen.clear();  // call sites seen once
         if (++t_graph_seen[key] < 2) return false;
         if (t_graphs.size() >= kMaxDropinGraphs) {
             for (auto& kv : t_graphs) cudaGraphExecDestroy(kv.second);
