@@ -36,6 +36,7 @@ STATUS = {
 # Every symbol include/b200q.h declares: (name, argtypes, restype).
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
+_ll = ctypes.c_longlong
 _fp = ctypes.POINTER(ctypes.c_float)
 SIGNATURES: dict[str, tuple[list, object]] = {}
 for _q in ("q4k", "q4k_r4", "q6k", "q6k_r4", "q6k_lm", "q8_0", "q4_0"):
@@ -77,10 +78,11 @@ SIGNATURES.update(
         "b200q_attention_decode_q": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp], _i),
         "b200q_rope_attention_decode": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _vp, _vp, _i, _vp, _vp, _i, _vp], _i),
         "b200q_rope_attention_decode_paged": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _i, _vp, _vp, _vp, _vp, _i,
-                                               _i, _vp, _i, _vp, _vp, _i, _vp], _i),
+                                               _i, _vp, _i, _vp, _vp, _i, _ll, _ll, _vp], _i),
         "b200q_rope_attention_decode_tokens": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _i, _vp, _vp, _i,
-                                                _vp], _i),
+                                                _ll, _ll, _vp], _i),
         "b200q_swiglu_q": ([_vp, _vp, _vp, _i, _i, _vp], _i),
+        "b200q_swiglu_rows": ([_vp, _vp, _i, _i, _vp], _i),
         "b200q_matmul_xq": ([_i, _i, _vp, _vp, _vp, _i, _i, _i, ctypes.c_float, ctypes.c_float, _i, _vp], _i),
         "b200q_matmul_norm": ([_i, _i, _vp, _vp, _f, _vp, _vp, _i, _i, _f, _f, _i, _vp], _i),
         "b200q_matmul_swiglu": ([_i, _i, _vp, _vp, _vp, _vp, _i, _i, _f, _f, _i, _vp], _i),

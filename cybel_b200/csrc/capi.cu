@@ -580,12 +580,14 @@ int b200q_rope_attention_decode(const float* q, const float* k, const float* v, 
 
 int b200q_rope_attention_decode_tokens(const float* q, const float* k, const float* v, int batch, int n_tokens,
                                        int n_heads, int n_kv_heads, int head_dim, int pos0, float theta, void* k_cache,
-                                       void* v_cache, int max_ctx, float* out, void* xq, int act_mode, void* stream) {
+                                       void* v_cache, int max_ctx, float* out, void* xq, int act_mode,
+                                       long long q_stride, long long kv_stride, void* stream) {
     Device* dev = nullptr;
     int rc = current_device_state(&dev);
     if (rc == B200Q_OK)
         rc = launch_rope_attention(q, k, v, batch, n_tokens, n_heads, n_kv_heads, head_dim, pos0, theta, k_cache,
-                                   v_cache, max_ctx, out, xq, act_mode, dev, static_cast<cudaStream_t>(stream));
+                                   v_cache, max_ctx, out, xq, act_mode, dev, static_cast<cudaStream_t>(stream),
+                                   q_stride, kv_stride);
     set_last_error(rc);
     return rc;
 }
@@ -594,13 +596,14 @@ int b200q_rope_attention_decode_paged(const float* q, const float* k, const floa
                                       int n_heads, int n_kv_heads, int head_dim, int pos, float theta, int kv_mode,
                                       void* k_pages, void* v_pages, float* k_scales, float* v_scales, int n_slots,
                                       int page_size, const int* page_table, int pages_per_seq, float* out, void* xq,
-                                      int act_mode, void* stream) {
+                                      int act_mode, long long q_stride, long long kv_stride, void* stream) {
     Device* dev = nullptr;
     int rc = current_device_state(&dev);
     if (rc == B200Q_OK)
         rc = launch_rope_attention_paged(q, k, v, batch, n_tokens, n_heads, n_kv_heads, head_dim, pos, theta, kv_mode,
                                          k_pages, v_pages, k_scales, v_scales, n_slots, page_size, page_table,
-                                         pages_per_seq, out, xq, act_mode, dev, static_cast<cudaStream_t>(stream));
+                                         pages_per_seq, out, xq, act_mode, dev, static_cast<cudaStream_t>(stream),
+                                         q_stride, kv_stride);
     set_last_error(rc);
     return rc;
 }
@@ -655,6 +658,12 @@ int b200q_matmul_swiglu(int qtype, int act_mode, const float* gate, const float*
     if (rc == B200Q_OK)
         rc = gemv_swiglu_f32(qtype, act_mode, w, gate, up, y, k, n, alpha, beta, dev, static_cast<cudaStream_t>(stream),
                              pdl_enabled(), flags);
+    set_last_error(rc);
+    return rc;
+}
+
+int b200q_swiglu_rows(const float* gate_up, float* out, int rows, int n, void* stream) {
+    const int rc = launch_swiglu_rows(gate_up, out, rows, n, static_cast<cudaStream_t>(stream));
     set_last_error(rc);
     return rc;
 }

@@ -553,7 +553,8 @@ template <int G, int DIG, int KVM>
 __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v, const KvArgs kv,
     float* __restrict__ part, int* __restrict__ counters, float* __restrict__ out, uint8_t* __restrict__ xq,
-    int n_heads, int n_kv, int pos, int n_tok, float log2_theta, float scale) {
+    int n_heads, int n_kv, int pos, int n_tok, long long q_stride, long long kv_stride, float log2_theta,
+    float scale) {
     griddep_launch_dependents();
     using KL = KvLane<KVM>;
     using Raw = typename KL::Raw;
@@ -590,10 +591,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 2) b200q_attn_decode_kernel(
     if (c >= n_chunks) return;
     const int ctx = my_pos + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const float* k_seq = k + (static_cast<long long>(seq) * n_tok * n_kv + kvh) * kHeadDim;  // token 0's k row
-    const float* v_seq = v + (static_cast<long long>(seq) * n_tok * n_kv + kvh) * kHeadDim;
-    const long long tok_stride = static_cast<long long>(n_kv) * kHeadDim;
-    q += (static_cast<long long>(b) * n_heads + kvh * G) * kHeadDim;
+    // q, k and v rows (one per (sequence, token)) lie q_stride / kv_stride
+    // floats apart: packed, or rows of one q|k|v projection output.
+    const float* k_seq = k + static_cast<long long>(seq) * n_tok * kv_stride + kvh * kHeadDim;  // token 0's k row
+    const float* v_seq = v + static_cast<long long>(seq) * n_tok * kv_stride + kvh * kHeadDim;
+    const long long tok_stride = kv_stride;
+    q += static_cast<long long>(b) * q_stride + kvh * G * kHeadDim;
     part += (static_cast<long long>(b) * n_heads + kvh * G) * gridDim.y * kPartStride;  // records [g][chunk]
     const int p0 = c * kAttnChunk;
     const int np = min(kAttnChunk, ctx - p0);
@@ -893,6 +896,18 @@ __global__ void b200q_swiglu_kernel(const float* __restrict__ g, const float* __
     out[i] = gv / (1.0f + expf(-gv)) * u[i];
 }
 
+// out[r][j] = silu(gu[r][j]) * gu[r][n + j] for rows of [gate n | up n]: the
+// SiLU * up step for several rows of one gate/up projection output.
+__global__ void b200q_swiglu_rows_kernel(const float* __restrict__ gu, float* __restrict__ out, int rows, int n) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<long long>(rows) * n) return;
+    const long long r = i / n, j = i - r * n;
+    const float gv = gu[r * 2 * n + j];
+    out[i] = gv / (1.0f + expf(-gv)) * gu[r * 2 * n + n + j];
+}
+
 // out[r][s * cols + j] = in[s][r][j]: the row-major [rows][shards * cols]
 // view of an all-gather of per-shard [rows][cols] blocks.
 __global__ void b200q_unshard_rows_kernel(const float* __restrict__ in, float* __restrict__ out, int shards, int rows,
@@ -1003,7 +1018,7 @@ namespace {
 // outputs, takes the scratch, and launches b200q_attn_decode_kernel<G, DIG, KVM>.
 int launch_attention(int kvm, const KvArgs& kv, const float* q, const float* k, const float* v, int batch,
                      int n_tok, int n_heads, int n_kv, int hd, int pos, float theta, float* out, void* xq,
-                     int act_mode, Device* dev, cudaStream_t st) {
+                     int act_mode, Device* dev, cudaStream_t st, long long q_stride = 0, long long kv_stride = 0) {
     if (!q || !k || !v || (!out && !xq) || batch <= 0 || n_tok <= 0 || n_heads <= 0 || n_kv <= 0 || !dev)
         return B200Q_EINVAL;
     if (xq && act_mode != B200Q_ACT_X8 && act_mode != B200Q_ACT_X16) return B200Q_EINVAL;
@@ -1012,7 +1027,12 @@ int launch_attention(int kvm, const KvArgs& kv, const float* q, const float* k, 
     if (rows > 65535) return B200Q_ESHAPE;
     const int G = n_heads / n_kv;
     if (G != 1 && G != 2 && G != 4 && G != 8) return B200Q_ESHAPE;
-    if ((out && !aligned16(out)) || (xq && !aligned16(xq)) || !aligned16(k) || !aligned16(v)) return B200Q_EALIGN;
+    if (q_stride == 0) q_stride = static_cast<long long>(n_heads) * kHeadDim;
+    if (kv_stride == 0) kv_stride = static_cast<long long>(n_kv) * kHeadDim;
+    if (q_stride < static_cast<long long>(n_heads) * kHeadDim || kv_stride < static_cast<long long>(n_kv) * kHeadDim)
+        return B200Q_ESHAPE;
+    if ((out && !aligned16(out)) || (xq && !aligned16(xq)) || !aligned16(k) || !aligned16(v) || (kv_stride & 3))
+        return B200Q_EALIGN;
     const int n_chunks = (pos + n_tok - 1) / kAttnChunk + 1;  // the last token's
     void* part = nullptr;
     void* cnt = nullptr;
@@ -1032,8 +1052,8 @@ int launch_attention(int kvm, const KvArgs& kv, const float* q, const float* k, 
     const int dig = !xq ? 0 : (act_mode == B200Q_ACT_X8 ? 1 : 2);
     auto go = [&](auto kern) {
         return cudaLaunchKernelEx(&cfg, kern, q, k, v, a, static_cast<float*>(part), static_cast<int*>(cnt), out,
-                                  static_cast<uint8_t*>(xq), n_heads, n_kv, pos, n_tok, log2f(theta),
-                                  1.0f / sqrtf(static_cast<float>(hd)));
+                                  static_cast<uint8_t*>(xq), n_heads, n_kv, pos, n_tok, q_stride, kv_stride,
+                                  log2f(theta), 1.0f / sqrtf(static_cast<float>(hd)));
     };
     cudaError_t e = cudaErrorInvalidValue;
 #define B200Q_ATTN_KVM(GG, DD)                                                          \
@@ -1059,7 +1079,7 @@ int launch_attention(int kvm, const KvArgs& kv, const float* q, const float* k, 
 
 int launch_rope_attention(const float* q, const float* k, const float* v, int batch, int n_tok, int n_heads, int n_kv,
                           int hd, int pos, float theta, void* kc, void* vc, int max_ctx, float* out, void* xq,
-                          int act_mode, Device* dev, cudaStream_t st) {
+                          int act_mode, Device* dev, cudaStream_t st, long long q_stride, long long kv_stride) {
     if (!kc || !vc || max_ctx <= 0 || n_tok <= 0) return B200Q_EINVAL;
     if (static_cast<long long>(pos) + n_tok > max_ctx) return B200Q_ESHAPE;
     if (!aligned16(kc) || !aligned16(vc)) return B200Q_EALIGN;  // key rows are read 16 bytes a lane
@@ -1068,13 +1088,14 @@ int launch_rope_attention(const float* q, const float* k, const float* v, int ba
     kv.v = vc;
     kv.max_ctx = max_ctx;
     return launch_attention(KV_CONTIG, kv, q, k, v, batch, n_tok, n_heads, n_kv, hd, pos, theta, out, xq, act_mode,
-                            dev, st);
+                            dev, st, q_stride, kv_stride);
 }
 
 int launch_rope_attention_paged(const float* q, const float* k, const float* v, int batch, int n_tok, int n_heads,
                                 int n_kv, int hd, int pos, float theta, int kv_mode, void* k_pages, void* v_pages,
                                 float* k_scales, float* v_scales, int n_slots, int page_size, const int* page_table,
-                                int pages_per_seq, float* out, void* xq, int act_mode, Device* dev, cudaStream_t st) {
+                                int pages_per_seq, float* out, void* xq, int act_mode, Device* dev, cudaStream_t st,
+                                long long q_stride, long long kv_stride) {
     const bool q8 = kv_mode == B200Q_KV_Q8;
     if ((kv_mode != B200Q_KV_F16 && !q8) || !k_pages || !v_pages || !page_table || n_slots <= 0 || page_size <= 0 ||
         pages_per_seq <= 0 || n_tok <= 0 || (q8 && (!k_scales || !v_scales)))
@@ -1094,7 +1115,7 @@ int launch_rope_attention_paged(const float* q, const float* k, const float* v, 
     kv.page = page_size;
     kv.n_slots = n_slots;
     return launch_attention(q8 ? KV_PAGED_Q8 : KV_PAGED, kv, q, k, v, batch, n_tok, n_heads, n_kv, hd, pos, theta, out,
-                            xq, act_mode, dev, st);
+                            xq, act_mode, dev, st, q_stride, kv_stride);
 }
 
 int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaStream_t st) {
@@ -1102,6 +1123,15 @@ int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaS
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), st, attr);
     return cudaLaunchKernelEx(&cfg, b200q_swiglu_kernel, g, u, out, n) == cudaSuccess ? B200Q_OK : B200Q_ECUDA;
+}
+
+int launch_swiglu_rows(const float* gu, float* out, int rows, int n, cudaStream_t st) {
+    if (!gu || !out || rows <= 0 || n <= 0) return B200Q_EINVAL;
+    const long long total = static_cast<long long>(rows) * n;
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pdl_cfg(dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), st, attr);
+    return cudaLaunchKernelEx(&cfg, b200q_swiglu_rows_kernel, gu, out, rows, n) == cudaSuccess ? B200Q_OK
+                                                                                             : B200Q_ECUDA;
 }
 
 int launch_unshard_rows(const float* in, float* out, int shards, int rows, int cols, cudaStream_t st) {

@@ -117,15 +117,20 @@ int launch_attention(const float* q, const void* kc, const void* vc, float* out,
 // RoPE + KV append + attention + chunk merge in one launch (b200q_attn_decode_kernel)
 // for n_tok consecutive tokens (positions pos .. pos + n_tok - 1) of each of
 // `batch` sequences.
+// q_stride / kv_stride: floats between consecutive q / k, v rows (0: packed).
 int launch_rope_attention(const float* q, const float* k, const float* v, int batch, int n_tok, int n_heads, int n_kv,
                           int hd, int pos, float theta, void* kc, void* vc, int max_ctx, float* out, void* xq,
-                          int act_mode, Device* dev, cudaStream_t st);
+                          int act_mode, Device* dev, cudaStream_t st, long long q_stride = 0,
+                          long long kv_stride = 0);
 // The same over a paged cache (b200q_rope_attention_decode_paged).
 int launch_rope_attention_paged(const float* q, const float* k, const float* v, int batch, int n_tok, int n_heads,
                                 int n_kv, int hd, int pos, float theta, int kv_mode, void* k_pages, void* v_pages,
                                 float* k_scales, float* v_scales, int n_slots, int page_size, const int* page_table,
-                                int pages_per_seq, float* out, void* xq, int act_mode, Device* dev, cudaStream_t st);
+                                int pages_per_seq, float* out, void* xq, int act_mode, Device* dev, cudaStream_t st,
+                                long long q_stride = 0, long long kv_stride = 0);
 int launch_swiglu(const float* g, const float* u, float* out, long long n, cudaStream_t st);
+// SiLU(gate) * up for `rows` rows of [gate n | up n] (b200q_swiglu_rows).
+int launch_swiglu_rows(const float* gu, float* out, int rows, int n, cudaStream_t st);
 // dst[0..n) = src[0..n) from page-locked host memory mapped into the device
 // (src_mapped: its device address), by a kernel that lets a PDL-launched
 // GEMV behind it start streaming weights (ops.cu).

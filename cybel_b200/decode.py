@@ -323,8 +323,8 @@ class DecodeStack:
             s = self.shape
             h, kv, f = s.hidden, s.kv_dim, s.ffn
             z = (lambda *shape: torch.zeros(shape, dtype=torch.float32, device=self.dev))
-            bufs = dict(x=z(m, h), hn=z(m, h), q=z(m, h), k=z(m, kv), v=z(m, kv), att=z(m, h), o=z(m, h),
-                        g=z(m, f), u=z(m, f), sw=z(m, f), d=z(m, h), logits=z(m, s.vocab),
+            bufs = dict(x=z(m, h), hn=z(m, h), qkv=z(m, h + 2 * kv), att=z(m, h), o=z(m, h), gu=z(m, 2 * f),
+                        sw=z(m, f), d=z(m, h), logits=z(m, s.vocab),
                         tok=torch.zeros(m, dtype=torch.int32, device=self.dev))
             self._vbufs[m] = bufs
         return bufs
@@ -338,8 +338,9 @@ class DecodeStack:
         asks the engine for the logits of each drafted prefix in turn
         (cpu_speculative_decode.py:740-769): every quantized linear runs once
         over the m rows (b200q_matmul_ex with B200Q_TILE_FROM_2: the tcgen05
-        tile kernel for Q4_K from 2 rows, the GEMV for the other qtypes),
-        and one attention launch per layer
+        tile kernel for Q4_K from 2 rows, the GEMV for the other qtypes; q, k
+        and v as one linear, gate and up as one), and one attention launch per
+        layer, reading q, k and v straight from the rows of the q|k|v output,
         appends the m keys/values and attends causally
         (b200q_rope_attention_decode_tokens / the paged form). The cache then
         holds all m tokens; positions past the accepted prefix are simply
@@ -374,23 +375,21 @@ class DecodeStack:
         for li, lay in enumerate(self.layers):
             self._check(L.b200q_add_rmsnorm(P["x"], delta, lay.attn_norm.data_ptr(), P["hn"], h, m, s.eps, st),
                         "attn norm")
-            lin(lay.wqkv, 0, h, P["hn"], P["q"], h)
-            lin(lay.wqkv, h, kv, P["hn"], P["k"], h)
-            lin(lay.wqkv, h + kv, kv, P["hn"], P["v"], h)
+            lin(lay.wqkv, 0, h + 2 * kv, P["hn"], P["qkv"], h)
+            qp, kp, vp = P["qkv"], P["qkv"] + 4 * h, P["qkv"] + 4 * (h + kv)
+            row = h + 2 * kv  # floats between consecutive tokens' q (and k, v) rows
             if self.kv_cache is not None:
-                self.kv_cache.attention(li, P["q"], P["k"], P["v"], pos0, s.heads, s.rope_theta, P["att"], None, 0, st,
-                                        n_tokens=m)
+                self.kv_cache.attention(li, qp, kp, vp, pos0, s.heads, s.rope_theta, P["att"], None, 0, st,
+                                        n_tokens=m, q_stride=row, kv_stride=row)
             else:
                 self._check(L.b200q_rope_attention_decode_tokens(
-                    P["q"], P["k"], P["v"], 1, m, s.heads, s.kv_heads, hd, pos0, s.rope_theta,
-                    self.k_cache[li].data_ptr(), self.v_cache[li].data_ptr(), self.max_ctx, P["att"], None, 0, st),
-                    "verify attention")
+                    qp, kp, vp, 1, m, s.heads, s.kv_heads, hd, pos0, s.rope_theta, self.k_cache[li].data_ptr(),
+                    self.v_cache[li].data_ptr(), self.max_ctx, P["att"], None, 0, row, row, st), "verify attention")
             lin(lay.wo, 0, h, P["att"], P["o"], h)
             self._check(L.b200q_add_rmsnorm(P["x"], P["o"], lay.ffn_norm.data_ptr(), P["hn"], h, m, s.eps, st),
                         "ffn norm")
-            lin(lay.w_gu, 0, f, P["hn"], P["g"], h)
-            lin(lay.w_gu, f, f, P["hn"], P["u"], h)
-            self._check(L.b200q_swiglu(P["g"], P["u"], P["sw"], m * f, st), "swiglu")
+            lin(lay.w_gu, 0, 2 * f, P["hn"], P["gu"], h)
+            self._check(L.b200q_swiglu_rows(P["gu"], P["sw"], m, f, st), "swiglu")
             lin(lay.w_down, 0, h, P["sw"], P["d"], f)
             delta = P["d"]
         self._check(L.b200q_add_rmsnorm(P["x"], delta, self.out_norm.data_ptr(), P["hn"], h, m, s.eps, st),

@@ -179,12 +179,13 @@ class PagedKVCache:
         return self.table.data_ptr() + 4 * layer * self.batch * self.pages_per_seq
 
     def attention(self, layer: int, q: int, k: int, v: int, pos: int, n_heads: int, theta: float, out: int | None,
-                  xq: int | None, act_mode: int, stream: int, n_tokens: int = 1) -> None:
+                  xq: int | None, act_mode: int, stream: int, n_tokens: int = 1, q_stride: int = 0,
+                  kv_stride: int = 0) -> None:
         """RoPE + append + attention of layer `layer` for n_tokens
         consecutive tokens of every sequence, token t at pos + t attending
         over 0..pos + t (device pointers; q [batch][n_tokens][n_heads][128], k
-        and v [batch][n_tokens][kv_heads][128]); the pages of those positions
-        must have been ensured."""
+        and v [batch][n_tokens][kv_heads][128], or rows q_stride / kv_stride
+        floats apart); the pages of those positions must have been ensured."""
         if self.dev.type != "cuda":
             raise RuntimeError("the paged attention runs on a CUDA device")
         L = _native.lib()
@@ -193,7 +194,7 @@ class PagedKVCache:
         _native.check(L.b200q_rope_attention_decode_paged(
             q, k, v, self.batch, n_tokens, n_heads, self.kv_heads, self.head_dim, pos, theta, self.kv_mode, self.k.data_ptr(),
             self.v.data_ptr(), ks, vs, self.n_slots, self.page_size, self.table_ptr(layer), self.pages_per_seq, out,
-            xq, act_mode, stream), "paged attention")
+            xq, act_mode, q_stride, kv_stride, stream), "paged attention")
 
     def rows(self, layer: int, seq: int, kv_head: int, p0: int, p1: int):
         """Stored (codes or fp16 values, scales or None) of positions p0..p1-1

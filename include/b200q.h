@@ -305,11 +305,14 @@ B200Q_API int b200q_rope_attention_decode(const float* q, const float* k, const 
  * One launch for the rows a speculative verify feeds through the stack at
  * once, in place of n_tokens single-token steps (the sequential verify loop
  * of cpu_speculative_decode.py:740-769). k and v 16-byte aligned;
- * pos0 + n_tokens <= max_ctx. */
+ * pos0 + n_tokens <= max_ctx. q_stride / kv_stride: floats between
+ * consecutive q / k and v rows (0: packed, n_heads * 128 / n_kv_heads * 128);
+ * rows of one q|k|v projection output pass its row length for both. */
 B200Q_API int b200q_rope_attention_decode_tokens(const float* q, const float* k, const float* v, int batch,
                                                  int n_tokens, int n_heads, int n_kv_heads, int head_dim, int pos0,
                                                  float theta, void* k_cache, void* v_cache, int max_ctx, float* out,
-                                                 void* xq, int act_mode, void* stream);
+                                                 void* xq, int act_mode, long long q_stride, long long kv_stride,
+                                                 void* stream);
 
 /* The same over a paged KV cache: the reference's PagedKVStore
  * (model_graph.cpp:1413-1576: pages of page_size positions, allocated per
@@ -330,15 +333,19 @@ B200Q_API int b200q_rope_attention_decode_tokens(const float* q, const float* k,
  * or no page at pos, is recorded as device status bit 2 (value 2) and the
  * position is masked. pos + n_tokens <= pages_per_seq * page_size; pools 16-byte
  * aligned. n_tokens consecutive tokens per sequence as in
- * b200q_rope_attention_decode_tokens (1 for a decode step); the pages of
- * pos .. pos + n_tokens - 1 assigned before the call. */
+ * b200q_rope_attention_decode_tokens (1 for a decode step), with its row
+ * strides; the pages of pos .. pos + n_tokens - 1 assigned before the call. */
 B200Q_API int b200q_rope_attention_decode_paged(const float* q, const float* k, const float* v, int batch,
                                                 int n_tokens, int n_heads, int n_kv_heads, int head_dim, int pos,
                                                 float theta, int kv_mode, void* k_pages, void* v_pages,
                                                 float* k_scales, float* v_scales, int n_slots, int page_size,
                                                 const int* page_table, int pages_per_seq, float* out, void* xq,
-                                                int act_mode, void* stream);
+                                                int act_mode, long long q_stride, long long kv_stride, void* stream);
 B200Q_API int b200q_swiglu_q(const float* gate, const float* up, void* xq, int act_mode, int n, void* stream);
+/* out[r][j] = silu(gate_up[r][j]) * gate_up[r][n + j] for `rows` rows of one
+ * gate|up projection output ([gate n | up n] per row): the SwiGLU step of a
+ * multi-token pass (QM:2380-2412). */
+B200Q_API int b200q_swiglu_rows(const float* gate_up, float* out, int rows, int n, void* stream);
 
 /* y = alpha * (W x) + beta * y for m activation rows given as codes written
  * by the *_q steps above (row pitch b200q_xq_row_bytes(k, act_mode)); y rows

@@ -130,7 +130,7 @@ def test_f16_pages_match_contiguous_cache(H, KV, act, n_tok):
             _native.check(L.b200q_rope_attention_decode_tokens(q.data_ptr(), k.data_ptr(), v.data_ptr(), B, n_tok, H,
                                                                KV, HD, pos, theta, contig_k.data_ptr(),
                                                                contig_v.data_ptr(), max_ctx, out.data_ptr(), xp, act,
-                                                               _st()), "contiguous tokens")
+                                                               0, 0, _st()), "contiguous tokens")
         torch.cuda.synchronize()
         outs.append(out.cpu().numpy())
         xqs.append(xq.cpu().numpy())
@@ -204,22 +204,24 @@ def test_paged_entry_rejects_bad_arguments():
     p, fp, tp = buf.data_ptr(), f.data_ptr(), tbl.data_ptr()
     st = _st()
     args = dict(q=fp, k=fp, v=fp, batch=1, H=8, KV=8, hd=HD, pos=10, theta=1e4, mode=_native.KV_Q8, kp=p, vp=p,
-                ks=fp, vs=fp, n_slots=1, page=64, table=tp, pps=1, out=fp, xq=None, act=0)
+                ks=fp, vs=fp, n_slots=1, page=64, table=tp, pps=1, out=fp, xq=None, act=0, qs=0, kvs=0)
 
     def call(**over):
         a = dict(args, **over)
         return L.b200q_rope_attention_decode_paged(a["q"], a["k"], a["v"], a["batch"], 1, a["H"], a["KV"], a["hd"],
                                                    a["pos"], a["theta"], a["mode"], a["kp"], a["vp"], a["ks"],
                                                    a["vs"], a["n_slots"], a["page"], a["table"], a["pps"], a["out"],
-                                                   a["xq"], a["act"], st)
+                                                   a["xq"], a["act"], a["qs"], a["kvs"], st)
 
     assert call(ks=None) == -1           # Q8 without scales
     assert call(mode=5) == -1            # unknown storage mode
     assert call(table=None) == -1
     assert call(pos=64) == -3            # past pages_per_seq * page_size
     assert call(hd=64) == -3
-    assert call(kp=p + 2) == -4          # Q8 pools 4-byte aligned
-    assert call(mode=_native.KV_F16, ks=None, vs=None, kp=p + 4) == -4  # fp16 pools 8-byte aligned
+    assert call(kp=p + 2) == -4          # pools 16-byte aligned
+    assert call(qs=8 * HD - 4) == -3     # q rows overlapping
+    assert call(kvs=8 * HD + 2) == -4    # k / v rows not 16-byte aligned
+    assert call(mode=_native.KV_F16, ks=None, vs=None, kp=p + 4) == -4  # fp16 pools too
     torch.cuda.synchronize()
 
 
