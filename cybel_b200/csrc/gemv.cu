@@ -84,7 +84,9 @@ int make_plan(int qtype, int dig, int k, int n, int MR, int num_sms, Plan& pl, b
     const int nb = k / f.elems;
     const long long rb = static_cast<long long>(nb) * f.bytes;
     const int S = (nb + f.blocks_per_slice - 1) / f.blocks_per_slice;
-    int max_warps = (dig == 1 && MR == 1) ? 16 : 12;  // kGemvWarps in gemv.cuh
+    // kGemvWarps in gemv.cuh; x16 takes 14 only for tall matrices (measured:
+    // 14 warps were faster from ~8K rows, slower on 4096-row matrices)
+    int max_warps = (dig == 1 && MR == 1) ? 16 : ((dig == 2 && MR == 1 && n >= 8192) ? 14 : 12);
     if (S > max_warps) return B200Q_ESHAPE;
     // B200Q_GEMV_WARPS caps the warps (never below one per k-slice).
     static const int warps_cap = env_int("B200Q_GEMV_WARPS", 0);

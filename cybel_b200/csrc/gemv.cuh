@@ -37,10 +37,11 @@ namespace b200q {
 
 // Consumer warps per CTA (one more warp is the producer). With 17 warps a
 // thread may hold up to 96 registers (each SM sub-partition runs 5 warps);
-// with 13, up to 128 -- the heavier instantiations (x16, several activation
-// rows) take 12 consumer warps.
+// with 13-15, up to 128 -- the heavier instantiations take fewer: x16 up to
+// 14 (the planner uses 14 for matrices of >= 8192 rows, 12 below: measured),
+// several activation rows 12.
 template <int DIG, int MR>
-constexpr int kGemvWarps = (DIG == 1 && MR == 1) ? 16 : 12;
+constexpr int kGemvWarps = (DIG == 1 && MR == 1) ? 16 : ((DIG == 2 && MR == 1) ? 14 : 12);
 constexpr int kGemvMaxWarps = 16;
 // Rows a consumer warp carries per iteration (independent chains, and the
 // loop and reduction overhead shared between them).

@@ -35,9 +35,12 @@ def _rows_per_iter(qt, act, mr):
     return 2 if mr == 1 else 1
 
 
-def _max_warps(act, mr):
-    """Consumer warps of the kernel instance (kGemvWarps in gemv.cuh)."""
-    return 16 if (act == 1 and mr == 1) else 12
+def _max_warps(act, mr, n=0):
+    """Consumer warps the planner allows (kGemvWarps in gemv.cuh; x16 single
+    rows take 14 for matrices of >= 8192 rows)."""
+    if act == 1 and mr == 1:
+        return 16
+    return 14 if (act == 2 and mr == 1 and n >= 8192) else 12
 
 
 def _check(qt, act, k, n, mr, p):
@@ -46,7 +49,7 @@ def _check(qt, act, k, n, mr, p):
     rb = nb * nbytes
     assert p["row_bytes"] == rb
     assert p["S"] == -(-nb // BLOCKS_PER_SLICE[qt])
-    assert p["G"] * p["SW"] == p["WR"] and p["S"] * p["WR"] <= _max_warps(act, mr)
+    assert p["G"] * p["SW"] == p["WR"] and p["S"] * p["WR"] <= _max_warps(act, mr, n)
     assert p["threads"] == (p["S"] * p["WR"] + 1) * 32  # consumer warps and the producer warp
     assert p["grid"] == min(SMS, -(-n // 4))
     assert p["rows_cta"] * p["grid"] >= n
@@ -87,7 +90,7 @@ def _no_plan_expected(qt, act, k, n, mr, fq):
     nb = k // elems
     rb = nb * nbytes
     S = -(-nb // BLOCKS_PER_SLICE[qt])
-    if S > _max_warps(act, mr):
+    if S > _max_warps(act, mr, n):
         return True
     r4 = qt in (112, 114)
     U = _rows_per_iter(qt, act, mr)
@@ -109,7 +112,7 @@ def _no_plan_expected(qt, act, k, n, mr, fq):
     NS = min(48, room // stride if room > 0 else 0)
     if NS < 2:
         return True
-    walkers = max(1, _max_warps(act, mr) // S)
+    walkers = max(1, _max_warps(act, mr, n) // S)
     SW = max(1, min(walkers, -(-R // U)))
     G = min(max(1, walkers // SW), NS)
     NS -= NS % G
