@@ -97,7 +97,7 @@ def _no_plan_expected(qt, act, k, n, mr, fq):
     n_quads = -(-n // 4)
     grid = min(SMS, n_quads)
     rows_cta = 4 * (-(-n_quads // grid))
-    R = U * max(1, (32 * 1024 + U * rb // 2) // (U * rb))
+    R = U * max(1, (48 * 1024 + U * rb // 2) // (U * rb))
     R = min(R, max(U, -(-rows_cta // U) * U))
     if r4:
         R = -(-R // 4) * 4
