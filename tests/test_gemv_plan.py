@@ -108,7 +108,8 @@ def _no_plan_expected(qt, act, k, n, mr, fq):
     stride = -(-(R * rb + 48) // 128) * 128
     kp = k + 16 * (-(-k // 256))
     x_bytes = mr * (-(-(act * kp + (k // 32) * 8) // 16) * 16)
-    room = 220 * 1024 - x_bytes - (48 * 16 + 20 + 16 * 4 + rows_cta * mr * S * 4 + 64)
+    budget = (220 if k >= 8192 else 200) * 1024  # ring budget by row length
+    room = budget - x_bytes - (48 * 16 + 20 + 16 * 4 + rows_cta * mr * S * 4 + 64)
     NS = min(48, room // stride if room > 0 else 0)
     if NS < 2:
         return True
