@@ -115,6 +115,9 @@ def _no_plan_expected(qt, act, k, n, mr, fq):
         return True
     walkers = max(1, _max_warps(act, mr, n) // S)
     SW = max(1, min(walkers, -(-R // U)))
+    if act == 1 and k >= 8192:  # x8, long rows: SW divides the walkers
+        while SW > 1 and walkers % SW:
+            SW -= 1
     G = min(max(1, walkers // SW), NS)
     NS -= NS % G
     nx = -(-(mr * k * 4) // stride) if fq else 0
