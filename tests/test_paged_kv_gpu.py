@@ -225,11 +225,13 @@ def test_paged_entry_rejects_bad_arguments():
     torch.cuda.synchronize()
 
 
+@pytest.mark.parametrize("pos0", [90, 62])
 @pytest.mark.parametrize("n_tok", [3, 5])
-def test_q8_multi_token_pages_not_aligned_to_chunks(n_tok):
+def test_q8_multi_token_pages_not_aligned_to_chunks(n_tok, pos0):
     """Several tokens per sequence in one call over Q8 pages of 48 positions
-    (pages and 64-position attention chunks cross each other): each token
-    attends causally over the cache and the tokens before it; the rows the
+    (pages and 64-position attention chunks cross each other; from pos0 = 62
+    the call's tokens span one or two chunks): each token attends causally
+    over the cache and the tokens before it; the rows the
     call appends are the restated quantizer's codes (values bit-exact) and
     every token's output matches the restated attention over the stored
     rows, within 1e-4 of max |ref|."""
@@ -240,7 +242,8 @@ def test_q8_multi_token_pages_not_aligned_to_chunks(n_tok):
     from oracle.paged_kv_ref import PagedKVStoreRef, q8_rows, rope
 
     B, H, KV, P, theta = 2, 16, 4, 48, 1.0
-    pos0 = 90  # the call covers positions 90 .. 90 + n_tok - 1 (pages 1 and 2, chunk 1)
+    # pos0 = 90: the call covers pages 1 and 2 inside chunk 1; pos0 = 62: its
+    # tokens straddle the first 64-position chunk boundary (1 or 2 chunks each)
     cache = PagedKVCache(layers=1, kv_heads=KV, max_seq=192, batch=B, page_size=P, q8=True)
     rng = np.random.default_rng(40 + n_tok)
     out1 = torch.empty((B, H, HD), device="cuda")
