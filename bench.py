@@ -73,33 +73,89 @@ def _traffic_per_launch():
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """SM clock and throttle reasons sampled during the timed region: through
+    NVML in-process (a sample every ~0.5 ms, so even a region of a few
+    milliseconds is covered), else nvidia-smi every 200 ms."""
 
     FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    # NVML clocks-event reason bits
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, device: int):
         self.device = device
-        self.samples = []
+        self.samples = []  # (sm_mhz, max_mhz, reasons set)
         self._stop = threading.Event()
         self._t = None
+        self._nvml = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            try:
+                uuid = str(torch.cuda.get_device_properties(device).uuid)
+                h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            get_r = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self._nvml = (pynvml, h, get_r, pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self.source = "nvml"
+        except Exception:
+            self._nvml = None
+            self.source = "nvidia-smi"
+
+    def _sample_nvml(self):
+        p, h, get_r, mx = self._nvml
+        sm = p.nvmlDeviceGetClockInfo(h, p.NVML_CLOCK_SM)
+        bits = int(get_r(h))
+        return float(sm), float(mx), {n for n, b in self.REASON_BITS.items() if bits & b}
+
+    def _sample_smi(self):
+        out = subprocess.run(
+            ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
+            capture_output=True, text=True, timeout=5,
+        ).stdout.strip()
+        if not out:
+            return None
+        f = [x.strip() for x in out.split(",")]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm = float(f[1]) if f[1].replace(".", "").isdigit() else None
+        mx = float(f[2]) if f[2].replace(".", "").isdigit() else None
+        return sm, mx, {names[i] for i in range(4) if len(f) > 5 + i and f[5 + i] == "Active"}
+
+    def sample_now(self):
+        try:
+            smp = self._sample_nvml() if self._nvml else None
+            if smp is not None:
+                self.samples.append(smp)
+        except Exception:
+            pass
 
     def _run(self):
         while not self._stop.is_set():
             try:
-                out = subprocess.run(
-                    ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits"],
-                    capture_output=True, text=True, timeout=5,
-                ).stdout.strip()
-                if out:
-                    self.samples.append([s.strip() for s in out.split(",")])
+                smp = self._sample_nvml() if self._nvml else self._sample_smi()
+                if smp is not None:
+                    self.samples.append(smp)
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(0.0005 if self._nvml else 0.2)
 
     def __enter__(self):
         self._t = threading.Thread(target=self._run, daemon=True)
         self._t.start()
+        t0 = time.perf_counter()  # sampling is running before the timed region opens
+        while not self.samples and time.perf_counter() - t0 < 2.0:
+            time.sleep(0.0005)
         return self
+
+    def mark(self):
+        """The timed region opens: keep only the samples taken from here on
+        (the last earlier one stays as a fallback for a region shorter than
+        one sample)."""
+        self._before = self.samples[-1:] if self.samples else []
+        self.samples = []
 
     def __exit__(self, *a):
         self._stop.set()
@@ -107,17 +163,19 @@ class ClockSampler:
             self._t.join(timeout=10)
 
     def summary(self):
+        if not self.samples and getattr(self, "_before", None):
+            self.samples = list(self._before)
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 5 + i and s[5 + i] == "Active"})
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "source": self.source}
+        sm = [s[0] for s in self.samples if s[0] is not None]
+        mx = [s[1] for s in self.samples if s[1] is not None]
+        reasons = sorted(set().union(*(s[2] for s in self.samples)))
         return {
             "sm_mhz": statistics.median(sm) if sm else None,
             "sm_max_mhz": max(mx) if mx else None,
             "reasons": reasons,
             "samples": len(self.samples),
+            "source": self.source,
         }
 
 
@@ -844,10 +902,12 @@ def run_ours(args, ws, rank, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier()
+        clk.mark()
         e0.record(st)
         for _ in range(args.steps):
             graph.replay()
         e1.record(st)
+        clk.sample_now()  # the queued replays are still running on the device
         barrier()
     ms_total = e0.elapsed_time(e1)
     # One matvec alone (events around a single eager call, same stream).
