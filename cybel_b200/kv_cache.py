@@ -141,7 +141,10 @@ class PagedKVCache:
             raise ValueError("slot outside the pool")
         if slot in self._free:
             self._free.remove(slot)
+        old = int(self.table_host[layer, seq, page])
         self.table_host[layer, seq, page] = slot
+        if old >= 0 and old != slot and not (self.table_host == old).any():
+            self._free.append(old)  # the page it replaced is referenced nowhere else
 
     def sync_table(self) -> None:
         """Copy the host page table to the device (current stream)."""

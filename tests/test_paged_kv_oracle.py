@@ -100,3 +100,13 @@ def test_page_bookkeeping_on_host():
     assert c.pages_in_use == 9 and int(c.table[1, 0, 2]) == free
     with pytest.raises(MemoryError):
         c.ensure(32)
+    # Replacing a page: the old slot returns to the pool unless another
+    # entry still uses it (a page shared between two sequences).
+    shared = int(c.table_host[0, 0, 0])
+    c.assign(0, 1, 0, shared)  # sequence 1's own page 0 is freed
+    assert c.pages_in_use == 8
+    old = int(c.table_host[0, 0, 1])
+    c.assign(0, 0, 1, shared)
+    assert c.pages_in_use == 7 and old not in set(c.table_host[c.table_host >= 0].tolist())
+    c.assign(0, 0, 1, old)  # shared stays in use by (0, 0, 0) and (0, 1, 0)
+    assert c.pages_in_use == 8 and int(c.table_host[0, 1, 0]) == shared
