@@ -18,6 +18,7 @@ and call the asynchronous ``b200q_matmul`` on the current stream.
 from __future__ import annotations
 
 import ctypes
+import warnings
 from dataclasses import dataclass, field
 from typing import Iterable, Optional
 
@@ -204,7 +205,12 @@ class DeviceMatrix:
         import torch
 
         if not isinstance(data, torch.Tensor):
-            data = torch.from_numpy(np.ascontiguousarray(data, dtype=np.uint8))
+            arr = np.ascontiguousarray(data, dtype=np.uint8)
+            with warnings.catch_warnings():
+                # A read-only array (a memory-mapped GGUF file) is only read here:
+                # it is copied to the device just below.
+                warnings.simplefilter("ignore", UserWarning)
+                data = torch.from_numpy(arr)
         if data.device.type != "cuda":
             data = data.cuda()
         e, b = BLOCK_SPECS[qtype]
