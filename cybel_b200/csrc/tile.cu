@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(tile_threads(NP), 1)
     constexpr int kXWarp = NI + 1;      // activation chunks and B2 tiles
     constexpr int NSX = SM::NSX;
     constexpr int kFirstDeqWarp = first_deq_warp(NP);
-    constexpr int kRanges = 16 / DW;  // qs quarters per dequant thread
+    constexpr int kRanges = 2;  // qs quarters per dequant pass
     constexpr int kNS = SM::kNS;
     constexpr uint32_t kABase = SM::kABase;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM::kBars);
@@ -288,10 +288,10 @@ __global__ void __launch_bounds__(tile_threads(NP), 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < kNSW; ++i) {
             mbar_init(smem_addr(wfull + i), 1);
-            mbar_init(smem_addr(wempty + i), DW);
+            mbar_init(smem_addr(wempty + i), 4);  // the four warps of the block's dequant group
         }
         for (int i = 0; i < kNS; ++i) {
-            mbar_init(smem_addr(full + i), DW);
+            mbar_init(smem_addr(full + i), 4);
             mbar_init(smem_addr(empty + i), NI);
         }
         for (int i = 0; i < SM::NSX; ++i) {
@@ -389,72 +389,78 @@ __global__ void __launch_bounds__(tile_threads(NP), 1)
             if (!ok) *p.status = STATUS_TIMEOUT;
         }
     } else if (warp < kFirstDeqWarp + DW) {
-        // ---------------- dequantizers (warps NI+1 .. NI+DW) ----------------
-        // A warp reaches tensor-memory lanes 32 (warp % 4) .. + 31, so thread
-        // (t, h0) takes tile row t = 32 (warp % 4) + lane and, for each of its
-        // quarters h = h0 + u DW/4, qs bytes [32h, 32h+32) of each block:
-        // sub-block 2h (low nibbles) into slot columns 32h .. 32h+15,
-        // sub-block 2h+1 (high nibbles) into 32h+16 .. 32h+31 (two
-        // consecutive K elements per column). The last warp group also writes
-        // the block's mins tile A2 and d/dmin.
+        // ---------------- dequantizers (warps NI+2 .. NI+DW+1) ----------------
+        // Groups of four warps take alternate blocks (group g: blocks g,
+        // g + DW/4, ...), so one group's tensor-memory stores and barrier
+        // waits overlap the other's arithmetic. A warp reaches tensor-memory
+        // lanes 32 (warp % 4) .. + 31, so thread (t, g) takes tile row t =
+        // 32 (warp % 4) + lane of its group's blocks and all four quarters h
+        // of it, qs bytes [32h, 32h+32), kRanges per pass: sub-block 2h (low
+        // nibbles) into slot columns 32h .. 32h+15, sub-block 2h+1 (high
+        // nibbles) into 32h+16 .. 32h+31 (two consecutive K elements per
+        // column); then row t of the block's mins tile A2 and its d/dmin.
+        constexpr int kGroups = DW / 4;
+        constexpr int kPasses = 4 / kRanges;
         const int t = 32 * (warp & 3) + lane;
-        const int h0 = (warp - kFirstDeqWarp) >> 2;
-        const bool mins_group = h0 == DW / 4 - 1;
+        const int grp = (warp - kFirstDeqWarp) >> 2;
         const uint32_t lane_addr = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-        for (int bl = 0; bl < nblk && ok; ++bl) {
+        for (int bl = grp; bl < nblk && ok; bl += kGroups) {
             const int s = bl % kNS, ws = bl % kNSW, hb = bl % kNM;
             ok = mbar_wait_bounded(smem_addr(empty + s), ((bl / kNS) & 1) ^ 1) &&
-                 mbar_wait_bounded(smem_addr(wfull + ws), (bl / kNSW) & 1);
-            if (ok && mins_group) ok = mbar_wait_bounded(smem_addr(dfree + hb), ((bl / kNM) & 1) ^ 1);
+                 mbar_wait_bounded(smem_addr(wfull + ws), (bl / kNSW) & 1) &&
+                 mbar_wait_bounded(smem_addr(dfree + hb), ((bl / kNM) & 1) ^ 1);
             ok = __all_sync(0xFFFFFFFFu, ok);  // warp-uniform: the tensor-memory store is warp-collective
             if (!ok) break;
             // Row t of block column bl (quantized_matmul.cpp:1323-1375 layout):
             // d, dmin (fp16), 12 scale bytes, 128 nibble bytes.
             const uint32_t blk = smem_addr(smem + SM::kPacked + ws * kPackedBytes + t * kBlockBytes);
             const uint4 hd = lds128(blk);
-            // Both quarters' bytes first, then their fp16 products, then the
-            // tensor-memory stores, so the quarters' load and arithmetic
-            // latencies overlap.
-            uint32_t qw[kRanges][8];
 #pragma unroll
-            for (int u = 0; u < kRanges; ++u) {
-                const int h = h0 + u * (DW / 4);
-                const uint4 qa = lds128(blk + 16u + 32u * h);
-                const uint4 qb = lds128(blk + 32u + 32u * h);
-                qw[u][0] = qa.x; qw[u][1] = qa.y; qw[u][2] = qa.z; qw[u][3] = qa.w;
-                qw[u][4] = qb.x; qw[u][5] = qb.y; qw[u][6] = qb.z; qw[u][7] = qb.w;
-            }
-            uint32_t r[kRanges][32];
+            for (int pass = 0; pass < kPasses; ++pass) {
+                // A pass's quarters' bytes first, then their fp16 products, then
+                // the tensor-memory stores, so the quarters' load and arithmetic
+                // latencies overlap.
+                uint32_t qw[kRanges][8];
 #pragma unroll
-            for (int u = 0; u < kRanges; ++u) {
-                const int h = h0 + u * (DW / 4);
-                __half2 sc2[2], off2[2];
+                for (int u = 0; u < kRanges; ++u) {
+                    const int h = pass + u * kPasses;
+                    const uint4 qa = lds128(blk + 16u + 32u * h);
+                    const uint4 qb = lds128(blk + 32u + 32u * h);
+                    qw[u][0] = qa.x; qw[u][1] = qa.y; qw[u][2] = qa.z; qw[u][3] = qa.w;
+                    qw[u][4] = qb.x; qw[u][5] = qb.y; qw[u][6] = qb.z; qw[u][7] = qb.w;
+                }
+                uint32_t r[kRanges][32];
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {  // sub-block j = 2h + half
-                    const int j = 2 * h + half;
-                    const uint32_t sb_lo = (j < 4 ? hd.y : hd.w) >> (8 * (j & 3));
-                    const uint32_t sc = j < 4 ? (sb_lo & 63u) : ((sb_lo & 15u) | ((hd.y >> (8 * (j & 3)) >> 2) & 0x30u));
-                    // low nibbles: (1024 + q) sc - 1024 sc; high: (1024 + 16 q) sc/16 - 64 sc
-                    sc2[half] = __float2half2_rn(half ? static_cast<float>(sc) * 0.0625f : static_cast<float>(sc));
-                    off2[half] = __float2half2_rn(-static_cast<float>(sc) * (half ? 64.0f : 1024.0f));
+                for (int u = 0; u < kRanges; ++u) {
+                    const int h = pass + u * kPasses;
+                    __half2 sc2[2], off2[2];
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {  // sub-block j = 2h + half
+                        const int j = 2 * h + half;
+                        const uint32_t sb_lo = (j < 4 ? hd.y : hd.w) >> (8 * (j & 3));
+                        const uint32_t sc = j < 4 ? (sb_lo & 63u) : ((sb_lo & 15u) | ((hd.y >> (8 * (j & 3)) >> 2) & 0x30u));
+                        // low nibbles: (1024 + q) sc - 1024 sc; high: (1024 + 16 q) sc/16 - 64 sc
+                        sc2[half] = __float2half2_rn(half ? static_cast<float>(sc) * 0.0625f : static_cast<float>(sc));
+                        off2[half] = __float2half2_rn(-static_cast<float>(sc) * (half ? 64.0f : 1024.0f));
+                    }
+#pragma unroll
+                    for (int w8 = 0; w8 < 8; ++w8) {  // bytes 4 w8 .. 4 w8 + 3: elements e0..e3 of both sub-blocks
+                        // Column pairs hold elements (e0, e2) and (e1, e3); the
+                        // activation chunks use the same order.
+                        const uint32_t w = qw[u][w8], w_8 = qw[u][w8] >> 8;
+                        r[u][2 * w8] = nib_times((w & 0x000F000Fu) | 0x64006400u, sc2[0], off2[0]);
+                        r[u][2 * w8 + 1] = nib_times((w_8 & 0x000F000Fu) | 0x64006400u, sc2[0], off2[0]);
+                        r[u][16 + 2 * w8] = nib_times((w & 0x00F000F0u) | 0x64006400u, sc2[1], off2[1]);
+                        r[u][16 + 2 * w8 + 1] = nib_times((w_8 & 0x00F000F0u) | 0x64006400u, sc2[1], off2[1]);
+                    }
                 }
 #pragma unroll
-                for (int w8 = 0; w8 < 8; ++w8) {  // bytes 4 w8 .. 4 w8 + 3: elements e0..e3 of both sub-blocks
-                    // Column pairs hold elements (e0, e2) and (e1, e3); the
-                    // activation chunks use the same order.
-                    const uint32_t w = qw[u][w8], w_8 = qw[u][w8] >> 8;
-                    r[u][2 * w8] = nib_times((w & 0x000F000Fu) | 0x64006400u, sc2[0], off2[0]);
-                    r[u][2 * w8 + 1] = nib_times((w_8 & 0x000F000Fu) | 0x64006400u, sc2[0], off2[0]);
-                    r[u][16 + 2 * w8] = nib_times((w & 0x00F000F0u) | 0x64006400u, sc2[1], off2[1]);
-                    r[u][16 + 2 * w8 + 1] = nib_times((w_8 & 0x00F000F0u) | 0x64006400u, sc2[1], off2[1]);
+                for (int u = 0; u < kRanges; ++u) {
+                    const int h = pass + u * kPasses;
+                    tmem_st32(tmem_base + lane_addr + kABase + static_cast<uint32_t>(s) * kAColsPerChunk + 32u * h, r[u]);
                 }
             }
-#pragma unroll
-            for (int u = 0; u < kRanges; ++u) {
-                const int h = h0 + u * (DW / 4);
-                tmem_st32(tmem_base + lane_addr + kABase + static_cast<uint32_t>(s) * kAColsPerChunk + 32u * h, r[u]);
-            }
-            if (mins_group) {
+            {
                 // The block's mins tile A2 (row t: mn_0..7, twice, as fp16)
                 // and its d / dmin, into buffer bl % kNM (released by the
                 // epilogue of block bl - kNM, waited for above).
@@ -489,7 +495,7 @@ __global__ void __launch_bounds__(tile_threads(NP), 1)
             if (lane == 0) {
                 mbar_arrive(smem_addr(full + s));
                 mbar_arrive(smem_addr(wempty + ws));
-                if (mins_group) mbar_arrive(smem_addr(mready + hb));
+                mbar_arrive(smem_addr(mready + hb));
             }
         }
         if (!ok) *p.status = STATUS_TIMEOUT;
